@@ -1,0 +1,320 @@
+// Persistent, warp-specialised grouped GEMM for sm_100a (tcgen05 + TMEM + TMA).
+//
+//   out[row_map(r), n] = epilogue( sum_k A[r, k] * B[expert(seg), n, k] )
+//
+// A is a row-major [rows_total, K] activation buffer whose rows are grouped in
+// "segments" (one segment = consecutive rows that share an expert weight, e.g.
+// the rows that source rank s sent to local expert e).  B is the stacked
+// expert weight tensor [E * N, K] (K-major, i.e. nn.Linear layout).
+//
+// Roles inside one CTA (192 threads, one CTA per SM):
+//   warp 0      TMA producer: streams 128-row A tiles and BN-row B tiles into
+//               an S-stage shared-memory ring (128-byte swizzle, no multicast).
+//   warp 1      owns the TMEM allocation; one elected lane issues tcgen05.mma
+//               (M=128, N=BN, fp32 accumulators in TMEM, two accumulator
+//               buffers so the epilogue of tile i overlaps the MMAs of i+1).
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator rows, bias, activation,
+//               optional per-row scale, and vector stores to a local or
+//               NVLink-peer output pointer chosen per segment.
+//
+// Reference behaviour being replaced: the per-expert index_select / two
+// torch matmuls / index_copy_ loop of rlccl/transport/reference_full_moe.py:271-280.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "sm100_ptx.cuh"
+
+namespace raiccl {
+
+template <int BN, bool TF32>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int ELEM = TF32 ? 4 : 2;
+  static constexpr int BK = 128 / ELEM;           // one 128-byte swizzle atom of K
+  static constexpr int UK = 32 / ELEM;            // K per tcgen05.mma (32 bytes)
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM_BUDGET = 200 * 1024;
+  static constexpr int STAGES_RAW = SMEM_BUDGET / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int TMEM_COLS = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128 : (2 * BN) <= 256 ? 256 : 512;
+  static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, BM, BN);
+  static constexpr int SMEM_TOTAL = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/;
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+  static_assert(STAGES >= 2, "pipeline needs two stages");
+};
+
+__device__ __forceinline__ float apply_act(float x, Act a) {
+  switch (a) {
+    case Act::kRelu: return x > 0.f ? x : 0.f;
+    case Act::kGelu: return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+    case Act::kSilu: return x / (1.f + __expf(-x));
+    default: return x;
+  }
+}
+
+__device__ __forceinline__ int find_segment(const int* prefix, int nseg, int tile) {
+  int lo = 0, hi = nseg - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (__ldg(prefix + mid) <= tile) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+template <int BN, bool TF32, Act ACT, typename OutT>
+__global__ void __launch_bounds__(192, 1)
+grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                    const __grid_constant__ CUtensorMap tmap_b,
+                    GroupedGemmParams p) {
+  using C = GemmCfg<BN, TF32>;
+  constexpr int kKernelId = 100 + BN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* stage_base = smem;
+  uint64_t* bars = (uint64_t*)(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + C::STAGES;
+  uint64_t* tfull_bar = bars + 2 * C::STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = (uint32_t*)(drain_bar + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tfull_bar[a], 1); mbar_init(&tempty_bar[a], 4); }
+    mbar_init(drain_bar, 1);
+    fence_mbarrier_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) { tmem_alloc(tmem_slot, C::TMEM_COLS); tmem_relinquish(); }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_tiles = __ldg(p.tile_prefix + p.num_segs);
+  const int nblocks = p.N / BN;
+  const int kblocks = (p.K + C::BK - 1) / C::BK;
+  const uint64_t lim = p.timeout_ns;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one_sync()) {
+      int stage = 0; uint32_t phase = 0;
+      for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+        const int s = find_segment(p.tile_prefix, p.num_segs, t);
+        const GemmSegment seg = p.segs[s];
+        const int local = t - __ldg(p.tile_prefix + s);
+        const int mb = local / nblocks, nb = local % nblocks;
+        const int arow = seg.a_row0 + mb * C::BM;
+        const int brow = seg.expert * p.N + nb * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, p.status, kKernelId, lim)) { ok = false; break; }
+          uint8_t* sa = stage_base + stage * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+          tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * C::BK, arow);
+          tma_load_2d(sa + C::A_BYTES, &tmap_b, &full_bar[stage], kb * C::BK, brow);
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one_sync()) {
+      int stage = 0; uint32_t phase = 0; int iter = 0;
+      for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++iter) {
+        const int acc = iter & 1;
+        const uint32_t acc_phase = (iter >> 1) & 1;
+        if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1u, p.status, kKernelId, lim)) break;
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(&full_bar[stage], phase, p.status, kKernelId, lim)) { ok = false; break; }
+          tc_fence_after_sync();
+          const uint32_t a_addr = smem_u32(stage_base + stage * C::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < C::BK / C::UK; ++k) {
+            const uint64_t ad = umma_desc_k_sw128(a_addr + k * 32);
+            const uint64_t bd = umma_desc_k_sw128(b_addr + k * 32);
+            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            if (TF32) umma_tf32(d_tmem, ad, bd, C::IDESC, accum);
+            else umma_f16(d_tmem, ad, bd, C::IDESC, accum);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);
+      }
+      // Drain: every MMA issued above has completed before TMEM is freed.
+      umma_commit(drain_bar);
+      mbar_wait_bounded(drain_bar, 0, p.status, kKernelId, lim);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int iter = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++iter) {
+      const int acc = iter & 1;
+      const uint32_t acc_phase = (iter >> 1) & 1;
+      const int s = find_segment(p.tile_prefix, p.num_segs, t);
+      const GemmSegment seg = p.segs[s];
+      const int local = t - __ldg(p.tile_prefix + s);
+      const int mb = local / nblocks, nb = local % nblocks;
+      if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.status, kKernelId, lim)) break;
+      tc_fence_after_sync();
+      const int r_local = mb * C::BM + row_in_tile;
+      const bool valid = r_local < seg.rows;
+      const int arow = seg.a_row0 + r_local;
+      long long orow = 0;
+      float scale = 1.f;
+      if (valid) {
+        orow = p.row_map ? (long long)__ldg(p.row_map + arow) : (long long)(seg.out_row0 + r_local);
+        if (p.row_scale) scale = __ldg(p.row_scale + arow);
+      }
+      OutT* out = (OutT*)p.out_ptrs[seg.out_slot];
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      const float* bias = p.bias ? p.bias + (long long)seg.expert * p.N + nb * BN : nullptr;
+      if constexpr (ACT == Act::kSwiGLU) {
+        // Tile columns [0, BN/2) hold gate features, [BN/2, BN) the matching up features.
+        constexpr int HALF = BN / 2;
+        static_assert(HALF % 16 == 0, "SwiGLU tile needs BN multiple of 32");
+#pragma unroll 1
+        for (int c = 0; c < HALF; c += 16) {
+          uint32_t g[16], u[16];
+          tmem_ld16(t_row + c, g);
+          tmem_ld16(t_row + HALF + c, u);
+          tmem_ld_wait();
+          if (valid) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float gv = __uint_as_float(g[j]) + (bias ? __ldg(bias + c + j) : 0.f);
+              float uv = __uint_as_float(u[j]) + (bias ? __ldg(bias + HALF + c + j) : 0.f);
+              v[j] = (gv / (1.f + __expf(-gv))) * uv * scale;
+            }
+            OutT* dst = out + orow * p.ldo + nb * HALF + c;
+            if constexpr (sizeof(OutT) == 4) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4)
+                *(float4*)(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; j += 8) {
+                uint4 w;
+                __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
+                __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
+                __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+                w.x = *(uint32_t*)&h0; w.y = *(uint32_t*)&h1; w.z = *(uint32_t*)&h2; w.w = *(uint32_t*)&h3;
+                *(uint4*)(dst + j) = w;
+              }
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(t_row + c, r);
+          tmem_ld_wait();
+          if (valid) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float x = __uint_as_float(r[j]) + (bias ? __ldg(bias + c + j) : 0.f);
+              v[j] = apply_act(x, ACT) * scale;
+            }
+            OutT* dst = out + orow * p.ldo + nb * BN + c;
+            if constexpr (sizeof(OutT) == 4) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4)
+                *(float4*)(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; j += 8) {
+                uint4 w;
+                __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
+                __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
+                __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+                w.x = *(uint32_t*)&h0; w.y = *(uint32_t*)&h1; w.z = *(uint32_t*)&h2; w.w = *(uint32_t*)&h3;
+                *(uint4*)(dst + j) = w;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------
+// Host-side dispatch over the compile-time tile width and activation.
+// ---------------------------------------------------------------------------
+template <int BN, bool TF32, Act ACT, typename OutT>
+inline void launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GroupedGemmParams& p,
+                       int grid, cudaStream_t stream) {
+  using C = GemmCfg<BN, TF32>;
+  auto kern = grouped_gemm_kernel<BN, TF32, ACT, OutT>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_TOTAL);
+    configured = true;
+  }
+  kern<<<grid, 192, C::SMEM_TOTAL, stream>>>(ta, tb, p);
+}
+
+template <bool TF32, Act ACT, typename OutT>
+inline void dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb,
+                        const GroupedGemmParams& p, int grid, cudaStream_t stream) {
+  switch (bn) {
+    case 16: if constexpr (ACT != Act::kSwiGLU) { launch_one<16, TF32, ACT, OutT>(ta, tb, p, grid, stream); return; } break;
+    case 32: launch_one<32, TF32, ACT, OutT>(ta, tb, p, grid, stream); return;
+    case 64: launch_one<64, TF32, ACT, OutT>(ta, tb, p, grid, stream); return;
+    case 128: launch_one<128, TF32, ACT, OutT>(ta, tb, p, grid, stream); return;
+    case 256: launch_one<256, TF32, ACT, OutT>(ta, tb, p, grid, stream); return;
+    default: break;
+  }
+  throw std::runtime_error("grouped_gemm: unsupported BN " + std::to_string(bn));
+}
+
+template <bool TF32, typename OutT>
+inline void dispatch_act(int act, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
+                         const GroupedGemmParams& p, int grid, cudaStream_t stream) {
+  switch ((Act)act) {
+    case Act::kNone: dispatch_bn<TF32, Act::kNone, OutT>(bn, ta, tb, p, grid, stream); return;
+    case Act::kRelu: dispatch_bn<TF32, Act::kRelu, OutT>(bn, ta, tb, p, grid, stream); return;
+    case Act::kGelu: dispatch_bn<TF32, Act::kGelu, OutT>(bn, ta, tb, p, grid, stream); return;
+    case Act::kSilu: dispatch_bn<TF32, Act::kSilu, OutT>(bn, ta, tb, p, grid, stream); return;
+    case Act::kSwiGLU: dispatch_bn<TF32, Act::kSwiGLU, OutT>(bn, ta, tb, p, grid, stream); return;
+  }
+  throw std::runtime_error("grouped_gemm: unknown activation");
+}
+
+
+}  // namespace raiccl

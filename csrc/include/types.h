@@ -1,0 +1,57 @@
+// Plain data types shared by device code and host C++ (no CUDA builtins here).
+#pragma once
+
+#include <cstdint>
+
+namespace raiccl {
+
+// ---------------------------------------------------------------------------
+// Status / error reporting (no __trap, no device assert anywhere).
+// ---------------------------------------------------------------------------
+enum StatusCode : int {
+  kOk = 0,
+  kTimeoutPipeline = 1,     // an intra-CTA mbarrier wait ran out (a bug)
+  kTimeoutPeerSignal = 2,   // a peer's ready/return signal never arrived
+  kTimeoutChunkFlag = 3,    // a router chunk flag never arrived
+  kBoundsViolation = 4,     // an index failed its capacity check
+  kBadConfig = 5,           // launch parameters inconsistent
+  kTimeoutPermit = 6,       // the scheduler permit for a descriptor never arrived
+  kSeqMismatch = 7,         // a signal carried an unexpected sequence number
+};
+
+struct DeviceStatus {
+  int code;        // first error code recorded (0 = ok)
+  int kernel_id;   // which kernel recorded it
+  int block;       // blockIdx.x of the recorder
+  int thread;      // threadIdx.x of the recorder
+  long long index; // offending index / waited-on slot
+  long long bound; // capacity or expected value
+};
+
+enum class Act : int { kNone = 0, kRelu = 1, kGelu = 2, kSilu = 3, kSwiGLU = 4 };
+
+struct GemmSegment {
+  int a_row0;    // first A row of the segment
+  int rows;      // valid rows in the segment (may be 0)
+  int expert;    // weight slice index into B / bias
+  int out_slot;  // index into GroupedGemmParams::out_ptrs (local or peer buffer)
+  int out_row0;  // first output row when no row map is given
+  int pad0, pad1, pad2;
+};
+
+struct GroupedGemmParams {
+  const GemmSegment* segs;   // [num_segs]
+  const int* tile_prefix;    // [num_segs + 1] cumulative tile counts (device computed)
+  int num_segs;
+  int N;                     // GEMM N (for SwiGLU: 2 * output width, interleaved per BN tile)
+  int K;
+  const float* bias;         // [E, N] or nullptr
+  const int* row_map;        // [rows_total] output row of each A row, or nullptr
+  const float* row_scale;    // [rows_total] multiplier applied after activation, or nullptr
+  void* const* out_ptrs;     // output base pointers (device or peer)
+  long long ldo;             // output row stride in elements
+  DeviceStatus* status;
+  unsigned long long timeout_ns;
+};
+
+}  // namespace raiccl

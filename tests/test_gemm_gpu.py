@@ -1,0 +1,125 @@
+"""Numerics of the tcgen05 grouped GEMM against a plain PyTorch fp32 reference."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _gg():
+    from revealaiccl_b200.ops import grouped_gemm as gg
+    return gg
+
+
+def _ref(A, B, segs_list, n, act, bias=None, row_scale=None, out_rows=None):
+    out = torch.zeros((out_rows, n if act != "swiglu" else n // 2), dtype=torch.float32, device=A.device)
+    for (a0, rows, e, _slot, o0) in segs_list:
+        x = A[a0:a0 + rows].float()
+        w = B[e * n:(e + 1) * n].float()
+        y = x @ w.t()
+        if bias is not None:
+            y = y + bias.view(-1, n)[e]
+        if act == "relu":
+            y = torch.relu(y)
+        elif act == "gelu":
+            y = torch.nn.functional.gelu(y)
+        elif act == "silu":
+            y = torch.nn.functional.silu(y)
+        if row_scale is not None:
+            y = y * row_scale[a0:a0 + rows, None]
+        out[o0:o0 + rows] = y
+    return out
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 128, 128), (256, 256, 512), (300, 64, 1024)])
+def test_bf16_dense_single_segment(m, n, k):
+    gg = _gg()
+    torch.manual_seed(0)
+    dev = torch.device("cuda")
+    A = torch.randn(m, k, device=dev).bfloat16()
+    B = torch.randn(n, k, device=dev).bfloat16() / k ** 0.5
+    segs_list = [(0, m, 0, 0, 0)]
+    segs = gg.make_segments(segs_list, dev)
+    out = torch.zeros(m, n, device=dev)
+    gg.grouped_gemm(A, B, segs, n=n, out=out, check=True)
+    ref = _ref(A, B, segs_list, n, "none", out_rows=m)
+    torch.testing.assert_close(out, ref, atol=2e-3, rtol=2e-3)
+
+
+def test_tf32_relu_partial_tiles():
+    gg = _gg()
+    torch.manual_seed(1)
+    dev = torch.device("cuda")
+    m, n, k = 300, 32, 2048
+    A = torch.randn(m, k, device=dev)
+    B = torch.randn(n, k, device=dev) / k ** 0.5
+    bias = torch.randn(n, device=dev) * 0.01
+    segs_list = [(0, m, 0, 0, 0)]
+    out = torch.zeros(m, n, device=dev)
+    gg.grouped_gemm(A, B, gg.make_segments(segs_list, dev), n=n, act="relu", bias=bias, out=out, check=True)
+    ref = _ref(A, B, segs_list, n, "relu", bias=bias, out_rows=m)
+    torch.testing.assert_close(out, ref, atol=5e-3, rtol=5e-3)
+
+
+def test_tf32_n16_k32():
+    gg = _gg()
+    torch.manual_seed(2)
+    dev = torch.device("cuda")
+    m, n, k = 200, 16, 32
+    A = torch.randn(m, k, device=dev)
+    B = torch.randn(2 * n, k, device=dev) / k ** 0.5
+    segs_list = [(0, 120, 1, 0, 0), (120, 80, 0, 0, 120)]
+    out = torch.zeros(m, n, device=dev)
+    gg.grouped_gemm(A, B, gg.make_segments(segs_list, dev), n=n, out=out, check=True)
+    ref = _ref(A, B, segs_list, n, "none", out_rows=m)
+    torch.testing.assert_close(out, ref, atol=3e-3, rtol=3e-3)
+
+
+def test_bf16_multi_segment_rowmap_scale_gelu_bf16_out():
+    gg = _gg()
+    torch.manual_seed(3)
+    dev = torch.device("cuda")
+    k, n, E = 256, 128, 3
+    seg_rows = [(0, 130, 2), (200, 0, 1), (200, 57, 0), (400, 256, 1)]
+    total = 700
+    A = torch.randn(total, k, device=dev).bfloat16()
+    B = (torch.randn(E * n, k, device=dev) / k ** 0.5).bfloat16()
+    bias = torch.randn(E * n, device=dev) * 0.1
+    scale = torch.rand(total, device=dev)
+    perm = torch.randperm(total, device=dev).int()
+    segs_list = [(a0, r, e, 0, a0) for (a0, r, e) in seg_rows]
+    out = torch.zeros(total, n, device=dev, dtype=torch.bfloat16)
+    gg.grouped_gemm(A, B, gg.make_segments(segs_list, dev), n=n, act="gelu", bias=bias,
+                    row_map=perm, row_scale=scale, out=out, check=True)
+    ref_rows = _ref(A, B, segs_list, n, "gelu", bias=bias, row_scale=scale, out_rows=total)
+    ref = torch.zeros_like(ref_rows)
+    valid = torch.zeros(total, dtype=torch.bool, device=dev)
+    for (a0, r, e) in seg_rows:
+        valid[a0:a0 + r] = True
+    ref[perm.long()[valid]] = ref_rows[valid]
+    got = out.float()
+    mask = torch.zeros(total, dtype=torch.bool, device=dev)
+    mask[perm.long()[valid]] = True
+    torch.testing.assert_close(got[mask], ref[mask], atol=2e-2, rtol=2e-2)
+
+
+def test_bf16_swiglu():
+    gg = _gg()
+    torch.manual_seed(4)
+    dev = torch.device("cuda")
+    m, k, f, E = 260, 512, 256, 2
+    A = torch.randn(m, k, device=dev).bfloat16()
+    wg = (torch.randn(E, f, k, device=dev) / k ** 0.5).bfloat16()
+    wu = (torch.randn(E, f, k, device=dev) / k ** 0.5).bfloat16()
+    bn = 256
+    B = gg.swiglu_interleave(wg, wu, bn).reshape(E * 2 * f, k)
+    segs_list = [(0, 100, 1, 0, 0), (100, 160, 0, 0, 100)]
+    out = torch.zeros(m, f, device=dev)
+    gg.grouped_gemm(A, B, gg.make_segments(segs_list, dev), n=2 * f, act="swiglu", bn=bn, out=out, check=True)
+    ref = torch.zeros(m, f, device=dev)
+    for (a0, r, e, _, o0) in segs_list:
+        x = A[a0:a0 + r].float()
+        g = x @ wg[e].float().t()
+        u = x @ wu[e].float().t()
+        ref[o0:o0 + r] = torch.nn.functional.silu(g) * u
+    torch.testing.assert_close(out, ref, atol=5e-3, rtol=5e-3)
