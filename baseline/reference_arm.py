@@ -1,0 +1,121 @@
+"""Reference arm of bench.py: the unmodified reference build, stock code path.
+
+The reference source tree has no packaging metadata, so ``pip install
+--target baseline/_ref`` refuses it; ``baseline/_ref`` holds a verbatim copy of
+the tree instead and nothing in it is edited.  This module only performs
+what the reference's own driver ``scripts/run_r4_a0_c0_full_moe.py::main``
+does before calling ``_run_arm`` (topology load, static plan compile, JIT
+build of its C++ event bridge, seeded router and expert weights, case
+inputs, streams) and then calls the reference's ``_run_arm`` for the early
+("C") and delayed ("D") arms, paired per step.  The reported latency is the
+reference's own full-MoE primary makespan (first Router launch -> combined
+output, ``timing.primary_makespan_us``), max over ranks.
+
+The reference driver hard-codes a world size of two (``main`` raises on any
+other size), so every other GPU count prints an ``unavailable`` line.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+from pathlib import Path
+import statistics
+import sys
+
+REF_ROOT = Path(__file__).resolve().parent / "_ref"
+
+
+def _unavailable(why: str) -> dict:
+    return {"impl": "reference", "unavailable": why}
+
+
+def run_reference(args) -> dict | None:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if not (REF_ROOT / "scripts" / "run_r4_a0_c0_full_moe.py").exists():
+        return _unavailable("reference tree not present under baseline/_ref") if rank == 0 else None
+    if args.gpus != 2 or world != 2:
+        return _unavailable("the reference full-MoE driver requires exactly two ranks "
+                            "(scripts/run_r4_a0_c0_full_moe.py:1062)") if rank == 0 else None
+    if args.config != "r4_reference":
+        return _unavailable("the reference stock path implements only its R4 config "
+                            "(top-1, ReLU 2048->32->16, 4 experts)") if rank == 0 else None
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    sys.path.insert(0, str(REF_ROOT))
+    from scripts import run_r4_a0_c0_full_moe as r4  # noqa: E402  (reference module, unmodified)
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist.init_process_group("nccl", init_method="env://", timeout=timedelta(seconds=300))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    try:
+        topology, _ = r4._load_rear4_topology(REF_ROOT)
+        plan = r4.StaticPlanCompiler().compile(topology)
+        build = Path("/tmp") / f"raiccl_reference_bridge_rank{rank}"
+        ext = r4._load_bridge_extension(build)
+        allowed = sorted(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else [-1]
+        bridge = ext.IntegratedEventBridge(r4.CHUNKS, allowed[-(rank + 1)], rank)
+        router_stream = torch.cuda.Stream(device=device)
+        comm_stream = torch.cuda.Stream(device=device)
+        rw_cpu, rb_cpu = r4.seed_router_params(r4.D, r4.EXPERTS, r4.ROUTER_SEED)
+        router_weight = rw_cpu.to(device)
+        expert_weights = tuple(v.to(device) for v in r4.seed_reference_experts(
+            r4.D, r4.EXPERT_HIDDEN, r4.EXPERT_OUTPUT, r4.EXPERTS, r4.EXPERT_SEED))
+        case = "balanced"
+        case_data = r4._case_inputs(case, rank)
+        tokens = torch.from_numpy(case_data["tokens"]).to(device)
+        bias = (rb_cpu + torch.from_numpy(case_data["bias_delta"])).to(device)
+        T = r4.TOTAL_TOKENS
+        mask = torch.zeros((T, r4.EXPERTS), dtype=torch.bool, device=device)
+        mask[torch.arange(T, device=device), torch.from_numpy(case_data["topology_sources"]).to(device)] = True
+        chunks = tuple(tokens.narrow(0, case_data["chunk_offsets"][i], case_data["chunk_sizes"][i])
+                       for i in range(r4.CHUNKS))
+        masks = tuple(mask.narrow(0, case_data["chunk_offsets"][i], case_data["chunk_sizes"][i])
+                      for i in range(r4.CHUNKS))
+
+        def arm(name: str) -> float:
+            dist.barrier()
+            res = r4._run_arm(
+                arm=name, case_name=case, rank=rank, topology=topology, plan=plan, bridge=bridge,
+                case_data=case_data, tokens_device=tokens, token_chunks=chunks, mask_chunks=masks,
+                router_weight=router_weight, router_bias=bias, expert_weights=expert_weights,
+                router_stream=router_stream, comm_stream=comm_stream)
+            return float(res["timing"]["primary_makespan_us"]) / 1e3
+
+        for _ in range(args.warmup):
+            arm("C")
+            arm("D")
+        early, delayed = [], []
+        for _ in range(args.steps):
+            early.append(arm("C"))
+            delayed.append(arm("D"))
+        t = torch.tensor([early, delayed], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        early, delayed = t[0].tolist(), t[1].tolist()
+        bridge.stop()
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    p50 = statistics.median(early)
+    return {
+        "impl": "reference", "metric": "full MoE layer p50 ms + Delta=T_delayed-T_early", "value": round(p50, 4),
+        "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(statistics.fmean(early), 4), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": round(p50 / 480.265, 6), "dtype": "fp32",
+        "data": "synthetic (reference balanced case; seeded reference weights)",
+        "config": {"model": "r4_reference: 4 experts top-1, D=2048, expert 2048->32 relu->16",
+                   "global_batch": r4.TOTAL_TOKENS * world, "seq_len": r4.TOTAL_TOKENS, "parallelism": f"ep{world}",
+                   "timing": "reference primary makespan (host monotonic ns), max over ranks"},
+        "p50_early_ms": round(p50, 4), "p50_delayed_ms": round(statistics.median(delayed), 4),
+        "delta_ms": round(statistics.median([d - e for e, d in zip(early, delayed)]), 4),
+    }
+
+
+if __name__ == "__main__":  # pragma: no cover
+    print(json.dumps(_unavailable("run through bench.py --impl reference")))

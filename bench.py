@@ -1,0 +1,258 @@
+#!/usr/bin/env python
+"""Full progressive MoE layer benchmark (one rank per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config r4_reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N --steps K --warmup W
+    python bench.py --impl reference ...     (the unmodified reference build)
+
+Metric: full MoE layer p50 latency (first Router launch -> combined output),
+device-timed with CUDA events on the layer's stream, max over ranks per step,
+plus the progressive gain Delta = T_delayed - T_early (paired per step).
+Every step of both arms starts after an L2 flush (a 256 MiB write) and a
+device-side cross-GPU barrier; the flush and barrier are outside the step's
+events.  Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+# Published reference number this metric is compared with: full-MoE primary
+# makespan p50, early arm, 2 x V100 (docs/phase_r4/R4_F0_REPORT.md:62).
+PUBLISHED_P50_MS = 480.265
+METRIC = "full MoE layer p50 ms + Delta=T_delayed-T_early"
+
+
+def _env_world() -> tuple[int, int, int]:
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons of the given PCI bus ids."""
+
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_ids: list[str]):
+        self.bus_ids = {b.lower()[-12:] for b in bus_ids}
+        self.rows: list[list[str]] = []
+        self._stop = threading.Event()
+        self._thread: threading.Thread | None = None
+
+    def _run(self) -> None:
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
+                                     capture_output=True, text=True, timeout=5).stdout
+                for line in out.strip().splitlines():
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) >= 10 and parts[1].lower()[-12:] in self.bus_ids:
+                        self.rows.append(parts)
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=10)
+
+    def summary(self) -> dict:
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in self.rows if r[3].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[6:10]) if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def _max_over_ranks(values, world: int, device):
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.cpu().tolist()
+
+
+def run_product(args) -> dict | None:
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from revealaiccl_b200.moe.config import preset
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    rank, world, local = _env_world()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    cfg = preset(args.config)
+    layer = ProgressiveMoELayer(cfg, device=dev, timeout_s=10.0)
+    try:
+        # correctness gate (untimed): both arms verified, outputs identical
+        layer.forward("early")
+        layer.verify()
+        ref_out = layer.out.clone()
+        layer.forward("delayed")
+        layer.verify()
+        if not torch.equal(ref_out, layer.out):
+            raise RuntimeError("early and delayed arms produced different outputs")
+        launches = {"early": layer.capture("early"), "delayed": layer.capture("delayed")}
+        flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+        cs = layer.comm_stream
+
+        def step(arm):
+            with torch.cuda.stream(cs):
+                flush.zero_()
+            layer.device_barrier()
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record(cs)
+            layer.replay(arm)
+            e.record(cs)
+            return s, e
+
+        for _ in range(args.warmup):
+            step("early")
+            step("delayed")
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        bus = torch.cuda.get_device_properties(dev).pci_bus_id if hasattr(torch.cuda.get_device_properties(dev), "pci_bus_id") else None
+        bus_ids = [bus] if bus else []
+        if world > 1:
+            gathered = [None] * world
+            dist.all_gather_object(gathered, bus)
+            bus_ids = [b for b in gathered if b]
+        sampler = ClockSampler(bus_ids) if rank == 0 else None
+        if sampler:
+            sampler.__enter__()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        t_begin = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_begin.record(cs)
+        events = []
+        for _ in range(args.steps):
+            events.append((step("early"), step("delayed")))
+        t_end.record(cs)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        if sampler:
+            sampler.__exit__(None, None, None)
+        layer.check_status()
+        early = [a[0].elapsed_time(a[1]) for a, _ in events]
+        delayed = [b[0].elapsed_time(b[1]) for _, b in events]
+        bracket = t_begin.elapsed_time(t_end)
+        early = _max_over_ranks(early, world, dev)
+        delayed = _max_over_ranks(delayed, world, dev)
+        bracket = _max_over_ranks([bracket], world, dev)[0]
+        deltas = [d - e for e, d in zip(early, delayed)]
+        layer.verify()  # the timed replays left a checkable last call
+
+        # end-to-end through the public call: pinned H2D of the step's tokens,
+        # digests, the layer (captured graph), D2H of the combined output
+        host_in = torch.empty(layer.inputs.tokens.shape, dtype=layer.inputs.tokens.dtype, pin_memory=True)
+        host_in.copy_(layer.inputs.tokens.cpu())
+        host_out = torch.empty(layer.out.shape, dtype=layer.out.dtype, pin_memory=True)
+        e2e = []
+        for i in range(args.warmup + args.steps):
+            with torch.cuda.stream(cs):
+                flush.zero_()
+            layer.device_barrier()
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record(cs)
+            layer(host_in, host_out, arm="early")
+            e.record(cs)
+            if i >= args.warmup:
+                e2e.append((s, e))
+        torch.cuda.synchronize(dev)
+        e2e_ms = _max_over_ranks([s.elapsed_time(e) for s, e in e2e], world, dev)
+        clocks = sampler.summary() if sampler else None
+        if rank != 0:
+            return None
+        p50 = statistics.median(early)
+        tokens_total = cfg.tokens_per_rank * world
+        return {
+            "metric": METRIC, "value": round(p50, 4), "unit": "ms", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(statistics.fmean(early), 4),
+            "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": round(p50 / PUBLISHED_P50_MS, 6),
+            "dtype": "fp32-tf32" if cfg.dtype == "fp32" else "bf16",
+            "data": "synthetic (reference seeded token/router/expert recipes; random-init weights)",
+            "config": {"model": f"{cfg.name}: {cfg.experts} experts top-{cfg.top_k}, D={cfg.hidden}, "
+                                f"expert {cfg.hidden}->{cfg.ffn_hidden} {cfg.activation}->{cfg.out_dim}",
+                       "global_batch": tokens_total, "seq_len": cfg.tokens_per_rank,
+                       "tokens_per_rank": cfg.tokens_per_rank, "chunks": cfg.chunks,
+                       "parallelism": f"ep{world}", "l2": "256 MiB flush before every timed step"},
+            "p50_early_ms": round(p50, 4), "p50_delayed_ms": round(statistics.median(delayed), 4),
+            "delta_ms": round(statistics.median(deltas), 4),
+            "p95_early_ms": round(sorted(early)[max(0, int(0.95 * len(early)) - 1)], 4),
+            "tokens_per_s": round(tokens_total / (p50 / 1e3), 1),
+            "bracket_ms": round(bracket, 3),
+            "e2e": {"value": round(statistics.median(e2e_ms), 4), "unit": "ms",
+                    "h2d_bytes_per_step": int(layer.inputs.tokens.numel() * layer.inputs.tokens.element_size()),
+                    "d2h_bytes_per_step": int(layer.out.numel() * layer.out.element_size())},
+            "gpu_launches": int((launches["early"] + launches["delayed"]) * args.steps),
+            "clocks": clocks, "verified": True,
+        }
+    finally:
+        try:
+            layer.close()
+        except Exception:
+            pass
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="r4_reference")
+    ap.add_argument("--impl", choices=("product", "reference"), default="product")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        from baseline.reference_arm import run_reference
+
+        out = run_reference(args)
+    else:
+        out = run_product(args)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

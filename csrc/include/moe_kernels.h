@@ -1,0 +1,129 @@
+// Launch parameter records of the MoE data-plane and control-plane kernels
+// (plain data shared by the host bindings and the .cu launch units).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "moe_layout.h"
+#include "sched_core.h"
+#include "types.h"
+
+namespace raiccl {
+
+struct RouterParams {
+  const void* tokens;       // [T, D] fp32 or bf16
+  const void* weight;       // [E, D] same dtype
+  const float* bias;        // [E]
+  const float* chunk_bias;  // [E] additive bias of this chunk, or nullptr
+  const uint8_t* block_mask;  // [E] 1 = this rank may not route there, or nullptr
+  int row0, row1;           // rows routed by this launch (one router chunk)
+  int hidden, experts, top_k, gate_mode, mask_mode, pad;
+  int32_t* expert_ids;      // [T, k]
+  float* gates;             // [T, k]
+};
+
+struct DispatchParams {
+  MoEDims dims;
+  SymLayout layout;
+  PeerBases peers;
+  const void* tokens;
+  const int32_t* expert_ids;
+  const float* gates;
+  const long long* token_ids;
+  const long long* feat_digest;
+  const long long* checksum_base;
+  const int32_t* chunk_offsets;
+  int desc, t0, t1, pad;
+  int32_t* sent_base;       // [E] rows already sent to (e, this rank) in earlier descriptors
+  int32_t* desc_counts;     // [n_desc, E]
+  int32_t* done_counter;    // [n_desc]
+  const unsigned long long* permit;  // [n_desc] == epoch when the guard committed the descriptor
+  const unsigned long long* epoch;   // device word holding this call's sequence number
+  DeviceStatus* status;
+};
+
+struct PlanParams {
+  MoEDims dims;
+  SymLayout layout;
+  PeerBases peers;
+  GemmSegment* segs;        // [E_slot * W]
+  int32_t* rows_out;        // [E_slot * W]
+  const unsigned long long* epoch;
+  unsigned long long timeout_ns;
+  DeviceStatus* status;
+};
+
+struct ReturnMetaParams {
+  MoEDims dims;
+  SymLayout layout;
+  PeerBases peers;
+  const GemmSegment* segs;
+  DeviceStatus* status;
+};
+
+struct SignalParams {
+  MoEDims dims;
+  SymLayout layout;
+  PeerBases peers;
+  const unsigned long long* epoch;
+};
+
+struct CombineParams {
+  MoEDims dims;
+  SymLayout layout;
+  PeerBases peers;
+  void* out;                // [T, Dout]
+  const unsigned long long* epoch;
+  unsigned long long timeout_ns;
+  DeviceStatus* status;
+};
+
+struct BarrierParams {
+  MoEDims dims;
+  SymLayout layout;
+  PeerBases peers;
+  unsigned long long* counter;  // this rank's barrier sequence (device word)
+  unsigned long long timeout_ns;
+  DeviceStatus* status;
+};
+
+// Device-resident compiled-scheduler control plane (one CTA).
+struct ControlParams {
+  sched::PlanView plan;
+  sched::StateView st;
+  const int32_t* expert_ids;   // [T, k]
+  const int32_t* chunk_offsets;  // [C + 1]
+  int top_k, chunks, partial_chunks, desc;
+  int ctl_per_chunk, ctl_nodes, max_cands, log_stride;
+  // scalars kept across triggers of one layer call:
+  // [0] staged_count [1] revealed_count [2] state_version [3] completed bitmap
+  // [4] revealed bitmap [5] dispatched bitmap [6] future_access [7] unrevealed_execution
+  // [8] duplicate_dispatch [9] stale_dispatch [10] pending bitmap [11..11+C) chunk starts
+  // [11+C..11+2C) chunk counts
+  long long* scalars;
+  sched::Cand* cand_buf;       // [max_cands]
+  int* keep_buf;               // [max_cands]
+  int64_t* action_buf;         // [2 * max_tokens]
+  int* log;                    // [n_desc, log_stride]
+  unsigned long long* permit;  // [n_desc]
+  const unsigned long long* epoch;
+  DeviceStatus* status;
+};
+
+void launch_feature_digest(const void* rows, long long row_bytes, int nrows, long long* digest,
+                           cudaStream_t s);
+void launch_checksum_base(const long long* token_ids, const long long* digest, const int* chunk_offsets,
+                          int chunks, int rank, int n, long long* base, cudaStream_t s);
+void launch_router(const RouterParams& p, bool bf16, cudaStream_t s);
+void launch_dispatch(const DispatchParams& p, bool bf16, int grid, cudaStream_t s);
+void launch_expert_plan(const PlanParams& p, cudaStream_t s);
+void launch_return_meta(const ReturnMetaParams& p, int grid, cudaStream_t s);
+void launch_return_signal(const SignalParams& p, cudaStream_t s);
+void launch_combine(const CombineParams& p, bool bf16, int grid, cudaStream_t s);
+void launch_layer_reset(int* sent_base, int experts, int* desc_counts, int n_desc, int* done_counter,
+                        unsigned long long* epoch, cudaStream_t s);
+void launch_control(const ControlParams& p, cudaStream_t s);
+void launch_device_barrier(const BarrierParams& p, cudaStream_t s);
+
+}  // namespace raiccl

@@ -84,6 +84,8 @@ void grouped_gemm(torch::Tensor A, torch::Tensor B, torch::Tensor segs, torch::T
 
 }  // namespace
 
+void register_moe(py::module_& m);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "revealaiccl_b200 sm_100a kernels (tcgen05/TMEM/TMA, NVLink peer stores)";
   m.def("grouped_gemm", &grouped_gemm, "tcgen05 grouped GEMM with fused epilogue",
@@ -91,4 +93,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bn"), py::arg("act"), py::arg("bias"), py::arg("row_map"), py::arg("row_scale"),
         py::arg("out_ptrs"), py::arg("ldo"), py::arg("out_bf16"), py::arg("status"),
         py::arg("grid"), py::arg("timeout_ns"));
+  register_moe(m);
 }

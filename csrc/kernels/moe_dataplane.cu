@@ -1,0 +1,520 @@
+// Progressive MoE data plane for sm_100a: router top-k, revealed-only
+// dispatch straight into peers' receive buffers over NVLink, expert plan,
+// return identity rows, return/ready signalling and the device combine.
+//
+// Reference call sites replaced (rlccl / scripts):
+//   router_topk (rlccl/transport/reference_router.py:15-25)          -> moe_router_kernel
+//   FastProgressiveDataPrep.mark_completed/build_delta_payload + the
+//     count all_to_all_single + the two payload all_to_all_single
+//     (scripts/run_r4_a0_c0_full_moe.py:104-207)                      -> moe_dispatch_kernel
+//   pack_return_payload + return all_to_all_single (:628-695)          -> moe_return_meta_kernel
+//                                                                        + grouped GEMM-2 epilogue
+//   NumPy position scatter combine (:833-838)                          -> moe_combine_kernel
+//
+// Every cross-GPU wait is bounded (globaltimer deadline) and reports through
+// DeviceStatus; there is no __trap and no intra-GPU wait on another kernel.
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "launchers.h"
+#include "moe_kernels.h"
+#include "sm100_ptx.cuh"
+
+namespace raiccl {
+
+__constant__ unsigned long long c_checksum_coeff[8] = {1000003ULL, 1000033ULL, 1000037ULL, 1000081ULL,
+                                                      1000099ULL, 1000117ULL, 1000121ULL, 1000133ULL};
+
+__device__ __forceinline__ float to_f(float x) { return x; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+// splitmix64 finaliser (Steele, Lea & Flood 2014 / Vigna), used as the word
+// mixer of the order-dependent row digest below.
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ULL;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ uint64_t addmod(uint64_t a, uint64_t b) {
+  uint64_t s = a + b;  // a, b < M < 2^63: no overflow
+  return s >= kChecksumModulus ? s - kChecksumModulus : s;
+}
+
+__device__ __forceinline__ uint64_t mulmod_coeff(uint64_t v, uint64_t c) {
+  unsigned __int128 p = (unsigned __int128)(v % kChecksumModulus) * c;
+  return (uint64_t)(p % kChecksumModulus);
+}
+
+// ---------------------------------------------------------------------------
+// Row digest: (sum_i splitmix64((i << 32) | w_i)) mod 2^64, masked to 62 bits,
+// over the row's 32-bit words.  One warp per row.
+// ---------------------------------------------------------------------------
+__global__ void moe_feature_digest_kernel(const uint32_t* rows, long long words_per_row, int nrows,
+                                          long long* digest) {
+  const int warps = blockDim.x >> 5;
+  const int row = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= nrows) return;
+  const uint32_t* r = rows + (long long)row * words_per_row;
+  uint64_t acc = 0;
+  for (long long i = lane; i < words_per_row; i += 32)
+    acc += splitmix64(((uint64_t)i << 32) | (uint64_t)__ldg(r + i));
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) digest[row] = (long long)(acc & ((1ULL << 62) - 1));
+}
+
+// identity_checksum(token, src, 0, 0, chunk, chunk_offset, position, digest):
+// the destination and expert terms are added per assignment at dispatch time
+// (the checksum is linear in every field).
+__global__ void moe_checksum_base_kernel(const long long* token_ids, const long long* digest,
+                                         const int* chunk_offsets, int chunks, int rank, int n,
+                                         long long* base) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n) return;
+  int c = 0;
+  while (c + 1 < chunks && chunk_offsets[c + 1] <= t) ++c;
+  const uint64_t fields[8] = {(uint64_t)token_ids[t], (uint64_t)rank, 0, 0, (uint64_t)c,
+                              (uint64_t)(t - chunk_offsets[c]), (uint64_t)t, (uint64_t)digest[t]};
+  uint64_t acc = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc = addmod(acc, mulmod_coeff(fields[i], c_checksum_coeff[i]));
+  base[t] = (long long)acc;
+}
+
+// ---------------------------------------------------------------------------
+// Router: logits = x @ W^T + b (+ chunk bias), masks, stable top-k (ties pick
+// the smaller expert id), gates.  One warp per token row, fp32 accumulation
+// (exact fp32 for fp32 inputs).  W is [E, D] in the token dtype.
+// ---------------------------------------------------------------------------
+template <typename T, int EMAX>
+__global__ void __launch_bounds__(256) moe_router_kernel(RouterParams p) {
+  const T* __restrict__ tokens = (const T*)p.tokens;
+  const T* __restrict__ w = (const T*)p.weight;
+  const int warps = blockDim.x >> 5;
+  const int t = p.row0 + blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= p.row1) return;
+  const int D = p.hidden, E = p.experts;
+  constexpr int VEC = 16 / sizeof(T);
+  float acc[EMAX];
+#pragma unroll
+  for (int e = 0; e < EMAX; ++e) acc[e] = 0.f;
+  const T* x = tokens + (long long)t * D;
+  for (int base = lane * VEC; base < D; base += 32 * VEC) {
+    T xv[VEC];
+    *(uint4*)xv = __ldg((const uint4*)(x + base));
+#pragma unroll
+    for (int e = 0; e < EMAX; ++e) {
+      if (e < E) {
+        T wv[VEC];
+        *(uint4*)wv = __ldg((const uint4*)(w + (long long)e * D + base));
+        float s = 0.f;
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) s = fmaf(to_f(xv[v]), to_f(wv[v]), s);
+        acc[e] += s;
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < EMAX; ++e) {
+    if (e < E) {
+      float v = acc[e];
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      acc[e] = v;
+    }
+  }
+  if (lane != 0) return;
+  float logit[EMAX];
+  bool taken[EMAX];
+  const float ninf = -__int_as_float(0x7f800000);
+#pragma unroll
+  for (int e = 0; e < EMAX; ++e) {
+    taken[e] = false;
+    if (e < E) {
+      float l = acc[e] + p.bias[e] + (p.chunk_bias ? p.chunk_bias[e] : 0.f);
+      const bool masked = (p.mask_mode == 1 && e == (t % E)) || (p.block_mask && p.block_mask[e]);
+      logit[e] = masked ? ninf : l;
+    } else {
+      logit[e] = ninf;
+    }
+  }
+  float sel_logit[8];
+  int sel[8];
+  for (int j = 0; j < p.top_k; ++j) {
+    int best = -1;
+#pragma unroll
+    for (int e = 0; e < EMAX; ++e)
+      if (e < E && !taken[e] && (best < 0 || logit[e] > logit[best])) best = e;
+#pragma unroll
+    for (int e = 0; e < EMAX; ++e)
+      if (e == best) taken[e] = true;
+    sel[j] = best;
+    sel_logit[j] = logit[best];
+  }
+  float g[8];
+  if (p.gate_mode == 1) {
+    float sum = 0.f;
+    for (int j = 0; j < p.top_k; ++j) { g[j] = __expf(sel_logit[j] - sel_logit[0]); sum += g[j]; }
+    for (int j = 0; j < p.top_k; ++j) g[j] /= sum;
+  } else if (p.gate_mode == 2) {
+    float mx = sel_logit[0], sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < EMAX; ++e)
+      if (e < E && logit[e] != ninf) sum += __expf(logit[e] - mx);
+    for (int j = 0; j < p.top_k; ++j) g[j] = __expf(sel_logit[j] - mx) / sum;
+  } else {
+    for (int j = 0; j < p.top_k; ++j) g[j] = 1.f;
+  }
+  for (int j = 0; j < p.top_k; ++j) {
+    p.expert_ids[(long long)t * p.top_k + j] = sel[j];
+    p.gates[(long long)t * p.top_k + j] = g[j];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dispatch of one revealed descriptor (a run of router chunks) straight into
+// the owners' receive regions.  Rows keep the reference's deterministic order
+// inside every (expert, source) region: descriptor order, then token order.
+// The last CTA publishes per-expert counts into each owner's header and then
+// one release store of the sequence number per destination rank (sent even
+// for zero rows, like the reference's header-only zero-payload slot).
+// ---------------------------------------------------------------------------
+constexpr int kDispatchThreads = 512;
+constexpr int kDispatchMaxItems = 4096;
+constexpr int kMaxExperts = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(DispatchParams p) {
+  const MoEDims& d = p.dims;
+  __shared__ int hist[kMaxExperts];
+  __shared__ int run[kMaxExperts];
+  __shared__ int item_pos[kDispatchMaxItems];
+  __shared__ int s_last;
+  __shared__ int s_permitted;
+  const int k = d.top_k;
+  const int E = d.experts;
+  const int ntok = p.t1 - p.t0;
+  const int per = (ntok + gridDim.x - 1) / gridDim.x;
+  const int a = p.t0 + min(ntok, (int)blockIdx.x * per);
+  const int b = p.t0 + min(ntok, (int)(blockIdx.x + 1) * per);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+
+  for (int e = threadIdx.x; e < E; e += blockDim.x) { hist[e] = 0; run[e] = 0; }
+  const unsigned long long epoch = *p.epoch;
+  if (threadIdx.x == 0) s_permitted = (p.permit[p.desc] == epoch) ? 1 : 0;
+  __syncthreads();
+  const bool permitted = s_permitted != 0;
+  if (!permitted && threadIdx.x == 0 && blockIdx.x == 0)
+    record_status(p.status, kTimeoutPermit, 20, p.desc, (long long)epoch);
+
+  if (permitted && (long long)(b - a) * k > kDispatchMaxItems) {
+    if (threadIdx.x == 0) record_status(p.status, kBadConfig, 22, (long long)(b - a) * k, kDispatchMaxItems);
+  } else if (permitted && a < b) {
+    // rows of earlier tokens of this descriptor per expert
+    for (long long i = (long long)p.t0 * k + threadIdx.x; i < (long long)a * k; i += blockDim.x)
+      atomicAdd(&hist[p.expert_ids[i]], 1);
+    // in-order rank of every item of this CTA within its expert
+    if (warp == 0) {
+      const long long i0 = (long long)a * k, i1 = (long long)b * k;
+      for (long long base = i0; base < i1; base += 32) {
+        const long long i = base + lane;
+        const bool valid = i < i1;
+        const int e = valid ? p.expert_ids[i] : E;  // sentinel groups the tail lanes
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const int rank_in = __popc(peers & ((1u << lane) - 1u));
+        const int prev = valid ? run[e] : 0;
+        if (valid) item_pos[i - i0] = prev + rank_in;
+        __syncwarp();
+        if (valid && lane == __ffs(peers) - 1) run[e] = prev + __popc(peers);
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x)
+      if (run[e]) atomicAdd(&p.desc_counts[(long long)p.desc * E + e], run[e]);
+
+    // copy features + identity rows, one warp per item
+    const long long nitems = (long long)(b - a) * k;
+    const int vec_per_row = d.hidden * d.feat_bytes / 16;
+    for (long long li = warp; li < nitems; li += nwarps) {
+      const long long i = (long long)a * k + li;
+      const int t = (int)(i / k), j = (int)(i % k);
+      const int e = p.expert_ids[i];
+      const int r = expert_owner(d, e), le = expert_slot(d, e);
+      const long long row = (long long)p.sent_base[e] + hist[e] + item_pos[li];
+      if (row >= d.cap || r >= d.world || le >= d.expert_slots) {
+        if (lane == 0) record_status(p.status, kBoundsViolation, 21, row, d.cap);
+        continue;
+      }
+      const long long grow = ((long long)le * d.world + d.rank) * d.cap + row;
+      uint8_t* base = (uint8_t*)p.peers.base[r];
+      uint4* dst = (uint4*)(base + p.layout.recv_feat + grow * d.hidden * d.feat_bytes);
+      const uint4* src = (const uint4*)((const uint8_t*)p.tokens + (long long)t * d.hidden * d.feat_bytes);
+      for (int v = lane; v < vec_per_row; v += 32) dst[v] = __ldg(src + v);
+      if (lane < kFwdMetaFields) {
+        int c = 0;
+        while (c + 1 < d.chunks && p.chunk_offsets[c + 1] <= t) ++c;
+        long long val;
+        switch (lane) {
+          case 0: val = p.token_ids[t]; break;
+          case 1: val = d.rank; break;
+          case 2: val = r; break;
+          case 3: val = e; break;
+          case 4: val = c; break;
+          case 5: val = t - p.chunk_offsets[c]; break;
+          case 6: val = t; break;
+          case 7: val = p.feat_digest[t]; break;
+          default: {
+            uint64_t cs = (uint64_t)p.checksum_base[t];
+            cs = addmod(cs, mulmod_coeff((uint64_t)r, c_checksum_coeff[2]));
+            cs = addmod(cs, mulmod_coeff((uint64_t)e, c_checksum_coeff[3]));
+            val = (long long)cs;
+          }
+        }
+        ((long long*)(base + p.layout.recv_meta))[grow * kFwdMetaFields + lane] = val;
+      } else if (lane == 16) {
+        ((int*)(base + p.layout.recv_retrow))[grow] = t * k + j;
+      } else if (lane == 17) {
+        ((float*)(base + p.layout.recv_gate))[grow] = d.gate_mode ? p.gates[i] : 1.f;
+      }
+    }
+  }
+
+  // completion: the last CTA of the launch publishes counts and signals
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const int prev = atomicAdd(&p.done_counter[p.desc], 1);
+    s_last = (prev == (int)gridDim.x - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int cnt = atomicAdd(&p.desc_counts[(long long)p.desc * E + e], 0);
+    const int r = expert_owner(d, e), le = expert_slot(d, e);
+    uint8_t* base = (uint8_t*)p.peers.base[r];
+    ((int*)(base + p.layout.recv_count))[((long long)le * d.world + d.rank) * d.n_desc + p.desc] = cnt;
+    p.sent_base[e] += cnt;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int r = 0; r < d.world; ++r) {
+      uint8_t* base = (uint8_t*)p.peers.base[r];
+      st_release_sys_u64((uint64_t*)(base + p.layout.recv_flag) + (long long)d.rank * d.n_desc + p.desc,
+                         epoch);
+    }
+    p.done_counter[p.desc] = 0;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Expert plan: wait (bounded) for every (source, descriptor) ready signal,
+// then emit one grouped-GEMM segment per (local expert slot, source).
+// ---------------------------------------------------------------------------
+__global__ void moe_expert_plan_kernel(PlanParams p) {
+  const MoEDims& d = p.dims;
+  const uint8_t* mine = (const uint8_t*)p.peers.base[d.rank];
+  const uint64_t* flags = (const uint64_t*)(mine + p.layout.recv_flag);
+  __shared__ int s_ok;
+  const unsigned long long epoch = *p.epoch;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  for (int i = threadIdx.x; i < d.world * d.n_desc; i += blockDim.x) {
+    if (!wait_flag_geq_sys(flags + i, epoch, p.status, kTimeoutPeerSignal, 30, i, p.timeout_ns))
+      s_ok = 0;
+  }
+  __syncthreads();
+  const int* counts = (const int*)(mine + p.layout.recv_count);
+  for (int s = threadIdx.x; s < d.expert_slots * d.world; s += blockDim.x) {
+    int rows = 0;
+    if (s_ok) {
+      for (int q = 0; q < d.n_desc; ++q) rows += counts[(long long)s * d.n_desc + q];
+      if (rows > d.cap) { record_status(p.status, kBoundsViolation, 31, rows, d.cap); rows = 0; }
+    }
+    GemmSegment seg;
+    seg.a_row0 = (int)((long long)s * d.cap);
+    seg.rows = rows;
+    seg.expert = s / d.world;
+    seg.out_slot = s % d.world;
+    seg.out_row0 = seg.a_row0;
+    seg.pad0 = seg.pad1 = seg.pad2 = 0;
+    p.segs[s] = seg;
+    p.rows_out[s] = rows;
+  }
+}
+
+// Return identity rows to the token's source rank, at row (position * k + j)
+// of its return region (rlccl/transport/reference_full_moe.py:143-182 order:
+// token, source, expert rank, expert, original position, chunk, chunk offset,
+// checksum).
+__global__ void moe_return_meta_kernel(ReturnMetaParams p) {
+  const MoEDims& d = p.dims;
+  const uint8_t* mine = (const uint8_t*)p.peers.base[d.rank];
+  const long long* meta = (const long long*)(mine + p.layout.recv_meta);
+  const int* retrow = (const int*)(mine + p.layout.recv_retrow);
+  const long long total = (long long)d.expert_slots * d.world * d.cap;
+  for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < total;
+       g += (long long)gridDim.x * blockDim.x) {
+    const int s = (int)(g / d.cap);
+    const long long r = g % d.cap;
+    if (r >= p.segs[s].rows) continue;
+    const int src = s % d.world;
+    const long long* m = meta + g * kFwdMetaFields;
+    const uint64_t f[7] = {(uint64_t)m[0], (uint64_t)src, (uint64_t)d.rank, (uint64_t)m[3],
+                           (uint64_t)m[6], (uint64_t)m[4], (uint64_t)m[5]};
+    uint64_t cs = 0;
+#pragma unroll
+    for (int i = 0; i < 7; ++i) cs = addmod(cs, mulmod_coeff(f[i], c_checksum_coeff[i]));
+    const long long dst_row = retrow[g];
+    if (dst_row < 0 || dst_row >= (long long)d.tokens * d.top_k) {
+      record_status(p.status, kBoundsViolation, 40, dst_row, (long long)d.tokens * d.top_k);
+      continue;
+    }
+    long long* out = (long long*)((uint8_t*)p.peers.base[src] + p.layout.ret_meta) + dst_row * kRetMetaFields;
+#pragma unroll
+    for (int i = 0; i < 7; ++i) out[i] = (long long)f[i];
+    out[7] = (long long)cs;
+  }
+}
+
+// One thread: make this rank's return stores visible, then publish its return
+// sequence number at every source rank.
+__global__ void moe_return_signal_kernel(SignalParams p) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const MoEDims& d = p.dims;
+  const unsigned long long epoch = *p.epoch;
+  __threadfence_system();
+  for (int r = 0; r < d.world; ++r)
+    st_release_sys_u64((uint64_t*)((uint8_t*)p.peers.base[r] + p.layout.ret_flag) + d.rank, epoch);
+}
+
+// Combine: wait (bounded) for every expert rank's return signal, then
+// out[t] = sum_j ret_out[t * k + j] (rows already carry their gate weight).
+template <typename OutT>
+__global__ void moe_combine_kernel(CombineParams p) {
+  const MoEDims& d = p.dims;
+  const uint8_t* mine = (const uint8_t*)p.peers.base[d.rank];
+  __shared__ int s_ok;
+  const unsigned long long epoch = *p.epoch;
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  if (threadIdx.x < d.world) {
+    const uint64_t* f = (const uint64_t*)(mine + p.layout.ret_flag) + threadIdx.x;
+    if (!wait_flag_geq_sys(f, epoch, p.status, kTimeoutPeerSignal, 50, threadIdx.x, p.timeout_ns))
+      s_ok = 0;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+  const OutT* ret = (const OutT*)(mine + p.layout.ret_out);
+  OutT* out = (OutT*)p.out;
+  const int k = d.top_k, n = d.out_dim;
+  const long long total = (long long)d.tokens * n;
+  for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < total;
+       g += (long long)gridDim.x * blockDim.x) {
+    const long long t = g / n, c = g % n;
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) acc += to_f(ret[(t * k + j) * n + c]);
+    if constexpr (sizeof(OutT) == 4) out[g] = acc;
+    else out[g] = __float2bfloat16(acc);
+  }
+}
+
+// Cross-GPU barrier: publish this rank's barrier sequence at every peer, then
+// wait (bounded) until every peer's sequence arrived here.  Used to align the
+// ranks before a timed layer call without a host round-trip.
+__global__ void moe_device_barrier_kernel(BarrierParams p) {
+  const MoEDims& d = p.dims;
+  __shared__ unsigned long long seq;
+  if (threadIdx.x == 0) {
+    seq = *p.counter + 1;
+    *p.counter = seq;
+    __threadfence_system();
+    for (int r = 0; r < d.world; ++r)
+      st_release_sys_u64((uint64_t*)((uint8_t*)p.peers.base[r] + p.layout.bar_flag) + d.rank, seq);
+  }
+  __syncthreads();
+  if (threadIdx.x < d.world) {
+    const uint64_t* f = (const uint64_t*)((const uint8_t*)p.peers.base[d.rank] + p.layout.bar_flag) + threadIdx.x;
+    wait_flag_geq_sys(f, seq, p.status, kTimeoutPeerSignal, 70, threadIdx.x, p.timeout_ns);
+  }
+}
+
+void launch_device_barrier(const BarrierParams& p, cudaStream_t s) {
+  moe_device_barrier_kernel<<<1, 32, 0, s>>>(p);
+}
+
+// Per-call reset of the dispatch cursors and counters; advances the call's
+// sequence number (the value every ready / return / permit word is compared to).
+__global__ void moe_layer_reset_kernel(int* sent_base, int experts, int* desc_counts, int n_desc,
+                                       int* done_counter, unsigned long long* epoch) {
+  if (threadIdx.x == 0) *epoch += 1;
+  for (int i = threadIdx.x; i < experts; i += blockDim.x) sent_base[i] = 0;
+  for (int i = threadIdx.x; i < experts * n_desc; i += blockDim.x) desc_counts[i] = 0;
+  for (int i = threadIdx.x; i < n_desc; i += blockDim.x) done_counter[i] = 0;
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+void launch_feature_digest(const void* rows, long long row_bytes, int nrows, long long* digest,
+                           cudaStream_t s) {
+  const int warps = 8;
+  moe_feature_digest_kernel<<<(nrows + warps - 1) / warps, warps * 32, 0, s>>>(
+      (const uint32_t*)rows, row_bytes / 4, nrows, digest);
+}
+
+void launch_checksum_base(const long long* token_ids, const long long* digest, const int* chunk_offsets,
+                          int chunks, int rank, int n, long long* base, cudaStream_t s) {
+  moe_checksum_base_kernel<<<(n + 255) / 256, 256, 0, s>>>(token_ids, digest, chunk_offsets, chunks,
+                                                            rank, n, base);
+}
+
+void launch_router(const RouterParams& p, bool bf16, cudaStream_t s) {
+  const int rows = p.row1 - p.row0;
+  if (rows <= 0) return;
+  const int warps = 8;
+  const dim3 grid((rows + warps - 1) / warps);
+  if (p.experts <= 8) {
+    if (bf16) moe_router_kernel<__nv_bfloat16, 8><<<grid, warps * 32, 0, s>>>(p);
+    else moe_router_kernel<float, 8><<<grid, warps * 32, 0, s>>>(p);
+  } else if (p.experts <= 16) {
+    if (bf16) moe_router_kernel<__nv_bfloat16, 16><<<grid, warps * 32, 0, s>>>(p);
+    else moe_router_kernel<float, 16><<<grid, warps * 32, 0, s>>>(p);
+  } else {
+    if (bf16) moe_router_kernel<__nv_bfloat16, 64><<<grid, warps * 32, 0, s>>>(p);
+    else moe_router_kernel<float, 64><<<grid, warps * 32, 0, s>>>(p);
+  }
+}
+
+void launch_dispatch(const DispatchParams& p, bool bf16, int grid, cudaStream_t s) {
+  if (bf16) moe_dispatch_kernel<__nv_bfloat16><<<grid, kDispatchThreads, 0, s>>>(p);
+  else moe_dispatch_kernel<float><<<grid, kDispatchThreads, 0, s>>>(p);
+}
+
+void launch_expert_plan(const PlanParams& p, cudaStream_t s) {
+  moe_expert_plan_kernel<<<1, 256, 0, s>>>(p);
+}
+
+void launch_return_meta(const ReturnMetaParams& p, int grid, cudaStream_t s) {
+  moe_return_meta_kernel<<<grid, 256, 0, s>>>(p);
+}
+
+void launch_return_signal(const SignalParams& p, cudaStream_t s) {
+  moe_return_signal_kernel<<<1, 32, 0, s>>>(p);
+}
+
+void launch_combine(const CombineParams& p, bool bf16, int grid, cudaStream_t s) {
+  if (bf16) moe_combine_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(p);
+  else moe_combine_kernel<float><<<grid, 256, 0, s>>>(p);
+}
+
+void launch_layer_reset(int* sent_base, int experts, int* desc_counts, int n_desc, int* done_counter,
+                        unsigned long long* epoch, cudaStream_t s) {
+  moe_layer_reset_kernel<<<1, 256, 0, s>>>(sent_base, experts, desc_counts, n_desc, done_counter, epoch);
+}
+
+}  // namespace raiccl

@@ -1,0 +1,540 @@
+// Native executor of one progressive MoE layer on one rank.
+//
+// The runner owns no policy: the Python layer (revealaiccl_b200/moe/layer.py)
+// allocates every buffer, maps the peers' symmetric regions and hands the
+// runner device pointers once.  `forward(delayed)` then enqueues the whole
+// layer — router chunks on the router stream, and on the comm stream the
+// per-trigger control plane, the revealed-only dispatches (each right after
+// its trigger in the early arm, all after the final trigger in the delayed
+// arm), the expert plan, both grouped GEMMs, the return rows and signals and
+// the combine — with no host synchronisation.  `capture`/`replay` record the
+// same sequence once in a CUDA graph and relaunch it (the call's sequence
+// number lives in device memory, so replays need no new parameters).
+//
+// Orchestration being replaced: scripts/run_r4_a0_c0_full_moe.py:264-839
+// (_run_arm: producer thread + host consume/schedule/build/communicate loop).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "launchers.h"
+#include "moe_kernels.h"
+#include "tma_host.h"
+
+namespace {
+
+using raiccl::GemmSegment;
+
+void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+template <typename T>
+T* ptr(const py::dict& t, const char* key) {
+  if (!t.contains(key)) throw std::invalid_argument(std::string("missing tensor ") + key);
+  py::object o = t[key];
+  if (o.is_none()) return nullptr;
+  torch::Tensor x = o.cast<torch::Tensor>();
+  if (!x.is_cuda()) throw std::invalid_argument(std::string("tensor not on CUDA: ") + key);
+  if (!x.is_contiguous()) throw std::invalid_argument(std::string("tensor not contiguous: ") + key);
+  return reinterpret_cast<T*>(x.data_ptr());
+}
+
+template <typename T>
+T* opt_ptr(const py::dict& t, const char* key) {
+  if (!t.contains(key)) return nullptr;
+  return ptr<T>(t, key);
+}
+
+int geti(const py::dict& d, const char* key) {
+  if (!d.contains(key)) throw std::invalid_argument(std::string("missing int ") + key);
+  return d[key].cast<int>();
+}
+
+class MoELayerRunner {
+ public:
+  MoELayerRunner(py::dict ints, py::dict tensors, std::vector<int64_t> peer_bases,
+                 std::vector<int64_t> chunk_offsets, int64_t router_stream, int64_t comm_stream)
+      : tensors_(tensors), chunk_offsets_(chunk_offsets.begin(), chunk_offsets.end()) {
+    router_ = reinterpret_cast<cudaStream_t>(router_stream);
+    comm_ = reinterpret_cast<cudaStream_t>(comm_stream);
+    // keep every tensor alive for the runner's lifetime
+    for (auto item : tensors) held_.push_back(py::reinterpret_borrow<py::object>(item.second));
+
+    auto& d = dims_;
+    d.world = geti(ints, "world");
+    d.rank = geti(ints, "rank");
+    d.tokens = geti(ints, "tokens");
+    d.hidden = geti(ints, "hidden");
+    d.out_dim = geti(ints, "out_dim");
+    d.experts = geti(ints, "experts");
+    d.expert_slots = geti(ints, "expert_slots");
+    d.top_k = geti(ints, "top_k");
+    d.chunks = geti(ints, "chunks");
+    partial_ = geti(ints, "partial_chunks");
+    d.n_desc = partial_ < d.chunks ? partial_ + 1 : d.chunks;
+    feat_bf16_ = geti(ints, "feat_bf16") != 0;
+    out_bf16_ = geti(ints, "out_bf16") != 0;
+    d.feat_bytes = feat_bf16_ ? 2 : 4;
+    d.out_bytes = out_bf16_ ? 2 : 4;
+    d.placement = geti(ints, "placement");
+    d.gate_mode = geti(ints, "gate_mode");
+    d.mask_mode = geti(ints, "mask_mode");
+    d.ctl_per_chunk = geti(ints, "ctl_per_chunk");
+    d.ctl_nodes = geti(ints, "ctl_nodes");
+    d.pad0 = 0;
+    d.cap = d.tokens;
+    ffn_ = geti(ints, "ffn");
+    n1_ = geti(ints, "n1");
+    act1_ = geti(ints, "act1");
+    bn1_ = geti(ints, "bn1");
+    bn2_ = geti(ints, "bn2");
+    timeout_ns_ = (unsigned long long)ints["timeout_ns"].cast<int64_t>();
+    max_cands_ = geti(ints, "max_cands");
+    log_stride_ = geti(ints, "log_stride");
+    max_ctl_tokens_ = geti(ints, "max_ctl_tokens");
+    grid_sms_ = geti(ints, "sms");
+    if (d.world < 1 || d.world > raiccl::kMaxRanks) throw std::invalid_argument("world size 1..8");
+    if ((int)peer_bases.size() != d.world) throw std::invalid_argument("peer base count != world");
+    if ((int)chunk_offsets_.size() != d.chunks + 1) throw std::invalid_argument("chunk offsets");
+    if (d.top_k > 8 || d.experts > 255) throw std::invalid_argument("top_k <= 8 and experts <= 255");
+    if (d.chunks > 60) throw std::invalid_argument("at most 60 chunks");
+    layout_ = raiccl::make_sym_layout(d);
+    for (int r = 0; r < raiccl::kMaxRanks; ++r) peers_.base[r] = r < d.world ? (unsigned long long)peer_bases[r] : 0ULL;
+
+    // tensor maps of both GEMMs are built once (every buffer is fixed)
+    const long long rows = (long long)d.expert_slots * d.world * d.cap;
+    const CUtensorMapDataType dt = feat_bf16_ ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const int eb = d.feat_bytes, bk = 128 / eb;
+    void* recv_feat = reinterpret_cast<uint8_t*>(peers_.base[d.rank]) + layout_.recv_feat;
+    ta1_ = raiccl::make_tmap_2d_sw128(recv_feat, dt, eb, rows, d.hidden, d.hidden, 128, bk);
+    tb1_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "w1"), dt, eb, (uint64_t)d.expert_slots * n1_, d.hidden, d.hidden, bn1_, bk);
+    ta2_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "h"), dt, eb, rows, ffn_, ffn_, 128, bk);
+    tb2_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "w2"), dt, eb, (uint64_t)d.expert_slots * d.out_dim, ffn_, ffn_, bn2_, bk);
+
+    ck(cudaEventCreateWithFlags(&ev_start_, cudaEventDisableTiming), "cudaEventCreate");
+    ev_chunk_.resize(d.chunks);
+    for (auto& e : ev_chunk_) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+  }
+
+  ~MoELayerRunner() {
+    for (int a = 0; a < 2; ++a) {
+      if (exec_[a]) cudaGraphExecDestroy(exec_[a]);
+      if (graph_[a]) cudaGraphDestroy(graph_[a]);
+    }
+    for (auto& e : ev_chunk_) cudaEventDestroy(e);
+    if (ev_start_) cudaEventDestroy(ev_start_);
+  }
+
+  // Enqueue one layer call; returns the number of kernels launched.
+  int forward(bool delayed) {
+    const auto& d = dims_;
+    const py::dict& t = tensors_;
+    int launches = 0;
+    auto* status = ptr<raiccl::DeviceStatus>(t, "status");
+    auto* epoch = ptr<unsigned long long>(t, "epoch");
+    auto* sent_base = ptr<int>(t, "sent_base");
+    auto* desc_counts = ptr<int>(t, "desc_counts");
+    auto* done_counter = ptr<int>(t, "done_counter");
+    auto* permit = ptr<unsigned long long>(t, "permit");
+    auto* expert_ids = ptr<int>(t, "expert_ids");
+    auto* gates = ptr<float>(t, "gates");
+    auto* chunk_offsets_dev = ptr<int>(t, "chunk_offsets");
+
+    raiccl::launch_layer_reset(sent_base, d.experts, desc_counts, d.n_desc, done_counter, epoch, comm_);
+    ++launches;
+    ck(cudaEventRecord(ev_start_, comm_), "cudaEventRecord");
+    ck(cudaStreamWaitEvent(router_, ev_start_, 0), "cudaStreamWaitEvent");
+
+    // router chunks
+    raiccl::RouterParams rp{};
+    rp.tokens = ptr<void>(t, "tokens");
+    rp.weight = ptr<void>(t, "router_w");
+    rp.bias = ptr<float>(t, "router_b");
+    rp.block_mask = opt_ptr<uint8_t>(t, "block_mask");
+    const float* chunk_bias = opt_ptr<float>(t, "chunk_bias");
+    rp.hidden = d.hidden;
+    rp.experts = d.experts;
+    rp.top_k = d.top_k;
+    rp.gate_mode = d.gate_mode;
+    rp.mask_mode = d.mask_mode;
+    rp.expert_ids = expert_ids;
+    rp.gates = gates;
+    for (int c = 0; c < d.chunks; ++c) {
+      rp.row0 = (int)chunk_offsets_[c];
+      rp.row1 = (int)chunk_offsets_[c + 1];
+      rp.chunk_bias = chunk_bias ? chunk_bias + (long long)c * d.experts : nullptr;
+      if (rp.row1 > rp.row0) { raiccl::launch_router(rp, feat_bf16_, router_); ++launches; }
+      ck(cudaEventRecord(ev_chunk_[c], router_), "cudaEventRecord");
+    }
+
+    // control plane + dispatch
+    raiccl::ControlParams cp{};
+    cp.plan.E = geti_t("plan_E");
+    cp.plan.G = geti_t("plan_G");
+    cp.plan.V = d.ctl_nodes;
+    cp.plan.edge_src = ptr<int32_t>(t, "edge_src");
+    cp.plan.edge_tgt = ptr<int32_t>(t, "edge_tgt");
+    cp.plan.cap_units = ptr<int64_t>(t, "cap_units");
+    cp.plan.group_limits = opt_ptr<int64_t>(t, "group_limits");
+    cp.plan.group_ptr = ptr<int32_t>(t, "group_ptr");
+    cp.plan.group_members = opt_ptr<int32_t>(t, "group_members");
+    cp.plan.edge_group_ptr = ptr<int32_t>(t, "edge_group_ptr");
+    cp.plan.edge_group_members = opt_ptr<int32_t>(t, "edge_group_members");
+    cp.plan.distances = ptr<int32_t>(t, "distances");
+    cp.plan.tmpl_ptr = ptr<int32_t>(t, "tmpl_ptr");
+    cp.plan.tmpl_edge = opt_ptr<int32_t>(t, "tmpl_edge");
+    cp.plan.tmpl_src = opt_ptr<int32_t>(t, "tmpl_src");
+    cp.plan.tmpl_tgt = opt_ptr<int32_t>(t, "tmpl_tgt");
+    cp.plan.tmpl_tdist = opt_ptr<int32_t>(t, "tmpl_tdist");
+    cp.st.max_tokens = max_ctl_tokens_;
+    cp.st.sources = ptr<int32_t>(t, "st_sources");
+    cp.st.destinations = ptr<int32_t>(t, "st_destinations");
+    cp.st.holders = ptr<uint8_t>(t, "st_holders");
+    cp.st.ready = ptr<uint8_t>(t, "st_ready");
+    cp.st.committed = ptr<uint8_t>(t, "st_committed");
+    cp.st.residual = ptr<uint8_t>(t, "st_residual");
+    cp.st.remaining_hops = ptr<int32_t>(t, "st_remaining_hops");
+    cp.st.residual_demand = ptr<int64_t>(t, "st_residual_demand");
+    cp.st.link_credits = ptr<int64_t>(t, "st_link_credits");
+    cp.st.group_credits = opt_ptr<int64_t>(t, "st_group_credits");
+    cp.st.scratch_selected = ptr<uint8_t>(t, "st_scratch_selected");
+    cp.st.scratch_seen = ptr<uint8_t>(t, "st_scratch_seen");
+    cp.st.scratch_edge_load = ptr<int64_t>(t, "st_scratch_edge_load");
+    cp.expert_ids = expert_ids;
+    cp.chunk_offsets = chunk_offsets_dev;
+    cp.top_k = d.top_k;
+    cp.chunks = d.chunks;
+    cp.partial_chunks = partial_;
+    cp.ctl_per_chunk = d.ctl_per_chunk;
+    cp.ctl_nodes = d.ctl_nodes;
+    cp.max_cands = max_cands_;
+    cp.log_stride = log_stride_;
+    cp.scalars = ptr<long long>(t, "ctl_scalars");
+    cp.cand_buf = ptr<raiccl::sched::Cand>(t, "ctl_cands");
+    cp.keep_buf = ptr<int>(t, "ctl_keep");
+    cp.action_buf = ptr<int64_t>(t, "ctl_actions");
+    cp.log = ptr<int>(t, "ctl_log");
+    cp.permit = permit;
+    cp.epoch = epoch;
+    cp.status = status;
+
+    raiccl::DispatchParams dp{};
+    dp.dims = d;
+    dp.layout = layout_;
+    dp.peers = peers_;
+    dp.tokens = rp.tokens;
+    dp.expert_ids = expert_ids;
+    dp.gates = gates;
+    dp.token_ids = ptr<long long>(t, "token_ids");
+    dp.feat_digest = ptr<long long>(t, "feat_digest");
+    dp.checksum_base = ptr<long long>(t, "checksum_base");
+    dp.chunk_offsets = chunk_offsets_dev;
+    dp.sent_base = sent_base;
+    dp.desc_counts = desc_counts;
+    dp.done_counter = done_counter;
+    dp.permit = permit;
+    dp.epoch = epoch;
+    dp.status = status;
+
+    auto dispatch = [&](int q) {
+      const int c_lo = q < partial_ ? q : partial_;
+      const int c_hi = q < partial_ ? q : d.chunks - 1;
+      dp.desc = q;
+      dp.t0 = (int)chunk_offsets_[c_lo];
+      dp.t1 = (int)chunk_offsets_[c_hi + 1];
+      const int ntok = dp.t1 - dp.t0;
+      const int tpc = std::max(1, 16 / d.top_k);
+      const int grid = std::max(1, std::min(4 * grid_sms_, (ntok + tpc - 1) / tpc));
+      raiccl::launch_dispatch(dp, feat_bf16_, grid, comm_);
+      ++launches;
+    };
+    for (int q = 0; q < d.n_desc; ++q) {
+      const int last_chunk = q < partial_ ? q : d.chunks - 1;
+      ck(cudaStreamWaitEvent(comm_, ev_chunk_[last_chunk], 0), "cudaStreamWaitEvent");
+      cp.desc = q;
+      raiccl::launch_control(cp, comm_);
+      ++launches;
+      if (!delayed) dispatch(q);
+    }
+    if (delayed)
+      for (int q = 0; q < d.n_desc; ++q) dispatch(q);
+
+    // expert side
+    auto* segs = ptr<GemmSegment>(t, "segs");
+    raiccl::PlanParams pp{};
+    pp.dims = d;
+    pp.layout = layout_;
+    pp.peers = peers_;
+    pp.segs = segs;
+    pp.rows_out = ptr<int>(t, "rows_out");
+    pp.epoch = epoch;
+    pp.timeout_ns = timeout_ns_;
+    pp.status = status;
+    raiccl::launch_expert_plan(pp, comm_);
+    ++launches;
+
+    const int S = d.expert_slots * d.world;
+    raiccl::GroupedGemmParams g1{};
+    g1.segs = segs;
+    int* prefix1 = ptr<int>(t, "prefix1");
+    g1.tile_prefix = prefix1;
+    g1.num_segs = S;
+    g1.N = n1_;
+    g1.K = d.hidden;
+    g1.bias = opt_ptr<float>(t, "b1");
+    g1.row_map = nullptr;
+    g1.row_scale = nullptr;
+    g1.out_ptrs = reinterpret_cast<void* const*>(ptr<int64_t>(t, "out_ptrs1"));
+    g1.ldo = ffn_;
+    g1.status = status;
+    g1.timeout_ns = timeout_ns_;
+    raiccl::launch_tile_plan(segs, S, n1_ / bn1_, prefix1, comm_);
+    raiccl::launch_grouped_gemm(!feat_bf16_, feat_bf16_, act1_, bn1_, ta1_, tb1_, g1, grid_sms_, comm_);
+    launches += 2;
+
+    raiccl::GroupedGemmParams g2{};
+    g2.segs = segs;
+    int* prefix2 = ptr<int>(t, "prefix2");
+    g2.tile_prefix = prefix2;
+    g2.num_segs = S;
+    g2.N = d.out_dim;
+    g2.K = ffn_;
+    g2.bias = opt_ptr<float>(t, "b2");
+    g2.row_map = reinterpret_cast<const int*>(reinterpret_cast<uint8_t*>(peers_.base[d.rank]) + layout_.recv_retrow);
+    g2.row_scale = reinterpret_cast<const float*>(reinterpret_cast<uint8_t*>(peers_.base[d.rank]) + layout_.recv_gate);
+    g2.out_ptrs = reinterpret_cast<void* const*>(ptr<int64_t>(t, "out_ptrs2"));
+    g2.ldo = d.out_dim;
+    g2.status = status;
+    g2.timeout_ns = timeout_ns_;
+    raiccl::launch_tile_plan(segs, S, d.out_dim / bn2_, prefix2, comm_);
+    raiccl::launch_grouped_gemm(!feat_bf16_, out_bf16_, 0, bn2_, ta2_, tb2_, g2, grid_sms_, comm_);
+    launches += 2;
+
+    raiccl::ReturnMetaParams rm{};
+    rm.dims = d;
+    rm.layout = layout_;
+    rm.peers = peers_;
+    rm.segs = segs;
+    rm.status = status;
+    raiccl::launch_return_meta(rm, grid_sms_, comm_);
+    raiccl::SignalParams sp{};
+    sp.dims = d;
+    sp.layout = layout_;
+    sp.peers = peers_;
+    sp.epoch = epoch;
+    raiccl::launch_return_signal(sp, comm_);
+    raiccl::CombineParams cb{};
+    cb.dims = d;
+    cb.layout = layout_;
+    cb.peers = peers_;
+    cb.out = ptr<void>(t, "out");
+    cb.epoch = epoch;
+    cb.timeout_ns = timeout_ns_;
+    cb.status = status;
+    raiccl::launch_combine(cb, out_bf16_, grid_sms_, comm_);
+    launches += 3;
+    ck(cudaGetLastError(), "MoE layer launch");
+    return launches;
+  }
+
+  // Record one layer call of the given arm into that arm's CUDA graph slot.
+  int capture(bool delayed) {
+    const int a = delayed ? 1 : 0;
+    if (exec_[a]) { cudaGraphExecDestroy(exec_[a]); exec_[a] = nullptr; }
+    if (graph_[a]) { cudaGraphDestroy(graph_[a]); graph_[a] = nullptr; }
+    ck(cudaStreamBeginCapture(comm_, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+    int n = 0;
+    try {
+      n = forward(delayed);
+    } catch (...) {
+      cudaGraph_t g = nullptr;
+      cudaStreamEndCapture(comm_, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    ck(cudaStreamEndCapture(comm_, &graph_[a]), "cudaStreamEndCapture");
+    ck(cudaGraphInstantiate(&exec_[a], graph_[a], 0), "cudaGraphInstantiate");
+    graph_launches_[a] = n;
+    return n;
+  }
+
+  bool has_graph(bool delayed) const { return exec_[delayed ? 1 : 0] != nullptr; }
+
+  int replay(bool delayed) {
+    const int a = delayed ? 1 : 0;
+    if (!exec_[a]) throw std::runtime_error("no captured graph for this arm");
+    ck(cudaGraphLaunch(exec_[a], comm_), "cudaGraphLaunch");
+    return graph_launches_[a];
+  }
+
+  // Align all ranks on the device (no host round-trip) before a timed call.
+  void device_barrier() {
+    raiccl::BarrierParams bp{};
+    bp.dims = dims_;
+    bp.layout = layout_;
+    bp.peers = peers_;
+    bp.counter = ptr<unsigned long long>(tensors_, "bar_counter");
+    bp.timeout_ns = timeout_ns_;
+    bp.status = ptr<raiccl::DeviceStatus>(tensors_, "status");
+    raiccl::launch_device_barrier(bp, comm_);
+    ck(cudaGetLastError(), "device barrier launch");
+  }
+
+  long long sym_bytes() const { return layout_.total; }
+
+  py::dict layout() const {
+    py::dict o;
+    o["recv_feat"] = layout_.recv_feat;
+    o["recv_meta"] = layout_.recv_meta;
+    o["recv_retrow"] = layout_.recv_retrow;
+    o["recv_gate"] = layout_.recv_gate;
+    o["recv_count"] = layout_.recv_count;
+    o["recv_flag"] = layout_.recv_flag;
+    o["ret_out"] = layout_.ret_out;
+    o["ret_meta"] = layout_.ret_meta;
+    o["ret_flag"] = layout_.ret_flag;
+    o["bar_flag"] = layout_.bar_flag;
+    o["total"] = layout_.total;
+    return o;
+  }
+
+ private:
+  int geti_t(const char* key) const {
+    py::object o = tensors_[key];
+    return o.cast<int>();
+  }
+
+  py::dict tensors_;
+  std::vector<py::object> held_;
+  std::vector<long long> chunk_offsets_;
+  raiccl::MoEDims dims_{};
+  raiccl::SymLayout layout_{};
+  raiccl::PeerBases peers_{};
+  int partial_ = 0, ffn_ = 0, n1_ = 0, act1_ = 0, bn1_ = 0, bn2_ = 0;
+  int max_cands_ = 0, log_stride_ = 0, max_ctl_tokens_ = 0, grid_sms_ = 148;
+  bool feat_bf16_ = false, out_bf16_ = false;
+  unsigned long long timeout_ns_ = 0;
+  CUtensorMap ta1_{}, tb1_{}, ta2_{}, tb2_{};
+  cudaStream_t router_ = nullptr, comm_ = nullptr;
+  cudaEvent_t ev_start_ = nullptr;
+  std::vector<cudaEvent_t> ev_chunk_;
+  cudaGraph_t graph_[2] = {nullptr, nullptr};
+  cudaGraphExec_t exec_[2] = {nullptr, nullptr};
+  int graph_launches_[2] = {0, 0};
+};
+
+// Standalone router launch (tests and the router-only benchmark).
+void router_topk(torch::Tensor tokens, torch::Tensor weight, torch::Tensor bias,
+                 c10::optional<torch::Tensor> chunk_bias, c10::optional<torch::Tensor> block_mask,
+                 int64_t row0, int64_t row1, int64_t top_k, int64_t gate_mode, int64_t mask_mode,
+                 torch::Tensor expert_ids, torch::Tensor gates) {
+  TORCH_CHECK(tokens.is_cuda() && tokens.is_contiguous() && weight.is_contiguous(), "router: layout");
+  TORCH_CHECK(tokens.scalar_type() == weight.scalar_type(), "router: dtypes");
+  TORCH_CHECK(tokens.size(1) % (16 / tokens.element_size()) == 0, "router: hidden alignment");
+  TORCH_CHECK(weight.size(0) <= 64 && top_k <= 8 && top_k <= weight.size(0), "router: E <= 64, k <= 8");
+  TORCH_CHECK(bias.scalar_type() == torch::kFloat32 && expert_ids.scalar_type() == torch::kInt32 &&
+                  gates.scalar_type() == torch::kFloat32, "router: aux dtypes");
+  c10::cuda::CUDAGuard guard(tokens.device());
+  raiccl::RouterParams p{};
+  p.tokens = tokens.data_ptr();
+  p.weight = weight.data_ptr();
+  p.bias = bias.data_ptr<float>();
+  p.chunk_bias = chunk_bias ? chunk_bias->data_ptr<float>() : nullptr;
+  p.block_mask = block_mask ? block_mask->data_ptr<uint8_t>() : nullptr;
+  p.row0 = (int)row0;
+  p.row1 = (int)row1;
+  p.hidden = (int)tokens.size(1);
+  p.experts = (int)weight.size(0);
+  p.top_k = (int)top_k;
+  p.gate_mode = (int)gate_mode;
+  p.mask_mode = (int)mask_mode;
+  p.expert_ids = expert_ids.data_ptr<int>();
+  p.gates = gates.data_ptr<float>();
+  raiccl::launch_router(p, tokens.scalar_type() == torch::kBFloat16, at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void feature_digest(torch::Tensor rows, torch::Tensor digest) {
+  TORCH_CHECK(rows.is_cuda() && rows.is_contiguous() && rows.dim() == 2, "digest: rows");
+  TORCH_CHECK((rows.size(1) * rows.element_size()) % 4 == 0, "digest: row bytes % 4");
+  c10::cuda::CUDAGuard guard(rows.device());
+  raiccl::launch_feature_digest(rows.data_ptr(), rows.size(1) * rows.element_size(), (int)rows.size(0),
+                                reinterpret_cast<long long*>(digest.data_ptr<int64_t>()), at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void checksum_base(torch::Tensor token_ids, torch::Tensor digest, torch::Tensor chunk_offsets,
+                   int64_t rank, torch::Tensor out) {
+  c10::cuda::CUDAGuard guard(token_ids.device());
+  raiccl::launch_checksum_base(reinterpret_cast<const long long*>(token_ids.data_ptr<int64_t>()),
+                               reinterpret_cast<const long long*>(digest.data_ptr<int64_t>()),
+                               chunk_offsets.data_ptr<int>(), (int)chunk_offsets.numel() - 1, (int)rank,
+                               (int)token_ids.numel(), reinterpret_cast<long long*>(out.data_ptr<int64_t>()),
+                               at::cuda::getCurrentCUDAStream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+int64_t sym_layout_bytes(py::dict ints) {
+  raiccl::MoEDims d{};
+  d.world = geti(ints, "world");
+  d.tokens = geti(ints, "tokens");
+  d.hidden = geti(ints, "hidden");
+  d.out_dim = geti(ints, "out_dim");
+  d.expert_slots = geti(ints, "expert_slots");
+  d.top_k = geti(ints, "top_k");
+  d.n_desc = geti(ints, "n_desc");
+  d.feat_bytes = geti(ints, "feat_bf16") ? 2 : 4;
+  d.out_bytes = geti(ints, "out_bf16") ? 2 : 4;
+  d.cap = d.tokens;
+  return raiccl::make_sym_layout(d).total;
+}
+
+py::dict sym_layout(py::dict ints) {
+  raiccl::MoEDims d{};
+  d.world = geti(ints, "world");
+  d.tokens = geti(ints, "tokens");
+  d.hidden = geti(ints, "hidden");
+  d.out_dim = geti(ints, "out_dim");
+  d.expert_slots = geti(ints, "expert_slots");
+  d.top_k = geti(ints, "top_k");
+  d.n_desc = geti(ints, "n_desc");
+  d.feat_bytes = geti(ints, "feat_bf16") ? 2 : 4;
+  d.out_bytes = geti(ints, "out_bf16") ? 2 : 4;
+  d.cap = d.tokens;
+  auto L = raiccl::make_sym_layout(d);
+  py::dict o;
+  o["recv_feat"] = L.recv_feat; o["recv_meta"] = L.recv_meta; o["recv_retrow"] = L.recv_retrow;
+  o["recv_gate"] = L.recv_gate; o["recv_count"] = L.recv_count; o["recv_flag"] = L.recv_flag;
+  o["ret_out"] = L.ret_out; o["ret_meta"] = L.ret_meta; o["ret_flag"] = L.ret_flag;
+  o["bar_flag"] = L.bar_flag; o["total"] = L.total;
+  return o;
+}
+
+}  // namespace
+
+void register_moe(py::module_& m) {
+  py::class_<MoELayerRunner>(m, "MoELayerRunner")
+      .def(py::init<py::dict, py::dict, std::vector<int64_t>, std::vector<int64_t>, int64_t, int64_t>(),
+           py::arg("ints"), py::arg("tensors"), py::arg("peer_bases"), py::arg("chunk_offsets"),
+           py::arg("router_stream"), py::arg("comm_stream"))
+      .def("forward", &MoELayerRunner::forward, py::arg("delayed"))
+      .def("capture", &MoELayerRunner::capture, py::arg("delayed"))
+      .def("replay", &MoELayerRunner::replay, py::arg("delayed"))
+      .def("has_graph", &MoELayerRunner::has_graph, py::arg("delayed"))
+      .def("device_barrier", &MoELayerRunner::device_barrier)
+      .def("sym_bytes", &MoELayerRunner::sym_bytes)
+      .def("layout", &MoELayerRunner::layout);
+  m.def("router_topk", &router_topk, py::arg("tokens"), py::arg("weight"), py::arg("bias"),
+        py::arg("chunk_bias"), py::arg("block_mask"), py::arg("row0"), py::arg("row1"), py::arg("top_k"),
+        py::arg("gate_mode"), py::arg("mask_mode"), py::arg("expert_ids"), py::arg("gates"));
+  m.def("feature_digest", &feature_digest, py::arg("rows"), py::arg("digest"));
+  m.def("checksum_base", &checksum_base, py::arg("token_ids"), py::arg("digest"), py::arg("chunk_offsets"),
+        py::arg("rank"), py::arg("out"));
+  m.def("sym_layout_bytes", &sym_layout_bytes, py::arg("ints"));
+  m.def("sym_layout", &sym_layout, py::arg("ints"));
+}

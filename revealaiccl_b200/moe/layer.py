@@ -1,0 +1,318 @@
+"""ProgressiveMoELayer — the public entry point of the B200 data plane.
+
+One instance per rank.  Construction (untimed set-up, like the reference's
+fast data-prep precompute, rlccl/transport/fast_progressive_data_prep.py:56-67):
+deterministic inputs and weights, the compiled control plan of the control
+topology uploaded to the device, the symmetric peer region mapped on every
+rank, per-token feature digests and linear checksum bases, and the native
+runner.  ``forward(arm)`` then enqueues the whole layer without any host
+synchronisation: ``arm="early"`` dispatches each descriptor right after its
+scheduler trigger, ``arm="delayed"`` holds every dispatch until the final
+Router chunk (the reference's C/E1 and D/D1 arms).
+
+``verify()`` is the untimed, fail-closed post-hoc checker: forward identity
+rows, return rows, expert outputs and the combined output against the fp32
+oracle, the revealed-only packing counters, and a differential replay of the
+device control-plane log through the compiled scheduler, the uncompiled
+planner and the trusted checker.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+import math
+import time
+from typing import Any
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from ..ops import status as _status
+from ..ops._native import host, kernels
+from ..ops.grouped_gemm import ACT_IDS, pick_bn, swiglu_interleave, swiglu_interleave_bias
+from ..parallel.peer import PeerChannel, device_view
+from ..scheduling.compiled import StaticPlanCompiler, _plan_flat
+from ..topology.loader import load_rear4_topology
+from .config import MoELayerConfig
+from .inputs import make_rank_inputs, make_weights
+from .oracle import layer_reference
+
+FWD_META = 9
+RET_META = 8
+LOG_HEADER = 8
+
+
+@dataclass
+class LayerTiming:
+    device_ms: float
+    launches: int
+
+
+class ProgressiveMoELayer:
+    def __init__(self, cfg: MoELayerConfig, *, device: torch.device | str | None = None,
+                 world: int | None = None, rank: int | None = None, group=None,
+                 timeout_s: float = 10.0, seed: int = 0, control_topology=None) -> None:
+        self.cfg = cfg
+        if world is None:
+            world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        if rank is None:
+            rank = dist.get_rank(group) if world > 1 else 0
+        self.world, self.rank, self.group = int(world), int(rank), group
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if self.device.type != "cuda":
+            raise RuntimeError("ProgressiveMoELayer runs on CUDA devices (sm_100a)")
+        torch.cuda.set_device(self.device)
+        self._k = kernels()
+        self._h = host()
+        dev = self.device
+        W, T, D, E, k = self.world, cfg.tokens_per_rank, cfg.hidden, cfg.experts, cfg.top_k
+        self.slots = cfg.expert_slots(W)
+        bf16 = cfg.dtype == "bf16"
+        dt = torch.bfloat16 if bf16 else torch.float32
+
+        # ---- inputs and weights (deterministic)
+        self.inputs = make_rank_inputs(cfg, self.rank, W, dev, seed=seed)
+        self.weights = make_weights(cfg, dev, seed=seed)
+        swiglu = cfg.activation == "swiglu"
+        self.bn1 = pick_bn(cfg.gemm1_n, swiglu)
+        self.bn2 = pick_bn(cfg.out_dim)
+        F_, O = cfg.ffn_hidden, cfg.out_dim
+        w1l = torch.zeros((self.slots, cfg.gemm1_n, D), dtype=dt, device=dev)
+        w2l = torch.zeros((self.slots, O, F_), dtype=dt, device=dev)
+        b1l = torch.zeros((self.slots, cfg.gemm1_n), dtype=torch.float32, device=dev)
+        b2l = torch.zeros((self.slots, O), dtype=torch.float32, device=dev)
+        self.local_experts: list[int] = []
+        for s in range(self.slots):
+            e = s * W + self.rank if cfg.placement == "modulo" else self.rank * self.slots + s
+            if e >= E:
+                self.local_experts.append(-1)
+                continue
+            self.local_experts.append(e)
+            if swiglu:
+                w1l[s] = swiglu_interleave(self.weights.w1[e:e + 1, :F_], self.weights.w1[e:e + 1, F_:], self.bn1)[0]
+                if self.weights.b1 is not None:
+                    b1l[s] = swiglu_interleave_bias(self.weights.b1[e:e + 1, :F_], self.weights.b1[e:e + 1, F_:], self.bn1)[0]
+            else:
+                w1l[s] = self.weights.w1[e]
+                if self.weights.b1 is not None:
+                    b1l[s] = self.weights.b1[e]
+            w2l[s] = self.weights.w2[e]
+            if self.weights.b2 is not None:
+                b2l[s] = self.weights.b2[e]
+        has_b1 = self.weights.b1 is not None
+        has_b2 = self.weights.b2 is not None
+
+        # ---- control plan (compiled once) on the device
+        topo = control_topology if control_topology is not None else load_rear4_topology()[0]
+        if int(topo.V) != cfg.ctl_nodes:
+            raise ValueError("control topology node count must equal cfg.ctl_nodes")
+        self.plan = StaticPlanCompiler().compile(topo)
+        flat = _plan_flat(self.plan)
+        max_tmpl = max(len(g) for g in self.plan.templates_by_destination) if self.plan.templates_by_destination else 1
+        self.max_ctl_tokens = max(1, cfg.chunks * cfg.ctl_per_chunk)
+        self.max_cands = max(1, self.max_ctl_tokens * max(1, max_tmpl))
+        self.log_stride = LOG_HEADER + 2 * self.max_ctl_tokens + 4 * self.max_cands
+        V, Ep, G = self.plan.nodes, len(self.plan.edges), len(self.plan.group_edges)
+        Tc = self.max_ctl_tokens
+
+        def dev_t(a, dtype=None):
+            return torch.as_tensor(np.ascontiguousarray(a), device=dev, dtype=dtype)
+
+        # ---- symmetric region shared with the peers
+        ints = {
+            "world": W, "rank": self.rank, "tokens": T, "hidden": D, "out_dim": O, "experts": E,
+            "expert_slots": self.slots, "top_k": k, "chunks": cfg.chunks,
+            "partial_chunks": cfg.progressive_chunks, "n_desc": cfg.n_desc,
+            "feat_bf16": int(bf16), "out_bf16": int(bf16),
+            "placement": 0 if cfg.placement == "modulo" else 1,
+            "gate_mode": {"none": 0, "topk_softmax": 1, "softmax": 2}[cfg.gate_mode],
+            "mask_mode": {"none": 0, "topology_source": 1}[cfg.mask_mode],
+            "ctl_per_chunk": cfg.ctl_per_chunk, "ctl_nodes": cfg.ctl_nodes, "ffn": F_,
+            "n1": cfg.gemm1_n, "act1": ACT_IDS[cfg.activation], "bn1": self.bn1, "bn2": self.bn2,
+            "timeout_ns": int(timeout_s * 1e9), "max_cands": self.max_cands,
+            "log_stride": self.log_stride, "max_ctl_tokens": Tc,
+            "sms": torch.cuda.get_device_properties(dev).multi_processor_count,
+        }
+        self.layout = self._k.sym_layout(ints)
+        self.channel = PeerChannel(self.layout["total"], dev, group=group)
+        if self.channel.world != W:
+            raise RuntimeError("process group world size differs from the layer's world size")
+
+        # ---- per-token precompute (untimed): digests and checksum bases
+        self.chunk_offsets_dev = dev_t(np.asarray(cfg.chunk_offsets, dtype=np.int32))
+        self.feat_digest = torch.empty(T, dtype=torch.int64, device=dev)
+        self.checksum_base = torch.empty(T, dtype=torch.int64, device=dev)
+        if T > 0:
+            self._k.feature_digest(self.inputs.tokens, self.feat_digest)
+            self._k.checksum_base(self.inputs.token_ids, self.feat_digest, self.chunk_offsets_dev,
+                                  self.rank, self.checksum_base)
+
+        rows = self.slots * W * T
+        self.h = torch.empty((max(rows, 1), F_), dtype=dt, device=dev)
+        self.out = torch.zeros((T, O), dtype=dt, device=dev)
+        self.expert_ids = torch.zeros((T, k), dtype=torch.int32, device=dev)
+        self.gates = torch.zeros((T, k), dtype=torch.float32, device=dev)
+        self.status = _status.new_status(dev)
+        self.epoch = torch.zeros(1, dtype=torch.int64, device=dev)
+        nseg = self.slots * W
+        self.segs = torch.zeros((nseg, 8), dtype=torch.int32, device=dev)
+        self.rows_out = torch.zeros(nseg, dtype=torch.int32, device=dev)
+        out_ptrs2 = [b + self.layout["ret_out"] for b in self.channel.bases]
+        self.tensors: dict[str, Any] = {
+            "tokens": self.inputs.tokens, "router_w": self.weights.router_w, "router_b": self.weights.router_b,
+            "chunk_bias": self.inputs.chunk_bias, "block_mask": self.inputs.block_mask,
+            "expert_ids": self.expert_ids, "gates": self.gates,
+            "token_ids": self.inputs.token_ids, "feat_digest": self.feat_digest,
+            "checksum_base": self.checksum_base, "chunk_offsets": self.chunk_offsets_dev,
+            "sent_base": torch.zeros(E, dtype=torch.int32, device=dev),
+            "desc_counts": torch.zeros(cfg.n_desc * E, dtype=torch.int32, device=dev),
+            "done_counter": torch.zeros(cfg.n_desc, dtype=torch.int32, device=dev),
+            "permit": torch.zeros(cfg.n_desc, dtype=torch.int64, device=dev),
+            "epoch": self.epoch, "status": self.status,
+            "bar_counter": torch.zeros(1, dtype=torch.int64, device=dev),
+            "segs": self.segs, "rows_out": self.rows_out,
+            "prefix1": torch.zeros(nseg + 1, dtype=torch.int32, device=dev),
+            "prefix2": torch.zeros(nseg + 1, dtype=torch.int32, device=dev),
+            "w1": w1l.reshape(self.slots * cfg.gemm1_n, D).contiguous(),
+            "b1": b1l.reshape(-1).contiguous() if has_b1 else None,
+            "w2": w2l.reshape(self.slots * O, F_).contiguous(),
+            "b2": b2l.reshape(-1).contiguous() if has_b2 else None,
+            "h": self.h, "out": self.out,
+            "out_ptrs1": torch.tensor([self.h.data_ptr()] * W, dtype=torch.int64, device=dev),
+            "out_ptrs2": torch.tensor(out_ptrs2, dtype=torch.int64, device=dev),
+            # control plan + state
+            "plan_E": Ep, "plan_G": G,
+            "edge_src": dev_t(flat["edge_src"]), "edge_tgt": dev_t(flat["edge_tgt"]),
+            "cap_units": dev_t(flat["cap_units"]),
+            "group_limits": dev_t(flat["group_limits"]) if G else torch.zeros(1, dtype=torch.int64, device=dev),
+            "group_ptr": dev_t(flat["group_ptr"]),
+            "group_members": dev_t(flat["group_members"]) if flat["group_members"].size else torch.zeros(1, dtype=torch.int32, device=dev),
+            "edge_group_ptr": dev_t(flat["edge_group_ptr"]),
+            "edge_group_members": dev_t(flat["edge_group_members"]) if flat["edge_group_members"].size else torch.zeros(1, dtype=torch.int32, device=dev),
+            "distances": dev_t(flat["distances"]), "tmpl_ptr": dev_t(flat["tmpl_ptr"]),
+            "tmpl_edge": dev_t(flat["tmpl_edge"]) if flat["tmpl_edge"].size else torch.zeros(1, dtype=torch.int32, device=dev),
+            "tmpl_src": dev_t(flat["tmpl_src"]) if flat["tmpl_src"].size else torch.zeros(1, dtype=torch.int32, device=dev),
+            "tmpl_tgt": dev_t(flat["tmpl_tgt"]) if flat["tmpl_tgt"].size else torch.zeros(1, dtype=torch.int32, device=dev),
+            "tmpl_tdist": dev_t(flat["tmpl_tdist"]) if flat["tmpl_tdist"].size else torch.zeros(1, dtype=torch.int32, device=dev),
+            "st_sources": torch.zeros(Tc, dtype=torch.int32, device=dev),
+            "st_destinations": torch.zeros(Tc, dtype=torch.int32, device=dev),
+            "st_holders": torch.zeros(Tc * V, dtype=torch.uint8, device=dev),
+            "st_ready": torch.zeros(Tc, dtype=torch.uint8, device=dev),
+            "st_committed": torch.zeros(Tc * Ep, dtype=torch.uint8, device=dev),
+            "st_residual": torch.zeros(Tc, dtype=torch.uint8, device=dev),
+            "st_remaining_hops": torch.zeros(Tc, dtype=torch.int32, device=dev),
+            "st_residual_demand": torch.zeros(V * V, dtype=torch.int64, device=dev),
+            "st_link_credits": torch.zeros(Ep, dtype=torch.int64, device=dev),
+            "st_group_credits": torch.zeros(max(G, 1), dtype=torch.int64, device=dev),
+            "st_scratch_selected": torch.zeros(Tc, dtype=torch.uint8, device=dev),
+            "st_scratch_seen": torch.zeros(Tc, dtype=torch.uint8, device=dev),
+            "st_scratch_edge_load": torch.zeros(Ep, dtype=torch.int64, device=dev),
+            "ctl_scalars": torch.zeros(11 + 2 * cfg.chunks, dtype=torch.int64, device=dev),
+            "ctl_cands": torch.zeros(self.max_cands * 4, dtype=torch.int32, device=dev),
+            "ctl_keep": torch.zeros(self.max_cands, dtype=torch.int32, device=dev),
+            "ctl_actions": torch.zeros(2 * Tc, dtype=torch.int64, device=dev),
+            "ctl_log": torch.zeros(cfg.n_desc * self.log_stride, dtype=torch.int32, device=dev),
+        }
+        self.tensors = {kk: v for kk, v in self.tensors.items() if v is not None}
+        self.router_stream = torch.cuda.Stream(device=dev)
+        self.comm_stream = torch.cuda.Stream(device=dev)
+        torch.cuda.synchronize(dev)
+        self.runner = self._k.MoELayerRunner(
+            ints, self.tensors, [int(b) for b in self.channel.bases], list(cfg.chunk_offsets),
+            self.router_stream.cuda_stream, self.comm_stream.cuda_stream)
+        self._graph_arm: str | None = None
+        self.launches_per_call = 0
+        if W > 1:
+            dist.barrier(group=group)
+
+    # ------------------------------------------------------------------ run
+    def forward(self, arm: str = "early") -> torch.Tensor:
+        """Enqueue one layer call on the layer's comm stream (no host sync)."""
+        if arm not in ("early", "delayed"):
+            raise ValueError("arm must be 'early' or 'delayed'")
+        self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+        self.launches_per_call = self.runner.forward(arm == "delayed")
+        return self.out
+
+    def capture(self, arm: str = "early") -> int:
+        """Record one layer call of ``arm`` as a CUDA graph (call ``forward`` once before)."""
+        torch.cuda.synchronize(self.device)
+        n = self.runner.capture(arm == "delayed")
+        self._graph_arm = arm
+        self.launches_per_call = n
+        return n
+
+    def replay(self, arm: str | None = None) -> torch.Tensor:
+        """Relaunch the captured graph of ``arm`` (default: the last captured arm)."""
+        arm = arm or self._graph_arm or "early"
+        self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+        self.launches_per_call = self.runner.replay(arm == "delayed")
+        return self.out
+
+    def device_barrier(self) -> None:
+        """Align every rank on the device (cross-GPU flag barrier on the comm stream)."""
+        self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+        self.runner.device_barrier()
+
+    def load_tokens_(self, host_tokens: torch.Tensor) -> None:
+        """Copy a new [T, D] token batch from (pinned) host memory on the comm
+        stream and refresh its per-token digests and checksum bases."""
+        with torch.cuda.stream(self.comm_stream):
+            self.inputs.tokens.copy_(host_tokens, non_blocking=True)
+            if self.cfg.tokens_per_rank:
+                self._k.feature_digest(self.inputs.tokens, self.feat_digest)
+                self._k.checksum_base(self.inputs.token_ids, self.feat_digest, self.chunk_offsets_dev,
+                                      self.rank, self.checksum_base)
+
+    def __call__(self, host_tokens: torch.Tensor, host_out: torch.Tensor | None = None,
+                 arm: str = "early") -> torch.Tensor:
+        """End-to-end call: pinned host tokens in, combined output back in host
+        memory (the captured graph of ``arm`` is used when one exists)."""
+        self.load_tokens_(host_tokens)
+        if self.runner.has_graph(arm == "delayed"):
+            self.launches_per_call = self.runner.replay(arm == "delayed") + 2
+        else:
+            self.launches_per_call = self.runner.forward(arm == "delayed") + 2
+        if host_out is None:
+            host_out = torch.empty(self.out.shape, dtype=self.out.dtype, pin_memory=True)
+        with torch.cuda.stream(self.comm_stream):
+            host_out.copy_(self.out, non_blocking=True)
+        return host_out
+
+    def clear_returns(self) -> None:
+        """Zero this rank's return region (so a lost return row cannot hide behind
+        a previous call's row); collective-free, call between layer calls."""
+        torch.cuda.synchronize(self.device)
+        n = self.layout["ret_flag"] - self.layout["ret_out"]
+        self._region("ret_out", (n,), torch.uint8).zero_()
+        torch.cuda.synchronize(self.device)
+
+    def wait(self) -> None:
+        torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
+
+    def check_status(self) -> None:
+        torch.cuda.synchronize(self.device)
+        _status.check(self.status)
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        self.runner = None
+        self.channel.close()
+
+    # --------------------------------------------------------------- checker
+    def _region(self, name: str, shape, dtype, rank: int | None = None) -> torch.Tensor:
+        return self.channel.view(self.layout[name], shape, dtype, rank)
+
+    def verify(self, *, atol: float | None = None, rtol: float | None = None,
+               replay_control: bool = True) -> dict[str, Any]:
+        """Fail-closed post-hoc checker of the last layer call (collective: every
+        rank must call it; it raises on any violation)."""
+        from .checker import verify_layer
+
+        return verify_layer(self, atol=atol, rtol=rtol, replay_control=replay_control)
+
+
+__all__ = ["LayerTiming", "ProgressiveMoELayer"]

@@ -1,0 +1,147 @@
+"""GPU tests of the progressive MoE data plane on one B200 (world size 1).
+
+Every kernel result is compared against a plain PyTorch fp32 reference of the
+same op; the full layer is checked by the fail-closed checker (identity rows,
+return rows, expert outputs, combined output, packing counters and the
+differential replay of the device control plane), and the early and delayed
+arms must produce bit-identical outputs.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _small(dtype="fp32", act="relu", k=2, **kw):
+    from revealaiccl_b200.moe.config import MoELayerConfig
+
+    return MoELayerConfig(
+        name=f"small_{dtype}_{act}", tokens_per_rank=1024, hidden=256, experts=4, top_k=k,
+        chunk_sizes=(128,) * 8, ffn_hidden=256 if act != "swiglu" else 128, out_dim=256,
+        activation=act, dtype=dtype, placement="contiguous",
+        gate_mode="topk_softmax" if k > 1 else "none", router_init="unit_logits",
+        expert_init="normal002", **kw)
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+@pytest.mark.parametrize("E,k", [(4, 1), (8, 2), (64, 6)])
+def test_router_kernel_matches_fp32_oracle(dtype, E, k):
+    from revealaiccl_b200.ops._native import kernels
+
+    torch.manual_seed(0)
+    dev = torch.device("cuda")
+    dt = torch.bfloat16 if dtype == "bf16" else torch.float32
+    T, D = 700, 512
+    x = torch.randn(T, D, device=dev).to(dt)
+    w = (torch.randn(E, D, device=dev) / D ** 0.5).to(dt)
+    b = torch.randn(E, device=dev) * 0.1
+    ids = torch.zeros(T, k, dtype=torch.int32, device=dev)
+    gates = torch.zeros(T, k, device=dev)
+    kernels().router_topk(x, w, b, None, None, 0, T, k, 1, 1, ids, gates)
+    logits = x.float() @ w.float().t() + b
+    pos = torch.arange(T, device=dev)
+    logits[pos, pos % E] = float("-inf")
+    vals, ref = torch.sort(logits, dim=-1, descending=True, stable=True)
+    ref = ref[:, :k].int()
+    gap_ok = (vals[:, :k] - logits.gather(1, ids.long())).abs() <= 1e-4 * (1 + vals[:, :1].abs())
+    assert ((ref == ids).all(dim=1) | gap_ok.all(dim=1)).all()
+    ref_g = torch.softmax(vals[:, :k], dim=-1)
+    same = (ref == ids).all(dim=1)
+    torch.testing.assert_close(gates[same], ref_g[same], atol=1e-4, rtol=1e-4)
+
+
+def test_router_ties_pick_smaller_expert():
+    from revealaiccl_b200.ops._native import kernels
+
+    dev = torch.device("cuda")
+    T, D, E = 64, 64, 8
+    x = torch.zeros(T, D, device=dev)
+    w = torch.zeros(E, D, device=dev)
+    b = torch.zeros(E, device=dev)
+    b[3] = b[5] = 1.0
+    ids = torch.zeros(T, 2, dtype=torch.int32, device=dev)
+    gates = torch.zeros(T, 2, device=dev)
+    kernels().router_topk(x, w, b, None, None, 0, T, 2, 0, 0, ids, gates)
+    assert (ids[:, 0] == 3).all() and (ids[:, 1] == 5).all()
+
+
+def test_feature_digest_matches_numpy():
+    from revealaiccl_b200.ops._native import kernels
+    from revealaiccl_b200.transport.formats import row_digest
+
+    dev = torch.device("cuda")
+    x = torch.randn(257, 384, device=dev)
+    dig = torch.empty(257, dtype=torch.int64, device=dev)
+    kernels().feature_digest(x, dig)
+    assert np.array_equal(dig.cpu().numpy(), row_digest(x.cpu().numpy()))
+
+
+@pytest.mark.parametrize("dtype,act,k", [("fp32", "relu", 1), ("fp32", "gelu", 2), ("bf16", "swiglu", 2)])
+def test_layer_world1_early_delayed_identical_and_verified(dtype, act, k):
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    layer = ProgressiveMoELayer(_small(dtype, act, k), timeout_s=5.0)
+    try:
+        layer.forward("early")
+        rep_e = layer.verify()
+        out_e = layer.out.clone()
+        layer.forward("delayed")
+        rep_d = layer.verify()
+        assert rep_e["pass"] and rep_d["pass"]
+        assert torch.equal(out_e, layer.out)
+        assert rep_e["control"]["total"] == layer.cfg.n_desc
+    finally:
+        layer.close()
+
+
+def test_r4_reference_config_world1():
+    from revealaiccl_b200.moe.config import preset
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    layer = ProgressiveMoELayer(preset("r4_reference"), timeout_s=5.0)
+    try:
+        layer.forward("early")
+        rep = layer.verify()
+        assert rep["pass"], rep["violations"]
+        assert rep["forward"]["tokens"] == 4096
+        out_e = layer.out.clone()
+        layer.forward("delayed")
+        assert layer.verify()["pass"]
+        assert torch.equal(out_e, layer.out)
+    finally:
+        layer.close()
+
+
+def test_r4_case_families_world1():
+    from revealaiccl_b200.moe.config import CASE_ORDER, r4_case
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    for case in CASE_ORDER:
+        layer = ProgressiveMoELayer(r4_case(case), timeout_s=5.0)
+        try:
+            layer.forward("early")
+            rep = layer.verify()
+            assert rep["pass"], (case, rep["violations"])
+        finally:
+            layer.close()
+
+
+def test_graph_capture_replay_repeated_calls():
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    layer = ProgressiveMoELayer(_small("bf16", "swiglu", 2), timeout_s=5.0)
+    try:
+        layer.forward("early")
+        ref = layer.out.clone()
+        n = layer.capture("early")
+        assert n > 10
+        for _ in range(3):
+            layer.replay()
+        torch.cuda.synchronize()
+        rep = layer.verify()
+        assert rep["pass"] and rep["epoch"] == 4
+        assert torch.equal(ref, layer.out)
+    finally:
+        layer.close()
