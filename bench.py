@@ -48,7 +48,7 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, bus_ids: list[str]):
-        self.bus_ids = {b.lower()[-12:] for b in bus_ids}
+        self.bus_ids = {str(b).lower()[-7:] for b in bus_ids}
         self.rows: list[list[str]] = []
         self._stop = threading.Event()
         self._thread: threading.Thread | None = None
@@ -60,7 +60,7 @@ class ClockSampler:
                                      capture_output=True, text=True, timeout=5).stdout
                 for line in out.strip().splitlines():
                     parts = [p.strip() for p in line.split(",")]
-                    if len(parts) >= 10 and parts[1].lower()[-12:] in self.bus_ids:
+                    if len(parts) >= 10 and parts[1].lower()[-7:] in self.bus_ids:
                         self.rows.append(parts)
             except Exception:
                 pass
@@ -144,7 +144,9 @@ def run_product(args) -> dict | None:
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
-        bus = torch.cuda.get_device_properties(dev).pci_bus_id if hasattr(torch.cuda.get_device_properties(dev), "pci_bus_id") else None
+        props = torch.cuda.get_device_properties(dev)
+        bus = (f"{int(props.pci_bus_id):02X}:{int(props.pci_device_id):02X}.0"
+               if hasattr(props, "pci_bus_id") and hasattr(props, "pci_device_id") else None)
         bus_ids = [bus] if bus else []
         if world > 1:
             gathered = [None] * world

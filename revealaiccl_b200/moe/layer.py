@@ -117,7 +117,7 @@ class ProgressiveMoELayer:
         Tc = self.max_ctl_tokens
 
         def dev_t(a, dtype=None):
-            return torch.as_tensor(np.ascontiguousarray(a), device=dev, dtype=dtype)
+            return torch.as_tensor(np.array(a, copy=True), device=dev, dtype=dtype)
 
         # ---- symmetric region shared with the peers
         ints = {
@@ -233,6 +233,7 @@ class ProgressiveMoELayer:
             raise ValueError("arm must be 'early' or 'delayed'")
         self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
         self.launches_per_call = self.runner.forward(arm == "delayed")
+        torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
         return self.out
 
     def capture(self, arm: str = "early") -> int:
@@ -248,6 +249,7 @@ class ProgressiveMoELayer:
         arm = arm or self._graph_arm or "early"
         self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
         self.launches_per_call = self.runner.replay(arm == "delayed")
+        torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
         return self.out
 
     def device_barrier(self) -> None:
@@ -278,6 +280,7 @@ class ProgressiveMoELayer:
             host_out = torch.empty(self.out.shape, dtype=self.out.dtype, pin_memory=True)
         with torch.cuda.stream(self.comm_stream):
             host_out.copy_(self.out, non_blocking=True)
+        torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
         return host_out
 
     def clear_returns(self) -> None:
