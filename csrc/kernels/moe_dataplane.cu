@@ -88,32 +88,59 @@ __global__ void moe_checksum_base_kernel(const long long* token_ids, const long 
 // the smaller expert id), gates.  One warp per token row, fp32 accumulation
 // (exact fp32 for fp32 inputs).  W is [E, D] in the token dtype.
 // ---------------------------------------------------------------------------
-template <typename T, int EMAX>
+// Router rows are streamed with UNROLL independent 16-byte loads in flight per
+// lane (the kernel is HBM-bound for small E); W is staged once per CTA in
+// shared memory when it fits (SMEM_W), else read through the read-only cache.
+constexpr int kRouterUnroll = 8;
+
+template <typename T, int EMAX, bool SMEM_W>
 __global__ void __launch_bounds__(256) moe_router_kernel(RouterParams p) {
+  extern __shared__ __align__(16) uint8_t router_smem[];
   const T* __restrict__ tokens = (const T*)p.tokens;
+  const int D = p.hidden, E = p.experts;
   const T* __restrict__ w = (const T*)p.weight;
+  if constexpr (SMEM_W) {
+    uint4* ws = (uint4*)router_smem;
+    const uint4* wg = (const uint4*)p.weight;
+    const int nvec = E * D * (int)sizeof(T) / 16;
+    for (int i = threadIdx.x; i < nvec; i += blockDim.x) ws[i] = __ldg(wg + i);
+    __syncthreads();
+    w = (const T*)router_smem;
+  }
   const int warps = blockDim.x >> 5;
   const int t = p.row0 + blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= p.row1) return;
-  const int D = p.hidden, E = p.experts;
   constexpr int VEC = 16 / sizeof(T);
   float acc[EMAX];
 #pragma unroll
   for (int e = 0; e < EMAX; ++e) acc[e] = 0.f;
   const T* x = tokens + (long long)t * D;
-  for (int base = lane * VEC; base < D; base += 32 * VEC) {
-    T xv[VEC];
-    *(uint4*)xv = __ldg((const uint4*)(x + base));
+  constexpr int STEP = 32 * VEC * kRouterUnroll;
+  for (int base0 = 0; base0 < D; base0 += STEP) {
+    uint4 xr[kRouterUnroll];
 #pragma unroll
-    for (int e = 0; e < EMAX; ++e) {
-      if (e < E) {
-        T wv[VEC];
-        *(uint4*)wv = __ldg((const uint4*)(w + (long long)e * D + base));
-        float s = 0.f;
+    for (int u = 0; u < kRouterUnroll; ++u) {
+      const int base = base0 + (u * 32 + lane) * VEC;
+      xr[u] = base < D ? __ldg((const uint4*)(x + base)) : make_uint4(0, 0, 0, 0);
+    }
 #pragma unroll
-        for (int v = 0; v < VEC; ++v) s = fmaf(to_f(xv[v]), to_f(wv[v]), s);
-        acc[e] += s;
+    for (int u = 0; u < kRouterUnroll; ++u) {
+      const int base = base0 + (u * 32 + lane) * VEC;
+      if (base >= D) break;
+      const T* xv = (const T*)&xr[u];
+#pragma unroll
+      for (int e = 0; e < EMAX; ++e) {
+        if (e < E) {
+          uint4 wr;
+          if constexpr (SMEM_W) wr = *(const uint4*)(w + (long long)e * D + base);
+          else wr = __ldg((const uint4*)(w + (long long)e * D + base));
+          const T* wv = (const T*)&wr;
+          float s = 0.f;
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) s = fmaf(to_f(xv[v]), to_f(wv[v]), s);
+          acc[e] += s;
+        }
       }
     }
   }
@@ -252,7 +279,20 @@ __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(Dispatch
       uint8_t* base = (uint8_t*)p.peers.base[r];
       uint4* dst = (uint4*)(base + p.layout.recv_feat + grow * d.hidden * d.feat_bytes);
       const uint4* src = (const uint4*)((const uint8_t*)p.tokens + (long long)t * d.hidden * d.feat_bytes);
-      for (int v = lane; v < vec_per_row; v += 32) dst[v] = __ldg(src + v);
+      constexpr int U = 8;  // 16-byte loads in flight per lane before the stores
+      for (int v0 = 0; v0 < vec_per_row; v0 += 32 * U) {
+        uint4 r[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int v = v0 + u * 32 + lane;
+          if (v < vec_per_row) r[u] = __ldg(src + v);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int v = v0 + u * 32 + lane;
+          if (v < vec_per_row) dst[v] = r[u];
+        }
+      }
       if (lane < kFwdMetaFields) {
         int c = 0;
         while (c + 1 < d.chunks && p.chunk_offsets[c + 1] <= t) ++c;
@@ -478,16 +518,31 @@ void launch_router(const RouterParams& p, bool bf16, cudaStream_t s) {
   if (rows <= 0) return;
   const int warps = 8;
   const dim3 grid((rows + warps - 1) / warps);
+  const long long wbytes = (long long)p.experts * p.hidden * (bf16 ? 2 : 4);
+  const bool smem_w = wbytes <= 96 * 1024;
+  const int smem = smem_w ? (int)wbytes : 0;
+#define RAICCL_ROUTER(T, EM)                                                                    \
+  do {                                                                                          \
+    if (smem_w) {                                                                               \
+      static bool attr = false;                                                                 \
+      if (!attr) {                                                                              \
+        cudaFuncSetAttribute(moe_router_kernel<T, EM, true>,                                    \
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);           \
+        attr = true;                                                                            \
+      }                                                                                         \
+      moe_router_kernel<T, EM, true><<<grid, warps * 32, smem, s>>>(p);                         \
+    } else {                                                                                    \
+      moe_router_kernel<T, EM, false><<<grid, warps * 32, 0, s>>>(p);                           \
+    }                                                                                           \
+  } while (0)
   if (p.experts <= 8) {
-    if (bf16) moe_router_kernel<__nv_bfloat16, 8><<<grid, warps * 32, 0, s>>>(p);
-    else moe_router_kernel<float, 8><<<grid, warps * 32, 0, s>>>(p);
+    if (bf16) RAICCL_ROUTER(__nv_bfloat16, 8); else RAICCL_ROUTER(float, 8);
   } else if (p.experts <= 16) {
-    if (bf16) moe_router_kernel<__nv_bfloat16, 16><<<grid, warps * 32, 0, s>>>(p);
-    else moe_router_kernel<float, 16><<<grid, warps * 32, 0, s>>>(p);
+    if (bf16) RAICCL_ROUTER(__nv_bfloat16, 16); else RAICCL_ROUTER(float, 16);
   } else {
-    if (bf16) moe_router_kernel<__nv_bfloat16, 64><<<grid, warps * 32, 0, s>>>(p);
-    else moe_router_kernel<float, 64><<<grid, warps * 32, 0, s>>>(p);
+    if (bf16) RAICCL_ROUTER(__nv_bfloat16, 64); else RAICCL_ROUTER(float, 64);
   }
+#undef RAICCL_ROUTER
 }
 
 void launch_dispatch(const DispatchParams& p, bool bf16, int grid, cudaStream_t s) {

@@ -176,6 +176,9 @@ class MoELayerRunner {
     raiccl::ControlParams cp{};
     cp.plan.E = geti_t("plan_E");
     cp.plan.G = geti_t("plan_G");
+    cp.n_group_members = geti_t("plan_NGM");
+    cp.n_edge_group_members = geti_t("plan_NEGM");
+    cp.n_tmpl = geti_t("plan_NT");
     cp.plan.V = d.ctl_nodes;
     cp.plan.edge_src = ptr<int32_t>(t, "edge_src");
     cp.plan.edge_tgt = ptr<int32_t>(t, "edge_tgt");

@@ -182,7 +182,8 @@ class ProgressiveMoELayer:
             "out_ptrs1": torch.tensor([self.h.data_ptr()] * W, dtype=torch.int64, device=dev),
             "out_ptrs2": torch.tensor(out_ptrs2, dtype=torch.int64, device=dev),
             # control plan + state
-            "plan_E": Ep, "plan_G": G,
+            "plan_E": Ep, "plan_G": G, "plan_NGM": int(flat["group_members"].size),
+            "plan_NEGM": int(flat["edge_group_members"].size), "plan_NT": int(flat["tmpl_edge"].size),
             "edge_src": dev_t(flat["edge_src"]), "edge_tgt": dev_t(flat["edge_tgt"]),
             "cap_units": dev_t(flat["cap_units"]),
             "group_limits": dev_t(flat["group_limits"]) if G else torch.zeros(1, dtype=torch.int64, device=dev),
