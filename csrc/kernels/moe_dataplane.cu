@@ -323,15 +323,17 @@ __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(Dispatch
   }
 
   // completion: the last CTA of the launch publishes counts and signals
+  // Ordering: every thread's stores -> bar.sync -> thread 0's device-scope
+  // acq_rel increment; the last CTA's acquiring increment sees all of them,
+  // and its st.release.sys below is cumulative, so a peer that acquires the
+  // ready word also sees every row of every CTA (no per-CTA system fence).
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
-    const int prev = atomicAdd(&p.done_counter[p.desc], 1);
+    const int prev = atom_add_acq_rel_gpu(&p.done_counter[p.desc], 1);
     s_last = (prev == (int)gridDim.x - 1) ? 1 : 0;
   }
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     const int cnt = atomicAdd(&p.desc_counts[(long long)p.desc * E + e], 0);
     const int r = expert_owner(d, e), le = expert_slot(d, e);
@@ -341,7 +343,6 @@ __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(Dispatch
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
     for (int r = 0; r < d.world; ++r) {
       uint8_t* base = (uint8_t*)p.peers.base[r];
       st_release_sys_u64((uint64_t*)(base + p.layout.recv_flag) + (long long)d.rank * d.n_desc + p.desc,
