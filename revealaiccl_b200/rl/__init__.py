@@ -1,1 +1,1 @@
-"""rl subpackage."""
+"""Schedule-search RL stack: slot decoder, PPO, scenarios/evaluator, CLIs, XML export."""
