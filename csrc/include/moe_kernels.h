@@ -6,6 +6,7 @@
 #include <cstdint>
 
 #include "moe_layout.h"
+#include "control_layout.h"
 #include "sched_core.h"
 #include "types.h"
 
@@ -90,6 +91,9 @@ struct BarrierParams {
 
 // Device-resident compiled-scheduler control plane (one CTA).
 struct ControlParams {
+  // Working set as one blob laid out by control_layout(); plan/st below are
+  // typed views of the same memory (the kernel stages the blob instead).
+  uint8_t* blob;
   sched::PlanView plan;
   sched::StateView st;
   const int32_t* expert_ids;   // [T, k]

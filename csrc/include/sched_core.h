@@ -101,9 +101,30 @@ SCHED_HD int enumerate(const PlanView& p, const StateView& st, int revealed, Can
   return n;
 }
 
+// Candidates of one ordinal in template order (the device control plane
+// enumerates ordinals in parallel: ordinal o's candidates land at
+// out[prefix(o) ...], the same positions the sequential loop gives them).
+SCHED_HD int enumerate_one(const PlanView& p, const StateView& st, int o, Cand* out, int cap) {
+  if (!st.ready[o] || !st.residual[o]) return 0;
+  const int d = st.destinations[o];
+  const int before = st.remaining_hops[o];
+  if (before <= 0 || before >= kInf) return 0;
+  const uint8_t* h = st.holders + (long long)o * p.V;
+  int n = 0;
+  for (int k = p.tmpl_ptr[d]; k < p.tmpl_ptr[d + 1]; ++k) {
+    if (h[p.tmpl_src[k]] && !h[p.tmpl_tgt[k]] && p.tmpl_tdist[k] == before - 1) {
+      if (out != nullptr && n < cap) out[n] = Cand{o, p.tmpl_edge[k], before, before - 1};
+      ++n;
+    }
+  }
+  return n;
+}
+
 // Greedy selection; writes the kept candidate indices to keep[]; returns count.
-SCHED_HD int select(const PlanView& p, StateView& st, const Cand* c, int n, int revealed, int* keep) {
-  reset_slot_credits(p, st);
+// `credits_reset`: the caller already reset the slot credits and selection scratch.
+SCHED_HD int select(const PlanView& p, StateView& st, const Cand* c, int n, int revealed, int* keep,
+                    bool credits_reset = false) {
+  if (!credits_reset) reset_slot_credits(p, st);
   int kept = 0;
   for (int i = 0; i < n; ++i) {
     const int o = c[i].ordinal, e = c[i].edge;
@@ -125,9 +146,11 @@ SCHED_HD int select(const PlanView& p, StateView& st, const Cand* c, int n, int 
 
 // actions: n pairs (ordinal or -1, edge).  Returns a Reason.
 SCHED_HD int check(const PlanView& p, StateView& st, const int64_t* actions, int n, int revealed,
-                   bool require_sched) {
-  for (int t = 0; t < st.max_tokens; ++t) st.scratch_seen[t] = 0;
-  for (int e = 0; e < p.E; ++e) st.scratch_edge_load[e] = 0;
+                   bool require_sched, bool scratch_reset = false) {
+  if (!scratch_reset) {
+    for (int t = 0; t < st.max_tokens; ++t) st.scratch_seen[t] = 0;
+    for (int e = 0; e < p.E; ++e) st.scratch_edge_load[e] = 0;
+  }
   for (int i = 0; i < n; ++i) {
     const int64_t o = actions[2 * i], e = actions[2 * i + 1];
     if (o < 0 || o >= revealed || !st.ready[o]) return kUnrevealed;
@@ -156,8 +179,9 @@ SCHED_HD int check(const PlanView& p, StateView& st, const int64_t* actions, int
   return kAccept;
 }
 
-SCHED_HD void apply(const PlanView& p, StateView& st, const int64_t* actions, int n) {
-  reset_slot_credits(p, st);
+SCHED_HD void apply(const PlanView& p, StateView& st, const int64_t* actions, int n,
+                    bool credits_reset = false) {
+  if (!credits_reset) reset_slot_credits(p, st);
   for (int i = 0; i < n; ++i) {
     const int64_t o = actions[2 * i], e = actions[2 * i + 1];
     const int t = p.edge_tgt[e];

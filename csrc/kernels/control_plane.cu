@@ -17,10 +17,10 @@
 // packing gate passed.  The dispatch kernel refuses to move a byte without it.
 // Every step is logged for the host's post-hoc differential replay.
 //
-// The scheduler itself is sequential; to keep its dependent accesses at
-// shared-memory latency the CTA stages the compiled plan and the state in
-// shared memory, one thread runs the trigger, and the CTA writes the state
-// back.
+// The CTA stages the compiled plan and the state in shared memory; the resets
+// and the per-ordinal candidate enumeration run across the CTA, and only the
+// order-dependent steps (staging, greedy selection, guard check, apply) run
+// on one thread, at shared-memory latency.  The CTA writes the state back.
 #include <cstdint>
 
 #include "launchers.h"
@@ -33,106 +33,103 @@ namespace {
 enum Scalar : int {
   kStaged = 0, kRevealedCount = 1, kVersion = 2, kCompleted = 3, kRevealedBits = 4,
   kDispatched = 5, kFuture = 6, kUnrevealed = 7, kDuplicate = 8, kStale = 9, kPending = 10,
-  kChunkStarts = 11
+  kChunkStarts = kCtlScalarHeader
 };
 constexpr int kLogHeader = 8;
+constexpr int kCtlStageMax = 1024;  // control-token destinations staged per trigger
+constexpr int kCtlMaxChunks = 64;   // chunk bitmaps are 64-bit words
 
-struct Carver {
-  uint8_t* base;
-  size_t off;
-  template <typename T>
-  __device__ T* take(long long n) {
-    off = (off + 15) & ~(size_t)15;
-    T* p = reinterpret_cast<T*>(base + off);
-    off += (size_t)(n > 0 ? n : 1) * sizeof(T);
-    return p;
+// 16-byte vector copy, four loads in flight per thread before the stores.
+__device__ __forceinline__ void copy16(uint4* dst, const uint4* src, long long n) {
+  for (long long i0 = threadIdx.x; i0 < n; i0 += 4LL * blockDim.x) {
+    uint4 r[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long i = i0 + (long long)u * blockDim.x;
+      if (i < n) r[u] = src[i];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long i = i0 + (long long)u * blockDim.x;
+      if (i < n) dst[i] = r[u];
+    }
   }
-};
+}
 
-template <typename T>
-__device__ void copy_arr(T* dst, const T* src, long long n) {
-  for (long long i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+ControlDims dims_of(const ControlParams& p) {
+  return ControlDims{p.plan.E, p.plan.G, p.plan.V, p.st.max_tokens, p.n_group_members,
+                     p.n_edge_group_members, p.n_tmpl, p.max_cands, p.chunks};
 }
 }  // namespace
 
-// Shared-memory bytes the kernel carves (mirrors the Carver sequence below).
-size_t control_smem_bytes(const ControlParams& p) {
-  size_t off = 0;
-  auto take = [&](long long n, size_t elem) {
-    off = (off + 15) & ~(size_t)15;
-    off += (size_t)(n > 0 ? n : 1) * elem;
-  };
-  const int E = p.plan.E, G = p.plan.G, V = p.plan.V, T = p.st.max_tokens;
-  take(E, 4); take(E, 4); take(E, 8); take(G, 8); take(G + 1, 4); take(p.n_group_members, 4);
-  take(E + 1, 4); take(p.n_edge_group_members, 4); take((long long)V * V, 4); take(V + 1, 4);
-  take(p.n_tmpl, 4); take(p.n_tmpl, 4); take(p.n_tmpl, 4); take(p.n_tmpl, 4);
-  take(T, 4); take(T, 4); take((long long)T * V, 1); take(T, 1); take((long long)T * E, 1); take(T, 1);
-  take(T, 4); take((long long)V * V, 8); take(E, 8); take(G, 8); take(T, 1); take(T, 1); take(E, 8);
-  take(p.max_cands, sizeof(sched::Cand)); take(p.max_cands, 4); take(2LL * T, 8);
-  take(kChunkStarts + 2LL * p.chunks, 8);
-  return off + 16;
-}
+// Shared-memory bytes of the kernel: the whole blob.
+size_t control_smem_bytes(const ControlParams& p) { return (size_t)control_layout(dims_of(p)).total; }
 
-__global__ void __launch_bounds__(256) moe_control_kernel(ControlParams p) {
+__global__ void __launch_bounds__(256) moe_control_kernel(ControlParams p, ControlDims dims) {
   extern __shared__ __align__(16) uint8_t csm[];
-  Carver cv{csm, 0};
-  const int E = p.plan.E, G = p.plan.G, V = p.plan.V, T = p.st.max_tokens, C = p.chunks;
-  // ---- plan -> shared
-  sched::PlanView plan = p.plan;
-  int32_t* s_edge_src = cv.take<int32_t>(E);
-  int32_t* s_edge_tgt = cv.take<int32_t>(E);
-  int64_t* s_cap = cv.take<int64_t>(E);
-  int64_t* s_glim = cv.take<int64_t>(G);
-  int32_t* s_gptr = cv.take<int32_t>(G + 1);
-  int32_t* s_gmem = cv.take<int32_t>(p.n_group_members);
-  int32_t* s_egptr = cv.take<int32_t>(E + 1);
-  int32_t* s_egmem = cv.take<int32_t>(p.n_edge_group_members);
-  int32_t* s_dist = cv.take<int32_t>((long long)V * V);
-  int32_t* s_tptr = cv.take<int32_t>(V + 1);
-  int32_t* s_tedge = cv.take<int32_t>(p.n_tmpl);
-  int32_t* s_tsrc = cv.take<int32_t>(p.n_tmpl);
-  int32_t* s_ttgt = cv.take<int32_t>(p.n_tmpl);
-  int32_t* s_ttd = cv.take<int32_t>(p.n_tmpl);
-  copy_arr(s_edge_src, p.plan.edge_src, E);
-  copy_arr(s_edge_tgt, p.plan.edge_tgt, E);
-  copy_arr(s_cap, p.plan.cap_units, E);
-  if (G) { copy_arr(s_glim, p.plan.group_limits, G); copy_arr(s_gmem, p.plan.group_members, p.n_group_members); }
-  copy_arr(s_gptr, p.plan.group_ptr, G + 1);
-  copy_arr(s_egptr, p.plan.edge_group_ptr, E + 1);
-  if (p.n_edge_group_members) copy_arr(s_egmem, p.plan.edge_group_members, p.n_edge_group_members);
-  copy_arr(s_dist, p.plan.distances, (long long)V * V);
-  copy_arr(s_tptr, p.plan.tmpl_ptr, V + 1);
-  if (p.n_tmpl) {
-    copy_arr(s_tedge, p.plan.tmpl_edge, p.n_tmpl); copy_arr(s_tsrc, p.plan.tmpl_src, p.n_tmpl);
-    copy_arr(s_ttgt, p.plan.tmpl_tgt, p.n_tmpl); copy_arr(s_ttd, p.plan.tmpl_tdist, p.n_tmpl);
+  const ControlLayout Lt = control_layout(dims);
+  const int E = dims.E, G = dims.G, V = dims.V, T = dims.T, C = dims.chunks;
+  // ---- stage plan (+ state after the first trigger) into shared memory: one vector copy
+  const long long stage_bytes = p.desc == 0 ? Lt.state_begin : Lt.state_end;
+  copy16(reinterpret_cast<uint4*>(csm), reinterpret_cast<const uint4*>(p.blob), stage_bytes / 16);
+  // control-token destinations of the trigger's chunks, fetched in parallel
+  __shared__ int s_dst[kCtlStageMax];
+  __shared__ int s_coff[kCtlMaxChunks + 1];
+  const int P = p.partial_chunks;
+  const bool final_trigger = p.desc >= P;
+  const int c_lo = final_trigger ? P : p.desc;
+  const int c_hi = final_trigger ? C - 1 : p.desc;
+  const int cpc = p.ctl_per_chunk;
+  const int n_stage = (c_hi - c_lo + 1) * cpc;
+  const bool staged = n_stage <= kCtlStageMax && C <= kCtlMaxChunks;
+  if (staged) {
+    for (int c = threadIdx.x; c <= C; c += blockDim.x) s_coff[c] = p.chunk_offsets[c];
+    for (int i = threadIdx.x; i < n_stage; i += blockDim.x) {
+      const int c = c_lo + i / cpc, j = i % cpc;
+      const int off = p.chunk_offsets[c];
+      const int size = p.chunk_offsets[c + 1] - off;
+      s_dst[i] = j < size ? p.expert_ids[(long long)(off + j) * p.top_k] % p.ctl_nodes : -1;
+    }
   }
-  plan.edge_src = s_edge_src; plan.edge_tgt = s_edge_tgt; plan.cap_units = s_cap;
-  plan.group_limits = s_glim; plan.group_ptr = s_gptr; plan.group_members = s_gmem;
-  plan.edge_group_ptr = s_egptr; plan.edge_group_members = s_egmem; plan.distances = s_dist;
-  plan.tmpl_ptr = s_tptr; plan.tmpl_edge = s_tedge; plan.tmpl_src = s_tsrc; plan.tmpl_tgt = s_ttgt;
-  plan.tmpl_tdist = s_ttd;
-  // ---- state -> shared (reset at the first trigger of a call)
+  auto at = [&](int a) { return csm + Lt.off[a]; };
+  sched::PlanView plan = p.plan;
+  int64_t* s_cap = reinterpret_cast<int64_t*>(at(kCtlCap));
+  int64_t* s_glim = reinterpret_cast<int64_t*>(at(kCtlGroupLimits));
+  plan.edge_src = reinterpret_cast<const int32_t*>(at(kCtlEdgeSrc));
+  plan.edge_tgt = reinterpret_cast<const int32_t*>(at(kCtlEdgeTgt));
+  plan.cap_units = s_cap;
+  plan.group_limits = s_glim;
+  plan.group_ptr = reinterpret_cast<const int32_t*>(at(kCtlGroupPtr));
+  plan.group_members = reinterpret_cast<const int32_t*>(at(kCtlGroupMembers));
+  plan.edge_group_ptr = reinterpret_cast<const int32_t*>(at(kCtlEdgeGroupPtr));
+  plan.edge_group_members = reinterpret_cast<const int32_t*>(at(kCtlEdgeGroupMembers));
+  plan.distances = reinterpret_cast<const int32_t*>(at(kCtlDistances));
+  plan.tmpl_ptr = reinterpret_cast<const int32_t*>(at(kCtlTmplPtr));
+  plan.tmpl_edge = reinterpret_cast<const int32_t*>(at(kCtlTmplEdge));
+  plan.tmpl_src = reinterpret_cast<const int32_t*>(at(kCtlTmplSrc));
+  plan.tmpl_tgt = reinterpret_cast<const int32_t*>(at(kCtlTmplTgt));
+  plan.tmpl_tdist = reinterpret_cast<const int32_t*>(at(kCtlTmplTdist));
   sched::StateView st;
   st.max_tokens = T;
-  st.sources = cv.take<int32_t>(T);
-  st.destinations = cv.take<int32_t>(T);
-  st.holders = cv.take<uint8_t>((long long)T * V);
-  st.ready = cv.take<uint8_t>(T);
-  st.committed = cv.take<uint8_t>((long long)T * E);
-  st.residual = cv.take<uint8_t>(T);
-  st.remaining_hops = cv.take<int32_t>(T);
-  st.residual_demand = cv.take<int64_t>((long long)V * V);
-  st.link_credits = cv.take<int64_t>(E);
-  st.group_credits = cv.take<int64_t>(G);
-  st.scratch_selected = cv.take<uint8_t>(T);
-  st.scratch_seen = cv.take<uint8_t>(T);
-  st.scratch_edge_load = cv.take<int64_t>(E);
-  sched::Cand* cand = cv.take<sched::Cand>(p.max_cands);
-  int* keep = cv.take<int>(p.max_cands);
-  int64_t* actions = cv.take<int64_t>(2LL * T);
-  long long* S = cv.take<long long>(kChunkStarts + 2LL * C);
-  const sched::StateView& gs = p.st;
-  if (p.desc == 0) {
+  st.sources = reinterpret_cast<int32_t*>(at(kCtlSources));
+  st.destinations = reinterpret_cast<int32_t*>(at(kCtlDestinations));
+  st.holders = at(kCtlHolders);
+  st.ready = at(kCtlReady);
+  st.committed = at(kCtlCommitted);
+  st.residual = at(kCtlResidual);
+  st.remaining_hops = reinterpret_cast<int32_t*>(at(kCtlRemainingHops));
+  st.residual_demand = reinterpret_cast<int64_t*>(at(kCtlResidualDemand));
+  st.link_credits = reinterpret_cast<int64_t*>(at(kCtlLinkCredits));
+  st.group_credits = reinterpret_cast<int64_t*>(at(kCtlGroupCredits));
+  st.scratch_selected = at(kCtlScratchSelected);
+  st.scratch_seen = at(kCtlScratchSeen);
+  st.scratch_edge_load = reinterpret_cast<int64_t*>(at(kCtlScratchEdgeLoad));
+  long long* S = reinterpret_cast<long long*>(at(kCtlScalars));
+  sched::Cand* cand = reinterpret_cast<sched::Cand*>(at(kCtlCands));
+  int* keep = reinterpret_cast<int*>(at(kCtlKeep));
+  int64_t* actions = reinterpret_cast<int64_t*>(at(kCtlActions));
+  __syncthreads();
+  if (p.desc == 0) {  // first trigger of a layer call: fresh state
     for (int i = threadIdx.x; i < T; i += blockDim.x) {
       st.sources[i] = -1; st.destinations[i] = -1; st.ready[i] = 0; st.residual[i] = 0;
       st.remaining_hops[i] = sched::kInf; st.scratch_selected[i] = 0; st.scratch_seen[i] = 0;
@@ -144,43 +141,29 @@ __global__ void __launch_bounds__(256) moe_control_kernel(ControlParams p) {
     for (int i = threadIdx.x; i < G; i += blockDim.x) st.group_credits[i] = s_glim[i];
     for (int i = threadIdx.x; i < kChunkStarts + 2 * C; i += blockDim.x)
       S[i] = (i >= kChunkStarts && i < kChunkStarts + C) ? -1 : 0;
-  } else {
-    copy_arr(st.sources, gs.sources, T); copy_arr(st.destinations, gs.destinations, T);
-    copy_arr(st.holders, gs.holders, (long long)T * V); copy_arr(st.ready, gs.ready, T);
-    copy_arr(st.committed, gs.committed, (long long)T * E); copy_arr(st.residual, gs.residual, T);
-    copy_arr(st.remaining_hops, gs.remaining_hops, T);
-    copy_arr(st.residual_demand, gs.residual_demand, (long long)V * V);
-    copy_arr(st.link_credits, gs.link_credits, E);
-    if (G) copy_arr(st.group_credits, gs.group_credits, G);
-    copy_arr(st.scratch_selected, gs.scratch_selected, T); copy_arr(st.scratch_seen, gs.scratch_seen, T);
-    copy_arr(st.scratch_edge_load, gs.scratch_edge_load, E);
-    copy_arr(S, p.scalars, kChunkStarts + 2LL * C);
   }
   __syncthreads();
-
-  __shared__ int s_n, s_kept;
+  __shared__ int s_n, s_kept, s_revealed, s_gate, s_accepted, s_code;
+  int* cnt = keep;  // per-ordinal candidate counts reuse the keep buffer before selection
+  // ---- phase A (one thread): complete + reveal
   if (threadIdx.x == 0) {
-    const int P = p.partial_chunks;
-    const bool final_trigger = p.desc >= P;
-    const int c_lo = final_trigger ? P : p.desc;
-    const int c_hi = final_trigger ? C - 1 : p.desc;
     long long* starts = S + kChunkStarts;
     long long* counts = S + kChunkStarts + C;
     bool gate_ok = true;
-    // complete: stage control tokens of each newly completed chunk
     for (int c = c_lo; c <= c_hi; ++c) {
       const long long bit = 1LL << c;
       if (S[kCompleted] & bit) { gate_ok = false; continue; }  // completed-chunk replay
       S[kCompleted] |= bit;
-      const int off = p.chunk_offsets[c];
-      const int size = p.chunk_offsets[c + 1] - off;
-      const int limit = size < p.ctl_per_chunk ? size : p.ctl_per_chunk;
+      const int off = staged ? s_coff[c] : p.chunk_offsets[c];
+      const int size = (staged ? s_coff[c + 1] : p.chunk_offsets[c + 1]) - off;
+      const int limit = size < cpc ? size : cpc;
       const long long start = S[kStaged];
       int n = 0;
       for (int i = 0; i < limit; ++i) {
         const int pos = off + i;
         const int src = pos % p.ctl_nodes;
-        const int dst = p.expert_ids[(long long)pos * p.top_k] % p.ctl_nodes;
+        const int dst = staged ? s_dst[(c - c_lo) * cpc + i]
+                               : p.expert_ids[(long long)pos * p.top_k] % p.ctl_nodes;
         if (src == dst) continue;
         if (start + n >= T) {
           record_status(p.status, kBoundsViolation, 60, start + n, T);
@@ -195,7 +178,6 @@ __global__ void __launch_bounds__(256) moe_control_kernel(ControlParams p) {
       S[kStaged] = start + n;
       S[kPending] |= bit;
     }
-    // reveal: activate pending chunks in ordinal order
     for (int c = c_lo; c <= c_hi; ++c) {
       const long long bit = 1LL << c;
       if (!(S[kCompleted] & bit)) { S[kFuture] += 1; gate_ok = false; continue; }
@@ -206,26 +188,67 @@ __global__ void __launch_bounds__(256) moe_control_kernel(ControlParams p) {
       S[kRevealedCount] += counts[c];
       S[kPending] &= ~bit;
     }
-    // schedule: enumerate -> select -> guard check -> apply
-    const int revealed = (int)S[kRevealedCount];
-    int n = sched::enumerate(plan, st, revealed, cand, p.max_cands);
+    s_revealed = (int)S[kRevealedCount];
+    s_gate = gate_ok ? 1 : 0;
+  }
+  __syncthreads();
+  // ---- phase B (CTA): slot-credit reset + per-ordinal candidate enumeration
+  const int revealed = s_revealed;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) st.link_credits[e] = s_cap[e];
+  for (int g = threadIdx.x; g < G; g += blockDim.x) st.group_credits[g] = s_glim[g];
+  for (int t = threadIdx.x; t < T; t += blockDim.x) st.scratch_selected[t] = 0;
+  for (int o = threadIdx.x; o < revealed; o += blockDim.x) cnt[o] = sched::enumerate_one(plan, st, o, nullptr, 0);
+  __syncthreads();
+  if (threadIdx.x == 0) {  // exclusive prefix over ordinals: candidate order = (ordinal, template)
+    int run = 0;
+    for (int o = 0; o < revealed; ++o) { const int c0 = cnt[o]; cnt[o] = run; run += c0; }
+    s_n = run;
+  }
+  __syncthreads();
+  for (int o = threadIdx.x; o < revealed; o += blockDim.x) {
+    const int base = cnt[o];
+    if (base < p.max_cands) sched::enumerate_one(plan, st, o, cand + base, p.max_cands - base);
+  }
+  __syncthreads();
+  // ---- phase C (one thread): greedy selection in candidate order
+  if (threadIdx.x == 0) {
+    int n = s_n;
     if (n > p.max_cands) {
       record_status(p.status, kBoundsViolation, 61, n, p.max_cands);
       n = p.max_cands;
-      gate_ok = false;
+      s_gate = 0;
     }
-    const int kept = sched::select(plan, st, cand, n, revealed, keep);
+    s_n = n;
+    const int kept = sched::select(plan, st, cand, n, revealed, keep, true);
     for (int i = 0; i < kept; ++i) {
       actions[2 * i] = cand[keep[i]].ordinal;
       actions[2 * i + 1] = cand[keep[i]].edge;
     }
-    const int code = sched::check(plan, st, actions, kept, revealed, true);
-    const bool accepted = code == sched::kAccept;
+    s_kept = kept;
+  }
+  __syncthreads();
+  // ---- phase D (CTA): guard scratch reset; phase E (one thread): guard check
+  for (int t = threadIdx.x; t < T; t += blockDim.x) st.scratch_seen[t] = 0;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) st.scratch_edge_load[e] = 0;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    s_code = sched::check(plan, st, actions, s_kept, revealed, true, true);
+    s_accepted = s_code == sched::kAccept ? 1 : 0;
+  }
+  __syncthreads();
+  // ---- phase F (CTA): credit reset for apply; phase G (one thread): apply, gate, permit
+  for (int e = threadIdx.x; e < E; e += blockDim.x) st.link_credits[e] = s_cap[e];
+  for (int g = threadIdx.x; g < G; g += blockDim.x) st.group_credits[g] = s_glim[g];
+  for (int t = threadIdx.x; t < T; t += blockDim.x) st.scratch_selected[t] = 0;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool accepted = s_accepted != 0;
+    const int kept = s_kept;
+    bool gate_ok = s_gate != 0;
     if (accepted && kept > 0) {
-      sched::apply(plan, st, actions, kept);
+      sched::apply(plan, st, actions, kept, true);
       S[kVersion] += 1;
     }
-    // packing gate over the descriptor's chunks
     for (int c = c_lo; c <= c_hi; ++c) {
       const long long bit = 1LL << c;
       if (!(S[kCompleted] & bit)) { S[kFuture] += 1; gate_ok = false; }
@@ -235,12 +258,10 @@ __global__ void __launch_bounds__(256) moe_control_kernel(ControlParams p) {
     if (gate_ok)
       for (int c = c_lo; c <= c_hi; ++c) S[kDispatched] |= 1LL << c;
     p.permit[p.desc] = (accepted && gate_ok) ? *p.epoch : 0ULL;
-    if (!(accepted && gate_ok)) record_status(p.status, kTimeoutPermit, 62, p.desc, code);
+    if (!(accepted && gate_ok)) record_status(p.status, kTimeoutPermit, 62, p.desc, s_code);
     int* L = p.log + (long long)p.desc * p.log_stride;
-    L[0] = n; L[1] = kept; L[2] = accepted ? 1 : 0; L[3] = code;
+    L[0] = s_n; L[1] = kept; L[2] = accepted ? 1 : 0; L[3] = s_code;
     L[4] = accepted ? kept : 0; L[5] = (int)S[kVersion]; L[6] = revealed; L[7] = gate_ok ? 1 : 0;
-    s_n = n;
-    s_kept = kept;
   }
   __syncthreads();
   // ---- log (parallel) and state write-back
@@ -257,16 +278,11 @@ __global__ void __launch_bounds__(256) moe_control_kernel(ControlParams p) {
       cl[4 * i + 2] = cand[i].before; cl[4 * i + 3] = cand[i].after;
     }
   }
-  copy_arr(gs.sources, st.sources, T); copy_arr(gs.destinations, st.destinations, T);
-  copy_arr(gs.holders, st.holders, (long long)T * V); copy_arr(gs.ready, st.ready, T);
-  copy_arr(gs.committed, st.committed, (long long)T * E); copy_arr(gs.residual, st.residual, T);
-  copy_arr(gs.remaining_hops, st.remaining_hops, T);
-  copy_arr(gs.residual_demand, st.residual_demand, (long long)V * V);
-  copy_arr(gs.link_credits, st.link_credits, E);
-  if (G) copy_arr(gs.group_credits, st.group_credits, G);
-  copy_arr(gs.scratch_selected, st.scratch_selected, T); copy_arr(gs.scratch_seen, st.scratch_seen, T);
-  copy_arr(gs.scratch_edge_load, st.scratch_edge_load, E);
-  copy_arr(p.scalars, S, kChunkStarts + 2LL * C);
+  __syncthreads();
+  // ---- state back to the blob: one vector copy (scratch stays in shared memory;
+  // the trigger's candidates and selection are in its log row)
+  copy16(reinterpret_cast<uint4*>(p.blob + Lt.state_begin), reinterpret_cast<const uint4*>(csm + Lt.state_begin),
+         (Lt.state_end - Lt.state_begin) / 16);
 }
 
 void launch_control(const ControlParams& p, cudaStream_t s) {
@@ -276,7 +292,7 @@ void launch_control(const ControlParams& p, cudaStream_t s) {
     cudaFuncSetAttribute(moe_control_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     configured = smem;
   }
-  moe_control_kernel<<<1, 256, smem, s>>>(p);
+  moe_control_kernel<<<1, 256, smem, s>>>(p, dims_of(p));
 }
 
 }  // namespace raiccl

@@ -211,6 +211,7 @@ __global__ void __launch_bounds__(256) moe_router_kernel(RouterParams p) {
 constexpr int kDispatchThreads = 512;
 constexpr int kDispatchMaxItems = 4096;
 constexpr int kMaxExperts = 256;
+constexpr int kDispatchMaxChunks = 128;  // chunk-offset table staged in shared memory
 
 template <typename T>
 __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(DispatchParams p) {
@@ -220,6 +221,8 @@ __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(Dispatch
   __shared__ int item_pos[kDispatchMaxItems];
   __shared__ int s_last;
   __shared__ int s_permitted;
+  __shared__ int s_sent[kMaxExperts];
+  __shared__ int s_coff[kDispatchMaxChunks + 1];
   const int k = d.top_k;
   const int E = d.experts;
   const int ntok = p.t1 - p.t0;
@@ -228,7 +231,9 @@ __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(Dispatch
   const int b = p.t0 + min(ntok, (int)(blockIdx.x + 1) * per);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
 
-  for (int e = threadIdx.x; e < E; e += blockDim.x) { hist[e] = 0; run[e] = 0; }
+  for (int e = threadIdx.x; e < E; e += blockDim.x) { hist[e] = 0; run[e] = 0; s_sent[e] = p.sent_base[e]; }
+  const int nc = min(d.chunks, kDispatchMaxChunks);
+  for (int c = threadIdx.x; c <= nc; c += blockDim.x) s_coff[c] = p.chunk_offsets[c];
   const unsigned long long epoch = *p.epoch;
   if (threadIdx.x == 0) s_permitted = (p.permit[p.desc] == epoch) ? 1 : 0;
   __syncthreads();
@@ -270,7 +275,7 @@ __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(Dispatch
       const int t = (int)(i / k), j = (int)(i % k);
       const int e = p.expert_ids[i];
       const int r = expert_owner(d, e), le = expert_slot(d, e);
-      const long long row = (long long)p.sent_base[e] + hist[e] + item_pos[li];
+      const long long row = (long long)s_sent[e] + hist[e] + item_pos[li];
       if (row >= d.cap || r >= d.world || le >= d.expert_slots) {
         if (lane == 0) record_status(p.status, kBoundsViolation, 21, row, d.cap);
         continue;
@@ -295,7 +300,8 @@ __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(Dispatch
       }
       if (lane < kFwdMetaFields) {
         int c = 0;
-        while (c + 1 < d.chunks && p.chunk_offsets[c + 1] <= t) ++c;
+        while (c + 1 < nc && s_coff[c + 1] <= t) ++c;
+        while (c + 1 < d.chunks && p.chunk_offsets[c + 1] <= t) ++c;  // beyond the staged table
         long long val;
         switch (lane) {
           case 0: val = p.token_ids[t]; break;
@@ -303,7 +309,7 @@ __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(Dispatch
           case 2: val = r; break;
           case 3: val = e; break;
           case 4: val = c; break;
-          case 5: val = t - p.chunk_offsets[c]; break;
+          case 5: val = t - (c <= nc ? s_coff[c] : p.chunk_offsets[c]); break;
           case 6: val = t; break;
           case 7: val = p.feat_digest[t]; break;
           default: {

@@ -180,34 +180,51 @@ class MoELayerRunner {
     cp.n_edge_group_members = geti_t("plan_NEGM");
     cp.n_tmpl = geti_t("plan_NT");
     cp.plan.V = d.ctl_nodes;
-    cp.plan.edge_src = ptr<int32_t>(t, "edge_src");
-    cp.plan.edge_tgt = ptr<int32_t>(t, "edge_tgt");
-    cp.plan.cap_units = ptr<int64_t>(t, "cap_units");
-    cp.plan.group_limits = opt_ptr<int64_t>(t, "group_limits");
-    cp.plan.group_ptr = ptr<int32_t>(t, "group_ptr");
-    cp.plan.group_members = opt_ptr<int32_t>(t, "group_members");
-    cp.plan.edge_group_ptr = ptr<int32_t>(t, "edge_group_ptr");
-    cp.plan.edge_group_members = opt_ptr<int32_t>(t, "edge_group_members");
-    cp.plan.distances = ptr<int32_t>(t, "distances");
-    cp.plan.tmpl_ptr = ptr<int32_t>(t, "tmpl_ptr");
-    cp.plan.tmpl_edge = opt_ptr<int32_t>(t, "tmpl_edge");
-    cp.plan.tmpl_src = opt_ptr<int32_t>(t, "tmpl_src");
-    cp.plan.tmpl_tgt = opt_ptr<int32_t>(t, "tmpl_tgt");
-    cp.plan.tmpl_tdist = opt_ptr<int32_t>(t, "tmpl_tdist");
     cp.st.max_tokens = max_ctl_tokens_;
-    cp.st.sources = ptr<int32_t>(t, "st_sources");
-    cp.st.destinations = ptr<int32_t>(t, "st_destinations");
-    cp.st.holders = ptr<uint8_t>(t, "st_holders");
-    cp.st.ready = ptr<uint8_t>(t, "st_ready");
-    cp.st.committed = ptr<uint8_t>(t, "st_committed");
-    cp.st.residual = ptr<uint8_t>(t, "st_residual");
-    cp.st.remaining_hops = ptr<int32_t>(t, "st_remaining_hops");
-    cp.st.residual_demand = ptr<int64_t>(t, "st_residual_demand");
-    cp.st.link_credits = ptr<int64_t>(t, "st_link_credits");
-    cp.st.group_credits = opt_ptr<int64_t>(t, "st_group_credits");
-    cp.st.scratch_selected = ptr<uint8_t>(t, "st_scratch_selected");
-    cp.st.scratch_seen = ptr<uint8_t>(t, "st_scratch_seen");
-    cp.st.scratch_edge_load = ptr<int64_t>(t, "st_scratch_edge_load");
+    cp.max_cands = max_cands_;
+    cp.chunks = d.chunks;
+    {
+      // plan, state, scalars and scratch live in one blob (control_layout.h)
+      const auto L = raiccl::control_layout(raiccl::ControlDims{
+          cp.plan.E, cp.plan.G, cp.plan.V, cp.st.max_tokens, cp.n_group_members, cp.n_edge_group_members,
+          cp.n_tmpl, cp.max_cands, d.chunks});
+      auto blob_t = t["ctl_blob"].cast<torch::Tensor>();
+      TORCH_CHECK(blob_t.is_cuda() && blob_t.is_contiguous() && blob_t.nbytes() >= (size_t)L.total,
+                  "ctl_blob must be a contiguous CUDA buffer of control_layout total bytes");
+      cp.blob = reinterpret_cast<uint8_t*>(blob_t.data_ptr());
+      auto at = [&](int a) { return cp.blob + L.off[a]; };
+      cp.plan.edge_src = reinterpret_cast<int32_t*>(at(raiccl::kCtlEdgeSrc));
+      cp.plan.edge_tgt = reinterpret_cast<int32_t*>(at(raiccl::kCtlEdgeTgt));
+      cp.plan.cap_units = reinterpret_cast<int64_t*>(at(raiccl::kCtlCap));
+      cp.plan.group_limits = reinterpret_cast<int64_t*>(at(raiccl::kCtlGroupLimits));
+      cp.plan.group_ptr = reinterpret_cast<int32_t*>(at(raiccl::kCtlGroupPtr));
+      cp.plan.group_members = reinterpret_cast<int32_t*>(at(raiccl::kCtlGroupMembers));
+      cp.plan.edge_group_ptr = reinterpret_cast<int32_t*>(at(raiccl::kCtlEdgeGroupPtr));
+      cp.plan.edge_group_members = reinterpret_cast<int32_t*>(at(raiccl::kCtlEdgeGroupMembers));
+      cp.plan.distances = reinterpret_cast<int32_t*>(at(raiccl::kCtlDistances));
+      cp.plan.tmpl_ptr = reinterpret_cast<int32_t*>(at(raiccl::kCtlTmplPtr));
+      cp.plan.tmpl_edge = reinterpret_cast<int32_t*>(at(raiccl::kCtlTmplEdge));
+      cp.plan.tmpl_src = reinterpret_cast<int32_t*>(at(raiccl::kCtlTmplSrc));
+      cp.plan.tmpl_tgt = reinterpret_cast<int32_t*>(at(raiccl::kCtlTmplTgt));
+      cp.plan.tmpl_tdist = reinterpret_cast<int32_t*>(at(raiccl::kCtlTmplTdist));
+      cp.st.sources = reinterpret_cast<int32_t*>(at(raiccl::kCtlSources));
+      cp.st.destinations = reinterpret_cast<int32_t*>(at(raiccl::kCtlDestinations));
+      cp.st.holders = at(raiccl::kCtlHolders);
+      cp.st.ready = at(raiccl::kCtlReady);
+      cp.st.committed = at(raiccl::kCtlCommitted);
+      cp.st.residual = at(raiccl::kCtlResidual);
+      cp.st.remaining_hops = reinterpret_cast<int32_t*>(at(raiccl::kCtlRemainingHops));
+      cp.st.residual_demand = reinterpret_cast<int64_t*>(at(raiccl::kCtlResidualDemand));
+      cp.st.link_credits = reinterpret_cast<int64_t*>(at(raiccl::kCtlLinkCredits));
+      cp.st.group_credits = reinterpret_cast<int64_t*>(at(raiccl::kCtlGroupCredits));
+      cp.st.scratch_selected = at(raiccl::kCtlScratchSelected);
+      cp.st.scratch_seen = at(raiccl::kCtlScratchSeen);
+      cp.st.scratch_edge_load = reinterpret_cast<int64_t*>(at(raiccl::kCtlScratchEdgeLoad));
+      cp.scalars = reinterpret_cast<long long*>(at(raiccl::kCtlScalars));
+      cp.cand_buf = reinterpret_cast<raiccl::sched::Cand*>(at(raiccl::kCtlCands));
+      cp.keep_buf = reinterpret_cast<int*>(at(raiccl::kCtlKeep));
+      cp.action_buf = reinterpret_cast<int64_t*>(at(raiccl::kCtlActions));
+    }
     cp.expert_ids = expert_ids;
     cp.chunk_offsets = chunk_offsets_dev;
     cp.top_k = d.top_k;
@@ -215,12 +232,7 @@ class MoELayerRunner {
     cp.partial_chunks = partial_;
     cp.ctl_per_chunk = d.ctl_per_chunk;
     cp.ctl_nodes = d.ctl_nodes;
-    cp.max_cands = max_cands_;
     cp.log_stride = log_stride_;
-    cp.scalars = ptr<long long>(t, "ctl_scalars");
-    cp.cand_buf = ptr<raiccl::sched::Cand>(t, "ctl_cands");
-    cp.keep_buf = ptr<int>(t, "ctl_keep");
-    cp.action_buf = ptr<int64_t>(t, "ctl_actions");
     cp.log = ptr<int>(t, "ctl_log");
     cp.permit = permit;
     cp.epoch = epoch;
@@ -518,6 +530,27 @@ py::dict sym_layout(py::dict ints) {
   return o;
 }
 
+py::dict control_layout_py(py::dict dims) {
+  const auto L = raiccl::control_layout(raiccl::ControlDims{
+      geti(dims, "E"), geti(dims, "G"), geti(dims, "V"), geti(dims, "T"), geti(dims, "n_gm"), geti(dims, "n_egm"),
+      geti(dims, "n_tmpl"), geti(dims, "max_cands"), geti(dims, "chunks")});
+  static const char* names[raiccl::kCtlArrays] = {
+      "edge_src", "edge_tgt", "cap_units", "group_limits", "group_ptr", "group_members", "edge_group_ptr",
+      "edge_group_members", "distances", "tmpl_ptr", "tmpl_edge", "tmpl_src", "tmpl_tgt", "tmpl_tdist",
+      "st_sources", "st_destinations", "st_holders", "st_ready", "st_committed", "st_residual",
+      "st_remaining_hops", "st_residual_demand", "st_link_credits", "st_group_credits", "st_scratch_selected",
+      "st_scratch_seen", "st_scratch_edge_load", "ctl_scalars", "ctl_cands", "ctl_keep", "ctl_actions"};
+  py::dict arrays;
+  for (int i = 0; i < raiccl::kCtlArrays; ++i)
+    arrays[names[i]] = py::make_tuple(L.off[i], L.count[i], L.elem[i]);
+  py::dict o;
+  o["arrays"] = arrays;
+  o["state_begin"] = L.state_begin;
+  o["state_end"] = L.state_end;
+  o["total"] = L.total;
+  return o;
+}
+
 }  // namespace
 
 void register_moe(py::module_& m) {
@@ -540,4 +573,5 @@ void register_moe(py::module_& m) {
         py::arg("rank"), py::arg("out"));
   m.def("sym_layout_bytes", &sym_layout_bytes, py::arg("ints"));
   m.def("sym_layout", &sym_layout, py::arg("ints"));
+  m.def("control_layout", &control_layout_py, py::arg("dims"));
 }

@@ -181,41 +181,14 @@ class ProgressiveMoELayer:
             "h": self.h, "out": self.out,
             "out_ptrs1": torch.tensor([self.h.data_ptr()] * W, dtype=torch.int64, device=dev),
             "out_ptrs2": torch.tensor(out_ptrs2, dtype=torch.int64, device=dev),
-            # control plan + state
+            # control plan + state: one blob (typed views below), staged by the control kernel
             "plan_E": Ep, "plan_G": G, "plan_NGM": int(flat["group_members"].size),
             "plan_NEGM": int(flat["edge_group_members"].size), "plan_NT": int(flat["tmpl_edge"].size),
-            "edge_src": dev_t(flat["edge_src"]), "edge_tgt": dev_t(flat["edge_tgt"]),
-            "cap_units": dev_t(flat["cap_units"]),
-            "group_limits": dev_t(flat["group_limits"]) if G else torch.zeros(1, dtype=torch.int64, device=dev),
-            "group_ptr": dev_t(flat["group_ptr"]),
-            "group_members": dev_t(flat["group_members"]) if flat["group_members"].size else torch.zeros(1, dtype=torch.int32, device=dev),
-            "edge_group_ptr": dev_t(flat["edge_group_ptr"]),
-            "edge_group_members": dev_t(flat["edge_group_members"]) if flat["edge_group_members"].size else torch.zeros(1, dtype=torch.int32, device=dev),
-            "distances": dev_t(flat["distances"]), "tmpl_ptr": dev_t(flat["tmpl_ptr"]),
-            "tmpl_edge": dev_t(flat["tmpl_edge"]) if flat["tmpl_edge"].size else torch.zeros(1, dtype=torch.int32, device=dev),
-            "tmpl_src": dev_t(flat["tmpl_src"]) if flat["tmpl_src"].size else torch.zeros(1, dtype=torch.int32, device=dev),
-            "tmpl_tgt": dev_t(flat["tmpl_tgt"]) if flat["tmpl_tgt"].size else torch.zeros(1, dtype=torch.int32, device=dev),
-            "tmpl_tdist": dev_t(flat["tmpl_tdist"]) if flat["tmpl_tdist"].size else torch.zeros(1, dtype=torch.int32, device=dev),
-            "st_sources": torch.zeros(Tc, dtype=torch.int32, device=dev),
-            "st_destinations": torch.zeros(Tc, dtype=torch.int32, device=dev),
-            "st_holders": torch.zeros(Tc * V, dtype=torch.uint8, device=dev),
-            "st_ready": torch.zeros(Tc, dtype=torch.uint8, device=dev),
-            "st_committed": torch.zeros(Tc * Ep, dtype=torch.uint8, device=dev),
-            "st_residual": torch.zeros(Tc, dtype=torch.uint8, device=dev),
-            "st_remaining_hops": torch.zeros(Tc, dtype=torch.int32, device=dev),
-            "st_residual_demand": torch.zeros(V * V, dtype=torch.int64, device=dev),
-            "st_link_credits": torch.zeros(Ep, dtype=torch.int64, device=dev),
-            "st_group_credits": torch.zeros(max(G, 1), dtype=torch.int64, device=dev),
-            "st_scratch_selected": torch.zeros(Tc, dtype=torch.uint8, device=dev),
-            "st_scratch_seen": torch.zeros(Tc, dtype=torch.uint8, device=dev),
-            "st_scratch_edge_load": torch.zeros(Ep, dtype=torch.int64, device=dev),
-            "ctl_scalars": torch.zeros(11 + 2 * cfg.chunks, dtype=torch.int64, device=dev),
-            "ctl_cands": torch.zeros(self.max_cands * 4, dtype=torch.int32, device=dev),
-            "ctl_keep": torch.zeros(self.max_cands, dtype=torch.int32, device=dev),
-            "ctl_actions": torch.zeros(2 * Tc, dtype=torch.int64, device=dev),
+            "ctl_blob": self._control_blob(flat, Ep, G, V, Tc, dev),
             "ctl_log": torch.zeros(cfg.n_desc * self.log_stride, dtype=torch.int32, device=dev),
         }
         self.tensors = {kk: v for kk, v in self.tensors.items() if v is not None}
+        self.tensors.update(self._ctl_views)
         self.router_stream = torch.cuda.Stream(device=dev)
         self.comm_stream = torch.cuda.Stream(device=dev)
         torch.cuda.synchronize(dev)
@@ -226,6 +199,34 @@ class ProgressiveMoELayer:
         self.launches_per_call = 0
         if W > 1:
             dist.barrier(group=group)
+
+    def _control_blob(self, flat, Ep: int, G: int, V: int, Tc: int, dev) -> torch.Tensor:
+        """One device buffer holding the compiled plan, the scheduler state, the
+        trigger scalars and scratch at the offsets of the native layout; the
+        plan part is filled here, the rest is (re)initialised by the kernel."""
+        cfg = self.cfg
+        if cfg.chunks > 64:
+            raise ValueError("the device control plane tracks at most 64 chunks (64-bit chunk bitmaps)")
+        lay = self._k.control_layout({
+            "E": Ep, "G": G, "V": V, "T": Tc, "n_gm": int(flat["group_members"].size),
+            "n_egm": int(flat["edge_group_members"].size), "n_tmpl": int(flat["tmpl_edge"].size),
+            "max_cands": self.max_cands, "chunks": cfg.chunks})
+        blob = torch.zeros(int(lay["total"]), dtype=torch.uint8, device=dev)
+        dtypes = {1: torch.uint8, 4: torch.int32, 8: torch.int64}
+        views = {}
+        for name, (off, count, elem) in lay["arrays"].items():
+            n = max(int(count), 1)
+            views[name] = blob[int(off):int(off) + n * int(elem)].view(dtypes[int(elem)])
+        for name in ("edge_src", "edge_tgt", "cap_units", "group_limits", "group_ptr", "group_members",
+                     "edge_group_ptr", "edge_group_members", "distances", "tmpl_ptr", "tmpl_edge", "tmpl_src",
+                     "tmpl_tgt", "tmpl_tdist"):
+            a = np.asarray(flat[name]).reshape(-1)
+            if a.size:
+                views[name][: a.size].copy_(torch.as_tensor(a.astype(np.int64 if views[name].dtype == torch.int64
+                                                                    else np.int32)))
+        self.control_layout = lay
+        self._ctl_views = views
+        return blob
 
     # ------------------------------------------------------------------ run
     def forward(self, arm: str = "early") -> torch.Tensor:
