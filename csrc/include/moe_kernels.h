@@ -100,7 +100,8 @@ struct ControlParams {
   const int32_t* chunk_offsets;  // [C + 1]
   int top_k, chunks, partial_chunks, desc;
   int ctl_per_chunk, ctl_nodes, max_cands, log_stride;
-  int n_group_members, n_edge_group_members, n_tmpl, pad_c;
+  int n_group_members, n_edge_group_members, n_tmpl, max_tmpl;  // max_tmpl: templates per destination
+  int force_serial;  // 1: always the CTA control kernel (the single-warp one otherwise, where it fits)
   // scalars kept across triggers of one layer call:
   // [0] staged_count [1] revealed_count [2] state_version [3] completed bitmap
   // [4] revealed bitmap [5] dispatched bitmap [6] future_access [7] unrevealed_execution

@@ -14,6 +14,8 @@
 // Every cross-GPU wait is bounded (globaltimer deadline) and reports through
 // DeviceStatus; there is no __trap and no intra-GPU wait on another kernel.
 #include <cuda_bf16.h>
+
+#include <algorithm>
 #include <cstdint>
 
 #include "launchers.h"
@@ -42,9 +44,23 @@ __device__ __forceinline__ uint64_t addmod(uint64_t a, uint64_t b) {
   return s >= kChecksumModulus ? s - kChecksumModulus : s;
 }
 
+// x mod M for M = 2^63 - 25 and any 64-bit x, from 2^63 = M + 25:
+// x = h * 2^63 + l (h <= 1) is congruent to l + 25 h < 2M.
+__device__ __forceinline__ uint64_t mod_m(uint64_t x) {
+  const uint64_t r = (x & ((1ULL << 63) - 1)) + (x >> 63) * 25ULL;
+  return r >= kChecksumModulus ? r - kChecksumModulus : r;
+}
+
+// (v mod M) * c mod M for a coefficient c < 2^32 (the identity coefficients are
+// about 10^6), without 128-bit division: with a = v mod M < 2^63 the product
+// a * c = hi * 2^64 + lo has hi < 2^32, and 2^64 = 2M + 50, so it is congruent
+// to (lo mod M) + 50 hi < M + 2^38 < 2M.
 __device__ __forceinline__ uint64_t mulmod_coeff(uint64_t v, uint64_t c) {
-  unsigned __int128 p = (unsigned __int128)(v % kChecksumModulus) * c;
-  return (uint64_t)(p % kChecksumModulus);
+  const uint64_t a = mod_m(v);
+  const uint64_t lo = a * c;
+  const uint64_t hi = __umul64hi(a, c);
+  const uint64_t r = mod_m(lo) + hi * 50ULL;
+  return r >= kChecksumModulus ? r - kChecksumModulus : r;
 }
 
 // ---------------------------------------------------------------------------
@@ -459,7 +475,56 @@ __global__ void moe_combine_kernel(CombineParams p) {
   const OutT* ret = (const OutT*)(mine + p.layout.ret_out);
   OutT* out = (OutT*)p.out;
   const int k = d.top_k, n = d.out_dim;
-  const long long total = (long long)d.tokens * n;
+  constexpr int VEC = 16 / sizeof(OutT);  // elements per 16-byte vector
+  constexpr int U = 4;                    // vectors in flight per lane
+  if (n % VEC == 0) {
+    // one warp per token row, lanes over 16-byte column vectors; the k return
+    // rows of a token are adjacent (row t * k + j), so each load is coalesced
+    const int nv = n / VEC;
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < d.tokens; t += warps) {
+      const uint4* src = reinterpret_cast<const uint4*>(ret + (long long)t * k * n);
+      uint4* dst = reinterpret_cast<uint4*>(out + (long long)t * n);
+      for (int v0 = lane; v0 < nv; v0 += 32 * U) {
+        float acc[U][VEC];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) acc[u][e] = 0.f;
+        for (int j = 0; j < k; ++j) {
+          uint4 x[U];
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int v = v0 + 32 * u;
+            if (v < nv) x[u] = src[(long long)j * nv + v];
+          }
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const OutT* xe = reinterpret_cast<const OutT*>(&x[u]);
+            if (v0 + 32 * u < nv)
+#pragma unroll
+              for (int e = 0; e < VEC; ++e) acc[u][e] += to_f(xe[e]);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int v = v0 + 32 * u;
+          if (v >= nv) continue;
+          uint4 y;
+          OutT* ye = reinterpret_cast<OutT*>(&y);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) {
+            if constexpr (sizeof(OutT) == 4) ye[e] = acc[u][e];
+            else ye[e] = __float2bfloat16(acc[u][e]);
+          }
+          dst[v] = y;
+        }
+      }
+    }
+    return;
+  }
+  const long long total = (long long)d.tokens * n;  // ragged widths: one element per thread
   for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < total;
        g += (long long)gridDim.x * blockDim.x) {
     const long long t = g / n, c = g % n;
@@ -570,8 +635,11 @@ void launch_return_signal(const SignalParams& p, cudaStream_t s) {
 }
 
 void launch_combine(const CombineParams& p, bool bf16, int grid, cudaStream_t s) {
-  if (bf16) moe_combine_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(p);
-  else moe_combine_kernel<float><<<grid, 256, 0, s>>>(p);
+  // enough warps for one token row each (capped at 8 CTAs per SM)
+  const int rows_grid = (p.dims.tokens + 7) / 8;
+  const int g = std::max(1, std::min(rows_grid, 8 * grid));
+  if (bf16) moe_combine_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(p);
+  else moe_combine_kernel<float><<<g, 256, 0, s>>>(p);
 }
 
 void launch_layer_reset(int* sent_base, int experts, int* desc_counts, int n_desc, int* done_counter,

@@ -62,6 +62,8 @@ class MoELayerRunner {
       : tensors_(tensors), chunk_offsets_(chunk_offsets.begin(), chunk_offsets.end()) {
     router_ = reinterpret_cast<cudaStream_t>(router_stream);
     comm_ = reinterpret_cast<cudaStream_t>(comm_stream);
+    device_ = tensors["tokens"].cast<torch::Tensor>().device().index();
+    c10::cuda::CUDAGuard guard(device_);
     // keep every tensor alive for the runner's lifetime
     for (auto item : tensors) held_.push_back(py::reinterpret_borrow<py::object>(item.second));
 
@@ -98,6 +100,7 @@ class MoELayerRunner {
     log_stride_ = geti(ints, "log_stride");
     max_ctl_tokens_ = geti(ints, "max_ctl_tokens");
     grid_sms_ = geti(ints, "sms");
+    control_serial_ = ints.contains("control_serial") && geti(ints, "control_serial") != 0;
     if (d.world < 1 || d.world > raiccl::kMaxRanks) throw std::invalid_argument("world size 1..8");
     if ((int)peer_bases.size() != d.world) throw std::invalid_argument("peer base count != world");
     if ((int)chunk_offsets_.size() != d.chunks + 1) throw std::invalid_argument("chunk offsets");
@@ -119,6 +122,11 @@ class MoELayerRunner {
     ck(cudaEventCreateWithFlags(&ev_start_, cudaEventDisableTiming), "cudaEventCreate");
     ev_chunk_.resize(d.chunks);
     for (auto& e : ev_chunk_) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+    ev_ctl_.resize(d.n_desc);
+    for (auto& e : ev_ctl_) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+    ck(cudaEventCreateWithFlags(&ev_disp_done_, cudaEventDisableTiming), "cudaEventCreate");
+    // dispatch chain: its own stream, so trigger q+1's control overlaps dispatch q
+    ck(cudaStreamCreateWithFlags(&disp_, cudaStreamNonBlocking), "cudaStreamCreate");
   }
 
   ~MoELayerRunner() {
@@ -127,11 +135,15 @@ class MoELayerRunner {
       if (graph_[a]) cudaGraphDestroy(graph_[a]);
     }
     for (auto& e : ev_chunk_) cudaEventDestroy(e);
+    for (auto& e : ev_ctl_) cudaEventDestroy(e);
+    if (ev_disp_done_) cudaEventDestroy(ev_disp_done_);
     if (ev_start_) cudaEventDestroy(ev_start_);
+    if (disp_) cudaStreamDestroy(disp_);
   }
 
   // Enqueue one layer call; returns the number of kernels launched.
   int forward(bool delayed) {
+    c10::cuda::CUDAGuard guard(device_);
     const auto& d = dims_;
     const py::dict& t = tensors_;
     int launches = 0;
@@ -179,6 +191,8 @@ class MoELayerRunner {
     cp.n_group_members = geti_t("plan_NGM");
     cp.n_edge_group_members = geti_t("plan_NEGM");
     cp.n_tmpl = geti_t("plan_NT");
+    cp.max_tmpl = geti_t("plan_MT");
+    cp.force_serial = control_serial_ ? 1 : 0;
     cp.plan.V = d.ctl_nodes;
     cp.st.max_tokens = max_ctl_tokens_;
     cp.max_cands = max_cands_;
@@ -265,19 +279,29 @@ class MoELayerRunner {
       const int ntok = dp.t1 - dp.t0;
       const int tpc = std::max(1, 16 / d.top_k);
       const int grid = std::max(1, std::min(4 * grid_sms_, (ntok + tpc - 1) / tpc));
-      raiccl::launch_dispatch(dp, feat_bf16_, grid, comm_);
+      raiccl::launch_dispatch(dp, feat_bf16_, grid, disp_);
       ++launches;
     };
+    // control triggers on comm_ (each after its router chunk); dispatch q on
+    // disp_ after control q (early arm) or after the last control (delayed arm)
     for (int q = 0; q < d.n_desc; ++q) {
       const int last_chunk = q < partial_ ? q : d.chunks - 1;
       ck(cudaStreamWaitEvent(comm_, ev_chunk_[last_chunk], 0), "cudaStreamWaitEvent");
       cp.desc = q;
       raiccl::launch_control(cp, comm_);
       ++launches;
-      if (!delayed) dispatch(q);
+      ck(cudaEventRecord(ev_ctl_[q], comm_), "cudaEventRecord");
+      if (!delayed) {
+        ck(cudaStreamWaitEvent(disp_, ev_ctl_[q], 0), "cudaStreamWaitEvent");
+        dispatch(q);
+      }
     }
-    if (delayed)
+    if (delayed) {
+      ck(cudaStreamWaitEvent(disp_, ev_ctl_[d.n_desc - 1], 0), "cudaStreamWaitEvent");
       for (int q = 0; q < d.n_desc; ++q) dispatch(q);
+    }
+    ck(cudaEventRecord(ev_disp_done_, disp_), "cudaEventRecord");
+    ck(cudaStreamWaitEvent(comm_, ev_disp_done_, 0), "cudaStreamWaitEvent");
 
     // expert side
     auto* segs = ptr<GemmSegment>(t, "segs");
@@ -359,6 +383,7 @@ class MoELayerRunner {
 
   // Record one layer call of the given arm into that arm's CUDA graph slot.
   int capture(bool delayed) {
+    c10::cuda::CUDAGuard guard(device_);
     const int a = delayed ? 1 : 0;
     if (exec_[a]) { cudaGraphExecDestroy(exec_[a]); exec_[a] = nullptr; }
     if (graph_[a]) { cudaGraphDestroy(graph_[a]); graph_[a] = nullptr; }
@@ -381,6 +406,7 @@ class MoELayerRunner {
   bool has_graph(bool delayed) const { return exec_[delayed ? 1 : 0] != nullptr; }
 
   int replay(bool delayed) {
+    c10::cuda::CUDAGuard guard(device_);
     const int a = delayed ? 1 : 0;
     if (!exec_[a]) throw std::runtime_error("no captured graph for this arm");
     ck(cudaGraphLaunch(exec_[a], comm_), "cudaGraphLaunch");
@@ -389,6 +415,7 @@ class MoELayerRunner {
 
   // Align all ranks on the device (no host round-trip) before a timed call.
   void device_barrier() {
+    c10::cuda::CUDAGuard guard(device_);
     raiccl::BarrierParams bp{};
     bp.dims = dims_;
     bp.layout = layout_;
@@ -432,12 +459,15 @@ class MoELayerRunner {
   raiccl::PeerBases peers_{};
   int partial_ = 0, ffn_ = 0, n1_ = 0, act1_ = 0, bn1_ = 0, bn2_ = 0;
   int max_cands_ = 0, log_stride_ = 0, max_ctl_tokens_ = 0, grid_sms_ = 148;
+  bool control_serial_ = false;  // run the CTA control kernel even where the single-warp one fits
   bool feat_bf16_ = false, out_bf16_ = false;
   unsigned long long timeout_ns_ = 0;
   CUtensorMap ta1_{}, tb1_{}, ta2_{}, tb2_{};
   cudaStream_t router_ = nullptr, comm_ = nullptr;
-  cudaEvent_t ev_start_ = nullptr;
-  std::vector<cudaEvent_t> ev_chunk_;
+  cudaStream_t disp_ = nullptr;
+  int device_ = 0;
+  cudaEvent_t ev_start_ = nullptr, ev_disp_done_ = nullptr;
+  std::vector<cudaEvent_t> ev_chunk_, ev_ctl_;
   cudaGraph_t graph_[2] = {nullptr, nullptr};
   cudaGraphExec_t exec_[2] = {nullptr, nullptr};
   int graph_launches_[2] = {0, 0};

@@ -37,7 +37,7 @@ from ..uncertainty.observation import PartialObservationState, RevealedDemandTok
 from ..uncertainty.problem import UncertainProblemInstance
 from .oracle import layer_reference, router_logits
 
-LOG_HEADER = 8
+LOG_HEADER = 16  # 8-word decision record + 8 phase-clock words
 
 
 class CheckerFailure(RuntimeError):

@@ -40,7 +40,7 @@ from .oracle import layer_reference
 
 FWD_META = 9
 RET_META = 8
-LOG_HEADER = 8
+LOG_HEADER = 16  # 8-word decision record + 8 phase-clock words
 
 
 @dataclass
@@ -52,7 +52,8 @@ class LayerTiming:
 class ProgressiveMoELayer:
     def __init__(self, cfg: MoELayerConfig, *, device: torch.device | str | None = None,
                  world: int | None = None, rank: int | None = None, group=None,
-                 timeout_s: float = 10.0, seed: int = 0, control_topology=None) -> None:
+                 timeout_s: float = 10.0, seed: int = 0, control_topology=None,
+                 control_path: str = "auto") -> None:
         self.cfg = cfg
         if world is None:
             world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -133,6 +134,7 @@ class ProgressiveMoELayer:
             "timeout_ns": int(timeout_s * 1e9), "max_cands": self.max_cands,
             "log_stride": self.log_stride, "max_ctl_tokens": Tc,
             "sms": torch.cuda.get_device_properties(dev).multi_processor_count,
+            "control_serial": {"auto": 0, "serial": 1}[control_path],
         }
         self.layout = self._k.sym_layout(ints)
         self.channel = PeerChannel(self.layout["total"], dev, group=group)
@@ -184,6 +186,7 @@ class ProgressiveMoELayer:
             # control plan + state: one blob (typed views below), staged by the control kernel
             "plan_E": Ep, "plan_G": G, "plan_NGM": int(flat["group_members"].size),
             "plan_NEGM": int(flat["edge_group_members"].size), "plan_NT": int(flat["tmpl_edge"].size),
+            "plan_MT": int(max_tmpl),
             "ctl_blob": self._control_blob(flat, Ep, G, V, Tc, dev),
             "ctl_log": torch.zeros(cfg.n_desc * self.log_stride, dtype=torch.int32, device=dev),
         }

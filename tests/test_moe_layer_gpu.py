@@ -145,3 +145,31 @@ def test_graph_capture_replay_repeated_calls():
         assert torch.equal(ref, layer.out)
     finally:
         layer.close()
+
+
+@pytest.mark.parametrize("case", ["balanced", "skewed", "empty_shard", "multiple_progressive_shards"])
+def test_warp_control_plane_matches_cta_kernel(case):
+    """The single-warp control kernel and the CTA kernel make the same decisions,
+    leave the same scheduler state and write the same log rows."""
+    from revealaiccl_b200.moe.config import r4_case
+    from revealaiccl_b200.moe.layer import LOG_HEADER, ProgressiveMoELayer
+
+    res = {}
+    for path in ("auto", "serial"):
+        layer = ProgressiveMoELayer(r4_case(case), timeout_s=5.0, control_path=path)
+        try:
+            layer.forward("early")
+            rep = layer.verify()
+            assert rep["pass"], (path, rep["violations"])
+            lay = layer.control_layout
+            blob = layer.tensors["ctl_blob"].cpu()
+            log = layer.tensors["ctl_log"].cpu().view(layer.cfg.n_desc, layer.log_stride)
+            res[path] = (blob[int(lay["state_begin"]):int(lay["state_end"])].clone(),
+                         torch.cat([log[:, :8], log[:, LOG_HEADER:]], dim=1).clone(),
+                         int(log[0, 15]), layer.out.clone())
+        finally:
+            layer.close()
+    assert res["auto"][2] == 1 and res["serial"][2] == 0  # which kernel ran
+    assert torch.equal(res["auto"][0], res["serial"][0])
+    assert torch.equal(res["auto"][1], res["serial"][1])
+    assert torch.equal(res["auto"][3], res["serial"][3])
