@@ -35,12 +35,16 @@ def run_reference(args) -> dict | None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if not (REF_ROOT / "scripts" / "run_r4_a0_c0_full_moe.py").exists():
         return _unavailable("reference tree not present under baseline/_ref") if rank == 0 else None
+    if args.config != "r4_reference":
+        return _unavailable(
+            "the reference's full-MoE path runs only its R4 shape: its driver hard-codes D=2048, 4 experts, "
+            "top-1 and a 2048->32->16 expert (scripts/run_r2_f0_integrated.py:59-66, "
+            "scripts/run_r4_a0_c0_full_moe.py:50-51, one expert per token in scripts/run_r3_a0_c0.py:155-161) "
+            "and its expert MLP is ReLU-only (rlccl/transport/reference_full_moe.py:263-281), so "
+            f"{args.config} (top-k > 1, GELU/SwiGLU experts) has no stock reference path") if rank == 0 else None
     if args.gpus != 2 or world != 2:
         return _unavailable("the reference full-MoE driver requires exactly two ranks "
                             "(scripts/run_r4_a0_c0_full_moe.py:1062)") if rank == 0 else None
-    if args.config != "r4_reference":
-        return _unavailable("the reference stock path implements only its R4 config "
-                            "(top-1, ReLU 2048->32->16, 4 experts)") if rank == 0 else None
     import torch
     import torch.distributed as dist
     from datetime import timedelta

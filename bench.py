@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Full progressive MoE layer benchmark (one rank per GPU).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config r4_reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config full_tf32|r4_reference|...]
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
         --master-port P bench.py --gpus N --steps K --warmup W
     python bench.py --impl reference ...     (the unmodified reference build)
@@ -241,7 +241,9 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="r4_reference")
+    # full_tf32: 4096 tokens/rank, hidden 1024, 8 experts top-2, 1024->4096 GELU->1024,
+    # fp32 storage with tf32 tensor-core math, 8 x 512 router chunks, softmax-gated combine
+    ap.add_argument("--config", default="full_tf32")
     ap.add_argument("--impl", choices=("product", "reference"), default="product")
     args = ap.parse_args()
     if args.warmup < 3:

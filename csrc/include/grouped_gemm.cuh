@@ -9,7 +9,7 @@
 //
 // Roles inside one CTA (192 threads, one CTA per SM):
 //   warp 0      TMA producer: streams 128-row A tiles and BN-row B tiles into
-//               an S-stage shared-memory ring (128-byte swizzle, no multicast).
+//               an S-stage shared-memory ring (128-byte swizzle, per-CTA loads).
 //   warp 1      owns the TMEM allocation; one elected lane issues tcgen05.mma
 //               (M=128, N=BN, fp32 accumulators in TMEM, two accumulator
 //               buffers so the epilogue of tile i overlaps the MMAs of i+1).

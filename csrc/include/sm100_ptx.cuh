@@ -126,7 +126,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ---------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor), no multicast anywhere in this framework.
+// TMA (cp.async.bulk.tensor): plain per-CTA tile loads only.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void* desc) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(desc) : "memory");
