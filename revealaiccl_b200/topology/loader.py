@@ -54,7 +54,7 @@ def parse_topology(data: dict) -> tuple[int, int, np.ndarray, np.ndarray, list]:
                             dtype=np.float64)
     edge_index: dict[tuple[int, int], int] = {}
     for i, (u, v) in enumerate(edges.tolist()):
-        edge_index.setdefault((u, v), i)
+        edge_index[(u, v)] = i  # a repeated (u, v) link: groups name its last occurrence
     shared: list[tuple[list[int], float]] = []
     for group in data.get("bandwidth_groups", {}).values():
         if not isinstance(group, dict) or "edges" not in group or "max_bandwidth" not in group:
