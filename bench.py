@@ -102,6 +102,7 @@ def run_product(args) -> dict | None:
     import torch.distributed as dist
     from datetime import timedelta
 
+    from revealaiccl_b200.bench.paired import bootstrap_median
     from revealaiccl_b200.moe.config import preset
     from revealaiccl_b200.moe.layer import ProgressiveMoELayer
 
@@ -203,6 +204,7 @@ def run_product(args) -> dict | None:
         if rank != 0:
             return None
         p50 = statistics.median(early)
+        ci = bootstrap_median(deltas)  # paired median CI, 10k resamples
         tokens_total = cfg.tokens_per_rank * world
         return {
             "metric": METRIC, "value": round(p50, 4), "unit": "ms", "n_gpus": world, "steps": args.steps,
@@ -218,6 +220,7 @@ def run_product(args) -> dict | None:
                        "parallelism": f"ep{world}", "l2": "256 MiB flush before every timed step"},
             "p50_early_ms": round(p50, 4), "p50_delayed_ms": round(statistics.median(delayed), 4),
             "delta_ms": round(statistics.median(deltas), 4),
+            "delta_ci95_ms": [round(ci["ci95_lower"], 4), round(ci["ci95_upper"], 4)],
             "p95_early_ms": round(sorted(early)[max(0, int(0.95 * len(early)) - 1)], 4),
             "tokens_per_s": round(tokens_total / (p50 / 1e3), 1),
             "bracket_ms": round(bracket, 3),
