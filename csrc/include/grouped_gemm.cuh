@@ -88,6 +88,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  if (p.trace != nullptr && threadIdx.x == 0) atomicMin(&p.trace->t_start, (unsigned long long)globaltimer_ns());
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
@@ -271,6 +272,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
   __syncthreads();
   tc_fence_after_sync();
   if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+  if (p.trace != nullptr && threadIdx.x == 0) {  // after the CTA-wide barrier: every role is done
+    atomicMax(&p.trace->t_end, (unsigned long long)globaltimer_ns());
+    atomicAdd(&p.trace->ctas, 1);
+  }
 }
 
 // ---------------------------------------------------------------------------

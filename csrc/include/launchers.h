@@ -12,7 +12,7 @@
 namespace raiccl {
 
 void launch_tile_plan(const GemmSegment* segs, int num_segs, int nblocks, int* prefix,
-                      cudaStream_t stream);
+                      cudaStream_t stream, TraceSlot* trace = nullptr);
 
 // in_tf32: A/B hold fp32 (tf32 math) else bf16; out_bf16 selects the output dtype.
 void launch_gg_tf32_f32(int act, int bn, const CUtensorMap& ta, const CUtensorMap& tb,

@@ -1,0 +1,304 @@
+// Device building blocks of the progressive MoE data plane, shared by the
+// one-launch-per-step kernels (csrc/kernels/moe_dataplane.cu) and the
+// persistent front-end kernel (csrc/kernels/moe_frontend.cu):
+//   * identity-checksum arithmetic mod 2^63 - 25;
+//   * router_token  — one warp routes one token (logits, mask, stable top-k, gates);
+//   * dispatch_rows — one CTA packs and stores its share of a revealed
+//                     descriptor's rows into the owners' receive regions;
+//   * dispatch_publish — the last CTA of a descriptor publishes its per-expert
+//                     counts and the per-destination ready words.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include <cstdint>
+
+#include "moe_kernels.h"
+#include "sm100_ptx.cuh"
+
+namespace raiccl {
+
+// Identity checksum coefficients c_0..c_7 (the reference's RouterAssignment
+// checksum, rlccl/transport/reference_a2av.py:20-29); one copy per unit.
+static __constant__ unsigned long long c_checksum_coeff[8] = {1000003ULL, 1000033ULL, 1000037ULL, 1000081ULL,
+                                                             1000099ULL, 1000117ULL, 1000121ULL, 1000133ULL};
+
+__device__ __forceinline__ float to_f(float x) { return x; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+// splitmix64 finaliser (Steele, Lea & Flood 2014 / Vigna), used as the word
+// mixer of the order-dependent row digest.
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ULL;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ uint64_t addmod(uint64_t a, uint64_t b) {
+  uint64_t s = a + b;  // a, b < M < 2^63: no overflow
+  return s >= kChecksumModulus ? s - kChecksumModulus : s;
+}
+
+// x mod M for M = 2^63 - 25 and any 64-bit x, from 2^63 = M + 25:
+// x = h * 2^63 + l (h <= 1) is congruent to l + 25 h < 2M.
+__device__ __forceinline__ uint64_t mod_m(uint64_t x) {
+  const uint64_t r = (x & ((1ULL << 63) - 1)) + (x >> 63) * 25ULL;
+  return r >= kChecksumModulus ? r - kChecksumModulus : r;
+}
+
+// (v mod M) * c mod M for a coefficient c < 2^32 (the identity coefficients are
+// about 10^6), without 128-bit division: with a = v mod M < 2^63 the product
+// a * c = hi * 2^64 + lo has hi < 2^32, and 2^64 = 2M + 50, so it is congruent
+// to (lo mod M) + 50 hi < M + 2^38 < 2M.
+__device__ __forceinline__ uint64_t mulmod_coeff(uint64_t v, uint64_t c) {
+  const uint64_t a = mod_m(v);
+  const uint64_t lo = a * c;
+  const uint64_t hi = __umul64hi(a, c);
+  const uint64_t r = mod_m(lo) + hi * 50ULL;
+  return r >= kChecksumModulus ? r - kChecksumModulus : r;
+}
+
+constexpr int kRouterUnroll = 8;
+constexpr int kDispatchMaxItems = 4096;
+constexpr int kMaxExperts = 256;
+constexpr int kDispatchMaxChunks = 128;  // chunk-offset table staged in shared memory
+
+// ---------------------------------------------------------------------------
+// Router of one token (warp collective): logits = x_t . W_e + b_e (+ chunk
+// bias), masked experts -inf, stable descending top-k (the smaller expert id
+// wins ties), gates per gate_mode; writes expert_ids / gates of row t.
+// Lane 0 returns the selected experts in sel_out[0..k).
+// SMEM_W: w points at a shared-memory copy of the weights.
+// ---------------------------------------------------------------------------
+template <typename T, int EMAX, bool SMEM_W>
+__device__ __forceinline__ void router_token(const RouterParams& p, const float* chunk_bias, int t,
+                                             const T* __restrict__ w, int* sel_out) {
+  const T* __restrict__ tokens = (const T*)p.tokens;
+  const int D = p.hidden, E = p.experts;
+  const int lane = threadIdx.x & 31;
+  constexpr int VEC = 16 / sizeof(T);
+  float acc[EMAX];
+#pragma unroll
+  for (int e = 0; e < EMAX; ++e) acc[e] = 0.f;
+  const T* x = tokens + (long long)t * D;
+  constexpr int STEP = 32 * VEC * kRouterUnroll;
+  for (int base0 = 0; base0 < D; base0 += STEP) {
+    uint4 xr[kRouterUnroll];
+#pragma unroll
+    for (int u = 0; u < kRouterUnroll; ++u) {
+      const int base = base0 + (u * 32 + lane) * VEC;
+      xr[u] = base < D ? __ldg((const uint4*)(x + base)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kRouterUnroll; ++u) {
+      const int base = base0 + (u * 32 + lane) * VEC;
+      if (base >= D) break;
+      const T* xv = (const T*)&xr[u];
+#pragma unroll
+      for (int e = 0; e < EMAX; ++e) {
+        if (e < E) {
+          uint4 wr;
+          if constexpr (SMEM_W) wr = *(const uint4*)(w + (long long)e * D + base);
+          else wr = __ldg((const uint4*)(w + (long long)e * D + base));
+          const T* wv = (const T*)&wr;
+          float s = 0.f;
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) s = fmaf(to_f(xv[v]), to_f(wv[v]), s);
+          acc[e] += s;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < EMAX; ++e) {
+    if (e < E) {
+      float v = acc[e];
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      acc[e] = v;
+    }
+  }
+  if (lane != 0) return;
+  float logit[EMAX];
+  bool taken[EMAX];
+  const float ninf = -__int_as_float(0x7f800000);
+#pragma unroll
+  for (int e = 0; e < EMAX; ++e) {
+    taken[e] = false;
+    if (e < E) {
+      float l = acc[e] + p.bias[e] + (chunk_bias ? chunk_bias[e] : 0.f);
+      const bool masked = (p.mask_mode == 1 && e == (t % E)) || (p.block_mask && p.block_mask[e]);
+      logit[e] = masked ? ninf : l;
+    } else {
+      logit[e] = ninf;
+    }
+  }
+  float sel_logit[8];
+  int sel[8];
+  for (int j = 0; j < p.top_k; ++j) {
+    int best = -1;
+#pragma unroll
+    for (int e = 0; e < EMAX; ++e)
+      if (e < E && !taken[e] && (best < 0 || logit[e] > logit[best])) best = e;
+#pragma unroll
+    for (int e = 0; e < EMAX; ++e)
+      if (e == best) taken[e] = true;
+    sel[j] = best;
+    sel_logit[j] = logit[best];
+  }
+  float g[8];
+  if (p.gate_mode == 1) {
+    float sum = 0.f;
+    for (int j = 0; j < p.top_k; ++j) { g[j] = __expf(sel_logit[j] - sel_logit[0]); sum += g[j]; }
+    for (int j = 0; j < p.top_k; ++j) g[j] /= sum;
+  } else if (p.gate_mode == 2) {
+    float mx = sel_logit[0], sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < EMAX; ++e)
+      if (e < E && logit[e] != ninf) sum += __expf(logit[e] - mx);
+    for (int j = 0; j < p.top_k; ++j) g[j] = __expf(sel_logit[j] - mx) / sum;
+  } else {
+    for (int j = 0; j < p.top_k; ++j) g[j] = 1.f;
+  }
+  for (int j = 0; j < p.top_k; ++j) {
+    p.expert_ids[(long long)t * p.top_k + j] = sel[j];
+    p.gates[(long long)t * p.top_k + j] = g[j];
+    if (sel_out) sel_out[j] = sel[j];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// One CTA's share [a, b) of a descriptor whose tokens start at t0: rows keep
+// the reference's deterministic order inside every (expert, source) region,
+// descriptor order then token order, so the row of item i (token t, choice j,
+// expert e) is base[e] + (items of expert e in [t0, a)) + (its in-order
+// rank inside [a, b)).  hist / run must be zero on entry (E entries); on
+// return run[e] holds this share's item count per expert.  Collective over the
+// CTA (contains __syncthreads); the caller checks (b - a) * k <= kDispatchMaxItems.
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, const int* base_e, int* hist, int* run,
+                              int* item_pos, const int* s_coff, int nc) {
+  const MoEDims& d = p.dims;
+  const int k = d.top_k;
+  const int E = d.experts;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  // rows of earlier tokens of this descriptor per expert: lanes holding the
+  // same expert elect one leader that adds the group's size (one shared-memory
+  // atomic per distinct expert per warp instead of one per item)
+  {
+    const long long i_end = (long long)a * k;
+    for (long long i0 = (long long)t0 * k + (long long)warp * 32; i0 < i_end; i0 += (long long)nwarps * 32) {
+      const long long i = i0 + lane;
+      const int e = i < i_end ? p.expert_ids[i] : E;  // sentinel groups the tail lanes
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      if (e < E && lane == __ffs(peers) - 1) atomicAdd(&hist[e], __popc(peers));
+    }
+  }
+  // in-order rank of every item of this share within its expert
+  if (warp == 0) {
+    const long long i0 = (long long)a * k, i1 = (long long)b * k;
+    for (long long base = i0; base < i1; base += 32) {
+      const long long i = base + lane;
+      const bool valid = i < i1;
+      const int e = valid ? p.expert_ids[i] : E;  // sentinel groups the tail lanes
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      const int rank_in = __popc(peers & ((1u << lane) - 1u));
+      const int prev = valid ? run[e] : 0;
+      if (valid) item_pos[i - i0] = prev + rank_in;
+      __syncwarp();
+      if (valid && lane == __ffs(peers) - 1) run[e] = prev + __popc(peers);
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // copy features + identity rows, one warp per item
+  const long long nitems = (long long)(b - a) * k;
+  const int vec_per_row = d.hidden * d.feat_bytes / 16;
+  for (long long li = warp; li < nitems; li += nwarps) {
+    const long long i = (long long)a * k + li;
+    const int t = (int)(i / k), j = (int)(i % k);
+    const int e = p.expert_ids[i];
+    const int r = expert_owner(d, e), le = expert_slot(d, e);
+    const long long row = (long long)base_e[e] + hist[e] + item_pos[li];
+    if (row >= d.cap || r >= d.world || le >= d.expert_slots) {
+      if (lane == 0) record_status(p.status, kBoundsViolation, 21, row, d.cap);
+      continue;
+    }
+    const long long grow = ((long long)le * d.world + d.rank) * d.cap + row;
+    uint8_t* base = (uint8_t*)p.peers.base[r];
+    uint4* dst = (uint4*)(base + p.layout.recv_feat + grow * d.hidden * d.feat_bytes);
+    const uint4* src = (const uint4*)((const uint8_t*)p.tokens + (long long)t * d.hidden * d.feat_bytes);
+    constexpr int U = 8;  // 16-byte loads in flight per lane before the stores
+    for (int v0 = 0; v0 < vec_per_row; v0 += 32 * U) {
+      uint4 rr[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int v = v0 + u * 32 + lane;
+        if (v < vec_per_row) rr[u] = __ldg(src + v);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int v = v0 + u * 32 + lane;
+        if (v < vec_per_row) dst[v] = rr[u];
+      }
+    }
+    if (lane < kFwdMetaFields) {
+      int c = 0;
+      while (c + 1 < nc && s_coff[c + 1] <= t) ++c;
+      while (c + 1 < d.chunks && p.chunk_offsets[c + 1] <= t) ++c;  // beyond the staged table
+      long long val;
+      switch (lane) {
+        case 0: val = p.token_ids[t]; break;
+        case 1: val = d.rank; break;
+        case 2: val = r; break;
+        case 3: val = e; break;
+        case 4: val = c; break;
+        case 5: val = t - (c <= nc ? s_coff[c] : p.chunk_offsets[c]); break;
+        case 6: val = t; break;
+        case 7: val = p.feat_digest[t]; break;
+        default: {
+          uint64_t cs = (uint64_t)p.checksum_base[t];
+          cs = addmod(cs, mulmod_coeff((uint64_t)r, c_checksum_coeff[2]));
+          cs = addmod(cs, mulmod_coeff((uint64_t)e, c_checksum_coeff[3]));
+          val = (long long)cs;
+        }
+      }
+      ((long long*)(base + p.layout.recv_meta))[grow * kFwdMetaFields + lane] = val;
+    } else if (lane == 16) {
+      ((int*)(base + p.layout.recv_retrow))[grow] = t * k + j;
+    } else if (lane == 17) {
+      ((float*)(base + p.layout.recv_gate))[grow] = d.gate_mode ? p.gates[i] : 1.f;
+    }
+  }
+}
+
+// Last CTA of a descriptor: per-expert counts into every owner's header
+// (optionally advancing sent_base), then one release store of the call's
+// sequence number per destination rank (sent for zero rows too).  Ordering:
+// every share's stores -> bar.sync -> the CTA's acq_rel increment of the
+// descriptor counter; the last CTA's acquiring increment sees them all and
+// its st.release.sys is cumulative, so a peer that acquires the ready word
+// sees every row.
+__device__ __forceinline__ void dispatch_publish(const DispatchParams& p, int desc, bool skip_signal,
+                                                 unsigned long long epoch, bool update_sent_base) {
+  const MoEDims& d = p.dims;
+  const int E = d.experts;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int cnt = atomicAdd(&p.desc_counts[(long long)desc * E + e], 0);
+    const int r = expert_owner(d, e), le = expert_slot(d, e);
+    uint8_t* base = (uint8_t*)p.peers.base[r];
+    ((int*)(base + p.layout.recv_count))[((long long)le * d.world + d.rank) * d.n_desc + desc] = cnt;
+    if (update_sent_base) p.sent_base[e] += cnt;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int r = 0; r < d.world && !skip_signal; ++r) {
+      uint8_t* base = (uint8_t*)p.peers.base[r];
+      st_release_sys_u64((uint64_t*)(base + p.layout.recv_flag) + (long long)d.rank * d.n_desc + desc, epoch);
+    }
+    p.done_counter[desc] = 0;
+  }
+}
+
+}  // namespace raiccl

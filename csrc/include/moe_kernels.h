@@ -22,6 +22,7 @@ struct RouterParams {
   int hidden, experts, top_k, gate_mode, mask_mode, pad;
   int32_t* expert_ids;      // [T, k]
   float* gates;             // [T, k]
+  TraceSlot* trace;
 };
 
 struct DispatchParams {
@@ -35,13 +36,15 @@ struct DispatchParams {
   const long long* feat_digest;
   const long long* checksum_base;
   const int32_t* chunk_offsets;
-  int desc, t0, t1, pad;
+  int desc, t0, t1;
+  int fault_skip_signal;    // test hook set by the host: 1 = publish no ready flag for this descriptor
   int32_t* sent_base;       // [E] rows already sent to (e, this rank) in earlier descriptors
   int32_t* desc_counts;     // [n_desc, E]
   int32_t* done_counter;    // [n_desc]
   const unsigned long long* permit;  // [n_desc] == epoch when the guard committed the descriptor
   const unsigned long long* epoch;   // device word holding this call's sequence number
   DeviceStatus* status;
+  TraceSlot* trace;
 };
 
 struct PlanParams {
@@ -53,6 +56,7 @@ struct PlanParams {
   const unsigned long long* epoch;
   unsigned long long timeout_ns;
   DeviceStatus* status;
+  TraceSlot* trace;
 };
 
 struct ReturnMetaParams {
@@ -61,6 +65,7 @@ struct ReturnMetaParams {
   PeerBases peers;
   const GemmSegment* segs;
   DeviceStatus* status;
+  TraceSlot* trace;
 };
 
 struct SignalParams {
@@ -68,6 +73,7 @@ struct SignalParams {
   SymLayout layout;
   PeerBases peers;
   const unsigned long long* epoch;
+  TraceSlot* trace;
 };
 
 struct CombineParams {
@@ -78,6 +84,7 @@ struct CombineParams {
   const unsigned long long* epoch;
   unsigned long long timeout_ns;
   DeviceStatus* status;
+  TraceSlot* trace;
 };
 
 struct BarrierParams {
@@ -87,6 +94,7 @@ struct BarrierParams {
   unsigned long long* counter;  // this rank's barrier sequence (device word)
   unsigned long long timeout_ns;
   DeviceStatus* status;
+  TraceSlot* trace;
 };
 
 // Device-resident compiled-scheduler control plane (one CTA).
@@ -115,7 +123,35 @@ struct ControlParams {
   unsigned long long* permit;  // [n_desc]
   const unsigned long long* epoch;
   DeviceStatus* status;
+  TraceSlot* trace;
 };
+
+// Persistent progressive front end (one cooperative launch per layer call):
+// CTA 0's first warp runs the control plane for every trigger, keeping the
+// compiled plan and scheduler state in shared memory; every other CTA routes
+// its share of each router chunk and, as descriptors are released, packs and
+// stores its share of their rows into the owners' receive regions.
+struct FrontendParams {
+  RouterParams rp;          // rp.chunk_bias: [C, E] base (row c per chunk) or nullptr
+  ControlParams cp;
+  DispatchParams dp;        // desc / t0 / t1 / fault_skip_signal are set per descriptor
+  int* chunk_done;          // [C] worker CTAs that finished router chunk c (zeroed per call)
+  int* chunk_counts;        // [C, E] router assignments per (chunk, expert) (zeroed per call)
+  int* disp_base;           // [n_desc, E] first receive row of (descriptor, expert)
+  unsigned long long* desc_ready;  // [n_desc] == epoch once the control warp released q
+  int delayed;              // 1: dispatch only after the final trigger
+  int fault_skip_desc;      // test hook: descriptor whose ready flags are withheld (-1: none)
+  unsigned long long timeout_ns;
+  TraceSlot* phase_trace;   // [C + 2 n_desc]: router c, control q, dispatch q; or nullptr
+  TraceSlot* trace;         // the launch
+  unsigned long long* cta_clock;  // [grid, 64] per-CTA %globaltimer stamps, or nullptr
+};
+
+// Returns false (nothing launched) when the device cannot co-schedule the grid.
+bool launch_frontend(const FrontendParams& f, bool bf16, int sms, cudaStream_t s);
+size_t control_smem_bytes(const ControlParams& p);
+ControlDims control_dims(const ControlParams& p);
+bool control_warp_path_ok(const ControlParams& p);
 
 void launch_feature_digest(const void* rows, long long row_bytes, int nrows, long long* digest,
                            cudaStream_t s);
@@ -128,7 +164,8 @@ void launch_return_meta(const ReturnMetaParams& p, int grid, cudaStream_t s);
 void launch_return_signal(const SignalParams& p, cudaStream_t s);
 void launch_combine(const CombineParams& p, bool bf16, int grid, cudaStream_t s);
 void launch_layer_reset(int* sent_base, int experts, int* desc_counts, int n_desc, int* done_counter,
-                        unsigned long long* epoch, cudaStream_t s);
+                        unsigned long long* epoch, TraceSlot* trace, int n_trace, int* chunk_words,
+                        int n_chunk_words, cudaStream_t s);
 void launch_control(const ControlParams& p, cudaStream_t s);
 void launch_device_barrier(const BarrierParams& p, cudaStream_t s);
 

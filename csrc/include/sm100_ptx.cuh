@@ -47,6 +47,21 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// Folds this CTA's start / end time into a launch trace slot (thread 0 only).
+// The destructor runs on every return path of the kernel.
+struct TraceScope {
+  TraceSlot* slot;
+  __device__ __forceinline__ explicit TraceScope(TraceSlot* s) : slot(s) {
+    if (slot != nullptr && threadIdx.x == 0) atomicMin(&slot->t_start, (unsigned long long)globaltimer_ns());
+  }
+  __device__ __forceinline__ ~TraceScope() {
+    if (slot != nullptr && threadIdx.x == 0) {
+      atomicMax(&slot->t_end, (unsigned long long)globaltimer_ns());
+      atomicAdd(&slot->ctas, 1);
+    }
+  }
+};
+
 // ---------------------------------------------------------------------------
 // Shared-memory address helpers
 // ---------------------------------------------------------------------------

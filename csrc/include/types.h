@@ -28,6 +28,17 @@ struct DeviceStatus {
   long long bound; // capacity or expected value
 };
 
+// Device trace ring entry: one per kernel launch of a layer call.  Every CTA
+// folds its first and last %globaltimer reading into the slot (min / max), so
+// the slot holds the launch's device span; `ctas` counts the CTAs that ran.
+struct TraceSlot {
+  unsigned long long t_start;  // ~0 until a CTA started (reset per call)
+  unsigned long long t_end;
+  int ctas;
+  int pad0;
+  long long pad1;
+};
+
 enum class Act : int { kNone = 0, kRelu = 1, kGelu = 2, kSilu = 3, kSwiGLU = 4 };
 
 struct GemmSegment {
@@ -52,6 +63,7 @@ struct GroupedGemmParams {
   long long ldo;             // output row stride in elements
   DeviceStatus* status;
   unsigned long long timeout_ns;
+  TraceSlot* trace;          // launch trace slot or nullptr
 };
 
 }  // namespace raiccl

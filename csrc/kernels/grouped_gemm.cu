@@ -5,13 +5,15 @@
 #include <string>
 
 #include "grouped_gemm.cuh"
+#include "sm100_ptx.cuh"
 #include "launchers.h"
 
 namespace raiccl {
 
 // One CTA: prefix[s] = sum_{j<s} ceil(rows_j / 128) * nblocks.
 __global__ void gemm_tile_plan_kernel(const GemmSegment* segs, int num_segs, int nblocks,
-                                      int* prefix) {
+                                      int* prefix, TraceSlot* trace) {
+  TraceScope trace_scope(trace);
   __shared__ int partial[1024];
   const int tid = threadIdx.x;
   int local = 0;
@@ -40,8 +42,8 @@ __global__ void gemm_tile_plan_kernel(const GemmSegment* segs, int num_segs, int
 }
 
 void launch_tile_plan(const GemmSegment* segs, int num_segs, int nblocks, int* prefix,
-                      cudaStream_t stream) {
-  gemm_tile_plan_kernel<<<1, 1024, 0, stream>>>(segs, num_segs, nblocks, prefix);
+                      cudaStream_t stream, TraceSlot* trace) {
+  gemm_tile_plan_kernel<<<1, 1024, 0, stream>>>(segs, num_segs, nblocks, prefix, trace);
 }
 
 // Instantiated combinations: tf32 inputs -> fp32 outputs; bf16 inputs -> bf16

@@ -20,48 +20,10 @@
 
 #include "launchers.h"
 #include "moe_kernels.h"
+#include "moe_device.cuh"
 #include "sm100_ptx.cuh"
 
 namespace raiccl {
-
-__constant__ unsigned long long c_checksum_coeff[8] = {1000003ULL, 1000033ULL, 1000037ULL, 1000081ULL,
-                                                      1000099ULL, 1000117ULL, 1000121ULL, 1000133ULL};
-
-__device__ __forceinline__ float to_f(float x) { return x; }
-__device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
-
-// splitmix64 finaliser (Steele, Lea & Flood 2014 / Vigna), used as the word
-// mixer of the order-dependent row digest below.
-__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
-  z += 0x9E3779B97F4A7C15ULL;
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
-  return z ^ (z >> 31);
-}
-
-__device__ __forceinline__ uint64_t addmod(uint64_t a, uint64_t b) {
-  uint64_t s = a + b;  // a, b < M < 2^63: no overflow
-  return s >= kChecksumModulus ? s - kChecksumModulus : s;
-}
-
-// x mod M for M = 2^63 - 25 and any 64-bit x, from 2^63 = M + 25:
-// x = h * 2^63 + l (h <= 1) is congruent to l + 25 h < 2M.
-__device__ __forceinline__ uint64_t mod_m(uint64_t x) {
-  const uint64_t r = (x & ((1ULL << 63) - 1)) + (x >> 63) * 25ULL;
-  return r >= kChecksumModulus ? r - kChecksumModulus : r;
-}
-
-// (v mod M) * c mod M for a coefficient c < 2^32 (the identity coefficients are
-// about 10^6), without 128-bit division: with a = v mod M < 2^63 the product
-// a * c = hi * 2^64 + lo has hi < 2^32, and 2^64 = 2M + 50, so it is congruent
-// to (lo mod M) + 50 hi < M + 2^38 < 2M.
-__device__ __forceinline__ uint64_t mulmod_coeff(uint64_t v, uint64_t c) {
-  const uint64_t a = mod_m(v);
-  const uint64_t lo = a * c;
-  const uint64_t hi = __umul64hi(a, c);
-  const uint64_t r = mod_m(lo) + hi * 50ULL;
-  return r >= kChecksumModulus ? r - kChecksumModulus : r;
-}
 
 // ---------------------------------------------------------------------------
 // Row digest: (sum_i splitmix64((i << 32) | w_i)) mod 2^64, masked to 62 bits,
@@ -107,113 +69,23 @@ __global__ void moe_checksum_base_kernel(const long long* token_ids, const long 
 // Router rows are streamed with UNROLL independent 16-byte loads in flight per
 // lane (the kernel is HBM-bound for small E); W is staged once per CTA in
 // shared memory when it fits (SMEM_W), else read through the read-only cache.
-constexpr int kRouterUnroll = 8;
-
 template <typename T, int EMAX, bool SMEM_W>
 __global__ void __launch_bounds__(256) moe_router_kernel(RouterParams p) {
+  TraceScope trace_scope(p.trace);
   extern __shared__ __align__(16) uint8_t router_smem[];
-  const T* __restrict__ tokens = (const T*)p.tokens;
-  const int D = p.hidden, E = p.experts;
   const T* __restrict__ w = (const T*)p.weight;
   if constexpr (SMEM_W) {
     uint4* ws = (uint4*)router_smem;
     const uint4* wg = (const uint4*)p.weight;
-    const int nvec = E * D * (int)sizeof(T) / 16;
+    const int nvec = p.experts * p.hidden * (int)sizeof(T) / 16;
     for (int i = threadIdx.x; i < nvec; i += blockDim.x) ws[i] = __ldg(wg + i);
     __syncthreads();
     w = (const T*)router_smem;
   }
   const int warps = blockDim.x >> 5;
   const int t = p.row0 + blockIdx.x * warps + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
   if (t >= p.row1) return;
-  constexpr int VEC = 16 / sizeof(T);
-  float acc[EMAX];
-#pragma unroll
-  for (int e = 0; e < EMAX; ++e) acc[e] = 0.f;
-  const T* x = tokens + (long long)t * D;
-  constexpr int STEP = 32 * VEC * kRouterUnroll;
-  for (int base0 = 0; base0 < D; base0 += STEP) {
-    uint4 xr[kRouterUnroll];
-#pragma unroll
-    for (int u = 0; u < kRouterUnroll; ++u) {
-      const int base = base0 + (u * 32 + lane) * VEC;
-      xr[u] = base < D ? __ldg((const uint4*)(x + base)) : make_uint4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int u = 0; u < kRouterUnroll; ++u) {
-      const int base = base0 + (u * 32 + lane) * VEC;
-      if (base >= D) break;
-      const T* xv = (const T*)&xr[u];
-#pragma unroll
-      for (int e = 0; e < EMAX; ++e) {
-        if (e < E) {
-          uint4 wr;
-          if constexpr (SMEM_W) wr = *(const uint4*)(w + (long long)e * D + base);
-          else wr = __ldg((const uint4*)(w + (long long)e * D + base));
-          const T* wv = (const T*)&wr;
-          float s = 0.f;
-#pragma unroll
-          for (int v = 0; v < VEC; ++v) s = fmaf(to_f(xv[v]), to_f(wv[v]), s);
-          acc[e] += s;
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int e = 0; e < EMAX; ++e) {
-    if (e < E) {
-      float v = acc[e];
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      acc[e] = v;
-    }
-  }
-  if (lane != 0) return;
-  float logit[EMAX];
-  bool taken[EMAX];
-  const float ninf = -__int_as_float(0x7f800000);
-#pragma unroll
-  for (int e = 0; e < EMAX; ++e) {
-    taken[e] = false;
-    if (e < E) {
-      float l = acc[e] + p.bias[e] + (p.chunk_bias ? p.chunk_bias[e] : 0.f);
-      const bool masked = (p.mask_mode == 1 && e == (t % E)) || (p.block_mask && p.block_mask[e]);
-      logit[e] = masked ? ninf : l;
-    } else {
-      logit[e] = ninf;
-    }
-  }
-  float sel_logit[8];
-  int sel[8];
-  for (int j = 0; j < p.top_k; ++j) {
-    int best = -1;
-#pragma unroll
-    for (int e = 0; e < EMAX; ++e)
-      if (e < E && !taken[e] && (best < 0 || logit[e] > logit[best])) best = e;
-#pragma unroll
-    for (int e = 0; e < EMAX; ++e)
-      if (e == best) taken[e] = true;
-    sel[j] = best;
-    sel_logit[j] = logit[best];
-  }
-  float g[8];
-  if (p.gate_mode == 1) {
-    float sum = 0.f;
-    for (int j = 0; j < p.top_k; ++j) { g[j] = __expf(sel_logit[j] - sel_logit[0]); sum += g[j]; }
-    for (int j = 0; j < p.top_k; ++j) g[j] /= sum;
-  } else if (p.gate_mode == 2) {
-    float mx = sel_logit[0], sum = 0.f;
-#pragma unroll
-    for (int e = 0; e < EMAX; ++e)
-      if (e < E && logit[e] != ninf) sum += __expf(logit[e] - mx);
-    for (int j = 0; j < p.top_k; ++j) g[j] = __expf(sel_logit[j] - mx) / sum;
-  } else {
-    for (int j = 0; j < p.top_k; ++j) g[j] = 1.f;
-  }
-  for (int j = 0; j < p.top_k; ++j) {
-    p.expert_ids[(long long)t * p.top_k + j] = sel[j];
-    p.gates[(long long)t * p.top_k + j] = g[j];
-  }
+  router_token<T, EMAX, SMEM_W>(p, p.chunk_bias, t, w, nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -225,12 +97,10 @@ __global__ void __launch_bounds__(256) moe_router_kernel(RouterParams p) {
 // for zero rows, like the reference's header-only zero-payload slot).
 // ---------------------------------------------------------------------------
 constexpr int kDispatchThreads = 512;
-constexpr int kDispatchMaxItems = 4096;
-constexpr int kMaxExperts = 256;
-constexpr int kDispatchMaxChunks = 128;  // chunk-offset table staged in shared memory
 
 template <typename T>
 __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(DispatchParams p) {
+  TraceScope trace_scope(p.trace);
   const MoEDims& d = p.dims;
   __shared__ int hist[kMaxExperts];
   __shared__ int run[kMaxExperts];
@@ -245,7 +115,6 @@ __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(Dispatch
   const int per = (ntok + gridDim.x - 1) / gridDim.x;
   const int a = p.t0 + min(ntok, (int)blockIdx.x * per);
   const int b = p.t0 + min(ntok, (int)(blockIdx.x + 1) * per);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
 
   for (int e = threadIdx.x; e < E; e += blockDim.x) { hist[e] = 0; run[e] = 0; s_sent[e] = p.sent_base[e]; }
   const int nc = min(d.chunks, kDispatchMaxChunks);
@@ -260,95 +129,12 @@ __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(Dispatch
   if (permitted && (long long)(b - a) * k > kDispatchMaxItems) {
     if (threadIdx.x == 0) record_status(p.status, kBadConfig, 22, (long long)(b - a) * k, kDispatchMaxItems);
   } else if (permitted && a < b) {
-    // rows of earlier tokens of this descriptor per expert
-    for (long long i = (long long)p.t0 * k + threadIdx.x; i < (long long)a * k; i += blockDim.x)
-      atomicAdd(&hist[p.expert_ids[i]], 1);
-    // in-order rank of every item of this CTA within its expert
-    if (warp == 0) {
-      const long long i0 = (long long)a * k, i1 = (long long)b * k;
-      for (long long base = i0; base < i1; base += 32) {
-        const long long i = base + lane;
-        const bool valid = i < i1;
-        const int e = valid ? p.expert_ids[i] : E;  // sentinel groups the tail lanes
-        const unsigned peers = __match_any_sync(0xffffffffu, e);
-        const int rank_in = __popc(peers & ((1u << lane) - 1u));
-        const int prev = valid ? run[e] : 0;
-        if (valid) item_pos[i - i0] = prev + rank_in;
-        __syncwarp();
-        if (valid && lane == __ffs(peers) - 1) run[e] = prev + __popc(peers);
-        __syncwarp();
-      }
-    }
-    __syncthreads();
+    dispatch_rows<T>(p, p.t0, a, b, s_sent, hist, run, item_pos, s_coff, nc);
     for (int e = threadIdx.x; e < E; e += blockDim.x)
       if (run[e]) atomicAdd(&p.desc_counts[(long long)p.desc * E + e], run[e]);
-
-    // copy features + identity rows, one warp per item
-    const long long nitems = (long long)(b - a) * k;
-    const int vec_per_row = d.hidden * d.feat_bytes / 16;
-    for (long long li = warp; li < nitems; li += nwarps) {
-      const long long i = (long long)a * k + li;
-      const int t = (int)(i / k), j = (int)(i % k);
-      const int e = p.expert_ids[i];
-      const int r = expert_owner(d, e), le = expert_slot(d, e);
-      const long long row = (long long)s_sent[e] + hist[e] + item_pos[li];
-      if (row >= d.cap || r >= d.world || le >= d.expert_slots) {
-        if (lane == 0) record_status(p.status, kBoundsViolation, 21, row, d.cap);
-        continue;
-      }
-      const long long grow = ((long long)le * d.world + d.rank) * d.cap + row;
-      uint8_t* base = (uint8_t*)p.peers.base[r];
-      uint4* dst = (uint4*)(base + p.layout.recv_feat + grow * d.hidden * d.feat_bytes);
-      const uint4* src = (const uint4*)((const uint8_t*)p.tokens + (long long)t * d.hidden * d.feat_bytes);
-      constexpr int U = 8;  // 16-byte loads in flight per lane before the stores
-      for (int v0 = 0; v0 < vec_per_row; v0 += 32 * U) {
-        uint4 r[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int v = v0 + u * 32 + lane;
-          if (v < vec_per_row) r[u] = __ldg(src + v);
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int v = v0 + u * 32 + lane;
-          if (v < vec_per_row) dst[v] = r[u];
-        }
-      }
-      if (lane < kFwdMetaFields) {
-        int c = 0;
-        while (c + 1 < nc && s_coff[c + 1] <= t) ++c;
-        while (c + 1 < d.chunks && p.chunk_offsets[c + 1] <= t) ++c;  // beyond the staged table
-        long long val;
-        switch (lane) {
-          case 0: val = p.token_ids[t]; break;
-          case 1: val = d.rank; break;
-          case 2: val = r; break;
-          case 3: val = e; break;
-          case 4: val = c; break;
-          case 5: val = t - (c <= nc ? s_coff[c] : p.chunk_offsets[c]); break;
-          case 6: val = t; break;
-          case 7: val = p.feat_digest[t]; break;
-          default: {
-            uint64_t cs = (uint64_t)p.checksum_base[t];
-            cs = addmod(cs, mulmod_coeff((uint64_t)r, c_checksum_coeff[2]));
-            cs = addmod(cs, mulmod_coeff((uint64_t)e, c_checksum_coeff[3]));
-            val = (long long)cs;
-          }
-        }
-        ((long long*)(base + p.layout.recv_meta))[grow * kFwdMetaFields + lane] = val;
-      } else if (lane == 16) {
-        ((int*)(base + p.layout.recv_retrow))[grow] = t * k + j;
-      } else if (lane == 17) {
-        ((float*)(base + p.layout.recv_gate))[grow] = d.gate_mode ? p.gates[i] : 1.f;
-      }
-    }
   }
 
   // completion: the last CTA of the launch publishes counts and signals
-  // Ordering: every thread's stores -> bar.sync -> thread 0's device-scope
-  // acq_rel increment; the last CTA's acquiring increment sees all of them,
-  // and its st.release.sys below is cumulative, so a peer that acquires the
-  // ready word also sees every row of every CTA (no per-CTA system fence).
   __syncthreads();
   if (threadIdx.x == 0) {
     const int prev = atom_add_acq_rel_gpu(&p.done_counter[p.desc], 1);
@@ -356,22 +142,7 @@ __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(Dispatch
   }
   __syncthreads();
   if (!s_last) return;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    const int cnt = atomicAdd(&p.desc_counts[(long long)p.desc * E + e], 0);
-    const int r = expert_owner(d, e), le = expert_slot(d, e);
-    uint8_t* base = (uint8_t*)p.peers.base[r];
-    ((int*)(base + p.layout.recv_count))[((long long)le * d.world + d.rank) * d.n_desc + p.desc] = cnt;
-    p.sent_base[e] += cnt;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int r = 0; r < d.world; ++r) {
-      uint8_t* base = (uint8_t*)p.peers.base[r];
-      st_release_sys_u64((uint64_t*)(base + p.layout.recv_flag) + (long long)d.rank * d.n_desc + p.desc,
-                         epoch);
-    }
-    p.done_counter[p.desc] = 0;
-  }
+  dispatch_publish(p, p.desc, p.fault_skip_signal != 0, epoch, true);
 }
 
 // ---------------------------------------------------------------------------
@@ -379,6 +150,7 @@ __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(Dispatch
 // then emit one grouped-GEMM segment per (local expert slot, source).
 // ---------------------------------------------------------------------------
 __global__ void moe_expert_plan_kernel(PlanParams p) {
+  TraceScope trace_scope(p.trace);
   const MoEDims& d = p.dims;
   const uint8_t* mine = (const uint8_t*)p.peers.base[d.rank];
   const uint64_t* flags = (const uint64_t*)(mine + p.layout.recv_flag);
@@ -415,6 +187,7 @@ __global__ void moe_expert_plan_kernel(PlanParams p) {
 // token, source, expert rank, expert, original position, chunk, chunk offset,
 // checksum).
 __global__ void moe_return_meta_kernel(ReturnMetaParams p) {
+  TraceScope trace_scope(p.trace);
   const MoEDims& d = p.dims;
   const uint8_t* mine = (const uint8_t*)p.peers.base[d.rank];
   const long long* meta = (const long long*)(mine + p.layout.recv_meta);
@@ -447,6 +220,7 @@ __global__ void moe_return_meta_kernel(ReturnMetaParams p) {
 // One thread: make this rank's return stores visible, then publish its return
 // sequence number at every source rank.
 __global__ void moe_return_signal_kernel(SignalParams p) {
+  TraceScope trace_scope(p.trace);
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   const MoEDims& d = p.dims;
   const unsigned long long epoch = *p.epoch;
@@ -459,6 +233,7 @@ __global__ void moe_return_signal_kernel(SignalParams p) {
 // out[t] = sum_j ret_out[t * k + j] (rows already carry their gate weight).
 template <typename OutT>
 __global__ void moe_combine_kernel(CombineParams p) {
+  TraceScope trace_scope(p.trace);
   const MoEDims& d = p.dims;
   const uint8_t* mine = (const uint8_t*)p.peers.base[d.rank];
   __shared__ int s_ok;
@@ -539,6 +314,7 @@ __global__ void moe_combine_kernel(CombineParams p) {
 // wait (bounded) until every peer's sequence arrived here.  Used to align the
 // ranks before a timed layer call without a host round-trip.
 __global__ void moe_device_barrier_kernel(BarrierParams p) {
+  TraceScope trace_scope(p.trace);
   const MoEDims& d = p.dims;
   __shared__ unsigned long long seq;
   if (threadIdx.x == 0) {
@@ -562,8 +338,15 @@ void launch_device_barrier(const BarrierParams& p, cudaStream_t s) {
 // Per-call reset of the dispatch cursors and counters; advances the call's
 // sequence number (the value every ready / return / permit word is compared to).
 __global__ void moe_layer_reset_kernel(int* sent_base, int experts, int* desc_counts, int n_desc,
-                                       int* done_counter, unsigned long long* epoch) {
+                                       int* done_counter, unsigned long long* epoch, TraceSlot* trace,
+                                       int n_trace, int* chunk_words, int n_chunk_words) {
   if (threadIdx.x == 0) *epoch += 1;
+  for (int i = threadIdx.x; i < n_chunk_words; i += blockDim.x) chunk_words[i] = 0;
+  for (int i = threadIdx.x; i < n_trace; i += blockDim.x) {
+    trace[i].t_start = ~0ULL;
+    trace[i].t_end = 0;
+    trace[i].ctas = 0;
+  }
   for (int i = threadIdx.x; i < experts; i += blockDim.x) sent_base[i] = 0;
   for (int i = threadIdx.x; i < experts * n_desc; i += blockDim.x) desc_counts[i] = 0;
   for (int i = threadIdx.x; i < n_desc; i += blockDim.x) done_counter[i] = 0;
@@ -643,8 +426,10 @@ void launch_combine(const CombineParams& p, bool bf16, int grid, cudaStream_t s)
 }
 
 void launch_layer_reset(int* sent_base, int experts, int* desc_counts, int n_desc, int* done_counter,
-                        unsigned long long* epoch, cudaStream_t s) {
-  moe_layer_reset_kernel<<<1, 256, 0, s>>>(sent_base, experts, desc_counts, n_desc, done_counter, epoch);
+                        unsigned long long* epoch, TraceSlot* trace, int n_trace, int* chunk_words,
+                        int n_chunk_words, cudaStream_t s) {
+  moe_layer_reset_kernel<<<1, 256, 0, s>>>(sent_base, experts, desc_counts, n_desc, done_counter, epoch, trace,
+                                           trace ? n_trace : 0, chunk_words, chunk_words ? n_chunk_words : 0);
 }
 
 }  // namespace raiccl

@@ -1,0 +1,355 @@
+// Persistent progressive front end of the MoE layer: router + device control
+// plane + revealed-only dispatch in ONE cooperative launch per layer call.
+//
+// The one-launch-per-step pipeline (moe_router_kernel per chunk on a router
+// stream, moe_control_*_kernel per trigger, moe_dispatch_kernel per
+// descriptor, joined by events) pays a launch, a cross-stream hop and a cold
+// instruction cache on every step, and the control kernel re-stages its state
+// from global memory at every trigger.  Here the grid (one CTA per SM) stays
+// resident for the whole front end:
+//
+//   CTA 0, warp 0 — the control plane (control_warp.cuh) for triggers 0..n_desc-1.
+//       Plan and scheduler state stay in shared memory across triggers.  Before
+//       trigger q it waits (bounded) until every worker CTA has finished the
+//       router chunks q depends on.  After it, the warp turns the chunks' per-expert
+//       router counts into the descriptor's receive bases and counts and
+//       releases desc_ready[q] = epoch.
+//   CTAs 1..W — workers.  For each router chunk: route a share of its tokens
+//       (one warp per token), add the per-expert counts, and release
+//       chunk_done[c].  In the early arm, a worker dispatches every descriptor
+//       already released between chunks (a non-blocking poll, so routing never
+//       waits on the control plane).  After the last chunk it dispatches the
+//       rest, waiting (bounded) for each release.  In the delayed arm nothing is
+//       dispatched before the final trigger.  Each worker packs and stores its
+//       token share of a descriptor (dispatch_rows).  The last worker to finish
+//       a descriptor publishes the counts and the per-destination ready words.
+//
+// All waits are between CTAs of this one launch, whose co-residency the
+// cooperative launch guarantees, and every wait has a %globaltimer deadline
+// after which the waiter records a status and returns.  Cross-GPU traffic is
+// the same P2P stores and release words as the step kernels (no TMA).
+// Decisions, rows, counts and flags are identical to the step pipeline's,
+// which the layer tests check against each other.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "control_warp.cuh"
+#include "launchers.h"
+#include "moe_device.cuh"
+#include "moe_kernels.h"
+#include "sm100_ptx.cuh"
+
+namespace raiccl {
+namespace {
+
+constexpr int kFrontThreads = 256;
+constexpr int kFrontKernelId = 70;
+
+__device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_gpu_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ void trace_begin(TraceSlot* s) {
+  if (s) atomicMin(&s->t_start, (unsigned long long)globaltimer_ns());
+}
+__device__ __forceinline__ void trace_end(TraceSlot* s) {
+  if (s) {
+    atomicMax(&s->t_end, (unsigned long long)globaltimer_ns());
+    atomicAdd(&s->ctas, 1);
+  }
+}
+
+// Per-CTA timeline (diagnostics): stamp k of this CTA, thread 0 only.
+__device__ __forceinline__ void cta_stamp(const FrontendParams& f, int k) {
+  if (f.cta_clock != nullptr && threadIdx.x == 0) f.cta_clock[(long long)blockIdx.x * 64 + k] = globaltimer_ns();
+}
+
+__device__ __forceinline__ int trigger_first_chunk(int q, int P) { return q < P ? q : P; }
+__device__ __forceinline__ int trigger_last_chunk(int q, int P, int C) { return q < P ? q : C - 1; }
+
+// Control-warp hooks: wait for the trigger's router chunks; publish the
+// descriptor's receive bases and counts, then release it.
+struct FrontHooks {
+  const FrontendParams* f;
+  int workers, P, C, E;
+  unsigned long long epoch;
+  int* s_sent;       // [E] rows already assigned per expert (shared, CTA 0)
+  int chunks_ready;  // chunks [0, chunks_ready) are known complete
+
+  __device__ bool before(int q) {
+    const int lane = threadIdx.x & 31;
+    const int need = trigger_last_chunk(q, P, C) + 1;
+    int ok = 1;
+    if (lane == 0) {
+      const unsigned long long deadline = globaltimer_ns() + f->timeout_ns;
+      for (int c = chunks_ready; c < need && ok; ++c) {
+        while (ld_acquire_gpu_s32(&f->chunk_done[c]) < workers) {
+          if (globaltimer_ns() > deadline) {
+            record_status(f->dp.status, kTimeoutChunkFlag, kFrontKernelId, c, workers);
+            ok = 0;
+            break;
+          }
+        }
+      }
+      __threadfence();
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    if (!ok) return false;
+    chunks_ready = need;
+    if (lane == 0 && f->phase_trace) trace_begin(&f->phase_trace[C + q]);
+    if (q < 16) cta_stamp(*f, 2 + 2 * q);
+    return true;
+  }
+
+  __device__ void after(int q, bool permitted) {
+    const int lane = threadIdx.x & 31;
+    const int c_lo = trigger_first_chunk(q, P), c_hi = trigger_last_chunk(q, P, C);
+    for (int e = lane; e < E; e += 32) {
+      int cnt = 0;
+      for (int c = c_lo; c <= c_hi; ++c) cnt += f->chunk_counts[(long long)c * E + e];
+      const int base = s_sent[e];
+      f->disp_base[(long long)q * E + e] = base;
+      f->dp.desc_counts[(long long)q * E + e] = permitted ? cnt : 0;
+      if (permitted) s_sent[e] = base + cnt;
+    }
+    __syncwarp();
+    if (q < 16) cta_stamp(*f, 3 + 2 * q);
+    if (lane == 0) {
+      if (f->phase_trace) trace_end(&f->phase_trace[C + q]);
+      __threadfence();
+      st_release_gpu_u64(&f->desc_ready[q], epoch);
+    }
+    __syncwarp();
+  }
+};
+
+// One worker's share of descriptor q (collective over the CTA).
+template <typename T>
+__device__ void worker_dispatch(const FrontendParams& f, int q, int w, int W, unsigned long long epoch,
+                                int* hist, int* run, int* item_pos, int* s_base, const int* s_coff, int nc,
+                                int* s_flag) {
+  const MoEDims& d = f.dp.dims;
+  const int P = f.cp.partial_chunks, C = d.chunks, E = d.experts, k = d.top_k;
+  const int t0 = s_coff[trigger_first_chunk(q, P)];
+  const int t1 = s_coff[trigger_last_chunk(q, P, C) + 1];
+  TraceSlot* slot = f.phase_trace ? &f.phase_trace[C + d.n_desc + q] : nullptr;
+  if (threadIdx.x == 0) trace_begin(slot);
+  cta_stamp(f, 24 + 2 * q);
+  const int ntok = t1 - t0;
+  const int per = (ntok + W - 1) / W;
+  const int a = t0 + min(ntok, w * per);
+  const int b = t0 + min(ntok, (w + 1) * per);
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    hist[e] = 0;
+    run[e] = 0;
+    s_base[e] = f.disp_base[(long long)q * E + e];
+  }
+  if (threadIdx.x == 0) *s_flag = (f.dp.permit[q] == epoch) ? 1 : 0;
+  __syncthreads();
+  const bool permitted = *s_flag != 0;
+  if (!permitted && threadIdx.x == 0 && w == 0) record_status(f.dp.status, kTimeoutPermit, 20, q, (long long)epoch);
+  if (permitted && (long long)(b - a) * k > kDispatchMaxItems) {
+    if (threadIdx.x == 0) record_status(f.dp.status, kBadConfig, 22, (long long)(b - a) * k, kDispatchMaxItems);
+  } else if (permitted && a < b) {
+    dispatch_rows<T>(f.dp, t0, a, b, s_base, hist, run, item_pos, s_coff, nc);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int prev = atom_add_acq_rel_gpu(&f.dp.done_counter[q], 1);
+    *s_flag = (prev == W - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  cta_stamp(f, 44 + q);
+  if (*s_flag) dispatch_publish(f.dp, q, q == f.fault_skip_desc, epoch, false);
+  if (threadIdx.x == 0) trace_end(slot);
+  cta_stamp(f, 25 + 2 * q);
+  __syncthreads();
+}
+
+// Whether descriptor q was released: 1 yes, 0 not yet (non-blocking poll),
+// -1 the bounded wait ran out (status recorded).  Collective over the CTA.
+__device__ int wait_released(const FrontendParams& f, int q, unsigned long long epoch, int* s_flag, bool block) {
+  if (threadIdx.x == 0) {
+    int ok = ld_acquire_gpu_u64(&f.desc_ready[q]) == epoch ? 1 : 0;
+    if (!ok && block) {
+      const unsigned long long deadline = globaltimer_ns() + f.timeout_ns;
+      while (ok == 0) {
+        ok = ld_acquire_gpu_u64(&f.desc_ready[q]) == epoch ? 1 : 0;
+        if (ok == 0 && globaltimer_ns() > deadline) {
+          record_status(f.dp.status, kTimeoutPermit, kFrontKernelId + 1, q, (long long)epoch);
+          ok = -1;
+        }
+      }
+    }
+    if (ok == 1) __threadfence();
+    *s_flag = ok;
+  }
+  __syncthreads();
+  const int v = *s_flag;
+  __syncthreads();
+  return v;
+}
+
+template <typename T, int EMAX, bool SMEM_W>
+__global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __grid_constant__ FrontendParams f) {
+  extern __shared__ __align__(16) uint8_t fsm[];
+  __shared__ int hist[kMaxExperts];
+  __shared__ int run[kMaxExperts];
+  __shared__ int s_base[kMaxExperts];
+  __shared__ int item_pos[kDispatchMaxItems];
+  __shared__ int s_coff[kDispatchMaxChunks + 1];
+  __shared__ int s_flag;
+  TraceScope trace_scope(f.trace);
+  const MoEDims& d = f.dp.dims;
+  const int C = d.chunks, E = d.experts, n_desc = d.n_desc;
+  const int W = (int)gridDim.x - 1;
+  const unsigned long long epoch = *f.dp.epoch;
+  const int nc = min(C, kDispatchMaxChunks);
+  for (int c = threadIdx.x; c <= nc; c += blockDim.x) s_coff[c] = f.dp.chunk_offsets[c];
+
+  if (blockIdx.x == 0) {
+    // ---------------- control CTA
+    __shared__ int s_dst[ctl::kCtlStageMax];
+    __shared__ int s_ccoff[ctl::kCtlMaxChunks + 1];
+    __shared__ uint32_t s_egmask[ctl::kWarpMaxE];
+    const ControlDims dims{f.cp.plan.E, f.cp.plan.G, f.cp.plan.V, f.cp.st.max_tokens, f.cp.n_group_members,
+                           f.cp.n_edge_group_members, f.cp.n_tmpl, f.cp.max_cands, f.cp.chunks};
+    const ControlLayout Lt = control_layout(dims);
+    ctl::copy16(reinterpret_cast<uint4*>(fsm), reinterpret_cast<const uint4*>(f.cp.blob), Lt.state_end / 16);
+    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;  // s_sent of the hooks
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      FrontHooks hooks{&f, W, f.cp.partial_chunks, C, E, epoch, hist, 0};
+      ctl::control_warp_run(f.cp, dims, fsm, s_dst, s_ccoff, s_egmask, 0, n_desc, true, hooks);
+      __syncwarp();
+      for (int e = threadIdx.x; e < E; e += 32) f.dp.sent_base[e] = hist[e];
+    }
+    __syncthreads();
+    ctl::copy16(reinterpret_cast<uint4*>(f.cp.blob + Lt.state_begin),
+                reinterpret_cast<const uint4*>(fsm + Lt.state_begin), (Lt.state_end - Lt.state_begin) / 16);
+    return;
+  }
+
+  // ---------------- worker CTAs
+  const int w = blockIdx.x - 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const T* wts = (const T*)f.rp.weight;
+  if constexpr (SMEM_W) {
+    uint4* ws = (uint4*)fsm;
+    const uint4* wg = (const uint4*)f.rp.weight;
+    const int nvec = E * f.rp.hidden * (int)sizeof(T) / 16;
+    for (int i = threadIdx.x; i < nvec; i += blockDim.x) ws[i] = __ldg(wg + i);
+    wts = (const T*)fsm;
+  }
+  cta_stamp(f, 0);
+  __syncthreads();
+  cta_stamp(f, 1);
+  int next = 0;
+  for (int c = 0; c < C; ++c) {
+    TraceSlot* rslot = f.phase_trace ? &f.phase_trace[c] : nullptr;
+    if (threadIdx.x == 0) trace_begin(rslot);
+    if (c < 8) cta_stamp(f, 2 + 2 * c);
+    for (int e = threadIdx.x; e < E; e += blockDim.x) run[e] = 0;  // per-chunk expert counts
+    __syncthreads();
+    const float* cbias = f.rp.chunk_bias ? f.rp.chunk_bias + (long long)c * E : nullptr;
+    const int t0 = s_coff[c], t1 = s_coff[c + 1];
+    for (int t = t0 + w * nwarps + warp; t < t1; t += W * nwarps) {
+      int sel[8];
+      router_token<T, EMAX, SMEM_W>(f.rp, cbias, t, wts, sel);
+      if (lane == 0)
+        for (int j = 0; j < f.rp.top_k; ++j) atomicAdd(&run[sel[j]], 1);
+    }
+    if (c < 8) cta_stamp(f, 52 + c);
+    __syncthreads();
+    if (c < 4) cta_stamp(f, 60 + c);
+    for (int e = threadIdx.x; e < E; e += blockDim.x)
+      if (run[e]) atomicAdd(&f.chunk_counts[(long long)c * E + e], run[e]);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      atomicAdd(&f.chunk_done[c], 1);
+      trace_end(rslot);
+    }
+    if (c < 8) cta_stamp(f, 3 + 2 * c);
+    // early arm: dispatch every descriptor already released (never waits)
+    if (!f.delayed) {
+      while (next < n_desc && wait_released(f, next, epoch, &s_flag, false) == 1) {
+        worker_dispatch<T>(f, next, w, W, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag);
+        ++next;
+      }
+    }
+  }
+  if (f.delayed && wait_released(f, n_desc - 1, epoch, &s_flag, true) != 1) return;
+  while (next < n_desc) {
+    if (wait_released(f, next, epoch, &s_flag, true) != 1) return;
+    worker_dispatch<T>(f, next, w, W, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag);
+    ++next;
+  }
+}
+
+template <typename T, int EMAX, bool SMEM_W>
+bool launch_one_frontend(const FrontendParams& f, int sms, size_t smem, cudaStream_t s) {
+  auto kern = moe_frontend_kernel<T, EMAX, SMEM_W>;
+  static size_t configured = 0;
+  if (smem > configured) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return false;
+    configured = smem;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFrontThreads, smem) != cudaSuccess ||
+      per_sm < 1)
+    return false;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sms);
+  cfg.blockDim = dim3(kFrontThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, f) == cudaSuccess;
+}
+
+}  // namespace
+
+bool launch_frontend(const FrontendParams& f, bool bf16, int sms, cudaStream_t s) {
+  if (sms < 2 || !control_warp_path_ok(f.cp) || f.dp.dims.experts > kMaxExperts || f.rp.top_k > 8 ||
+      f.dp.dims.chunks > kDispatchMaxChunks)
+    return false;
+  const long long wbytes = (long long)f.rp.experts * f.rp.hidden * (bf16 ? 2 : 4);
+  const bool smem_w = wbytes <= 96 * 1024;
+  const size_t blob = control_smem_bytes(f.cp);
+  const size_t smem = std::max<size_t>(blob, smem_w ? (size_t)wbytes : 0);
+#define RAICCL_FRONT(T, EM)                                                            \
+  return smem_w ? launch_one_frontend<T, EM, true>(f, sms, smem, s)                    \
+                : launch_one_frontend<T, EM, false>(f, sms, smem, s)
+  if (f.rp.experts <= 8) {
+    if (bf16) RAICCL_FRONT(__nv_bfloat16, 8); else RAICCL_FRONT(float, 8);
+  } else if (f.rp.experts <= 16) {
+    if (bf16) RAICCL_FRONT(__nv_bfloat16, 16); else RAICCL_FRONT(float, 16);
+  } else if (f.rp.experts <= 64) {
+    if (bf16) RAICCL_FRONT(__nv_bfloat16, 64); else RAICCL_FRONT(float, 64);
+  }
+#undef RAICCL_FRONT
+  return false;
+}
+
+}  // namespace raiccl

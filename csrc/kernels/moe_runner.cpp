@@ -64,6 +64,13 @@ class MoELayerRunner {
     comm_ = reinterpret_cast<cudaStream_t>(comm_stream);
     device_ = tensors["tokens"].cast<torch::Tensor>().device().index();
     c10::cuda::CUDAGuard guard(device_);
+    if (tensors.contains("trace")) {
+      auto tt = tensors["trace"].cast<torch::Tensor>();
+      TORCH_CHECK(tt.is_cuda() && tt.is_contiguous() && tt.nbytes() % sizeof(raiccl::TraceSlot) == 0,
+                  "trace must be a contiguous CUDA buffer of 32-byte slots");
+      trace_ = reinterpret_cast<raiccl::TraceSlot*>(tt.data_ptr());
+      trace_cap_ = (int)(tt.nbytes() / sizeof(raiccl::TraceSlot));
+    }
     // keep every tensor alive for the runner's lifetime
     for (auto item : tensors) held_.push_back(py::reinterpret_borrow<py::object>(item.second));
 
@@ -119,6 +126,17 @@ class MoELayerRunner {
     ta2_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "h"), dt, eb, rows, ffn_, ffn_, 128, bk);
     tb2_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "w2"), dt, eb, (uint64_t)d.expert_slots * d.out_dim, ffn_, ffn_, bn2_, bk);
 
+    {
+      int coop = 0;
+      cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device_);
+      const int mode = ints.contains("frontend") ? geti(ints, "frontend") : 1;
+      use_frontend_ = coop != 0 && mode != 0 && tensors.contains("chunk_words") && tensors.contains("disp_base") &&
+                      tensors.contains("desc_ready");
+      if (tensors.contains("chunk_words")) {
+        chunk_words_ = ptr<int>(tensors, "chunk_words");
+        n_chunk_words_ = d.chunks * (1 + d.experts);
+      }
+    }
     ck(cudaEventCreateWithFlags(&ev_start_, cudaEventDisableTiming), "cudaEventCreate");
     ev_chunk_.resize(d.chunks);
     for (auto& e : ev_chunk_) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
@@ -157,10 +175,12 @@ class MoELayerRunner {
     auto* gates = ptr<float>(t, "gates");
     auto* chunk_offsets_dev = ptr<int>(t, "chunk_offsets");
 
-    raiccl::launch_layer_reset(sent_base, d.experts, desc_counts, d.n_desc, done_counter, epoch, comm_);
+    trace_labels_.clear();
+    raiccl::TraceSlot* reset_slot = trace_slot("layer_reset", -1);
+    raiccl::launch_layer_reset(sent_base, d.experts, desc_counts, d.n_desc, done_counter, epoch, trace_,
+                               trace_cap_, chunk_words_, n_chunk_words_, comm_);
+    (void)reset_slot;
     ++launches;
-    ck(cudaEventRecord(ev_start_, comm_), "cudaEventRecord");
-    ck(cudaStreamWaitEvent(router_, ev_start_, 0), "cudaStreamWaitEvent");
 
     // router chunks
     raiccl::RouterParams rp{};
@@ -176,13 +196,21 @@ class MoELayerRunner {
     rp.mask_mode = d.mask_mode;
     rp.expert_ids = expert_ids;
     rp.gates = gates;
-    for (int c = 0; c < d.chunks; ++c) {
-      rp.row0 = (int)chunk_offsets_[c];
-      rp.row1 = (int)chunk_offsets_[c + 1];
-      rp.chunk_bias = chunk_bias ? chunk_bias + (long long)c * d.experts : nullptr;
-      if (rp.row1 > rp.row0) { raiccl::launch_router(rp, feat_bf16_, router_); ++launches; }
-      ck(cudaEventRecord(ev_chunk_[c], router_), "cudaEventRecord");
-    }
+    auto launch_routers = [&]() {
+      ck(cudaEventRecord(ev_start_, comm_), "cudaEventRecord");
+      ck(cudaStreamWaitEvent(router_, ev_start_, 0), "cudaStreamWaitEvent");
+      for (int c = 0; c < d.chunks; ++c) {
+        rp.row0 = (int)chunk_offsets_[c];
+        rp.row1 = (int)chunk_offsets_[c + 1];
+        rp.chunk_bias = chunk_bias ? chunk_bias + (long long)c * d.experts : nullptr;
+        if (rp.row1 > rp.row0) {
+          rp.trace = trace_slot("router", c);
+          raiccl::launch_router(rp, feat_bf16_, router_);
+          ++launches;
+        }
+        ck(cudaEventRecord(ev_chunk_[c], router_), "cudaEventRecord");
+      }
+    };
 
     // control plane + dispatch
     raiccl::ControlParams cp{};
@@ -279,15 +307,53 @@ class MoELayerRunner {
       const int ntok = dp.t1 - dp.t0;
       const int tpc = std::max(1, 16 / d.top_k);
       const int grid = std::max(1, std::min(4 * grid_sms_, (ntok + tpc - 1) / tpc));
+      dp.trace = trace_slot("dispatch", q);
+      dp.fault_skip_signal = (q == fault_skip_signal_desc_) ? 1 : 0;
       raiccl::launch_dispatch(dp, feat_bf16_, grid, disp_);
       ++launches;
     };
+    bool front = use_frontend_;
+    if (front) {
+      // router + control plane + dispatch: one persistent cooperative launch
+      raiccl::FrontendParams fp{};
+      fp.rp = rp;
+      fp.rp.chunk_bias = chunk_bias;
+      fp.cp = cp;
+      fp.dp = dp;
+      fp.chunk_done = chunk_words_;
+      fp.chunk_counts = chunk_words_ + d.chunks;
+      fp.disp_base = ptr<int>(t, "disp_base");
+      fp.desc_ready = ptr<unsigned long long>(t, "desc_ready");
+      fp.delayed = delayed ? 1 : 0;
+      fp.fault_skip_desc = fault_skip_signal_desc_;
+      fp.timeout_ns = timeout_ns_;
+      fp.cta_clock = opt_ptr<unsigned long long>(t, "fe_clock");
+      const size_t mark = trace_labels_.size();
+      fp.trace = trace_slot("frontend", -1);
+      raiccl::TraceSlot* first = nullptr;
+      for (int c = 0; c < d.chunks; ++c) {
+        raiccl::TraceSlot* sl = trace_slot("router", c);
+        if (c == 0) first = sl;
+      }
+      for (int q = 0; q < d.n_desc; ++q) trace_slot("control", q);
+      for (int q = 0; q < d.n_desc; ++q) trace_slot("dispatch", q);
+      fp.phase_trace = (first != nullptr && trace_labels_.size() == mark + 1 + d.chunks + 2 * d.n_desc) ? first
+                                                                                                       : nullptr;
+      if (raiccl::launch_frontend(fp, feat_bf16_, grid_sms_, comm_)) {
+        ++launches;
+      } else {
+        trace_labels_.resize(mark);
+        use_frontend_ = front = false;  // not co-schedulable here: step pipeline from now on
+      }
+    }
+    if (!front) launch_routers();
     // control triggers on comm_ (each after its router chunk); dispatch q on
     // disp_ after control q (early arm) or after the last control (delayed arm)
-    for (int q = 0; q < d.n_desc; ++q) {
+    for (int q = 0; q < d.n_desc && !front; ++q) {
       const int last_chunk = q < partial_ ? q : d.chunks - 1;
       ck(cudaStreamWaitEvent(comm_, ev_chunk_[last_chunk], 0), "cudaStreamWaitEvent");
       cp.desc = q;
+      cp.trace = trace_slot("control", q);
       raiccl::launch_control(cp, comm_);
       ++launches;
       ck(cudaEventRecord(ev_ctl_[q], comm_), "cudaEventRecord");
@@ -296,12 +362,14 @@ class MoELayerRunner {
         dispatch(q);
       }
     }
-    if (delayed) {
+    if (delayed && !front) {
       ck(cudaStreamWaitEvent(disp_, ev_ctl_[d.n_desc - 1], 0), "cudaStreamWaitEvent");
       for (int q = 0; q < d.n_desc; ++q) dispatch(q);
     }
-    ck(cudaEventRecord(ev_disp_done_, disp_), "cudaEventRecord");
-    ck(cudaStreamWaitEvent(comm_, ev_disp_done_, 0), "cudaStreamWaitEvent");
+    if (!front) {
+      ck(cudaEventRecord(ev_disp_done_, disp_), "cudaEventRecord");
+      ck(cudaStreamWaitEvent(comm_, ev_disp_done_, 0), "cudaStreamWaitEvent");
+    }
 
     // expert side
     auto* segs = ptr<GemmSegment>(t, "segs");
@@ -314,6 +382,7 @@ class MoELayerRunner {
     pp.epoch = epoch;
     pp.timeout_ns = timeout_ns_;
     pp.status = status;
+    pp.trace = trace_slot("expert_plan", -1);
     raiccl::launch_expert_plan(pp, comm_);
     ++launches;
 
@@ -332,7 +401,8 @@ class MoELayerRunner {
     g1.ldo = ffn_;
     g1.status = status;
     g1.timeout_ns = timeout_ns_;
-    raiccl::launch_tile_plan(segs, S, n1_ / bn1_, prefix1, comm_);
+    raiccl::launch_tile_plan(segs, S, n1_ / bn1_, prefix1, comm_, trace_slot("tile_plan", 1));
+    g1.trace = trace_slot("gemm1", -1);
     raiccl::launch_grouped_gemm(!feat_bf16_, feat_bf16_, act1_, bn1_, ta1_, tb1_, g1, grid_sms_, comm_);
     launches += 2;
 
@@ -350,7 +420,8 @@ class MoELayerRunner {
     g2.ldo = d.out_dim;
     g2.status = status;
     g2.timeout_ns = timeout_ns_;
-    raiccl::launch_tile_plan(segs, S, d.out_dim / bn2_, prefix2, comm_);
+    raiccl::launch_tile_plan(segs, S, d.out_dim / bn2_, prefix2, comm_, trace_slot("tile_plan", 2));
+    g2.trace = trace_slot("gemm2_return", -1);
     raiccl::launch_grouped_gemm(!feat_bf16_, out_bf16_, 0, bn2_, ta2_, tb2_, g2, grid_sms_, comm_);
     launches += 2;
 
@@ -360,12 +431,14 @@ class MoELayerRunner {
     rm.peers = peers_;
     rm.segs = segs;
     rm.status = status;
+    rm.trace = trace_slot("return_meta", -1);
     raiccl::launch_return_meta(rm, grid_sms_, comm_);
     raiccl::SignalParams sp{};
     sp.dims = d;
     sp.layout = layout_;
     sp.peers = peers_;
     sp.epoch = epoch;
+    sp.trace = trace_slot("return_signal", -1);
     raiccl::launch_return_signal(sp, comm_);
     raiccl::CombineParams cb{};
     cb.dims = d;
@@ -375,6 +448,7 @@ class MoELayerRunner {
     cb.epoch = epoch;
     cb.timeout_ns = timeout_ns_;
     cb.status = status;
+    cb.trace = trace_slot("combine", -1);
     raiccl::launch_combine(cb, out_bf16_, grid_sms_, comm_);
     launches += 3;
     ck(cudaGetLastError(), "MoE layer launch");
@@ -429,6 +503,19 @@ class MoELayerRunner {
 
   long long sym_bytes() const { return layout_.total; }
 
+  // Fault injection for failure-detection tests: the dispatch of descriptor
+  // `desc` moves its rows but publishes no ready flag, so every receiver's
+  // bounded wait runs out and reports through the status record (-1: off).
+  // Takes effect at the next forward() / capture().
+  void inject_skip_signal(int desc) { fault_skip_signal_desc_ = desc; }
+  bool persistent_frontend() const { return use_frontend_; }
+
+  py::list trace_labels() const {
+    py::list out;
+    for (const auto& kv : trace_labels_) out.append(py::make_tuple(kv.first, kv.second));
+    return out;
+  }
+
   py::dict layout() const {
     py::dict o;
     o["recv_feat"] = layout_.recv_feat;
@@ -466,6 +553,19 @@ class MoELayerRunner {
   cudaStream_t router_ = nullptr, comm_ = nullptr;
   cudaStream_t disp_ = nullptr;
   int device_ = 0;
+  int fault_skip_signal_desc_ = -1;
+  bool use_frontend_ = false;      // persistent cooperative front end (else one launch per step)
+  int* chunk_words_ = nullptr;     // [C] chunk_done + [C * E] chunk_counts, zeroed per call
+  int n_chunk_words_ = 0;  // host-side fault injection: descriptor whose ready flags are withheld
+  // device trace ring (optional tensor "trace"): one slot per launch of a call
+  raiccl::TraceSlot* trace_ = nullptr;
+  int trace_cap_ = 0;
+  std::vector<std::pair<std::string, int>> trace_labels_;
+  raiccl::TraceSlot* trace_slot(const char* kind, int arg) {
+    if (trace_ == nullptr || (int)trace_labels_.size() >= trace_cap_) return nullptr;
+    trace_labels_.emplace_back(kind, arg);
+    return trace_ + (trace_labels_.size() - 1);
+  }
   cudaEvent_t ev_start_ = nullptr, ev_disp_done_ = nullptr;
   std::vector<cudaEvent_t> ev_chunk_, ev_ctl_;
   cudaGraph_t graph_[2] = {nullptr, nullptr};
@@ -594,6 +694,9 @@ void register_moe(py::module_& m) {
       .def("has_graph", &MoELayerRunner::has_graph, py::arg("delayed"))
       .def("device_barrier", &MoELayerRunner::device_barrier)
       .def("sym_bytes", &MoELayerRunner::sym_bytes)
+      .def("trace_labels", &MoELayerRunner::trace_labels)
+      .def("inject_skip_signal", &MoELayerRunner::inject_skip_signal, py::arg("desc"))
+      .def("persistent_frontend", &MoELayerRunner::persistent_frontend)
       .def("layout", &MoELayerRunner::layout);
   m.def("router_topk", &router_topk, py::arg("tokens"), py::arg("weight"), py::arg("bias"),
         py::arg("chunk_bias"), py::arg("block_mask"), py::arg("row0"), py::arg("row1"), py::arg("top_k"),

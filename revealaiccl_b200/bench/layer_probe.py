@@ -1,6 +1,6 @@
 """Small-case driver of one MoE layer for kernel profiling.
 
-    python -m revealaiccl_b200.bench.layer_probe --config r4_reference --calls 4 [--graph]
+    python -m revealaiccl_b200.bench.layer_probe --config r4_reference --calls 4 [--graph] [--trace t.json]
 
 Builds one layer on cuda:0, runs ``--calls`` layer calls (eager launches, or
 replays of a captured graph with ``--graph``), verifies the last one and
@@ -26,12 +26,13 @@ def main() -> None:
     ap.add_argument("--arm", default="early", choices=("early", "delayed"))
     ap.add_argument("--graph", action="store_true")
     ap.add_argument("--tokens", type=int, default=0, help="override tokens per rank (uniform chunks)")
+    ap.add_argument("--trace", default=None, help="write a Chrome trace of the last call to this path")
     args = ap.parse_args()
     cfg = preset(args.config)
     if args.tokens:
         n = cfg.chunks
         cfg = cfg.with_overrides(tokens_per_rank=args.tokens, chunk_sizes=(args.tokens // n,) * n)
-    layer = ProgressiveMoELayer(cfg, device=torch.device("cuda", 0), timeout_s=10.0)
+    layer = ProgressiveMoELayer(cfg, device=torch.device("cuda", 0), timeout_s=10.0, trace=bool(args.trace))
     try:
         layer.forward(args.arm)
         if args.graph:
@@ -45,8 +46,15 @@ def main() -> None:
             torch.cuda.synchronize()
             times.append(s.elapsed_time(e))
         rep = layer.verify()
-        print(json.dumps({"config": cfg.name, "arm": args.arm, "graph": args.graph, "ms": times,
-                          "pass": rep["pass"], "launches_per_call": layer.launches_per_call}))
+        rec = {"config": cfg.name, "arm": args.arm, "graph": args.graph, "ms": times,
+               "pass": rep["pass"], "launches_per_call": layer.launches_per_call}
+        if args.trace:
+            from .trace import summarize, write_chrome
+
+            evs = layer.trace_events()
+            write_chrome(evs, args.trace, arm=args.arm)
+            rec["trace"] = summarize(evs)
+        print(json.dumps(rec))
     finally:
         layer.close()
 

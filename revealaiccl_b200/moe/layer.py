@@ -41,6 +41,7 @@ from .oracle import layer_reference
 FWD_META = 9
 RET_META = 8
 LOG_HEADER = 16  # 8-word decision record + 8 phase-clock words
+TRACE_SLOTS = 256
 
 
 @dataclass
@@ -53,7 +54,7 @@ class ProgressiveMoELayer:
     def __init__(self, cfg: MoELayerConfig, *, device: torch.device | str | None = None,
                  world: int | None = None, rank: int | None = None, group=None,
                  timeout_s: float = 10.0, seed: int = 0, control_topology=None,
-                 control_path: str = "auto") -> None:
+                 control_path: str = "auto", trace: bool = False, frontend: str = "persistent") -> None:
         self.cfg = cfg
         if world is None:
             world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -135,6 +136,7 @@ class ProgressiveMoELayer:
             "log_stride": self.log_stride, "max_ctl_tokens": Tc,
             "sms": torch.cuda.get_device_properties(dev).multi_processor_count,
             "control_serial": {"auto": 0, "serial": 1}[control_path],
+            "frontend": {"steps": 0, "persistent": 1}[frontend],
         }
         self.layout = self._k.sym_layout(ints)
         self.channel = PeerChannel(self.layout["total"], dev, group=group)
@@ -171,6 +173,10 @@ class ProgressiveMoELayer:
             "desc_counts": torch.zeros(cfg.n_desc * E, dtype=torch.int32, device=dev),
             "done_counter": torch.zeros(cfg.n_desc, dtype=torch.int32, device=dev),
             "permit": torch.zeros(cfg.n_desc, dtype=torch.int64, device=dev),
+            # persistent front end: chunk_done [C] + chunk_counts [C, E]; receive bases; release words
+            "chunk_words": torch.zeros(cfg.chunks * (1 + E), dtype=torch.int32, device=dev),
+            "disp_base": torch.zeros(cfg.n_desc * E, dtype=torch.int32, device=dev),
+            "desc_ready": torch.zeros(cfg.n_desc, dtype=torch.int64, device=dev),
             "epoch": self.epoch, "status": self.status,
             "bar_counter": torch.zeros(1, dtype=torch.int64, device=dev),
             "segs": self.segs, "rows_out": self.rows_out,
@@ -192,6 +198,8 @@ class ProgressiveMoELayer:
         }
         self.tensors = {kk: v for kk, v in self.tensors.items() if v is not None}
         self.tensors.update(self._ctl_views)
+        if trace:  # device trace ring: 32-byte slots, one per launch of a call
+            self.tensors["trace"] = torch.zeros(TRACE_SLOTS * 4, dtype=torch.int64, device=dev)
         self.router_stream = torch.cuda.Stream(device=dev)
         self.comm_stream = torch.cuda.Stream(device=dev)
         torch.cuda.synchronize(dev)
@@ -298,6 +306,40 @@ class ProgressiveMoELayer:
 
     def wait(self) -> None:
         torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
+
+    def trace_events(self) -> list[dict[str, Any]]:
+        """Device spans of the launches of the last layer call (layer built with
+        ``trace=True``): kernel kind, its argument (chunk / descriptor / -1),
+        %globaltimer start and end in ns, and the number of CTAs that ran."""
+        if "trace" not in self.tensors:
+            raise RuntimeError("layer was built without trace=True")
+        torch.cuda.synchronize(self.device)
+        raw = self.tensors["trace"].view(-1, 4).cpu()
+        out = []
+        for i, (kind, arg) in enumerate(self.runner.trace_labels()):
+            start, end, meta = (int(raw[i, 0]) & (2**64 - 1)), int(raw[i, 1]), int(raw[i, 2])
+            ctas = meta & 0xFFFFFFFF
+            if ctas == 0:
+                continue  # the launch did not run (or ran no CTA)
+            out.append({"kind": kind, "arg": int(arg), "start_ns": start, "end_ns": end, "ctas": ctas,
+                        "rank": self.rank})
+        return out
+
+    def inject_skip_signal(self, desc: int = -1) -> None:
+        """Host-side fault injection for failure-detection tests: descriptor
+        ``desc``'s dispatch withholds its ready flags (receivers time out after
+        ``timeout_s`` and record a status); -1 turns it off.  Applies to the
+        next ``forward`` (re-``capture`` a graph to include it)."""
+        self.runner.inject_skip_signal(int(desc))
+
+    def clear_status(self) -> None:
+        """Zero the device status record (after a reported failure)."""
+        self.status.zero_()
+        torch.cuda.synchronize(self.device)
+
+    def status_record(self) -> dict:
+        torch.cuda.synchronize(self.device)
+        return _status.decode(self.status)
 
     def check_status(self) -> None:
         torch.cuda.synchronize(self.device)

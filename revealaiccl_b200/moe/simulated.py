@@ -53,6 +53,10 @@ class SimResult:
     transport: dict[str, int] = field(default_factory=dict)
 
 
+class PeerSignalMissing(RuntimeError):
+    """A receiver found no ready signal for a (source, descriptor) slot."""
+
+
 class SimulatedMoE:
     def __init__(self, cfg: MoELayerConfig, world: int, *, seed: int = 0, backend: str = "numpy",
                  control_topology=None) -> None:
@@ -120,7 +124,15 @@ class SimulatedMoE:
         return decisions, actions
 
     # --------------------------------------------------------------------- run
-    def run(self, arm: str = "early", routes: list | None = None) -> SimResult:
+    def run(self, arm: str = "early", routes: list | None = None, *,
+            drop_signal: tuple[int, int, int] | None = None,
+            corrupt_count: tuple[int, int, int] | None = None) -> SimResult:
+        """One layer call over the simulated ranks.
+
+        Host-side fault injection (each must end in a fail-closed error, never a
+        silent result): ``drop_signal=(src, dst, desc)`` moves the rows of that
+        action but withholds its ready signal; ``corrupt_count=(src, dst, desc)``
+        rewrites the count header the receiver reads."""
         cfg, W = self.cfg, self.world
         routes = routes or self.route
         off = cfg.chunk_offsets
@@ -169,7 +181,7 @@ class SimulatedMoE:
                         if a.token_count else np.zeros((0, rec_bytes), dtype=np.uint8)
                     mem.stage_bytes(r, a, rows)
                     if arm == "early":
-                        mem.put_and_signal(a)
+                        self._put(mem, a, drop_signal, corrupt_count)
                     else:
                         pending.append(a)
                     start += a.token_count
@@ -179,13 +191,18 @@ class SimulatedMoE:
             for name in counters:
                 counters[name] += getattr(packing, {"future_access": "future_access_attempts"}.get(name, name))
         for a in pending:
-            mem.put_and_signal(a)
+            self._put(mem, a, drop_signal, corrupt_count)
         # expert ranks: receive, verify, compute, return
         fwd_checks, returns = [], {}
         for r in range(W):
             for src in range(W):
                 for d in range(cfg.n_desc):
-                    raw = mem.receive_bytes(r, src, d) if (mem.signals[r, src, d] >= 1 or src == r) else np.zeros((0, rec_bytes), np.uint8)
+                    if src != r and not mem.wait(r, src, d):
+                        # every remote (src, dst, descriptor) slot is signalled, even with zero rows
+                        raise PeerSignalMissing(f"rank {r}: no ready signal from rank {src} for descriptor {d}")
+                    raw = mem.receive_bytes(r, src, d)
+                    if raw.shape[0] * rec_bytes > layout.peer_stride - 8:
+                        raise RuntimeError(f"rank {r}: count header from rank {src} descriptor {d} exceeds its slot")
                     if raw.shape[0] == 0:
                         continue
                     meta = raw[:, :FORWARD_META_FIELDS * 8].copy().view(np.int64).reshape(-1, FORWARD_META_FIELDS)
@@ -235,6 +252,19 @@ class SimulatedMoE:
             if not torch.allclose(out, combined_ref, atol=2e-3, rtol=2e-3):
                 raise RuntimeError("simulated combine does not match the oracle")
         return SimResult(outputs, all_actions, counters, eq, fwd_checks, ret_checks, dict(mem.counters))
+
+    @staticmethod
+    def _put(mem: HostPeerMemory, a, drop_signal, corrupt_count) -> None:
+        key = (a.src_rank, a.dst_rank, a.descriptor_id)
+        if drop_signal is not None and key == tuple(drop_signal):
+            src = mem.buffers[a.src_rank][a.src_offset:a.src_offset + a.physical_bytes]
+            mem.buffers[a.dst_rank][a.dst_offset:a.dst_offset + a.physical_bytes] = src  # rows, no signal
+            return
+        mem.put_and_signal(a)
+        if corrupt_count is not None and key == tuple(corrupt_count):
+            off = a.dst_offset
+            bad = np.int64(a.token_count + 1)
+            mem.buffers[a.dst_rank][off:off + 8] = np.frombuffer(bad.tobytes(), np.uint8)
 
     @staticmethod
     def _sender(returns: list, row: np.ndarray) -> int:

@@ -136,7 +136,7 @@ def test_graph_capture_replay_repeated_calls():
         layer.forward("early")
         ref = layer.out.clone()
         n = layer.capture("early")
-        assert n > 10
+        assert n >= 9  # reset, front end (or its step kernels), plan, 2 x (tile plan, GEMM), return, combine
         for _ in range(3):
             layer.replay()
         torch.cuda.synchronize()
@@ -173,3 +173,35 @@ def test_warp_control_plane_matches_cta_kernel(case):
     assert torch.equal(res["auto"][0], res["serial"][0])
     assert torch.equal(res["auto"][1], res["serial"][1])
     assert torch.equal(res["auto"][3], res["serial"][3])
+
+
+@pytest.mark.parametrize("name", ["r4_reference", "full_tf32"])
+def test_persistent_frontend_matches_step_pipeline(name):
+    """The persistent cooperative front end and the one-launch-per-step pipeline
+    produce identical outputs, control state and log rows, in both arms."""
+    from revealaiccl_b200.moe.config import preset
+    from revealaiccl_b200.moe.layer import LOG_HEADER, ProgressiveMoELayer
+
+    res = {}
+    for fe in ("persistent", "steps"):
+        layer = ProgressiveMoELayer(preset(name), timeout_s=5.0, frontend=fe)
+        try:
+            outs = []
+            for arm in ("early", "delayed"):
+                layer.forward(arm)
+                rep = layer.verify()
+                assert rep["pass"], (fe, arm, rep["violations"])
+                outs.append(layer.out.clone())
+            assert layer.runner.persistent_frontend() == (fe == "persistent")
+            lay = layer.control_layout
+            blob = layer.tensors["ctl_blob"].cpu()
+            log = layer.tensors["ctl_log"].cpu().view(layer.cfg.n_desc, layer.log_stride)
+            res[fe] = (outs, blob[int(lay["state_begin"]):int(lay["state_end"])].clone(),
+                       torch.cat([log[:, :8], log[:, LOG_HEADER:]], dim=1).clone())
+        finally:
+            layer.close()
+    for i in range(2):
+        assert torch.equal(res["persistent"][0][i], res["steps"][0][i])
+    assert torch.equal(res["persistent"][0][0], res["persistent"][0][1])
+    assert torch.equal(res["persistent"][1], res["steps"][1])
+    assert torch.equal(res["persistent"][2], res["steps"][2])
