@@ -64,7 +64,7 @@ void grouped_gemm(torch::Tensor A, torch::Tensor B, torch::Tensor segs, torch::T
   const int nblocks = (int)(N / bn);
   raiccl::launch_tile_plan((const raiccl::GemmSegment*)segs.data_ptr<int>(), S, nblocks,
                            prefix.data_ptr<int>(), cur_stream());
-  raiccl::GroupedGemmParams p;
+  raiccl::GroupedGemmParams p{};  // value-initialised: fields this call does not set (trace, ...) are null
   p.segs = (const raiccl::GemmSegment*)segs.data_ptr<int>();
   p.tile_prefix = prefix.data_ptr<int>();
   p.num_segs = S;

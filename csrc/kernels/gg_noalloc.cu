@@ -195,7 +195,7 @@ __attribute__((visibility("default"))) int raiccl_grouped_gemm_noalloc(
     gg_noalloc_plan_kernel<<<1, 1024, 0, stream>>>(sg, num_segs, N / bn, out, scratch);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
-    GroupedGemmParams p;
+    GroupedGemmParams p{};  // value-initialised: fields this call does not set (trace, ...) are null
     p.segs = sg;
     p.tile_prefix = reinterpret_cast<const int*>(scratch + kOffPrefix);
     p.num_segs = num_segs;

@@ -27,12 +27,15 @@ def main() -> None:
     ap.add_argument("--graph", action="store_true")
     ap.add_argument("--tokens", type=int, default=0, help="override tokens per rank (uniform chunks)")
     ap.add_argument("--trace", default=None, help="write a Chrome trace of the last call to this path")
+    ap.add_argument("--frontend", default="persistent", choices=("persistent", "steps"),
+                    help="one cooperative front-end launch, or one launch per router chunk / trigger / descriptor")
     args = ap.parse_args()
     cfg = preset(args.config)
     if args.tokens:
         n = cfg.chunks
         cfg = cfg.with_overrides(tokens_per_rank=args.tokens, chunk_sizes=(args.tokens // n,) * n)
-    layer = ProgressiveMoELayer(cfg, device=torch.device("cuda", 0), timeout_s=10.0, trace=bool(args.trace))
+    layer = ProgressiveMoELayer(cfg, device=torch.device("cuda", 0), timeout_s=10.0, trace=bool(args.trace),
+                                frontend=args.frontend)
     try:
         layer.forward(args.arm)
         if args.graph:

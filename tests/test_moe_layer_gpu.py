@@ -156,7 +156,7 @@ def test_warp_control_plane_matches_cta_kernel(case):
 
     res = {}
     for path in ("auto", "serial"):
-        layer = ProgressiveMoELayer(r4_case(case), timeout_s=5.0, control_path=path)
+        layer = ProgressiveMoELayer(r4_case(case), timeout_s=5.0, control_path=path, frontend="steps")
         try:
             layer.forward("early")
             rep = layer.verify()
