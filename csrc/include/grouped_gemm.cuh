@@ -68,6 +68,94 @@ __device__ __forceinline__ int find_segment(const int* prefix, int nseg, int til
   return lo;
 }
 
+// Epilogue of one accumulator row (one thread per row): bias, activation,
+// optional per-row scale, vector stores to the segment's output pointer at
+// the mapped row.  t_row: TMEM address of the row's first column.
+template <int BN, Act ACT, typename OutT>
+__device__ __forceinline__ void gemm_epilogue_row(const GroupedGemmParams& p, const GemmSegment& seg, int nb,
+                                                  int r_local, uint32_t t_row) {
+  const bool valid = r_local < seg.rows;
+  const int arow = seg.a_row0 + r_local;
+  long long orow = 0;
+  float scale = 1.f;
+  if (valid) {
+    orow = p.row_map ? (long long)__ldg(p.row_map + arow) : (long long)(seg.out_row0 + r_local);
+    if (p.row_scale) scale = __ldg(p.row_scale + arow);
+  }
+  OutT* out = (OutT*)p.out_ptrs[seg.out_slot];
+  const float* bias = p.bias ? p.bias + (long long)seg.expert * p.N + nb * BN : nullptr;
+  if constexpr (ACT == Act::kSwiGLU) {
+    // Tile columns [0, BN/2) hold gate features, [BN/2, BN) the matching up features.
+    constexpr int HALF = BN / 2;
+    static_assert(HALF % 16 == 0, "SwiGLU tile needs BN multiple of 32");
+#pragma unroll 1
+    for (int c = 0; c < HALF; c += 16) {
+      uint32_t g[16], u[16];
+      tmem_ld16(t_row + c, g);
+      tmem_ld16(t_row + HALF + c, u);
+      tmem_ld_wait();
+      if (valid) {
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float gv = __uint_as_float(g[j]) + (bias ? __ldg(bias + c + j) : 0.f);
+          float uv = __uint_as_float(u[j]) + (bias ? __ldg(bias + HALF + c + j) : 0.f);
+          v[j] = (gv / (1.f + __expf(-gv))) * uv * scale;
+        }
+        OutT* dst = out + orow * p.ldo + nb * HALF + c;
+        if constexpr (sizeof(OutT) == 4) {
+#pragma unroll
+          for (int j = 0; j < 16; j += 4)
+            *(float4*)(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; j += 8) {
+            uint4 w;
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
+            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
+            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+            w.x = *(uint32_t*)&h0; w.y = *(uint32_t*)&h1; w.z = *(uint32_t*)&h2; w.w = *(uint32_t*)&h3;
+            *(uint4*)(dst + j) = w;
+          }
+        }
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      uint32_t r[16];
+      tmem_ld16(t_row + c, r);
+      tmem_ld_wait();
+      if (valid) {
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float x = __uint_as_float(r[j]) + (bias ? __ldg(bias + c + j) : 0.f);
+          v[j] = apply_act(x, ACT) * scale;
+        }
+        OutT* dst = out + orow * p.ldo + nb * BN + c;
+        if constexpr (sizeof(OutT) == 4) {
+#pragma unroll
+          for (int j = 0; j < 16; j += 4)
+            *(float4*)(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; j += 8) {
+            uint4 w;
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
+            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
+            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+            w.x = *(uint32_t*)&h0; w.y = *(uint32_t*)&h1; w.z = *(uint32_t*)&h2; w.w = *(uint32_t*)&h3;
+            *(uint4*)(dst + j) = w;
+          }
+        }
+      }
+    }
+  }
+}
+
 template <int BN, bool TF32, Act ACT, typename OutT>
 __global__ void __launch_bounds__(192, 1)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -181,87 +269,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.status, kKernelId, lim)) break;
       tc_fence_after_sync();
       const int r_local = mb * C::BM + row_in_tile;
-      const bool valid = r_local < seg.rows;
-      const int arow = seg.a_row0 + r_local;
-      long long orow = 0;
-      float scale = 1.f;
-      if (valid) {
-        orow = p.row_map ? (long long)__ldg(p.row_map + arow) : (long long)(seg.out_row0 + r_local);
-        if (p.row_scale) scale = __ldg(p.row_scale + arow);
-      }
-      OutT* out = (OutT*)p.out_ptrs[seg.out_slot];
-      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      const float* bias = p.bias ? p.bias + (long long)seg.expert * p.N + nb * BN : nullptr;
-      if constexpr (ACT == Act::kSwiGLU) {
-        // Tile columns [0, BN/2) hold gate features, [BN/2, BN) the matching up features.
-        constexpr int HALF = BN / 2;
-        static_assert(HALF % 16 == 0, "SwiGLU tile needs BN multiple of 32");
-#pragma unroll 1
-        for (int c = 0; c < HALF; c += 16) {
-          uint32_t g[16], u[16];
-          tmem_ld16(t_row + c, g);
-          tmem_ld16(t_row + HALF + c, u);
-          tmem_ld_wait();
-          if (valid) {
-            float v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              float gv = __uint_as_float(g[j]) + (bias ? __ldg(bias + c + j) : 0.f);
-              float uv = __uint_as_float(u[j]) + (bias ? __ldg(bias + HALF + c + j) : 0.f);
-              v[j] = (gv / (1.f + __expf(-gv))) * uv * scale;
-            }
-            OutT* dst = out + orow * p.ldo + nb * HALF + c;
-            if constexpr (sizeof(OutT) == 4) {
-#pragma unroll
-              for (int j = 0; j < 16; j += 4)
-                *(float4*)(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 16; j += 8) {
-                uint4 w;
-                __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
-                __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
-                __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
-                __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
-                w.x = *(uint32_t*)&h0; w.y = *(uint32_t*)&h1; w.z = *(uint32_t*)&h2; w.w = *(uint32_t*)&h3;
-                *(uint4*)(dst + j) = w;
-              }
-            }
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(t_row + c, r);
-          tmem_ld_wait();
-          if (valid) {
-            float v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              float x = __uint_as_float(r[j]) + (bias ? __ldg(bias + c + j) : 0.f);
-              v[j] = apply_act(x, ACT) * scale;
-            }
-            OutT* dst = out + orow * p.ldo + nb * BN + c;
-            if constexpr (sizeof(OutT) == 4) {
-#pragma unroll
-              for (int j = 0; j < 16; j += 4)
-                *(float4*)(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 16; j += 8) {
-                uint4 w;
-                __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
-                __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
-                __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
-                __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
-                w.x = *(uint32_t*)&h0; w.y = *(uint32_t*)&h1; w.z = *(uint32_t*)&h2; w.w = *(uint32_t*)&h3;
-                *(uint4*)(dst + j) = w;
-              }
-            }
-          }
-        }
-      }
+      gemm_epilogue_row<BN, ACT, OutT>(p, seg, nb, r_local, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);

@@ -1,0 +1,223 @@
+// CTA-pair variant of the grouped GEMM (tcgen05 cta_group::2, clusters of 2).
+//
+// Same math, segments, epilogues and outputs as grouped_gemm_kernel, with a
+// 256 x BN output tile per CTA pair instead of 128 x BN per CTA:
+//   * each CTA stages ITS 128 rows of A and HALF (BN/2 rows) of the B tile;
+//   * the pair leader (cluster rank 0) issues tcgen05.mma.cta_group::2 with
+//     M = 256, which reads A and B from both CTAs' shared memory and writes
+//     each CTA's 128 x BN accumulator into that CTA's TMEM;
+//   * both CTAs' TMA loads complete on the leader's stage barrier; the
+//     leader's MMA completion is committed to the stage-free barriers of both
+//     CTAs and to both CTAs' accumulator-ready barriers; both CTAs' epilogue
+//     warps report a drained accumulator to the leader's barrier.
+// Per CTA and K step this moves 128 + BN/2 operand rows instead of 128 + BN,
+// i.e. a third fewer bytes from L2 per FLOP at BN = 256.
+//
+// tile_prefix must count 256-row tiles (launch_tile_plan(..., bm = 256)).
+// Every wait is bounded; on a timeout each role stops and all threads still
+// meet at the final cluster barrier before the pair frees its TMEM, so no CTA
+// leaves while its partner may still address its shared memory.
+// All loads read this GPU's own memory (activations and weights); none uses
+// multicast.
+#pragma once
+
+#include "grouped_gemm.cuh"
+
+namespace raiccl {
+
+template <int BN, bool TF32>
+struct PairCfg {
+  static constexpr int BM = 128;                  // rows per CTA; the pair's tile has 256
+  static constexpr int BNH = BN / 2;              // B rows staged per CTA
+  static constexpr int ELEM = TF32 ? 4 : 2;
+  static constexpr int BK = 128 / ELEM;
+  static constexpr int UK = 32 / ELEM;
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BNH * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM_BUDGET = 200 * 1024;
+  static constexpr int STAGES_RAW = SMEM_BUDGET / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int TMEM_COLS = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128 : (2 * BN) <= 256 ? 256 : 512;
+  static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, 256, BN);
+  static constexpr int SMEM_TOTAL = 1024 + STAGES * STAGE_BYTES + 256;
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair tile: BN/2 rows of B per CTA, N <= 256");
+  static_assert(STAGES >= 2, "pipeline needs two stages");
+};
+
+template <int BN, bool TF32, Act ACT, typename OutT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                         GroupedGemmParams p) {
+  using C = PairCfg<BN, TF32>;
+  constexpr int kKernelId = 300 + BN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* stage_base = smem;
+  uint64_t* bars = (uint64_t*)(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* full_bar = bars;                   // used in the leader only
+  uint64_t* empty_bar = bars + C::STAGES;      // per CTA: stage free again
+  uint64_t* tfull_bar = bars + 2 * C::STAGES;  // per CTA: accumulator ready
+  uint64_t* tempty_bar = tfull_bar + 2;        // leader: accumulator drained by both CTAs
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = (uint32_t*)(drain_bar + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  if (p.trace != nullptr && threadIdx.x == 0) atomicMin(&p.trace->t_start, (unsigned long long)globaltimer_ns());
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tfull_bar[a], 1); mbar_init(&tempty_bar[a], 8); }
+    mbar_init(drain_bar, 1);
+    fence_mbarrier_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) { tmem_alloc_pair(tmem_slot, C::TMEM_COLS); tmem_relinquish_pair(); }
+  tc_fence_before_sync();
+  cluster_sync_all();  // barrier inits and the TMEM allocation are visible to the partner
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int total_tiles = __ldg(p.tile_prefix + p.num_segs);
+  const int nblocks = p.N / BN;
+  const int kblocks = (p.K + C::BK - 1) / C::BK;
+  const uint64_t lim = p.timeout_ns;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (elect_one_sync()) {
+      int stage = 0; uint32_t phase = 0;
+      for (int t = pair; t < total_tiles; t += npairs) {
+        const int s = find_segment(p.tile_prefix, p.num_segs, t);
+        const GemmSegment seg = p.segs[s];
+        const int local = t - __ldg(p.tile_prefix + s);
+        const int mb = local / nblocks, nb = local % nblocks;
+        const int arow = seg.a_row0 + mb * 2 * C::BM + (int)rank * C::BM;
+        const int brow = seg.expert * p.N + nb * BN + (int)rank * C::BNH;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, p.status, kKernelId, lim)) { ok = false; break; }
+          uint8_t* sa = stage_base + stage * C::STAGE_BYTES;
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * C::STAGE_BYTES);
+          const uint32_t leader_full = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          tma_load_2d_pair(sa, &tmap_a, leader_full, kb * C::BK, arow);
+          tma_load_2d_pair(sa + C::A_BYTES, &tmap_b, leader_full, kb * C::BK, brow);
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (rank == 0 && elect_one_sync()) {
+      int stage = 0; uint32_t phase = 0; int iter = 0;
+      for (int t = pair; t < total_tiles; t += npairs, ++iter) {
+        const int acc = iter & 1;
+        const uint32_t acc_phase = (iter >> 1) & 1;
+        if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1u, p.status, kKernelId, lim)) break;
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(&full_bar[stage], phase, p.status, kKernelId, lim)) { ok = false; break; }
+          tc_fence_after_sync();
+          const uint32_t a_addr = smem_u32(stage_base + stage * C::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < C::BK / C::UK; ++k) {
+            const uint64_t ad = umma_desc_k_sw128(a_addr + k * 32);
+            const uint64_t bd = umma_desc_k_sw128(b_addr + k * 32);
+            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            if (TF32) umma_tf32_pair(d_tmem, ad, bd, C::IDESC, accum);
+            else umma_f16_pair(d_tmem, ad, bd, C::IDESC, accum);
+          }
+          const uint32_t eb = smem_u32(&empty_bar[stage]);
+          umma_commit_pair(mapa_shared(eb, 0));
+          umma_commit_pair(mapa_shared(eb, 1));
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        const uint32_t tb = smem_u32(&tfull_bar[acc]);
+        umma_commit_pair(mapa_shared(tb, 0));
+        umma_commit_pair(mapa_shared(tb, 1));
+      }
+      // Drain: every MMA issued above has completed before TMEM is freed.
+      umma_commit_pair(mapa_shared(smem_u32(drain_bar), 0));
+      mbar_wait_bounded(drain_bar, 0, p.status, kKernelId, lim);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int iter = 0;
+    for (int t = pair; t < total_tiles; t += npairs, ++iter) {
+      const int acc = iter & 1;
+      const uint32_t acc_phase = (iter >> 1) & 1;
+      const int s = find_segment(p.tile_prefix, p.num_segs, t);
+      const GemmSegment seg = p.segs[s];
+      const int local = t - __ldg(p.tile_prefix + s);
+      const int mb = local / nblocks, nb = local % nblocks;
+      if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.status, kKernelId, lim)) break;
+      tc_fence_after_sync();
+      const int r_local = mb * 2 * C::BM + (int)rank * C::BM + row_in_tile;
+      gemm_epilogue_row<BN, ACT, OutT>(p, seg, nb, r_local, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN);
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
+    }
+  }
+
+  tc_fence_before_sync();
+  cluster_sync_all();  // both CTAs finished every role before the pair frees TMEM or exits
+  tc_fence_after_sync();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  if (p.trace != nullptr && threadIdx.x == 0) {
+    atomicMax(&p.trace->t_end, (unsigned long long)globaltimer_ns());
+    atomicAdd(&p.trace->ctas, 1);
+  }
+}
+
+template <int BN, bool TF32, Act ACT, typename OutT>
+inline void launch_one_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GroupedGemmParams& p, int grid,
+                            cudaStream_t stream) {
+  using C = PairCfg<BN, TF32>;
+  auto kern = grouped_gemm_pair_kernel<BN, TF32, ACT, OutT>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_TOTAL);
+    configured = true;
+  }
+  const int g = grid & ~1;  // whole pairs
+  kern<<<g < 2 ? 2 : g, 192, C::SMEM_TOTAL, stream>>>(ta, tb, p);
+}
+
+template <bool TF32, Act ACT, typename OutT>
+inline void dispatch_bn_pair(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GroupedGemmParams& p,
+                             int grid, cudaStream_t stream) {
+  switch (bn) {
+    case 64: launch_one_pair<64, TF32, ACT, OutT>(ta, tb, p, grid, stream); return;
+    case 128: launch_one_pair<128, TF32, ACT, OutT>(ta, tb, p, grid, stream); return;
+    case 256: launch_one_pair<256, TF32, ACT, OutT>(ta, tb, p, grid, stream); return;
+    default: break;
+  }
+  throw std::runtime_error("grouped_gemm (pair): unsupported BN " + std::to_string(bn));
+}
+
+template <bool TF32, typename OutT>
+inline void dispatch_act_pair(int act, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
+                              const GroupedGemmParams& p, int grid, cudaStream_t stream) {
+  switch ((Act)act) {
+    case Act::kNone: dispatch_bn_pair<TF32, Act::kNone, OutT>(bn, ta, tb, p, grid, stream); return;
+    case Act::kRelu: dispatch_bn_pair<TF32, Act::kRelu, OutT>(bn, ta, tb, p, grid, stream); return;
+    case Act::kGelu: dispatch_bn_pair<TF32, Act::kGelu, OutT>(bn, ta, tb, p, grid, stream); return;
+    case Act::kSilu: dispatch_bn_pair<TF32, Act::kSilu, OutT>(bn, ta, tb, p, grid, stream); return;
+    case Act::kSwiGLU: dispatch_bn_pair<TF32, Act::kSwiGLU, OutT>(bn, ta, tb, p, grid, stream); return;
+  }
+  throw std::runtime_error("grouped_gemm (pair): unknown activation");
+}
+
+}  // namespace raiccl

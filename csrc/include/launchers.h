@@ -11,8 +11,10 @@
 
 namespace raiccl {
 
+// prefix[s] = sum over segments j < s of ceil(rows_j / bm) * nblocks (bm = 128 for
+// the one-CTA kernel, 256 for the CTA-pair kernel).
 void launch_tile_plan(const GemmSegment* segs, int num_segs, int nblocks, int* prefix,
-                      cudaStream_t stream, TraceSlot* trace = nullptr);
+                      cudaStream_t stream, TraceSlot* trace = nullptr, int bm = 128);
 
 // in_tf32: A/B hold fp32 (tf32 math) else bf16; out_bf16 selects the output dtype.
 void launch_gg_tf32_f32(int act, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
@@ -21,6 +23,14 @@ void launch_gg_bf16_bf16(int act, int bn, const CUtensorMap& ta, const CUtensorM
                          const GroupedGemmParams& p, int grid, cudaStream_t stream);
 void launch_gg_bf16_f32(int act, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
                         const GroupedGemmParams& p, int grid, cudaStream_t stream);
+void launch_gg_pair_tf32_f32(int act, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
+                             const GroupedGemmParams& p, int grid, cudaStream_t stream);
+void launch_gg_pair_bf16_bf16(int act, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
+                              const GroupedGemmParams& p, int grid, cudaStream_t stream);
+void launch_gg_pair_bf16_f32(int act, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
+                             const GroupedGemmParams& p, int grid, cudaStream_t stream);
+// p.pair selects the CTA-pair kernel (BN in {64, 128, 256}; A tensor map box of
+// 128 rows, B box of bn / 2 rows; tile_prefix counted in 256-row tiles).
 void launch_grouped_gemm(bool in_tf32, bool out_bf16, int act, int bn, const CUtensorMap& ta,
                          const CUtensorMap& tb, const GroupedGemmParams& p, int grid,
                          cudaStream_t stream);

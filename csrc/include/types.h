@@ -64,6 +64,7 @@ struct GroupedGemmParams {
   DeviceStatus* status;
   unsigned long long timeout_ns;
   TraceSlot* trace;          // launch trace slot or nullptr
+  int pair;                  // 1: CTA-pair kernel (256-row tiles in tile_prefix), 0: one CTA per 128-row tile
 };
 
 }  // namespace raiccl

@@ -23,7 +23,7 @@ void grouped_gemm(torch::Tensor A, torch::Tensor B, torch::Tensor segs, torch::T
                   int64_t N, int64_t bn, int64_t act, c10::optional<torch::Tensor> bias,
                   c10::optional<torch::Tensor> row_map, c10::optional<torch::Tensor> row_scale,
                   torch::Tensor out_ptrs, int64_t ldo, bool out_bf16, torch::Tensor status,
-                  int64_t grid, int64_t timeout_ns) {
+                  int64_t grid, int64_t timeout_ns, bool pair) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && segs.is_cuda() && prefix.is_cuda() &&
                   out_ptrs.is_cuda() && status.is_cuda(),
               "grouped_gemm: CUDA tensors required");
@@ -38,6 +38,7 @@ void grouped_gemm(torch::Tensor A, torch::Tensor B, torch::Tensor segs, torch::T
   TORCH_CHECK(segs.size(0) >= 1, "grouped_gemm: at least one segment");
   TORCH_CHECK(bn == 16 || bn == 32 || bn == 64 || bn == 128 || bn == 256, "grouped_gemm: BN");
   TORCH_CHECK(N % bn == 0, "grouped_gemm: N must be a multiple of BN");
+  TORCH_CHECK(!pair || bn >= 64, "grouped_gemm: the CTA-pair kernel needs BN >= 64");
   TORCH_CHECK(B.size(0) % N == 0, "grouped_gemm: B rows must be E * N");
   TORCH_CHECK(out_ptrs.scalar_type() == torch::kInt64, "grouped_gemm: out_ptrs int64");
   TORCH_CHECK(status.numel() * status.element_size() >= (int64_t)sizeof(raiccl::DeviceStatus),
@@ -59,11 +60,11 @@ void grouped_gemm(torch::Tensor A, torch::Tensor B, torch::Tensor segs, torch::T
   CUtensorMap ta = raiccl::make_tmap_2d_sw128(A.data_ptr(), dt, elem, A.size(0), A.size(1),
                                               A.stride(0), 128, bk);
   CUtensorMap tb = raiccl::make_tmap_2d_sw128(B.data_ptr(), dt, elem, B.size(0), B.size(1),
-                                              B.stride(0), (uint32_t)bn, bk);
+                                              B.stride(0), (uint32_t)(pair ? bn / 2 : bn), bk);
   const int S = (int)segs.size(0);
   const int nblocks = (int)(N / bn);
   raiccl::launch_tile_plan((const raiccl::GemmSegment*)segs.data_ptr<int>(), S, nblocks,
-                           prefix.data_ptr<int>(), cur_stream());
+                           prefix.data_ptr<int>(), cur_stream(), nullptr, pair ? 256 : 128);
   raiccl::GroupedGemmParams p{};  // value-initialised: fields this call does not set (trace, ...) are null
   p.segs = (const raiccl::GemmSegment*)segs.data_ptr<int>();
   p.tile_prefix = prefix.data_ptr<int>();
@@ -77,6 +78,7 @@ void grouped_gemm(torch::Tensor A, torch::Tensor B, torch::Tensor segs, torch::T
   p.ldo = ldo;
   p.status = (raiccl::DeviceStatus*)status.data_ptr();
   p.timeout_ns = (unsigned long long)timeout_ns;
+  p.pair = pair ? 1 : 0;
   raiccl::launch_grouped_gemm(tf32, out_bf16, (int)act, (int)bn, ta, tb, p, (int)grid,
                               cur_stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -92,6 +94,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("A"), py::arg("B"), py::arg("segs"), py::arg("prefix"), py::arg("N"),
         py::arg("bn"), py::arg("act"), py::arg("bias"), py::arg("row_map"), py::arg("row_scale"),
         py::arg("out_ptrs"), py::arg("ldo"), py::arg("out_bf16"), py::arg("status"),
-        py::arg("grid"), py::arg("timeout_ns"));
+        py::arg("grid"), py::arg("timeout_ns"), py::arg("pair") = false);
   register_moe(m);
 }

@@ -12,7 +12,7 @@ namespace raiccl {
 
 // One CTA: prefix[s] = sum_{j<s} ceil(rows_j / 128) * nblocks.
 __global__ void gemm_tile_plan_kernel(const GemmSegment* segs, int num_segs, int nblocks,
-                                      int* prefix, TraceSlot* trace) {
+                                      int* prefix, TraceSlot* trace, int bm) {
   TraceScope trace_scope(trace);
   __shared__ int partial[1024];
   const int tid = threadIdx.x;
@@ -22,7 +22,7 @@ __global__ void gemm_tile_plan_kernel(const GemmSegment* segs, int num_segs, int
   const int s0 = tid * per;
   for (int s = s0; s < s0 + per && s < num_segs; ++s) {
     const int rows = segs[s].rows > 0 ? segs[s].rows : 0;
-    local += ((rows + 127) / 128) * nblocks;
+    local += ((rows + bm - 1) / bm) * nblocks;
   }
   partial[tid] = local;
   __syncthreads();
@@ -36,14 +36,14 @@ __global__ void gemm_tile_plan_kernel(const GemmSegment* segs, int num_segs, int
   for (int s = s0; s < s0 + per && s < num_segs; ++s) {
     prefix[s] = run;
     const int rows = segs[s].rows > 0 ? segs[s].rows : 0;
-    run += ((rows + 127) / 128) * nblocks;
+    run += ((rows + bm - 1) / bm) * nblocks;
   }
   if (tid == blockDim.x - 1) prefix[num_segs] = partial[tid];
 }
 
 void launch_tile_plan(const GemmSegment* segs, int num_segs, int nblocks, int* prefix,
-                      cudaStream_t stream, TraceSlot* trace) {
-  gemm_tile_plan_kernel<<<1, 1024, 0, stream>>>(segs, num_segs, nblocks, prefix, trace);
+                      cudaStream_t stream, TraceSlot* trace, int bm) {
+  gemm_tile_plan_kernel<<<1, 1024, 0, stream>>>(segs, num_segs, nblocks, prefix, trace, bm);
 }
 
 // Instantiated combinations: tf32 inputs -> fp32 outputs; bf16 inputs -> bf16
@@ -52,6 +52,17 @@ void launch_tile_plan(const GemmSegment* segs, int num_segs, int nblocks, int* p
 void launch_grouped_gemm(bool in_tf32, bool out_bf16, int act, int bn, const CUtensorMap& ta,
                          const CUtensorMap& tb, const GroupedGemmParams& p, int grid,
                          cudaStream_t stream) {
+  if (p.pair) {
+    if (in_tf32) {
+      if (out_bf16) throw std::runtime_error("grouped_gemm: tf32 inputs produce fp32 outputs");
+      launch_gg_pair_tf32_f32(act, bn, ta, tb, p, grid, stream);
+    } else if (out_bf16) {
+      launch_gg_pair_bf16_bf16(act, bn, ta, tb, p, grid, stream);
+    } else {
+      launch_gg_pair_bf16_f32(act, bn, ta, tb, p, grid, stream);
+    }
+    return;
+  }
   if (in_tf32) {
     if (out_bf16) throw std::runtime_error("grouped_gemm: tf32 inputs produce fp32 outputs");
     launch_gg_tf32_f32(act, bn, ta, tb, p, grid, stream);

@@ -102,6 +102,12 @@ class MoELayerRunner {
     act1_ = geti(ints, "act1");
     bn1_ = geti(ints, "bn1");
     bn2_ = geti(ints, "bn2");
+    {
+      // CTA-pair GEMM kernels (256 x BN tiles on clusters of two SMs) for BN >= 64
+      const bool allow = !ints.contains("gemm_pair") || geti(ints, "gemm_pair") != 0;
+      pair1_ = allow && bn1_ >= 64;
+      pair2_ = allow && bn2_ >= 64;
+    }
     timeout_ns_ = (unsigned long long)ints["timeout_ns"].cast<int64_t>();
     max_cands_ = geti(ints, "max_cands");
     log_stride_ = geti(ints, "log_stride");
@@ -122,9 +128,9 @@ class MoELayerRunner {
     const int eb = d.feat_bytes, bk = 128 / eb;
     void* recv_feat = reinterpret_cast<uint8_t*>(peers_.base[d.rank]) + layout_.recv_feat;
     ta1_ = raiccl::make_tmap_2d_sw128(recv_feat, dt, eb, rows, d.hidden, d.hidden, 128, bk);
-    tb1_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "w1"), dt, eb, (uint64_t)d.expert_slots * n1_, d.hidden, d.hidden, bn1_, bk);
+    tb1_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "w1"), dt, eb, (uint64_t)d.expert_slots * n1_, d.hidden, d.hidden, pair1_ ? bn1_ / 2 : bn1_, bk);
     ta2_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "h"), dt, eb, rows, ffn_, ffn_, 128, bk);
-    tb2_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "w2"), dt, eb, (uint64_t)d.expert_slots * d.out_dim, ffn_, ffn_, bn2_, bk);
+    tb2_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "w2"), dt, eb, (uint64_t)d.expert_slots * d.out_dim, ffn_, ffn_, pair2_ ? bn2_ / 2 : bn2_, bk);
 
     {
       int coop = 0;
@@ -401,7 +407,8 @@ class MoELayerRunner {
     g1.ldo = ffn_;
     g1.status = status;
     g1.timeout_ns = timeout_ns_;
-    raiccl::launch_tile_plan(segs, S, n1_ / bn1_, prefix1, comm_, trace_slot("tile_plan", 1));
+    g1.pair = pair1_ ? 1 : 0;
+    raiccl::launch_tile_plan(segs, S, n1_ / bn1_, prefix1, comm_, trace_slot("tile_plan", 1), pair1_ ? 256 : 128);
     g1.trace = trace_slot("gemm1", -1);
     raiccl::launch_grouped_gemm(!feat_bf16_, feat_bf16_, act1_, bn1_, ta1_, tb1_, g1, grid_sms_, comm_);
     launches += 2;
@@ -420,7 +427,9 @@ class MoELayerRunner {
     g2.ldo = d.out_dim;
     g2.status = status;
     g2.timeout_ns = timeout_ns_;
-    raiccl::launch_tile_plan(segs, S, d.out_dim / bn2_, prefix2, comm_, trace_slot("tile_plan", 2));
+    g2.pair = pair2_ ? 1 : 0;
+    raiccl::launch_tile_plan(segs, S, d.out_dim / bn2_, prefix2, comm_, trace_slot("tile_plan", 2),
+                             pair2_ ? 256 : 128);
     g2.trace = trace_slot("gemm2_return", -1);
     raiccl::launch_grouped_gemm(!feat_bf16_, out_bf16_, 0, bn2_, ta2_, tb2_, g2, grid_sms_, comm_);
     launches += 2;
@@ -545,6 +554,7 @@ class MoELayerRunner {
   raiccl::SymLayout layout_{};
   raiccl::PeerBases peers_{};
   int partial_ = 0, ffn_ = 0, n1_ = 0, act1_ = 0, bn1_ = 0, bn2_ = 0;
+  bool pair1_ = false, pair2_ = false;  // GEMM 1 / 2 on the CTA-pair kernel
   int max_cands_ = 0, log_stride_ = 0, max_ctl_tokens_ = 0, grid_sms_ = 148;
   bool control_serial_ = false;  // run the CTA control kernel even where the single-warp one fits
   bool feat_bf16_ = false, out_bf16_ = false;

@@ -54,7 +54,8 @@ class ProgressiveMoELayer:
     def __init__(self, cfg: MoELayerConfig, *, device: torch.device | str | None = None,
                  world: int | None = None, rank: int | None = None, group=None,
                  timeout_s: float = 10.0, seed: int = 0, control_topology=None,
-                 control_path: str = "auto", trace: bool = False, frontend: str = "persistent") -> None:
+                 control_path: str = "auto", trace: bool = False, frontend: str = "persistent",
+                 gemm_pair: bool = True) -> None:
         self.cfg = cfg
         if world is None:
             world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -137,6 +138,7 @@ class ProgressiveMoELayer:
             "sms": torch.cuda.get_device_properties(dev).multi_processor_count,
             "control_serial": {"auto": 0, "serial": 1}[control_path],
             "frontend": {"steps": 0, "persistent": 1}[frontend],
+            "gemm_pair": int(bool(gemm_pair)),
         }
         self.layout = self._k.sym_layout(ints)
         self.channel = PeerChannel(self.layout["total"], dev, group=group)

@@ -86,11 +86,13 @@ def grouped_gemm(
     grid: int | None = None,
     timeout_ns: int = DEFAULT_TIMEOUT_NS,
     check: bool = False,
+    pair: bool = False,
 ) -> torch.Tensor | None:
     """Launch the grouped GEMM on the current stream.
 
     Either ``out`` (a local tensor, slot 0) or ``out_ptrs`` (int64 device
-    pointers, one per ``out_slot``) must be given.  With ``check=True`` the
+    pointers, one per ``out_slot``) must be given.  ``pair=True`` runs the
+    CTA-pair kernel (256 x bn tiles on clusters of two SMs; bn >= 64).  With ``check=True`` the
     call synchronises and raises on a recorded device status.
     """
     mod = kernels()
@@ -112,7 +114,7 @@ def grouped_gemm(
         grid = num_sms(A.device)
     mod.grouped_gemm(
         A, B, segs, prefix, int(n), int(bn), ACT_IDS[act], bias, row_map, row_scale,
-        out_ptrs, int(ldo), bool(out_bf16), status, int(grid), int(timeout_ns),
+        out_ptrs, int(ldo), bool(out_bf16), status, int(grid), int(timeout_ns), bool(pair),
     )
     if check:
         torch.cuda.synchronize(A.device)

@@ -123,3 +123,48 @@ def test_bf16_swiglu():
         u = x @ wu[e].float().t()
         ref[o0:o0 + r] = torch.nn.functional.silu(g) * u
     torch.testing.assert_close(out, ref, atol=5e-3, rtol=5e-3)
+
+
+@pytest.mark.parametrize("dtype,act,bn", [("tf32", "gelu", 256), ("tf32", "none", 128), ("bf16", "relu", 64),
+                                          ("bf16", "swiglu", 256)])
+def test_cta_pair_kernel_matches_fp32_reference_and_single_cta(dtype, act, bn):
+    """The CTA-pair kernel (256-row tiles on clusters of two SMs) against the fp32
+    reference and bit-for-bit against the one-CTA kernel on ragged segments."""
+    gg = _gg()
+    torch.manual_seed(7)
+    dev = torch.device("cuda")
+    k, f, E = 512, 256, 3
+    n = 2 * f if act == "swiglu" else f
+    seg_rows = [(0, 300, 2), (300, 0, 1), (300, 57, 0), (400, 513, 1), (913, 129, 2)]
+    total = 1100
+    dt = torch.float32 if dtype == "tf32" else torch.bfloat16
+    A = torch.randn(total, k, device=dev).to(dt)
+    if act == "swiglu":
+        wg = (torch.randn(E, f, k, device=dev) / k ** 0.5).to(dt)
+        wu = (torch.randn(E, f, k, device=dev) / k ** 0.5).to(dt)
+        B = gg.swiglu_interleave(wg, wu, bn).reshape(E * n, k)
+    else:
+        B = (torch.randn(E * n, k, device=dev) / k ** 0.5).to(dt)
+    bias = None if act == "swiglu" else torch.randn(E * n, device=dev) * 0.1
+    segs_list = [(a0, r, e, 0, a0) for (a0, r, e) in seg_rows]
+    segs = gg.make_segments(segs_list, dev)
+    width = f if act == "swiglu" else n
+    outs = {}
+    for pair in (True, False):
+        out = torch.full((total, width), float("nan"), device=dev)
+        gg.grouped_gemm(A, B, segs, n=n, act=act, bias=bias, out=out, bn=bn, check=True, pair=pair)
+        outs[pair] = out
+    valid = torch.zeros(total, dtype=torch.bool, device=dev)
+    for (a0, r, e) in seg_rows:
+        valid[a0:a0 + r] = True
+    if act == "swiglu":
+        ref = torch.zeros(total, f, device=dev)
+        for (a0, r, e, _, o0) in segs_list:
+            x = A[a0:a0 + r].float()
+            ref[o0:o0 + r] = torch.nn.functional.silu(x @ wg[e].float().t()) * (x @ wu[e].float().t())
+    else:
+        ref = _ref(A, B, segs_list, n, act, bias=bias, out_rows=total)
+    tol = 5e-3 if dtype == "tf32" else 2e-2
+    torch.testing.assert_close(outs[True][valid], ref[valid], atol=tol, rtol=tol)
+    assert torch.equal(outs[True][valid], outs[False][valid])
+    assert torch.isnan(outs[True][~valid]).all()  # rows outside every segment are never written

@@ -205,3 +205,21 @@ def test_persistent_frontend_matches_step_pipeline(name):
     assert torch.equal(res["persistent"][0][0], res["persistent"][0][1])
     assert torch.equal(res["persistent"][1], res["steps"][1])
     assert torch.equal(res["persistent"][2], res["steps"][2])
+
+
+def test_cta_pair_gemms_leave_layer_output_unchanged():
+    """The layer's GEMMs on the CTA-pair kernel give bit-identical outputs."""
+    from revealaiccl_b200.moe.config import preset
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    outs = []
+    for pair in (True, False):
+        layer = ProgressiveMoELayer(preset("full_tf32").with_overrides(tokens_per_rank=2048, chunk_sizes=(256,) * 8),
+                                    timeout_s=5.0, gemm_pair=pair)
+        try:
+            layer.forward("early")
+            assert layer.verify()["pass"]
+            outs.append(layer.out.clone())
+        finally:
+            layer.close()
+    assert torch.equal(outs[0], outs[1])
