@@ -65,14 +65,17 @@ __device__ __forceinline__ unsigned lanemask_lt() {
   return m;
 }
 
+// kFetchesTokens: before(desc) has already placed the control-token
+// destinations of every chunk the trigger needs in s_dst[c * cpc + j].
 struct NoHooks {
+  static constexpr bool kFetchesTokens = false;
   __device__ __forceinline__ bool before(int) { return true; }
   __device__ __forceinline__ void after(int, bool) {}
 };
 
 // Called by one full warp.  csm holds the staged control blob; s_dst
-// (kCtlStageMax), s_coff (kCtlMaxChunks + 1) and s_egmask (kWarpMaxE) are
-// shared scratch.  reset: start a layer call (fresh scheduler state).
+// (kCtlStageMax >= chunks x ctl_per_chunk), s_coff (kCtlMaxChunks + 1) and
+// s_egmask (kWarpMaxE) are shared scratch.  reset: start a layer call (fresh scheduler state).
 template <class Hooks>
 __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims, uint8_t* csm, int* s_dst,
                                  int* s_coff, uint32_t* s_egmask, int q0, int q1, bool reset, Hooks& hooks) {
@@ -161,13 +164,16 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   const bool final_trigger = desc >= P;
   const int c_lo = final_trigger ? P : desc;
   const int c_hi = final_trigger ? C - 1 : desc;
-  const int n_stage = (c_hi - c_lo + 1) * cpc;
-  // control-token destinations of the trigger's chunks (router output)
-  for (int i = lane; i < n_stage; i += 32) {
-    const int c = c_lo + i / cpc, j = i % cpc;
-    const int off = s_coff[c];
-    const int size = s_coff[c + 1] - off;
-    s_dst[i] = j < size ? p.expert_ids[(long long)(off + j) * p.top_k] % p.ctl_nodes : -1;
+  // control-token destinations of the trigger's chunks (router output), kept
+  // by absolute chunk: s_dst[c * cpc + j]
+  if constexpr (!Hooks::kFetchesTokens) {
+    const int n_stage = (c_hi - c_lo + 1) * cpc;
+    for (int i = lane; i < n_stage; i += 32) {
+      const int c = c_lo + i / cpc, j = i % cpc;
+      const int off = s_coff[c];
+      const int size = s_coff[c + 1] - off;
+      s_dst[c * cpc + j] = j < size ? p.expert_ids[(long long)(off + j) * p.top_k] % p.ctl_nodes : -1;
+    }
   }
   __syncwarp();
   // trigger scalars live in (warp-uniform) registers until the end of the trigger
@@ -190,7 +196,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     const long long start = staged;
     const int pos = off + lane;
     const int src = pos % p.ctl_nodes;
-    const int dst = lane < limit ? s_dst[(c - c_lo) * cpc + lane] : -1;
+    const int dst = lane < limit ? s_dst[c * cpc + lane] : -1;
     const bool keep_tok = lane < limit && src != dst;
     const unsigned bal = __ballot_sync(FULL, keep_tok);
     const int nk = __popc(bal);

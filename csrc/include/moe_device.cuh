@@ -64,6 +64,66 @@ constexpr int kDispatchMaxItems = 4096;
 constexpr int kMaxExperts = 256;
 constexpr int kDispatchMaxChunks = 128;  // chunk-offset table staged in shared memory
 
+// Logits -> mask -> stable descending top-k (the smaller expert id wins ties)
+// -> gates; writes expert_ids / gates of row t (one thread per token).
+// bias / chunk_bias / block_mask may point at global memory or at shared
+// copies; the values, and so the routing, are the same.
+template <int EMAX>
+__device__ __forceinline__ void router_finish(const RouterParams& p, const float* bias, const float* chunk_bias,
+                                              const uint8_t* block_mask, int t, const float (&acc)[EMAX],
+                                              int* sel_out) {
+  const int E = p.experts;
+  float logit[EMAX];
+  bool taken[EMAX];
+  const float ninf = -__int_as_float(0x7f800000);
+#pragma unroll
+  for (int e = 0; e < EMAX; ++e) {
+    taken[e] = false;
+    if (e < E) {
+      float l = acc[e] + bias[e] + (chunk_bias ? chunk_bias[e] : 0.f);
+      const bool masked = (p.mask_mode == 1 && e == (t % E)) || (block_mask && block_mask[e]);
+      logit[e] = masked ? ninf : l;
+    } else {
+      logit[e] = ninf;
+    }
+  }
+  // the choice loop stays rolled: unrolled over k x EMAX it makes compile time explode
+  float sel_logit[8];
+  int sel[8];
+#pragma unroll 1
+  for (int j = 0; j < p.top_k; ++j) {
+    int best = -1;
+    float bv = ninf;
+#pragma unroll
+    for (int e = 0; e < EMAX; ++e)
+      if (e < E && !taken[e] && (best < 0 || logit[e] > bv)) { best = e; bv = logit[e]; }
+#pragma unroll
+    for (int e = 0; e < EMAX; ++e)
+      if (e == best) taken[e] = true;
+    sel[j] = best;
+    sel_logit[j] = bv;
+  }
+  float g[8];
+  if (p.gate_mode == 1) {
+    float sum = 0.f;
+    for (int j = 0; j < p.top_k; ++j) { g[j] = __expf(sel_logit[j] - sel_logit[0]); sum += g[j]; }
+    for (int j = 0; j < p.top_k; ++j) g[j] /= sum;
+  } else if (p.gate_mode == 2) {
+    float mx = sel_logit[0], sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < EMAX; ++e)
+      if (e < E && logit[e] != ninf) sum += __expf(logit[e] - mx);
+    for (int j = 0; j < p.top_k; ++j) g[j] = __expf(sel_logit[j] - mx) / sum;
+  } else {
+    for (int j = 0; j < p.top_k; ++j) g[j] = 1.f;
+  }
+  for (int j = 0; j < p.top_k; ++j) {
+    p.expert_ids[(long long)t * p.top_k + j] = sel[j];
+    p.gates[(long long)t * p.top_k + j] = g[j];
+    if (sel_out) sel_out[j] = sel[j];
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Router of one token (warp collective): logits = x_t . W_e + b_e (+ chunk
 // bias), masked experts -inf, stable descending top-k (the smaller expert id
@@ -119,52 +179,101 @@ __device__ __forceinline__ void router_token(const RouterParams& p, const float*
     }
   }
   if (lane != 0) return;
-  float logit[EMAX];
-  bool taken[EMAX];
-  const float ninf = -__int_as_float(0x7f800000);
+  router_finish<EMAX>(p, p.bias, chunk_bias, p.block_mask, t, acc, sel_out);
+}
+
+// Recursive-halving transpose reduction: each lane enters with 32 partial
+// sums v[0..31]; lane L leaves with the warp total of index L in v[0]
+// (5 exchange steps, 31 shuffles in all).
+__device__ __forceinline__ void warp_transpose_reduce32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
 #pragma unroll
-  for (int e = 0; e < EMAX; ++e) {
-    taken[e] = false;
-    if (e < E) {
-      float l = acc[e] + p.bias[e] + (chunk_bias ? chunk_bias[e] : 0.f);
-      const bool masked = (p.mask_mode == 1 && e == (t % E)) || (p.block_mask && p.block_mask[e]);
-      logit[e] = masked ? ninf : l;
-    } else {
-      logit[e] = ninf;
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int i = 0; i < s; ++i) {
+      const float send = upper ? v[i] : v[i + s];
+      const float recv = __shfl_xor_sync(0xffffffffu, send, s);
+      v[i] = (upper ? v[i + s] : v[i]) + recv;
     }
   }
-  float sel_logit[8];
-  int sel[8];
-  for (int j = 0; j < p.top_k; ++j) {
-    int best = -1;
+}
+
+// Whether router_group handles this shape: E <= 32 experts and a row of
+// 16-byte vectors that splits evenly over a CTA's 8 warps.
+__host__ __device__ __forceinline__ bool router_group_ok(int experts, int hidden, int elem_bytes) {
+  const int nv = hidden * elem_bytes / 16;
+  return experts <= 32 && (hidden * elem_bytes) % 16 == 0 && nv % 8 == 0 && nv > 0;
+}
+
+// Router of NT consecutive tokens [t_first, t_first + nt) by one CTA of 8 warps
+// (NT * EP = 32, EP >= experts): the hidden dimension is split over the warps;
+// every lane accumulates NT x EP partial dot products from 16-byte vectors, so
+// each weight vector is loaded once for all NT tokens; a transpose reduction
+// leaves one (token, expert) sum per lane; the 8 warp partials are added in
+// warp order; lane j of warp 0 finishes token j.  sel_counts (shared, per
+// expert, or nullptr) counts the selected experts.  Collective over the CTA;
+// red is 256 floats of shared scratch.
+//
+// wpre (optional): this lane's weight vectors wpre[e] = W_e[warp * 32 + lane]
+// when a row has exactly 8 x 32 vectors, held in registers across calls;
+// bias / block_mask: global or shared copies of the router tables.
+template <typename T, int NT, int EP>
+__device__ void router_group(const RouterParams& p, const float* bias, const float* chunk_bias,
+                             const uint8_t* block_mask, int t_first, int nt, float* red, int* sel_counts,
+                             const uint4* wpre) {
+  static_assert(NT * EP == 32, "one (token, expert) sum per lane");
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int D = p.hidden, E = p.experts;
+  constexpr int VEC = 16 / sizeof(T);
+  const int vpw = D / VEC / 8;
+  const T* __restrict__ tok = (const T*)p.tokens;
+  const T* __restrict__ w = (const T*)p.weight;
+  float v[32];
 #pragma unroll
-    for (int e = 0; e < EMAX; ++e)
-      if (e < E && !taken[e] && (best < 0 || logit[e] > logit[best])) best = e;
+  for (int i = 0; i < 32; ++i) v[i] = 0.f;
+  for (int vi = warp * vpw + lane; vi < (warp + 1) * vpw; vi += 32) {
+    uint4 x[NT];
 #pragma unroll
-    for (int e = 0; e < EMAX; ++e)
-      if (e == best) taken[e] = true;
-    sel[j] = best;
-    sel_logit[j] = logit[best];
-  }
-  float g[8];
-  if (p.gate_mode == 1) {
-    float sum = 0.f;
-    for (int j = 0; j < p.top_k; ++j) { g[j] = __expf(sel_logit[j] - sel_logit[0]); sum += g[j]; }
-    for (int j = 0; j < p.top_k; ++j) g[j] /= sum;
-  } else if (p.gate_mode == 2) {
-    float mx = sel_logit[0], sum = 0.f;
+    for (int j = 0; j < NT; ++j)
+      x[j] = j < nt ? __ldg((const uint4*)(tok + (long long)(t_first + j) * D) + vi) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-    for (int e = 0; e < EMAX; ++e)
-      if (e < E && logit[e] != ninf) sum += __expf(logit[e] - mx);
-    for (int j = 0; j < p.top_k; ++j) g[j] = __expf(sel_logit[j] - mx) / sum;
-  } else {
-    for (int j = 0; j < p.top_k; ++j) g[j] = 1.f;
+    for (int e = 0; e < EP; ++e) {
+      if (e < E) {
+        const uint4 wr = wpre ? wpre[e] : __ldg((const uint4*)(w + (long long)e * D) + vi);
+        const T* wv = (const T*)&wr;
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const T* xv = (const T*)&x[j];
+          float s = 0.f;
+#pragma unroll
+          for (int q = 0; q < VEC; ++q) s = fmaf(to_f(xv[q]), to_f(wv[q]), s);
+          v[j * EP + e] += s;
+        }
+      }
+    }
   }
-  for (int j = 0; j < p.top_k; ++j) {
-    p.expert_ids[(long long)t * p.top_k + j] = sel[j];
-    p.gates[(long long)t * p.top_k + j] = g[j];
-    if (sel_out) sel_out[j] = sel[j];
+  warp_transpose_reduce32(v);
+  red[warp * 32 + lane] = v[0];
+  __syncthreads();
+  if (warp == 0) {
+    float tot = 0.f;
+#pragma unroll
+    for (int w8 = 0; w8 < 8; ++w8) tot += red[w8 * 32 + lane];
+    __syncwarp();
+    red[lane] = tot;
+    __syncwarp();
+    if (lane < nt) {
+      float acc[EP];
+#pragma unroll
+      for (int e = 0; e < EP; ++e) acc[e] = red[lane * EP + e];
+      int sel[8];
+      router_finish<EP>(p, bias, chunk_bias, block_mask, t_first + lane, acc, sel);
+      if (sel_counts)
+        for (int j = 0; j < p.top_k; ++j) atomicAdd(&sel_counts[sel[j]], 1);
+    }
   }
+  __syncthreads();
 }
 
 // ---------------------------------------------------------------------------

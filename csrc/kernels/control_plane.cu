@@ -299,11 +299,10 @@ __global__ void __launch_bounds__(32) moe_control_warp_kernel(ControlParams p, C
 }
 
 bool control_warp_path_ok(const ControlParams& p) {
-  const int P = p.partial_chunks;
-  const int n_stage_final = (p.chunks - P) * p.ctl_per_chunk;
-  const int n_stage = n_stage_final > p.ctl_per_chunk ? n_stage_final : p.ctl_per_chunk;
+  // s_dst holds every chunk's control tokens (chunks x ctl_per_chunk entries)
   return p.plan.E <= kWarpMaxE && p.plan.G <= kWarpMaxG && p.max_tmpl <= kWarpMaxTmpl &&
-         p.ctl_per_chunk <= kWarpMaxPerChunk && p.chunks <= kCtlMaxChunks && n_stage <= kCtlStageMax;
+         p.ctl_per_chunk <= kWarpMaxPerChunk && p.chunks <= kCtlMaxChunks &&
+         p.chunks * p.ctl_per_chunk <= kCtlStageMax;
 }
 
 void launch_control(const ControlParams& p, cudaStream_t s) {

@@ -88,6 +88,19 @@ __global__ void __launch_bounds__(256) moe_router_kernel(RouterParams p) {
   router_token<T, EMAX, SMEM_W>(p, p.chunk_bias, t, w, nullptr);
 }
 
+// One router chunk with NT tokens per CTA (router_group).  Shapes router_group
+// handles use this kernel in the step pipeline and the same device function in
+// the persistent front end, so both paths compute bit-identical logits.
+template <typename T, int NT, int EP>
+__global__ void __launch_bounds__(256) moe_router_group_kernel(RouterParams p) {
+  TraceScope trace_scope(p.trace);
+  __shared__ float red[256];
+  const int t_first = p.row0 + blockIdx.x * NT;
+  const int nt = min(NT, p.row1 - t_first);
+  if (nt <= 0) return;
+  router_group<T, NT, EP>(p, p.bias, p.chunk_bias, p.block_mask, t_first, nt, red, nullptr, nullptr);
+}
+
 // ---------------------------------------------------------------------------
 // Dispatch of one revealed descriptor (a run of router chunks) straight into
 // the owners' receive regions.  Rows keep the reference's deterministic order
@@ -371,6 +384,20 @@ void launch_checksum_base(const long long* token_ids, const long long* digest, c
 void launch_router(const RouterParams& p, bool bf16, cudaStream_t s) {
   const int rows = p.row1 - p.row0;
   if (rows <= 0) return;
+  if (router_group_ok(p.experts, p.hidden, bf16 ? 2 : 4)) {
+#define RAICCL_ROUTER_GROUP(NT, EP)                                                  \
+  do {                                                                               \
+    const dim3 g((rows + NT - 1) / NT);                                              \
+    if (bf16) moe_router_group_kernel<__nv_bfloat16, NT, EP><<<g, 256, 0, s>>>(p);   \
+    else moe_router_group_kernel<float, NT, EP><<<g, 256, 0, s>>>(p);                \
+  } while (0)
+    if (p.experts <= 4) RAICCL_ROUTER_GROUP(8, 4);
+    else if (p.experts <= 8) RAICCL_ROUTER_GROUP(4, 8);
+    else if (p.experts <= 16) RAICCL_ROUTER_GROUP(2, 16);
+    else RAICCL_ROUTER_GROUP(1, 32);
+#undef RAICCL_ROUTER_GROUP
+    return;
+  }
   const int warps = 8;
   const dim3 grid((rows + warps - 1) / warps);
   const long long wbytes = (long long)p.experts * p.hidden * (bf16 ? 2 : 4);

@@ -15,7 +15,8 @@
 //       router counts into the descriptor's receive bases and counts and
 //       releases desc_ready[q] = epoch.
 //   CTAs 1..W — workers.  For each router chunk: route a share of its tokens
-//       (one warp per token), add the per-expert counts, and release
+//       (groups of tokens per CTA, or one warp per token for more than 32
+//       experts), add the per-expert counts, and release
 //       chunk_done[c].  In the early arm, a worker dispatches every descriptor
 //       already released between chunks (a non-blocking poll, so routing never
 //       waits on the control plane).  After the last chunk it dispatches the
@@ -59,6 +60,12 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned 
   return v;
 }
 
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void st_release_gpu_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -81,14 +88,22 @@ __device__ __forceinline__ void cta_stamp(const FrontendParams& f, int k) {
 __device__ __forceinline__ int trigger_first_chunk(int q, int P) { return q < P ? q : P; }
 __device__ __forceinline__ int trigger_last_chunk(int q, int P, int C) { return q < P ? q : C - 1; }
 
-// Control-warp hooks: wait for the trigger's router chunks; publish the
-// descriptor's receive bases and counts, then release it.
+// Control-warp hooks.  before(q): wait (bounded) for the router chunks trigger q
+// needs, then, in one round trip, fetch the control-token destinations and the
+// per-expert router counts of EVERY chunk complete by now into shared memory,
+// so later triggers usually read no global memory.  after(q): turn the chunks'
+// counts into the descriptor's receive bases and counts, then release it.
 struct FrontHooks {
+  static constexpr bool kFetchesTokens = true;
   const FrontendParams* f;
   int workers, P, C, E;
   unsigned long long epoch;
-  int* s_sent;       // [E] rows already assigned per expert (shared, CTA 0)
-  int chunks_ready;  // chunks [0, chunks_ready) are known complete
+  int* s_sent;         // [E] rows already assigned per expert (shared)
+  int* s_dst;          // [C * cpc] control-token destinations (shared)
+  const int* s_coff;   // [C + 1] chunk offsets (shared)
+  int* s_ccount;       // [C * E] router counts per (chunk, expert) (shared)
+  int cpc;
+  int chunks_ready;    // chunks [0, chunks_ready) complete and fetched
 
   __device__ bool before(int q) {
     const int lane = threadIdx.x & 31;
@@ -105,12 +120,32 @@ struct FrontHooks {
           }
         }
       }
-      __threadfence();
     }
     ok = __shfl_sync(0xffffffffu, ok, 0);
-    __syncwarp();
     if (!ok) return false;
-    chunks_ready = need;
+    // every further chunk that is already complete (one parallel poll)
+    int hi = need;
+    for (int base = need; base < C; base += 32) {
+      const int c = base + lane;
+      const bool done = c < C && ld_acquire_gpu_s32(&f->chunk_done[c]) >= workers;
+      const unsigned notdone = __ballot_sync(0xffffffffu, !done);
+      const int run = notdone ? __ffs(notdone) - 1 : 32;
+      hi = base + run;
+      if (run < 32) break;
+    }
+    if (hi > C) hi = C;
+    __threadfence();
+    __syncwarp();
+    const int lo = chunks_ready;
+    for (int i = lane; i < (hi - lo) * cpc; i += 32) {
+      const int c = lo + i / cpc, j = i % cpc;
+      const int off = s_coff[c];
+      const int size = s_coff[c + 1] - off;
+      s_dst[c * cpc + j] = j < size ? f->cp.expert_ids[(long long)(off + j) * f->cp.top_k] % f->cp.ctl_nodes : -1;
+    }
+    for (int i = lane; i < (hi - lo) * E; i += 32) s_ccount[lo * E + i] = f->chunk_counts[(long long)lo * E + i];
+    chunks_ready = hi;
+    __syncwarp();
     if (lane == 0 && f->phase_trace) trace_begin(&f->phase_trace[C + q]);
     if (q < 16) cta_stamp(*f, 2 + 2 * q);
     return true;
@@ -121,7 +156,7 @@ struct FrontHooks {
     const int c_lo = trigger_first_chunk(q, P), c_hi = trigger_last_chunk(q, P, C);
     for (int e = lane; e < E; e += 32) {
       int cnt = 0;
-      for (int c = c_lo; c <= c_hi; ++c) cnt += f->chunk_counts[(long long)c * E + e];
+      for (int c = c_lo; c <= c_hi; ++c) cnt += s_ccount[c * E + e];
       const int base = s_sent[e];
       f->disp_base[(long long)q * E + e] = base;
       f->dp.desc_counts[(long long)q * E + e] = permitted ? cnt : 0;
@@ -205,7 +240,10 @@ __device__ int wait_released(const FrontendParams& f, int q, unsigned long long 
   return v;
 }
 
-template <typename T, int EMAX, bool SMEM_W>
+// NT > 0: CTA-group router (router_group: NT tokens x EP experts per CTA step);
+// NT == 0: one warp per token (router_token, up to EMAX experts).  The step
+// pipeline makes the same choice (launch_router), so both route identically.
+template <typename T, int NT, int EP, int EMAX>
 __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __grid_constant__ FrontendParams f) {
   extern __shared__ __align__(16) uint8_t fsm[];
   __shared__ int hist[kMaxExperts];
@@ -214,6 +252,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   __shared__ int item_pos[kDispatchMaxItems];
   __shared__ int s_coff[kDispatchMaxChunks + 1];
   __shared__ int s_flag;
+  __shared__ float red[256];
   TraceScope trace_scope(f.trace);
   const MoEDims& d = f.dp.dims;
   const int C = d.chunks, E = d.experts, n_desc = d.n_desc;
@@ -234,7 +273,9 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;  // s_sent of the hooks
     __syncthreads();
     if (threadIdx.x < 32) {
-      FrontHooks hooks{&f, W, f.cp.partial_chunks, C, E, epoch, hist, 0};
+      int* s_ccount = reinterpret_cast<int*>(fsm + ((Lt.total + 15) & ~15LL));
+      FrontHooks hooks{&f, W, f.cp.partial_chunks, C, E, epoch, hist, s_dst, s_ccoff, s_ccount,
+                       f.cp.ctl_per_chunk, 0};
       ctl::control_warp_run(f.cp, dims, fsm, s_dst, s_ccoff, s_egmask, 0, n_desc, true, hooks);
       __syncwarp();
       for (int e = threadIdx.x; e < E; e += 32) f.dp.sent_base[e] = hist[e];
@@ -249,12 +290,40 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   const int w = blockIdx.x - 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const T* wts = (const T*)f.rp.weight;
-  if constexpr (SMEM_W) {
-    uint4* ws = (uint4*)fsm;
-    const uint4* wg = (const uint4*)f.rp.weight;
-    const int nvec = E * f.rp.hidden * (int)sizeof(T) / 16;
-    for (int i = threadIdx.x; i < nvec; i += blockDim.x) ws[i] = __ldg(wg + i);
-    wts = (const T*)fsm;
+  // router tables in shared memory for the whole launch: bias, block mask and
+  // (behind the blob area) the per-chunk bias rows
+  __shared__ float s_rbias[kMaxExperts];
+  __shared__ uint8_t s_rmask[kMaxExperts];
+  float* s_cbias = reinterpret_cast<float*>(fsm);
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    s_rbias[e] = f.rp.bias[e];
+    s_rmask[e] = f.rp.block_mask ? f.rp.block_mask[e] : 0;
+  }
+  if (f.rp.chunk_bias)
+    for (int i = threadIdx.x; i < C * E; i += blockDim.x) s_cbias[i] = f.rp.chunk_bias[i];
+  // this lane's weight slice, held in registers across chunks (rows of 8 x 32 vectors)
+  constexpr int kWP = NT > 0 ? EP : 1;
+  uint4 wpre[kWP];
+  const int nvec_row = f.rp.hidden * (int)sizeof(T) / 16;
+  const bool use_wpre = NT > 0 && nvec_row == 8 * 32;
+  if (use_wpre) {
+#pragma unroll
+    for (int e = 0; e < kWP; ++e)
+      wpre[e] = e < E ? __ldg((const uint4*)(wts + (long long)e * f.rp.hidden) + warp * 32 + lane) : make_uint4(0, 0, 0, 0);
+  }
+  // start pulling this worker's token rows of every chunk into L2
+  if constexpr (NT > 0) {
+    const int row_bytes = f.rp.hidden * (int)sizeof(T);
+    for (int c = 0; c < C; ++c) {
+      const int t0 = s_coff[c], t1 = s_coff[c + 1];
+      const int ngroups = (t1 - t0 + NT - 1) / NT;
+      for (int g = w; g < ngroups; g += W) {
+        const int tf = t0 + g * NT, nt = min(NT, t1 - tf);
+        const char* base = (const char*)f.rp.tokens + (long long)tf * row_bytes;
+        for (int off = threadIdx.x * 128; off < nt * row_bytes; off += blockDim.x * 128)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
+      }
+    }
   }
   cta_stamp(f, 0);
   __syncthreads();
@@ -264,15 +333,29 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     TraceSlot* rslot = f.phase_trace ? &f.phase_trace[c] : nullptr;
     if (threadIdx.x == 0) trace_begin(rslot);
     if (c < 8) cta_stamp(f, 2 + 2 * c);
+    // early arm: this chunk's poll of the next release is a relaxed load issued
+    // before the routing work and read after it (a fence makes it an acquire
+    // when it saw the release)
+    unsigned long long early_v = 0;
+    if (threadIdx.x == 0 && !f.delayed && next < n_desc) early_v = ld_relaxed_gpu_u64(&f.desc_ready[next]);
     for (int e = threadIdx.x; e < E; e += blockDim.x) run[e] = 0;  // per-chunk expert counts
     __syncthreads();
-    const float* cbias = f.rp.chunk_bias ? f.rp.chunk_bias + (long long)c * E : nullptr;
+    const float* cbias = f.rp.chunk_bias ? s_cbias + (long long)c * E : nullptr;
     const int t0 = s_coff[c], t1 = s_coff[c + 1];
-    for (int t = t0 + w * nwarps + warp; t < t1; t += W * nwarps) {
-      int sel[8];
-      router_token<T, EMAX, SMEM_W>(f.rp, cbias, t, wts, sel);
-      if (lane == 0)
-        for (int j = 0; j < f.rp.top_k; ++j) atomicAdd(&run[sel[j]], 1);
+    if constexpr (NT > 0) {
+      const int ngroups = (t1 - t0 + NT - 1) / NT;
+      for (int g = w; g < ngroups; g += W) {
+        const int tf = t0 + g * NT;
+        router_group<T, NT, EP>(f.rp, s_rbias, cbias, f.rp.block_mask ? s_rmask : nullptr, tf, min(NT, t1 - tf),
+                                red, run, use_wpre ? wpre : nullptr);
+      }
+    } else {
+      for (int t = t0 + w * nwarps + warp; t < t1; t += W * nwarps) {
+        int sel[8];
+        router_token<T, EMAX, false>(f.rp, cbias, t, wts, sel);
+        if (lane == 0)
+          for (int j = 0; j < f.rp.top_k; ++j) atomicAdd(&run[sel[j]], 1);
+      }
     }
     if (c < 8) cta_stamp(f, 52 + c);
     __syncthreads();
@@ -288,9 +371,17 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     if (c < 8) cta_stamp(f, 3 + 2 * c);
     // early arm: dispatch every descriptor already released (never waits)
     if (!f.delayed) {
-      while (next < n_desc && wait_released(f, next, epoch, &s_flag, false) == 1) {
+      if (threadIdx.x == 0) {
+        if (early_v == epoch) __threadfence();
+        s_flag = early_v == epoch ? 1 : 0;
+      }
+      __syncthreads();
+      bool ready = s_flag == 1;
+      __syncthreads();
+      while (next < n_desc && ready) {
         worker_dispatch<T>(f, next, w, W, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag);
         ++next;
+        ready = next < n_desc && wait_released(f, next, epoch, &s_flag, false) == 1;
       }
     }
   }
@@ -302,9 +393,9 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   }
 }
 
-template <typename T, int EMAX, bool SMEM_W>
+template <typename T, int NT, int EP, int EMAX>
 bool launch_one_frontend(const FrontendParams& f, int sms, size_t smem, cudaStream_t s) {
-  auto kern = moe_frontend_kernel<T, EMAX, SMEM_W>;
+  auto kern = moe_frontend_kernel<T, NT, EP, EMAX>;
   static size_t configured = 0;
   if (smem > configured) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
@@ -334,19 +425,29 @@ bool launch_frontend(const FrontendParams& f, bool bf16, int sms, cudaStream_t s
   if (sms < 2 || !control_warp_path_ok(f.cp) || f.dp.dims.experts > kMaxExperts || f.rp.top_k > 8 ||
       f.dp.dims.chunks > kDispatchMaxChunks)
     return false;
-  const long long wbytes = (long long)f.rp.experts * f.rp.hidden * (bf16 ? 2 : 4);
-  const bool smem_w = wbytes <= 96 * 1024;
-  const size_t blob = control_smem_bytes(f.cp);
-  const size_t smem = std::max<size_t>(blob, smem_w ? (size_t)wbytes : 0);
-#define RAICCL_FRONT(T, EM)                                                            \
-  return smem_w ? launch_one_frontend<T, EM, true>(f, sms, smem, s)                    \
-                : launch_one_frontend<T, EM, false>(f, sms, smem, s)
-  if (f.rp.experts <= 8) {
-    if (bf16) RAICCL_FRONT(__nv_bfloat16, 8); else RAICCL_FRONT(float, 8);
-  } else if (f.rp.experts <= 16) {
-    if (bf16) RAICCL_FRONT(__nv_bfloat16, 16); else RAICCL_FRONT(float, 16);
-  } else if (f.rp.experts <= 64) {
-    if (bf16) RAICCL_FRONT(__nv_bfloat16, 64); else RAICCL_FRONT(float, 64);
+  // dynamic shared memory holds the control blob (CTA 0); router weights are
+  // read through the read-only path
+  // CTA 0: control blob + per-(chunk, expert) router counts; workers: per-chunk bias rows
+  const size_t cwords = (size_t)f.dp.dims.chunks * f.dp.dims.experts * sizeof(int);
+  const size_t smem = std::max(((control_smem_bytes(f.cp) + 15) & ~(size_t)15) + cwords, cwords);
+#define RAICCL_FRONT(T, NT, EP, EM) return launch_one_frontend<T, NT, EP, EM>(f, sms, smem, s)
+  const int E = f.rp.experts;
+  if (router_group_ok(E, f.rp.hidden, bf16 ? 2 : 4)) {
+    if (E <= 4) {
+      if (bf16) RAICCL_FRONT(__nv_bfloat16, 8, 4, 4); else RAICCL_FRONT(float, 8, 4, 4);
+    } else if (E <= 8) {
+      if (bf16) RAICCL_FRONT(__nv_bfloat16, 4, 8, 8); else RAICCL_FRONT(float, 4, 8, 8);
+    } else if (E <= 16) {
+      if (bf16) RAICCL_FRONT(__nv_bfloat16, 2, 16, 16); else RAICCL_FRONT(float, 2, 16, 16);
+    } else {
+      if (bf16) RAICCL_FRONT(__nv_bfloat16, 1, 32, 32); else RAICCL_FRONT(float, 1, 32, 32);
+    }
+  } else if (E <= 8) {
+    if (bf16) RAICCL_FRONT(__nv_bfloat16, 0, 0, 8); else RAICCL_FRONT(float, 0, 0, 8);
+  } else if (E <= 16) {
+    if (bf16) RAICCL_FRONT(__nv_bfloat16, 0, 0, 16); else RAICCL_FRONT(float, 0, 0, 16);
+  } else if (E <= 64) {
+    if (bf16) RAICCL_FRONT(__nv_bfloat16, 0, 0, 64); else RAICCL_FRONT(float, 0, 0, 64);
   }
 #undef RAICCL_FRONT
   return false;
