@@ -264,3 +264,13 @@ def test_randomized_trajectory_equivalence(backend, seed):
         if world.is_complete():
             break
     assert state.full_rebuild_count == 0 and binder.runtime_bfs_calls == 0
+
+
+def test_equivalence_runner_reports_zero_mismatches():
+    """The E1/E2/E3 runner over the six-topology corpus (one random truth each)."""
+    from revealaiccl_b200.bench import equivalence as eq
+
+    rep = eq.run(cases=1, seed=7)
+    assert rep["pass"] and rep["e1"]["tests"] > 6 * 16
+    for be in rep["backends"].values():
+        assert be["e2"]["tests"] > 0 and be["e3"]["tests"] > 0 and be["latency"]["compiled_ms"]["count"] > 0
