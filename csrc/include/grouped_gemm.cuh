@@ -63,7 +63,7 @@ __device__ __forceinline__ int find_segment(const int* prefix, int nseg, int til
   int lo = 0, hi = nseg - 1;
   while (lo < hi) {
     int mid = (lo + hi + 1) >> 1;
-    if (__ldg(prefix + mid) <= tile) lo = mid; else hi = mid - 1;
+    if (prefix[mid] <= tile) lo = mid; else hi = mid - 1;  // plain load: written by the previous launch
   }
   return lo;
 }
@@ -176,7 +176,6 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (p.trace != nullptr && threadIdx.x == 0) atomicMin(&p.trace->t_start, (unsigned long long)globaltimer_ns());
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
@@ -191,8 +190,13 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  // The prologue above touches only this CTA's shared memory and TMEM; the
+  // tile table, segments and A rows are the previous launch's outputs.
+  griddep_wait();
+  griddep_launch_dependents();
+  if (p.trace != nullptr && threadIdx.x == 0) atomicMin(&p.trace->t_start, (unsigned long long)globaltimer_ns());
 
-  const int total_tiles = __ldg(p.tile_prefix + p.num_segs);
+  const int total_tiles = p.tile_prefix[p.num_segs];
   const int nblocks = p.N / BN;
   const int kblocks = (p.K + C::BK - 1) / C::BK;
   const uint64_t lim = p.timeout_ns;
@@ -204,7 +208,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
       for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
         const int s = find_segment(p.tile_prefix, p.num_segs, t);
         const GemmSegment seg = p.segs[s];
-        const int local = t - __ldg(p.tile_prefix + s);
+        const int local = t - p.tile_prefix[s];
         const int mb = local / nblocks, nb = local % nblocks;
         const int arow = seg.a_row0 + mb * C::BM;
         const int brow = seg.expert * p.N + nb * BN;
@@ -264,7 +268,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
       const uint32_t acc_phase = (iter >> 1) & 1;
       const int s = find_segment(p.tile_prefix, p.num_segs, t);
       const GemmSegment seg = p.segs[s];
-      const int local = t - __ldg(p.tile_prefix + s);
+      const int local = t - p.tile_prefix[s];
       const int mb = local / nblocks, nb = local % nblocks;
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.status, kKernelId, lim)) break;
       tc_fence_after_sync();
@@ -299,7 +303,7 @@ inline void launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const Group
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_TOTAL);
     configured = true;
   }
-  kern<<<grid, 192, C::SMEM_TOTAL, stream>>>(ta, tb, p);
+  launch_with_pdl(kern, dim3(grid), dim3(192), C::SMEM_TOTAL, stream, p.pdl != 0, ta, tb, p);
 }
 
 template <bool TF32, Act ACT, typename OutT>

@@ -66,7 +66,6 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  if (p.trace != nullptr && threadIdx.x == 0) atomicMin(&p.trace->t_start, (unsigned long long)globaltimer_ns());
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
@@ -81,8 +80,13 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
   cluster_sync_all();  // barrier inits and the TMEM allocation are visible to the partner
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  // Prologue: shared memory, TMEM and the partner only; the tile table,
+  // segments and A rows come from the previous launch.
+  griddep_wait();
+  griddep_launch_dependents();
+  if (p.trace != nullptr && threadIdx.x == 0) atomicMin(&p.trace->t_start, (unsigned long long)globaltimer_ns());
 
-  const int total_tiles = __ldg(p.tile_prefix + p.num_segs);
+  const int total_tiles = p.tile_prefix[p.num_segs];
   const int nblocks = p.N / BN;
   const int kblocks = (p.K + C::BK - 1) / C::BK;
   const uint64_t lim = p.timeout_ns;
@@ -94,7 +98,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
       for (int t = pair; t < total_tiles; t += npairs) {
         const int s = find_segment(p.tile_prefix, p.num_segs, t);
         const GemmSegment seg = p.segs[s];
-        const int local = t - __ldg(p.tile_prefix + s);
+        const int local = t - p.tile_prefix[s];
         const int mb = local / nblocks, nb = local % nblocks;
         const int arow = seg.a_row0 + mb * 2 * C::BM + (int)rank * C::BM;
         const int brow = seg.expert * p.N + nb * BN + (int)rank * C::BNH;
@@ -159,7 +163,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
       const uint32_t acc_phase = (iter >> 1) & 1;
       const int s = find_segment(p.tile_prefix, p.num_segs, t);
       const GemmSegment seg = p.segs[s];
-      const int local = t - __ldg(p.tile_prefix + s);
+      const int local = t - p.tile_prefix[s];
       const int mb = local / nblocks, nb = local % nblocks;
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.status, kKernelId, lim)) break;
       tc_fence_after_sync();
@@ -192,7 +196,7 @@ inline void launch_one_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
     configured = true;
   }
   const int g = grid & ~1;  // whole pairs
-  kern<<<g < 2 ? 2 : g, 192, C::SMEM_TOTAL, stream>>>(ta, tb, p);
+  launch_with_pdl(kern, dim3(g < 2 ? 2 : g), dim3(192), C::SMEM_TOTAL, stream, p.pdl != 0, ta, tb, p);
 }
 
 template <bool TF32, Act ACT, typename OutT>

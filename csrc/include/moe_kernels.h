@@ -57,6 +57,13 @@ struct PlanParams {
   unsigned long long timeout_ns;
   DeviceStatus* status;
   TraceSlot* trace;
+  // Optional GEMM tile tables ([E_slot * W + 1] each): prefix[s] counts the
+  // tiles of segments < s, a segment holding ceil(rows / bm) * nblocks tiles.
+  // Both are skipped when prefix1 is null.
+  int32_t* prefix1;
+  int32_t* prefix2;
+  int nblocks1, nblocks2;
+  int bm1, bm2;
 };
 
 struct ReturnMetaParams {
@@ -66,14 +73,10 @@ struct ReturnMetaParams {
   const GemmSegment* segs;
   DeviceStatus* status;
   TraceSlot* trace;
-};
-
-struct SignalParams {
-  MoEDims dims;
-  SymLayout layout;
-  PeerBases peers;
+  // Optional return-signal handoff (see CombineParams::ret_sync): when set,
+  // the grid's last CTA reports the metadata part done.
   const unsigned long long* epoch;
-  TraceSlot* trace;
+  unsigned long long* ret_sync;
 };
 
 struct CombineParams {
@@ -85,6 +88,14 @@ struct CombineParams {
   unsigned long long timeout_ns;
   DeviceStatus* status;
   TraceSlot* trace;
+  // Return-signal handoff words, zero at creation and only ever increased:
+  // [0] the epoch of the last call whose combine elected its reporting CTA,
+  // [1] return parts reported (two per call: the metadata grid and the
+  //     combine, which follows GEMM-2 in stream order), [2] metadata CTAs
+  //     finished.  The second part of a call to report publishes this rank's
+  //     return signal, so neither part waits for the other.  Null: the
+  //     combine publishes the signal itself.
+  unsigned long long* ret_sync;
 };
 
 struct BarrierParams {
@@ -159,10 +170,9 @@ void launch_checksum_base(const long long* token_ids, const long long* digest, c
                           int chunks, int rank, int n, long long* base, cudaStream_t s);
 void launch_router(const RouterParams& p, bool bf16, cudaStream_t s);
 void launch_dispatch(const DispatchParams& p, bool bf16, int grid, cudaStream_t s);
-void launch_expert_plan(const PlanParams& p, cudaStream_t s);
+void launch_expert_plan(const PlanParams& p, cudaStream_t s, bool pdl = false);
 void launch_return_meta(const ReturnMetaParams& p, int grid, cudaStream_t s);
-void launch_return_signal(const SignalParams& p, cudaStream_t s);
-void launch_combine(const CombineParams& p, bool bf16, int grid, cudaStream_t s);
+void launch_combine(const CombineParams& p, bool bf16, int grid, cudaStream_t s, bool pdl = false);
 void launch_layer_reset(int* sent_base, int experts, int* desc_counts, int n_desc, int* done_counter,
                         unsigned long long* epoch, TraceSlot* trace, int n_trace, int* chunk_words,
                         int n_chunk_words, cudaStream_t s);

@@ -10,6 +10,7 @@
 // code in a caller-provided status word and returns false, so a missing peer
 // signal or a protocol bug ends the kernel instead of hanging the GPU.
 #pragma once
+#include <utility>
 
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -49,6 +50,34 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 // Folds this CTA's start / end time into a launch trace slot (thread 0 only).
 // The destructor runs on every return path of the kernel.
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization may start (and run its
+// prologue) before the previous kernel in the stream has finished;
+// griddep_wait() blocks until that kernel has completed and its memory is
+// visible, so every read of its outputs (and every write the previous
+// kernel could still read) must come after it.  Without the attribute both
+// instructions are no-ops.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... Params, typename... Args>
+inline __host__ cudaError_t launch_with_pdl(void (*kern)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                   bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 struct TraceScope {
   TraceSlot* slot;
   __device__ __forceinline__ explicit TraceScope(TraceSlot* s) : slot(s) {

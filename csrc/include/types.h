@@ -65,6 +65,7 @@ struct GroupedGemmParams {
   unsigned long long timeout_ns;
   TraceSlot* trace;          // launch trace slot or nullptr
   int pair;                  // 1: CTA-pair kernel (256-row tiles in tile_prefix), 0: one CTA per 128-row tile
+  int pdl;                   // 1: launch as a programmatic dependent of the previous kernel in the stream
 };
 
 }  // namespace raiccl

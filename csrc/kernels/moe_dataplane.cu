@@ -163,6 +163,8 @@ __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(Dispatch
 // then emit one grouped-GEMM segment per (local expert slot, source).
 // ---------------------------------------------------------------------------
 __global__ void moe_expert_plan_kernel(PlanParams p) {
+  griddep_wait();  // programmatic dependent of the front end (no-op otherwise)
+  griddep_launch_dependents();
   TraceScope trace_scope(p.trace);
   const MoEDims& d = p.dims;
   const uint8_t* mine = (const uint8_t*)p.peers.base[d.rank];
@@ -177,7 +179,15 @@ __global__ void moe_expert_plan_kernel(PlanParams p) {
   }
   __syncthreads();
   const int* counts = (const int*)(mine + p.layout.recv_count);
-  for (int s = threadIdx.x; s < d.expert_slots * d.world; s += blockDim.x) {
+  // Each thread owns a contiguous run of segments, so the GEMM tile tables
+  // (exclusive prefix of ceil(rows / bm) * nblocks per segment, for both
+  // GEMMs) come out of one block scan in this same launch.
+  const int S = d.expert_slots * d.world;
+  const int per = (S + blockDim.x - 1) / blockDim.x;
+  const int s0 = threadIdx.x * per;
+  const int s1 = min(S, s0 + per);
+  int local1 = 0, local2 = 0;
+  for (int s = s0; s < s1; ++s) {
     int rows = 0;
     if (s_ok) {
       for (int q = 0; q < d.n_desc; ++q) rows += counts[(long long)s * d.n_desc + q];
@@ -192,7 +202,52 @@ __global__ void moe_expert_plan_kernel(PlanParams p) {
     seg.pad0 = seg.pad1 = seg.pad2 = 0;
     p.segs[s] = seg;
     p.rows_out[s] = rows;
+    if (p.prefix1 != nullptr) {
+      local1 += ((rows + p.bm1 - 1) / p.bm1) * p.nblocks1;
+      local2 += ((rows + p.bm2 - 1) / p.bm2) * p.nblocks2;
+    }
   }
+  if (p.prefix1 == nullptr) return;
+  __shared__ int s_scan1[256], s_scan2[256];
+  s_scan1[threadIdx.x] = local1;
+  s_scan2[threadIdx.x] = local2;
+  __syncthreads();
+  for (int off = 1; off < (int)blockDim.x; off <<= 1) {
+    const int v1 = threadIdx.x >= off ? s_scan1[threadIdx.x - off] : 0;
+    const int v2 = threadIdx.x >= off ? s_scan2[threadIdx.x - off] : 0;
+    __syncthreads();
+    s_scan1[threadIdx.x] += v1;
+    s_scan2[threadIdx.x] += v2;
+    __syncthreads();
+  }
+  int run1 = s_scan1[threadIdx.x] - local1, run2 = s_scan2[threadIdx.x] - local2;
+  for (int s = s0; s < s1; ++s) {
+    p.prefix1[s] = run1;
+    p.prefix2[s] = run2;
+    const int rows = p.rows_out[s];
+    run1 += ((rows + p.bm1 - 1) / p.bm1) * p.nblocks1;
+    run2 += ((rows + p.bm2 - 1) / p.bm2) * p.nblocks2;
+  }
+  if (threadIdx.x == blockDim.x - 1) {
+    p.prefix1[S] = s_scan1[threadIdx.x];
+    p.prefix2[S] = s_scan2[threadIdx.x];
+  }
+}
+
+// Publish this rank's return sequence number at every source rank.
+__device__ void publish_return_signal(const MoEDims& d, const SymLayout& L, const PeerBases& P,
+                                      unsigned long long epoch) {
+  __threadfence_system();
+  for (int r = 0; r < d.world; ++r)
+    st_release_sys_u64((uint64_t*)((uint8_t*)P.base[r] + L.ret_flag) + d.rank, epoch);
+}
+
+// One of the two return parts of a call is complete (its stores fenced at
+// system scope): the second to report publishes the return signal.
+__device__ void return_part_done(const MoEDims& d, const SymLayout& L, const PeerBases& P,
+                                 unsigned long long epoch, unsigned long long* ret_sync) {
+  __threadfence_system();
+  if (atomicAdd(ret_sync + 1, 1ULL) & 1ULL) publish_return_signal(d, L, P, epoch);
 }
 
 // Return identity rows to the token's source rank, at row (position * k + j)
@@ -228,32 +283,41 @@ __global__ void moe_return_meta_kernel(ReturnMetaParams p) {
     for (int i = 0; i < 7; ++i) out[i] = (long long)f[i];
     out[7] = (long long)cs;
   }
-}
-
-// One thread: make this rank's return stores visible, then publish its return
-// sequence number at every source rank.
-__global__ void moe_return_signal_kernel(SignalParams p) {
-  TraceScope trace_scope(p.trace);
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  const MoEDims& d = p.dims;
-  const unsigned long long epoch = *p.epoch;
-  __threadfence_system();
-  for (int r = 0; r < d.world; ++r)
-    st_release_sys_u64((uint64_t*)((uint8_t*)p.peers.base[r] + p.layout.ret_flag) + d.rank, epoch);
+  if (p.ret_sync == nullptr) return;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    // every call adds gridDim.x, so the CTA completing a multiple is the last
+    if ((atomicAdd(p.ret_sync + 2, 1ULL) + 1ULL) % gridDim.x == 0)
+      return_part_done(d, p.layout, p.peers, *p.epoch, p.ret_sync);
+  }
 }
 
 // Combine: wait (bounded) for every expert rank's return signal, then
 // out[t] = sum_j ret_out[t * k + j] (rows already carry their gate weight).
 template <typename OutT>
 __global__ void moe_combine_kernel(CombineParams p) {
+  griddep_wait();  // the return rows of GEMM-2 (previous launch) are complete and visible
   TraceScope trace_scope(p.trace);
   const MoEDims& d = p.dims;
   const uint8_t* mine = (const uint8_t*)p.peers.base[d.rank];
   __shared__ int s_ok;
   const unsigned long long epoch = *p.epoch;
-  if (threadIdx.x == 0) s_ok = 1;
+  if (threadIdx.x == 0) {
+    s_ok = 1;
+    // Whichever CTA runs first reports the return rows (written by the
+    // GEMM-2 launch before this one), so the signal never waits on the
+    // scheduling of a particular CTA.
+    if (p.ret_sync == nullptr) {
+      if (blockIdx.x == 0) publish_return_signal(d, p.layout, p.peers, epoch);
+    } else if (atomicMax(p.ret_sync, epoch) < epoch) {
+      return_part_done(d, p.layout, p.peers, epoch, p.ret_sync);
+    }
+  }
   __syncthreads();
-  if (threadIdx.x < d.world) {
+  // This rank's own rows come from the GEMM-2 launch that precedes this one
+  // in the stream; only the other ranks' signals need waiting for.
+  if (threadIdx.x < d.world && threadIdx.x != d.rank) {
     const uint64_t* f = (const uint64_t*)(mine + p.layout.ret_flag) + threadIdx.x;
     if (!wait_flag_geq_sys(f, epoch, p.status, kTimeoutPeerSignal, 50, threadIdx.x, p.timeout_ns))
       s_ok = 0;
@@ -432,24 +496,20 @@ void launch_dispatch(const DispatchParams& p, bool bf16, int grid, cudaStream_t 
   else moe_dispatch_kernel<float><<<grid, kDispatchThreads, 0, s>>>(p);
 }
 
-void launch_expert_plan(const PlanParams& p, cudaStream_t s) {
-  moe_expert_plan_kernel<<<1, 256, 0, s>>>(p);
+void launch_expert_plan(const PlanParams& p, cudaStream_t s, bool pdl) {
+  launch_with_pdl(moe_expert_plan_kernel, dim3(1), dim3(256), 0, s, pdl, p);
 }
 
 void launch_return_meta(const ReturnMetaParams& p, int grid, cudaStream_t s) {
   moe_return_meta_kernel<<<grid, 256, 0, s>>>(p);
 }
 
-void launch_return_signal(const SignalParams& p, cudaStream_t s) {
-  moe_return_signal_kernel<<<1, 32, 0, s>>>(p);
-}
-
-void launch_combine(const CombineParams& p, bool bf16, int grid, cudaStream_t s) {
+void launch_combine(const CombineParams& p, bool bf16, int grid, cudaStream_t s, bool pdl) {
   // enough warps for one token row each (capped at 8 CTAs per SM)
   const int rows_grid = (p.dims.tokens + 7) / 8;
   const int g = std::max(1, std::min(rows_grid, 8 * grid));
-  if (bf16) moe_combine_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(p);
-  else moe_combine_kernel<float><<<g, 256, 0, s>>>(p);
+  if (bf16) launch_with_pdl(moe_combine_kernel<__nv_bfloat16>, dim3(g), dim3(256), 0, s, pdl, p);
+  else launch_with_pdl(moe_combine_kernel<float>, dim3(g), dim3(256), 0, s, pdl, p);
 }
 
 void launch_layer_reset(int* sent_base, int experts, int* desc_counts, int n_desc, int* done_counter,

@@ -104,6 +104,7 @@ class MoELayerRunner {
     bn2_ = geti(ints, "bn2");
     {
       // CTA-pair GEMM kernels (256 x BN tiles on clusters of two SMs) for BN >= 64
+      pdl_ = !ints.contains("pdl") || geti(ints, "pdl") != 0;
       const bool allow = !ints.contains("gemm_pair") || geti(ints, "gemm_pair") != 0;
       pair1_ = allow && bn1_ >= 64;
       pair2_ = allow && bn2_ >= 64;
@@ -149,6 +150,8 @@ class MoELayerRunner {
     ev_ctl_.resize(d.n_desc);
     for (auto& e : ev_ctl_) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
     ck(cudaEventCreateWithFlags(&ev_disp_done_, cudaEventDisableTiming), "cudaEventCreate");
+    ck(cudaEventCreateWithFlags(&ev_plan_, cudaEventDisableTiming), "cudaEventCreate");
+    ck(cudaEventCreateWithFlags(&ev_retmeta_, cudaEventDisableTiming), "cudaEventCreate");
     // dispatch chain: its own stream, so trigger q+1's control overlaps dispatch q
     ck(cudaStreamCreateWithFlags(&disp_, cudaStreamNonBlocking), "cudaStreamCreate");
   }
@@ -161,6 +164,8 @@ class MoELayerRunner {
     for (auto& e : ev_chunk_) cudaEventDestroy(e);
     for (auto& e : ev_ctl_) cudaEventDestroy(e);
     if (ev_disp_done_) cudaEventDestroy(ev_disp_done_);
+    if (ev_plan_) cudaEventDestroy(ev_plan_);
+    if (ev_retmeta_) cudaEventDestroy(ev_retmeta_);
     if (ev_start_) cudaEventDestroy(ev_start_);
     if (disp_) cudaStreamDestroy(disp_);
   }
@@ -389,13 +394,40 @@ class MoELayerRunner {
     pp.timeout_ns = timeout_ns_;
     pp.status = status;
     pp.trace = trace_slot("expert_plan", -1);
-    raiccl::launch_expert_plan(pp, comm_);
+    // the plan also writes both GEMMs' tile tables
+    const int S = d.expert_slots * d.world;
+    int* prefix1 = ptr<int>(t, "prefix1");
+    int* prefix2 = ptr<int>(t, "prefix2");
+    pp.prefix1 = prefix1;
+    pp.prefix2 = prefix2;
+    pp.nblocks1 = n1_ / bn1_;
+    pp.nblocks2 = d.out_dim / bn2_;
+    pp.bm1 = pair1_ ? 256 : 128;
+    pp.bm2 = pair2_ ? 256 : 128;
+    raiccl::launch_expert_plan(pp, comm_, pdl_);
     ++launches;
 
-    const int S = d.expert_slots * d.world;
+    // Return metadata depends only on the plan: it runs on the dispatch
+    // stream beside the two GEMMs; whichever of it and the combine reports
+    // last publishes the return signal.
+    ck(cudaEventRecord(ev_plan_, comm_), "cudaEventRecord");
+    ck(cudaStreamWaitEvent(disp_, ev_plan_, 0), "cudaStreamWaitEvent");
+    raiccl::ReturnMetaParams rm{};
+    rm.dims = d;
+    rm.layout = layout_;
+    rm.peers = peers_;
+    rm.segs = segs;
+    rm.status = status;
+    rm.trace = trace_slot("return_meta", -1);
+    auto* ret_sync = reinterpret_cast<unsigned long long*>(ptr<int64_t>(t, "ret_sync"));
+    rm.epoch = epoch;
+    rm.ret_sync = ret_sync;
+    raiccl::launch_return_meta(rm, grid_sms_, disp_);
+    ck(cudaEventRecord(ev_retmeta_, disp_), "cudaEventRecord");
+    ++launches;
+
     raiccl::GroupedGemmParams g1{};
     g1.segs = segs;
-    int* prefix1 = ptr<int>(t, "prefix1");
     g1.tile_prefix = prefix1;
     g1.num_segs = S;
     g1.N = n1_;
@@ -408,14 +440,13 @@ class MoELayerRunner {
     g1.status = status;
     g1.timeout_ns = timeout_ns_;
     g1.pair = pair1_ ? 1 : 0;
-    raiccl::launch_tile_plan(segs, S, n1_ / bn1_, prefix1, comm_, trace_slot("tile_plan", 1), pair1_ ? 256 : 128);
+    g1.pdl = pdl_ ? 1 : 0;
     g1.trace = trace_slot("gemm1", -1);
     raiccl::launch_grouped_gemm(!feat_bf16_, feat_bf16_, act1_, bn1_, ta1_, tb1_, g1, grid_sms_, comm_);
-    launches += 2;
+    ++launches;
 
     raiccl::GroupedGemmParams g2{};
     g2.segs = segs;
-    int* prefix2 = ptr<int>(t, "prefix2");
     g2.tile_prefix = prefix2;
     g2.num_segs = S;
     g2.N = d.out_dim;
@@ -428,27 +459,11 @@ class MoELayerRunner {
     g2.status = status;
     g2.timeout_ns = timeout_ns_;
     g2.pair = pair2_ ? 1 : 0;
-    raiccl::launch_tile_plan(segs, S, d.out_dim / bn2_, prefix2, comm_, trace_slot("tile_plan", 2),
-                             pair2_ ? 256 : 128);
+    g2.pdl = pdl_ ? 1 : 0;
     g2.trace = trace_slot("gemm2_return", -1);
     raiccl::launch_grouped_gemm(!feat_bf16_, out_bf16_, 0, bn2_, ta2_, tb2_, g2, grid_sms_, comm_);
-    launches += 2;
+    ++launches;
 
-    raiccl::ReturnMetaParams rm{};
-    rm.dims = d;
-    rm.layout = layout_;
-    rm.peers = peers_;
-    rm.segs = segs;
-    rm.status = status;
-    rm.trace = trace_slot("return_meta", -1);
-    raiccl::launch_return_meta(rm, grid_sms_, comm_);
-    raiccl::SignalParams sp{};
-    sp.dims = d;
-    sp.layout = layout_;
-    sp.peers = peers_;
-    sp.epoch = epoch;
-    sp.trace = trace_slot("return_signal", -1);
-    raiccl::launch_return_signal(sp, comm_);
     raiccl::CombineParams cb{};
     cb.dims = d;
     cb.layout = layout_;
@@ -458,8 +473,11 @@ class MoELayerRunner {
     cb.timeout_ns = timeout_ns_;
     cb.status = status;
     cb.trace = trace_slot("combine", -1);
-    raiccl::launch_combine(cb, out_bf16_, grid_sms_, comm_);
-    launches += 3;
+    cb.ret_sync = ret_sync;
+    raiccl::launch_combine(cb, out_bf16_, grid_sms_, comm_, pdl_);
+    ++launches;
+    // join the dispatch stream (the metadata grid finished long before)
+    ck(cudaStreamWaitEvent(comm_, ev_retmeta_, 0), "cudaStreamWaitEvent");
     ck(cudaGetLastError(), "MoE layer launch");
     return launches;
   }
@@ -555,6 +573,7 @@ class MoELayerRunner {
   raiccl::PeerBases peers_{};
   int partial_ = 0, ffn_ = 0, n1_ = 0, act1_ = 0, bn1_ = 0, bn2_ = 0;
   bool pair1_ = false, pair2_ = false;  // GEMM 1 / 2 on the CTA-pair kernel
+  bool pdl_ = true;  // plan, GEMMs and combine as programmatic dependents of their predecessors
   int max_cands_ = 0, log_stride_ = 0, max_ctl_tokens_ = 0, grid_sms_ = 148;
   bool control_serial_ = false;  // run the CTA control kernel even where the single-warp one fits
   bool feat_bf16_ = false, out_bf16_ = false;
@@ -576,7 +595,7 @@ class MoELayerRunner {
     trace_labels_.emplace_back(kind, arg);
     return trace_ + (trace_labels_.size() - 1);
   }
-  cudaEvent_t ev_start_ = nullptr, ev_disp_done_ = nullptr;
+  cudaEvent_t ev_start_ = nullptr, ev_disp_done_ = nullptr, ev_plan_ = nullptr, ev_retmeta_ = nullptr;
   std::vector<cudaEvent_t> ev_chunk_, ev_ctl_;
   cudaGraph_t graph_[2] = {nullptr, nullptr};
   cudaGraphExec_t exec_[2] = {nullptr, nullptr};

@@ -19,8 +19,8 @@ from pathlib import Path
 from typing import Any, Iterable, Mapping, Sequence
 
 # Chrome-trace thread rows: one per pipeline role
-_ROWS = {"layer_reset": 0, "router": 1, "control": 2, "dispatch": 3, "expert_plan": 4, "tile_plan": 4,
-         "gemm1": 5, "gemm2_return": 5, "return_meta": 6, "return_signal": 6, "combine": 7}
+_ROWS = {"layer_reset": 0, "router": 1, "control": 2, "dispatch": 3, "expert_plan": 4,
+         "gemm1": 5, "gemm2_return": 5, "return_meta": 6, "combine": 7}
 
 
 def label(ev: Mapping[str, Any], arm: str | None = None) -> str:

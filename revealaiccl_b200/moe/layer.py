@@ -55,7 +55,7 @@ class ProgressiveMoELayer:
                  world: int | None = None, rank: int | None = None, group=None,
                  timeout_s: float = 10.0, seed: int = 0, control_topology=None,
                  control_path: str = "auto", trace: bool = False, frontend: str = "persistent",
-                 gemm_pair: bool = True) -> None:
+                 gemm_pair: bool = True, pdl: bool = True) -> None:
         self.cfg = cfg
         if world is None:
             world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -139,6 +139,7 @@ class ProgressiveMoELayer:
             "control_serial": {"auto": 0, "serial": 1}[control_path],
             "frontend": {"steps": 0, "persistent": 1}[frontend],
             "gemm_pair": int(bool(gemm_pair)),
+            "pdl": int(bool(pdl)),
         }
         self.layout = self._k.sym_layout(ints)
         self.channel = PeerChannel(self.layout["total"], dev, group=group)
@@ -181,6 +182,8 @@ class ProgressiveMoELayer:
             "desc_ready": torch.zeros(cfg.n_desc, dtype=torch.int64, device=dev),
             "epoch": self.epoch, "status": self.status,
             "bar_counter": torch.zeros(1, dtype=torch.int64, device=dev),
+            # return-signal handoff: [elected epoch, parts reported, metadata CTAs done, pad]
+            "ret_sync": torch.zeros(4, dtype=torch.int64, device=dev),
             "segs": self.segs, "rows_out": self.rows_out,
             "prefix1": torch.zeros(nseg + 1, dtype=torch.int32, device=dev),
             "prefix2": torch.zeros(nseg + 1, dtype=torch.int32, device=dev),

@@ -136,7 +136,7 @@ def test_graph_capture_replay_repeated_calls():
         layer.forward("early")
         ref = layer.out.clone()
         n = layer.capture("early")
-        assert n >= 9  # reset, front end (or its step kernels), plan, 2 x (tile plan, GEMM), return, combine
+        assert n >= 7  # reset, front end (or its step kernels), plan + tile tables, return meta, 2 GEMMs, combine
         for _ in range(3):
             layer.replay()
         torch.cuda.synchronize()
@@ -223,3 +223,32 @@ def test_cta_pair_gemms_leave_layer_output_unchanged():
         finally:
             layer.close()
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.gpu
+def test_programmatic_dependent_launch_matches_plain_launches():
+    """Plan, GEMMs and combine launched as programmatic dependents give the same
+    output as ordinary stream-ordered launches, over repeated calls and graph
+    replay (the return-signal handoff counters stay in step)."""
+    from revealaiccl_b200.moe.config import preset
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    outs = {}
+    for pdl in (True, False):
+        layer = ProgressiveMoELayer(preset("full_tf32").with_overrides(tokens_per_rank=2048, chunk_sizes=(256,) * 8),
+                                    timeout_s=5.0, pdl=pdl)
+        try:
+            for arm in ("early", "delayed", "early"):
+                layer.forward(arm)
+                assert layer.verify()["pass"], (pdl, arm)
+            layer.capture("early")
+            for _ in range(3):
+                layer.replay()
+            assert layer.verify()["pass"]
+            sync = layer.tensors["ret_sync"].cpu().tolist()
+            calls = int(layer.tensors["epoch"].cpu().item())
+            assert sync[0] == calls and sync[1] == 2 * calls  # one election and two parts per call
+            outs[pdl] = layer.out.clone()
+        finally:
+            layer.close()
+    assert torch.equal(outs[True], outs[False])
