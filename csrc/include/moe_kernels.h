@@ -173,6 +173,8 @@ void launch_dispatch(const DispatchParams& p, bool bf16, int grid, cudaStream_t 
 void launch_expert_plan(const PlanParams& p, cudaStream_t s, bool pdl = false);
 void launch_return_meta(const ReturnMetaParams& p, int grid, cudaStream_t s);
 void launch_combine(const CombineParams& p, bool bf16, int grid, cudaStream_t s, bool pdl = false);
+void launch_host_flag_signal(unsigned long long* flag, unsigned long long value, unsigned long long delay_ns,
+                             cudaStream_t s);
 void launch_layer_reset(int* sent_base, int experts, int* desc_counts, int n_desc, int* done_counter,
                         unsigned long long* epoch, TraceSlot* trace, int n_trace, int* chunk_words,
                         int n_chunk_words, cudaStream_t s);

@@ -429,6 +429,20 @@ __global__ void moe_layer_reset_kernel(int* sent_base, int experts, int* desc_co
   for (int i = threadIdx.x; i < n_desc; i += blockDim.x) done_counter[i] = 0;
 }
 
+// One thread: hold the stream for delay_ns (a fixed-length busy loop on
+// %globaltimer, capped at 10 ms), then publish value to a host-mapped word with
+// a system-scope release — the device side of the event bridge's flag slots.
+__global__ void host_flag_signal_kernel(unsigned long long* flag, unsigned long long value,
+                                        unsigned long long delay_ns) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  if (delay_ns > 10000000ULL) delay_ns = 10000000ULL;
+  const unsigned long long t0 = globaltimer_ns();
+  while (globaltimer_ns() - t0 < delay_ns) {
+  }
+  __threadfence_system();
+  st_release_sys_u64(reinterpret_cast<uint64_t*>(flag), value);
+}
+
 // ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
@@ -510,6 +524,11 @@ void launch_combine(const CombineParams& p, bool bf16, int grid, cudaStream_t s,
   const int g = std::max(1, std::min(rows_grid, 8 * grid));
   if (bf16) launch_with_pdl(moe_combine_kernel<__nv_bfloat16>, dim3(g), dim3(256), 0, s, pdl, p);
   else launch_with_pdl(moe_combine_kernel<float>, dim3(g), dim3(256), 0, s, pdl, p);
+}
+
+void launch_host_flag_signal(unsigned long long* flag, unsigned long long value, unsigned long long delay_ns,
+                             cudaStream_t s) {
+  host_flag_signal_kernel<<<1, 32, 0, s>>>(flag, value, delay_ns);
 }
 
 void launch_layer_reset(int* sent_base, int experts, int* desc_counts, int n_desc, int* done_counter,

@@ -710,6 +710,16 @@ py::dict control_layout_py(py::dict dims) {
   return o;
 }
 
+// Publish `value` at a host-mapped 64-bit word (device pointer) from the
+// current stream after `delay_ns` of device time.
+void signal_host_flag(int64_t device_ptr, int64_t value, int64_t delay_ns) {
+  TORCH_CHECK(device_ptr != 0 && (device_ptr & 7) == 0, "signal_host_flag: 8-byte aligned device pointer");
+  TORCH_CHECK(delay_ns >= 0, "signal_host_flag: delay_ns >= 0");
+  raiccl::launch_host_flag_signal(reinterpret_cast<unsigned long long*>(device_ptr), (unsigned long long)value,
+                                  (unsigned long long)delay_ns, at::cuda::getCurrentCUDAStream());
+  ck(cudaGetLastError(), "signal_host_flag");
+}
+
 }  // namespace
 
 void register_moe(py::module_& m) {
@@ -736,4 +746,5 @@ void register_moe(py::module_& m) {
   m.def("sym_layout_bytes", &sym_layout_bytes, py::arg("ints"));
   m.def("sym_layout", &sym_layout, py::arg("ints"));
   m.def("control_layout", &control_layout_py, py::arg("dims"));
+  m.def("signal_host_flag", &signal_host_flag, py::arg("device_ptr"), py::arg("value"), py::arg("delay_ns") = 0);
 }
