@@ -7,15 +7,16 @@
 // the rows that source rank s sent to local expert e).  B is the stacked
 // expert weight tensor [E * N, K] (K-major, i.e. nn.Linear layout).
 //
-// Roles inside one CTA (192 threads, one CTA per SM):
+// Roles inside one CTA (kGemmThreads = 320 threads, one CTA per SM):
 //   warp 0      TMA producer: streams 128-row A tiles and BN-row B tiles into
 //               an S-stage shared-memory ring (128-byte swizzle, per-CTA loads).
 //   warp 1      owns the TMEM allocation; one elected lane issues tcgen05.mma
 //               (M=128, N=BN, fp32 accumulators in TMEM, two accumulator
 //               buffers so the epilogue of tile i overlaps the MMAs of i+1).
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator rows, bias, activation,
+//   warps 2..9  epilogue: tcgen05.ld of the accumulator rows, bias, activation,
 //               optional per-row scale, and vector stores to a local or
-//               NVLink-peer output pointer chosen per segment.
+//               NVLink-peer output pointer chosen per segment (two warps per
+//               row quarter, each on half of the tile's columns).
 //
 // Reference behaviour being replaced: the per-expert index_select / two
 // torch matmuls / index_copy_ loop of rlccl/transport/reference_full_moe.py:271-280.
@@ -68,12 +69,48 @@ __device__ __forceinline__ int find_segment(const int* prefix, int nseg, int til
   return lo;
 }
 
-// Epilogue of one accumulator row (one thread per row): bias, activation,
-// optional per-row scale, vector stores to the segment's output pointer at
-// the mapped row.  t_row: TMEM address of the row's first column.
+// Epilogue warps per CTA.  tcgen05.ld lets warp w read TMEM lanes
+// [32 (w % 4), 32 (w % 4) + 32), so warps w and w + 4 share a row quarter and
+// split its columns: two warps per SM sub-partition hide each other's TMEM-load,
+// bias and store latency.
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+
+__device__ __forceinline__ void store16(float* dst, const float (&v)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; j += 4) *(float4*)(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+}
+
+__device__ __forceinline__ void store16(__nv_bfloat16* dst, const float (&v)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; j += 8) {
+    uint4 w;
+    __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
+    __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
+    __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
+    __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+    w.x = *(uint32_t*)&h0; w.y = *(uint32_t*)&h1; w.z = *(uint32_t*)&h2; w.w = *(uint32_t*)&h3;
+    *(uint4*)(dst + j) = w;
+  }
+}
+
+// 16 bias values as four 16-byte loads (zeros without a bias).
+__device__ __forceinline__ void load_bias16(const float* bias, float (&b)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; j += 4) {
+    const float4 q = bias ? __ldg((const float4*)(bias + j)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    b[j] = q.x; b[j + 1] = q.y; b[j + 2] = q.z; b[j + 3] = q.w;
+  }
+}
+
+// Epilogue of one accumulator row (one thread per row) over the tile columns
+// [c0, c1) (multiples of 16; for SwiGLU, columns of the gate half): bias,
+// activation, optional per-row scale, vector stores to the segment's output
+// pointer at the mapped row.  Two 16-column TMEM loads are in flight per wait.
+// t_row: TMEM address of the row's first column.
 template <int BN, Act ACT, typename OutT>
 __device__ __forceinline__ void gemm_epilogue_row(const GroupedGemmParams& p, const GemmSegment& seg, int nb,
-                                                  int r_local, uint32_t t_row) {
+                                                  int r_local, uint32_t t_row, int c0, int c1) {
   const bool valid = r_local < seg.rows;
   const int arow = seg.a_row0 + r_local;
   long long orow = 0;
@@ -89,75 +126,61 @@ __device__ __forceinline__ void gemm_epilogue_row(const GroupedGemmParams& p, co
     constexpr int HALF = BN / 2;
     static_assert(HALF % 16 == 0, "SwiGLU tile needs BN multiple of 32");
 #pragma unroll 1
-    for (int c = 0; c < HALF; c += 16) {
+    for (int c = c0; c < c1; c += 16) {
       uint32_t g[16], u[16];
       tmem_ld16(t_row + c, g);
       tmem_ld16(t_row + HALF + c, u);
       tmem_ld_wait();
       if (valid) {
-        float v[16];
+        float bg[16], bu[16], v[16];
+        load_bias16(bias ? bias + c : nullptr, bg);
+        load_bias16(bias ? bias + HALF + c : nullptr, bu);
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          float gv = __uint_as_float(g[j]) + (bias ? __ldg(bias + c + j) : 0.f);
-          float uv = __uint_as_float(u[j]) + (bias ? __ldg(bias + HALF + c + j) : 0.f);
+          const float gv = __uint_as_float(g[j]) + bg[j];
+          const float uv = __uint_as_float(u[j]) + bu[j];
           v[j] = (gv / (1.f + __expf(-gv))) * uv * scale;
         }
-        OutT* dst = out + orow * p.ldo + nb * HALF + c;
-        if constexpr (sizeof(OutT) == 4) {
-#pragma unroll
-          for (int j = 0; j < 16; j += 4)
-            *(float4*)(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; j += 8) {
-            uint4 w;
-            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
-            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
-            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
-            w.x = *(uint32_t*)&h0; w.y = *(uint32_t*)&h1; w.z = *(uint32_t*)&h2; w.w = *(uint32_t*)&h3;
-            *(uint4*)(dst + j) = w;
-          }
-        }
+        store16(out + orow * p.ldo + nb * HALF + c, v);
       }
     }
   } else {
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      uint32_t r[16];
-      tmem_ld16(t_row + c, r);
+    for (int c = c0; c < c1; c += 32) {
+      const bool two = c + 16 < c1;
+      uint32_t r0[16], r1[16];
+      tmem_ld16(t_row + c, r0);
+      if (two) tmem_ld16(t_row + c + 16, r1);
       tmem_ld_wait();
       if (valid) {
-        float v[16];
+        float b[16], v[16];
+        load_bias16(bias ? bias + c : nullptr, b);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float x = __uint_as_float(r[j]) + (bias ? __ldg(bias + c + j) : 0.f);
-          v[j] = apply_act(x, ACT) * scale;
-        }
-        OutT* dst = out + orow * p.ldo + nb * BN + c;
-        if constexpr (sizeof(OutT) == 4) {
+        for (int j = 0; j < 16; ++j) v[j] = apply_act(__uint_as_float(r0[j]) + b[j], ACT) * scale;
+        store16(out + orow * p.ldo + nb * BN + c, v);
+        if (two) {
+          load_bias16(bias ? bias + c + 16 : nullptr, b);
 #pragma unroll
-          for (int j = 0; j < 16; j += 4)
-            *(float4*)(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; j += 8) {
-            uint4 w;
-            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
-            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
-            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
-            w.x = *(uint32_t*)&h0; w.y = *(uint32_t*)&h1; w.z = *(uint32_t*)&h2; w.w = *(uint32_t*)&h3;
-            *(uint4*)(dst + j) = w;
-          }
+          for (int j = 0; j < 16; ++j) v[j] = apply_act(__uint_as_float(r1[j]) + b[j], ACT) * scale;
+          store16(out + orow * p.ldo + nb * BN + c + 16, v);
         }
       }
     }
   }
 }
 
+// Column range [c0, c1) of epilogue warp `ew` (0..kEpiWarps-1) in a tile
+// whose epilogue covers `cols` columns: warps ew and ew + 4 split the range
+// at a 16-column boundary.
+__device__ __forceinline__ void epi_columns(int ew, int cols, int& c0, int& c1) {
+  const int chunks = cols / 16;
+  const int first = (chunks + 1) / 2;
+  if (ew < 4) { c0 = 0; c1 = first * 16; }
+  else { c0 = first * 16; c1 = cols; }
+}
+
 template <int BN, bool TF32, Act ACT, typename OutT>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b,
                     GroupedGemmParams p) {
@@ -179,7 +202,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
-    for (int a = 0; a < 2; ++a) { mbar_init(&tfull_bar[a], 1); mbar_init(&tempty_bar[a], 4); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tfull_bar[a], 1); mbar_init(&tempty_bar[a], kEpiWarps); }
     mbar_init(drain_bar, 1);
     fence_mbarrier_init();
     tma_prefetch_desc(&tmap_a);
@@ -262,6 +285,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
     const int row_in_tile = quarter * 32 + lane;
+    int c0, c1;
+    epi_columns(warp - 2, ACT == Act::kSwiGLU ? BN / 2 : BN, c0, c1);
     int iter = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++iter) {
       const int acc = iter & 1;
@@ -273,7 +298,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.status, kKernelId, lim)) break;
       tc_fence_after_sync();
       const int r_local = mb * C::BM + row_in_tile;
-      gemm_epilogue_row<BN, ACT, OutT>(p, seg, nb, r_local, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN);
+      gemm_epilogue_row<BN, ACT, OutT>(p, seg, nb, r_local, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
+                                       c0, c1);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -303,7 +329,7 @@ inline void launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const Group
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_TOTAL);
     configured = true;
   }
-  launch_with_pdl(kern, dim3(grid), dim3(192), C::SMEM_TOTAL, stream, p.pdl != 0, ta, tb, p);
+  launch_with_pdl(kern, dim3(grid), dim3(kGemmThreads), C::SMEM_TOTAL, stream, p.pdl != 0, ta, tb, p);
 }
 
 template <bool TF32, Act ACT, typename OutT>

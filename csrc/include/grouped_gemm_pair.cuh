@@ -46,7 +46,7 @@ struct PairCfg {
 };
 
 template <int BN, bool TF32, Act ACT, typename OutT>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                          GroupedGemmParams p) {
   using C = PairCfg<BN, TF32>;
@@ -69,7 +69,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
-    for (int a = 0; a < 2; ++a) { mbar_init(&tfull_bar[a], 1); mbar_init(&tempty_bar[a], 8); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tfull_bar[a], 1); mbar_init(&tempty_bar[a], 2 * kEpiWarps); }
     mbar_init(drain_bar, 1);
     fence_mbarrier_init();
     tma_prefetch_desc(&tmap_a);
@@ -157,6 +157,8 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
+    int c0, c1;
+    epi_columns(warp - 2, ACT == Act::kSwiGLU ? BN / 2 : BN, c0, c1);
     int iter = 0;
     for (int t = pair; t < total_tiles; t += npairs, ++iter) {
       const int acc = iter & 1;
@@ -168,7 +170,8 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.status, kKernelId, lim)) break;
       tc_fence_after_sync();
       const int r_local = mb * 2 * C::BM + (int)rank * C::BM + row_in_tile;
-      gemm_epilogue_row<BN, ACT, OutT>(p, seg, nb, r_local, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN);
+      gemm_epilogue_row<BN, ACT, OutT>(p, seg, nb, r_local, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
+                                       c0, c1);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
@@ -196,7 +199,7 @@ inline void launch_one_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
     configured = true;
   }
   const int g = grid & ~1;  // whole pairs
-  launch_with_pdl(kern, dim3(g < 2 ? 2 : g), dim3(192), C::SMEM_TOTAL, stream, p.pdl != 0, ta, tb, p);
+  launch_with_pdl(kern, dim3(g < 2 ? 2 : g), dim3(kGemmThreads), C::SMEM_TOTAL, stream, p.pdl != 0, ta, tb, p);
 }
 
 template <bool TF32, Act ACT, typename OutT>

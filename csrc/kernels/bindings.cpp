@@ -44,7 +44,8 @@ void grouped_gemm(torch::Tensor A, torch::Tensor B, torch::Tensor segs, torch::T
   TORCH_CHECK(status.numel() * status.element_size() >= (int64_t)sizeof(raiccl::DeviceStatus),
               "grouped_gemm: status buffer too small");
   if (bias) TORCH_CHECK(bias->scalar_type() == torch::kFloat32 && bias->is_contiguous() &&
-                            bias->numel() == B.size(0), "grouped_gemm: bias fp32 [E*N]");
+                            bias->numel() == B.size(0) && (reinterpret_cast<uintptr_t>(bias->data_ptr()) & 15) == 0,
+                        "grouped_gemm: bias fp32 [E*N], 16-byte aligned");
   if (row_map) TORCH_CHECK(row_map->scalar_type() == torch::kInt32 && row_map->numel() >= A.size(0),
                            "grouped_gemm: row_map int32 [rows_total]");
   if (row_scale) TORCH_CHECK(row_scale->scalar_type() == torch::kFloat32 &&
