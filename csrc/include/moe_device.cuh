@@ -59,6 +59,65 @@ __device__ __forceinline__ uint64_t mulmod_coeff(uint64_t v, uint64_t c) {
   return r >= kChecksumModulus ? r - kChecksumModulus : r;
 }
 
+// Row digest (sum_i splitmix64((i << 32) | w_i) mod 2^64 over the row's 32-bit
+// words, masked to 62 bits); moe_feature_digest_kernel computes the same value.
+// Token rows are read through L2 only (ld.global.cg) everywhere in the front
+// end: with streamed inputs they land while the launch is running, so the
+// non-coherent read-only path must not be used for them.
+
+// Digest terms of the four 32-bit words of 16-byte vector v of a row.
+__device__ __forceinline__ uint64_t digest_vec(uint4 x, int v) {
+  const uint64_t i = (uint64_t)(4 * v);
+  return splitmix64((i << 32) | x.x) + splitmix64(((i + 1) << 32) | x.y) + splitmix64(((i + 2) << 32) | x.z) +
+         splitmix64(((i + 3) << 32) | x.w);
+}
+
+// The digest of one row of nvec 16-byte vectors, by one warp; every lane returns it.
+__device__ __forceinline__ long long warp_row_digest(const uint4* row, int nvec) {
+  const int lane = threadIdx.x & 31;
+  constexpr int U = 8;  // loads in flight per lane
+  uint64_t acc = 0;
+  for (int v0 = 0; v0 < nvec; v0 += 32 * U) {
+    uint4 x[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int v = v0 + u * 32 + lane;
+      x[u] = v < nvec ? __ldcg(row + v) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int v = v0 + u * 32 + lane;
+      if (v < nvec) acc += digest_vec(x[u], v);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  return (long long)(acc & ((1ULL << 62) - 1));
+}
+
+// identity_checksum(token, src, 0, 0, chunk, chunk_offset, position, digest):
+// the destination and expert terms are added per assignment at dispatch time
+// (the checksum is linear in every field).
+__device__ __forceinline__ long long token_checksum_base(long long token_id, int rank, int chunk, int chunk_pos,
+                                                         int t, long long digest) {
+  const uint64_t fields[8] = {(uint64_t)token_id, (uint64_t)rank, 0, 0, (uint64_t)chunk, (uint64_t)chunk_pos,
+                              (uint64_t)t, (uint64_t)digest};
+  uint64_t acc = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc = addmod(acc, mulmod_coeff(fields[i], c_checksum_coeff[i]));
+  return (long long)acc;
+}
+
+// Where a router pass writes the per-token digests and checksum bases of the
+// rows it reads (tokens of router chunk `chunk`, which starts at chunk_first).
+struct DigestSink {
+  long long* digest;
+  long long* csbase;
+  const long long* token_ids;
+  int rank, chunk, chunk_first;
+  unsigned long long* red;  // shared scratch: 8 warps x NT partial sums
+};
+
 constexpr int kRouterUnroll = 8;
 constexpr int kDispatchMaxItems = 4096;
 constexpr int kMaxExperts = 256;
@@ -148,7 +207,7 @@ __device__ __forceinline__ void router_token(const RouterParams& p, const float*
 #pragma unroll
     for (int u = 0; u < kRouterUnroll; ++u) {
       const int base = base0 + (u * 32 + lane) * VEC;
-      xr[u] = base < D ? __ldg((const uint4*)(x + base)) : make_uint4(0, 0, 0, 0);
+      xr[u] = base < D ? __ldcg((const uint4*)(x + base)) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < kRouterUnroll; ++u) {
@@ -221,7 +280,7 @@ __host__ __device__ __forceinline__ bool router_group_ok(int experts, int hidden
 template <typename T, int NT, int EP>
 __device__ void router_group(const RouterParams& p, const float* bias, const float* chunk_bias,
                              const uint8_t* block_mask, int t_first, int nt, float* red, int* sel_counts,
-                             const uint4* wpre) {
+                             const uint4* wpre, const DigestSink* dsink = nullptr) {
   static_assert(NT * EP == 32, "one (token, expert) sum per lane");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int D = p.hidden, E = p.experts;
@@ -232,11 +291,19 @@ __device__ void router_group(const RouterParams& p, const float* bias, const flo
   float v[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = 0.f;
+  uint64_t dg[NT];  // digest partial sums of the group's rows (with a sink only)
+#pragma unroll
+  for (int j = 0; j < NT; ++j) dg[j] = 0;
   for (int vi = warp * vpw + lane; vi < (warp + 1) * vpw; vi += 32) {
     uint4 x[NT];
 #pragma unroll
     for (int j = 0; j < NT; ++j)
-      x[j] = j < nt ? __ldg((const uint4*)(tok + (long long)(t_first + j) * D) + vi) : make_uint4(0, 0, 0, 0);
+      x[j] = j < nt ? __ldcg((const uint4*)(tok + (long long)(t_first + j) * D) + vi) : make_uint4(0, 0, 0, 0);
+    if (dsink != nullptr) {
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+        if (j < nt) dg[j] += digest_vec(x[j], vi);
+    }
 #pragma unroll
     for (int e = 0; e < EP; ++e) {
       if (e < E) {
@@ -255,7 +322,26 @@ __device__ void router_group(const RouterParams& p, const float* bias, const flo
   }
   warp_transpose_reduce32(v);
   red[warp * 32 + lane] = v[0];
+  if (dsink != nullptr) {
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      uint64_t a = dg[j];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0) dsink->red[warp * NT + j] = a;
+    }
+  }
   __syncthreads();
+  if (dsink != nullptr && warp == 1 && lane < nt) {  // warp 0 runs the top-k below
+    uint64_t a = 0;
+#pragma unroll
+    for (int w8 = 0; w8 < 8; ++w8) a += dsink->red[w8 * NT + lane];
+    const long long dgt = (long long)(a & ((1ULL << 62) - 1));
+    const int t = t_first + lane;
+    dsink->digest[t] = dgt;
+    dsink->csbase[t] = token_checksum_base(dsink->token_ids[t], dsink->rank, dsink->chunk, t - dsink->chunk_first,
+                                           t, dgt);
+  }
   if (warp == 0) {
     float tot = 0.f;
 #pragma unroll
@@ -287,7 +373,7 @@ __device__ void router_group(const RouterParams& p, const float* bias, const flo
 // ---------------------------------------------------------------------------
 template <typename T>
 __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, const int* base_e, int* hist, int* run,
-                              int* item_pos, const int* s_coff, int nc) {
+                              int* item_pos, const int* s_coff, int nc, bool streamed = false) {
   const MoEDims& d = p.dims;
   const int k = d.top_k;
   const int E = d.experts;
@@ -344,7 +430,9 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int v = v0 + u * 32 + lane;
-        if (v < vec_per_row) rr[u] = __ldg(src + v);
+        // rows streamed in during the launch are read through L2 only; resident
+        // rows through the read-only path (the second choice of a token hits L1)
+        if (v < vec_per_row) rr[u] = streamed ? __ldcg(src + v) : __ldg(src + v);
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {

@@ -156,6 +156,14 @@ struct FrontendParams {
   TraceSlot* phase_trace;   // [C + 2 n_desc]: router c, control q, dispatch q; or nullptr
   TraceSlot* trace;         // the launch
   unsigned long long* cta_clock;  // [grid, 64] per-CTA %globaltimer stamps, or nullptr
+  // Per-token feature digests and checksum bases written by the workers while
+  // they route (null: precomputed by the digest / checksum-base kernels).
+  long long* digest_out;    // [T]
+  long long* csbase_out;    // [T]
+  // Streamed inputs: router chunk c is read only once tok_ready[c] or
+  // tok_ready_all has reached this call's epoch (null: tokens resident).
+  const unsigned long long* tok_ready;      // [C], written by the copy stream after chunk c's rows
+  const unsigned long long* tok_ready_all;  // set by the layer reset when the batch was resident
 };
 
 // Returns false (nothing launched) when the device cannot co-schedule the grid.
@@ -177,7 +185,8 @@ void launch_host_flag_signal(unsigned long long* flag, unsigned long long value,
                              cudaStream_t s);
 void launch_layer_reset(int* sent_base, int experts, int* desc_counts, int n_desc, int* done_counter,
                         unsigned long long* epoch, TraceSlot* trace, int n_trace, int* chunk_words,
-                        int n_chunk_words, cudaStream_t s);
+                        int n_chunk_words, unsigned long long* tok_ready_all, unsigned long long* stream_pending,
+                        cudaStream_t s);
 void launch_control(const ControlParams& p, cudaStream_t s);
 void launch_device_barrier(const BarrierParams& p, cudaStream_t s);
 

@@ -17,6 +17,7 @@ enum StatusCode : int {
   kBadConfig = 5,           // launch parameters inconsistent
   kTimeoutPermit = 6,       // the scheduler permit for a descriptor never arrived
   kSeqMismatch = 7,         // a signal carried an unexpected sequence number
+  kTimeoutInput = 8,        // a streamed input chunk never landed
 };
 
 struct DeviceStatus {

@@ -43,9 +43,7 @@ __global__ void moe_feature_digest_kernel(const uint32_t* rows, long long words_
   if (lane == 0) digest[row] = (long long)(acc & ((1ULL << 62) - 1));
 }
 
-// identity_checksum(token, src, 0, 0, chunk, chunk_offset, position, digest):
-// the destination and expert terms are added per assignment at dispatch time
-// (the checksum is linear in every field).
+// Checksum base of every token (token_checksum_base) from precomputed digests.
 __global__ void moe_checksum_base_kernel(const long long* token_ids, const long long* digest,
                                          const int* chunk_offsets, int chunks, int rank, int n,
                                          long long* base) {
@@ -53,12 +51,7 @@ __global__ void moe_checksum_base_kernel(const long long* token_ids, const long 
   if (t >= n) return;
   int c = 0;
   while (c + 1 < chunks && chunk_offsets[c + 1] <= t) ++c;
-  const uint64_t fields[8] = {(uint64_t)token_ids[t], (uint64_t)rank, 0, 0, (uint64_t)c,
-                              (uint64_t)(t - chunk_offsets[c]), (uint64_t)t, (uint64_t)digest[t]};
-  uint64_t acc = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) acc = addmod(acc, mulmod_coeff(fields[i], c_checksum_coeff[i]));
-  base[t] = (long long)acc;
+  base[t] = token_checksum_base(token_ids[t], rank, c, t - chunk_offsets[c], t, digest[t]);
 }
 
 // ---------------------------------------------------------------------------
@@ -414,10 +407,22 @@ void launch_device_barrier(const BarrierParams& p, cudaStream_t s) {
 
 // Per-call reset of the dispatch cursors and counters; advances the call's
 // sequence number (the value every ready / return / permit word is compared to).
+// Start of a layer call: next epoch, zeroed per-call counters and trace slots.
+// Inputs: when the host announced a streamed call (*stream_pending != 0) the
+// copy stream publishes each chunk's arrival itself; otherwise the batch is
+// resident and tok_ready_all takes the new epoch.
 __global__ void moe_layer_reset_kernel(int* sent_base, int experts, int* desc_counts, int n_desc,
                                        int* done_counter, unsigned long long* epoch, TraceSlot* trace,
-                                       int n_trace, int* chunk_words, int n_chunk_words) {
-  if (threadIdx.x == 0) *epoch += 1;
+                                       int n_trace, int* chunk_words, int n_chunk_words,
+                                       unsigned long long* tok_ready_all, unsigned long long* stream_pending) {
+  if (threadIdx.x == 0) {
+    const unsigned long long e = *epoch + 1;
+    *epoch = e;
+    if (tok_ready_all != nullptr) {
+      if (*stream_pending != 0) *stream_pending = 0;
+      else *tok_ready_all = e;
+    }
+  }
   for (int i = threadIdx.x; i < n_chunk_words; i += blockDim.x) chunk_words[i] = 0;
   for (int i = threadIdx.x; i < n_trace; i += blockDim.x) {
     trace[i].t_start = ~0ULL;
@@ -533,9 +538,11 @@ void launch_host_flag_signal(unsigned long long* flag, unsigned long long value,
 
 void launch_layer_reset(int* sent_base, int experts, int* desc_counts, int n_desc, int* done_counter,
                         unsigned long long* epoch, TraceSlot* trace, int n_trace, int* chunk_words,
-                        int n_chunk_words, cudaStream_t s) {
+                        int n_chunk_words, unsigned long long* tok_ready_all, unsigned long long* stream_pending,
+                        cudaStream_t s) {
   moe_layer_reset_kernel<<<1, 256, 0, s>>>(sent_base, experts, desc_counts, n_desc, done_counter, epoch, trace,
-                                           trace ? n_trace : 0, chunk_words, chunk_words ? n_chunk_words : 0);
+                                           trace ? n_trace : 0, chunk_words, chunk_words ? n_chunk_words : 0,
+                                           tok_ready_all, stream_pending);
 }
 
 }  // namespace raiccl

@@ -177,7 +177,7 @@ struct FrontHooks {
 template <typename T>
 __device__ void worker_dispatch(const FrontendParams& f, int q, int w, int W, unsigned long long epoch,
                                 int* hist, int* run, int* item_pos, int* s_base, const int* s_coff, int nc,
-                                int* s_flag) {
+                                int* s_flag, bool streamed) {
   const MoEDims& d = f.dp.dims;
   const int P = f.cp.partial_chunks, C = d.chunks, E = d.experts, k = d.top_k;
   const int t0 = s_coff[trigger_first_chunk(q, P)];
@@ -201,7 +201,7 @@ __device__ void worker_dispatch(const FrontendParams& f, int q, int w, int W, un
   if (permitted && (long long)(b - a) * k > kDispatchMaxItems) {
     if (threadIdx.x == 0) record_status(f.dp.status, kBadConfig, 22, (long long)(b - a) * k, kDispatchMaxItems);
   } else if (permitted && a < b) {
-    dispatch_rows<T>(f.dp, t0, a, b, s_base, hist, run, item_pos, s_coff, nc);
+    dispatch_rows<T>(f.dp, t0, a, b, s_base, hist, run, item_pos, s_coff, nc, streamed);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -253,10 +253,12 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   __shared__ int s_coff[kDispatchMaxChunks + 1];
   __shared__ int s_flag;
   __shared__ float red[256];
+  __shared__ unsigned long long s_dred[8 * 8];  // digest partial sums: 8 warps x up to 8 tokens
   TraceScope trace_scope(f.trace);
   const MoEDims& d = f.dp.dims;
   const int C = d.chunks, E = d.experts, n_desc = d.n_desc;
-  const int W = (int)gridDim.x - 1;
+  const int W = (int)gridDim.x - 1;  // worker CTAs
+  const int w = (int)blockIdx.x - 1;  // this CTA's worker index
   const unsigned long long epoch = *f.dp.epoch;
   const int nc = min(C, kDispatchMaxChunks);
   for (int c = threadIdx.x; c <= nc; c += blockDim.x) s_coff[c] = f.dp.chunk_offsets[c];
@@ -287,7 +289,6 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   }
 
   // ---------------- worker CTAs
-  const int w = blockIdx.x - 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const T* wts = (const T*)f.rp.weight;
   // router tables in shared memory for the whole launch: bias, block mask and
@@ -311,8 +312,10 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     for (int e = 0; e < kWP; ++e)
       wpre[e] = e < E ? __ldg((const uint4*)(wts + (long long)e * f.rp.hidden) + warp * 32 + lane) : make_uint4(0, 0, 0, 0);
   }
+  // inputs resident at launch (not streamed in by the copy engine during this call)
+  const bool resident = f.tok_ready == nullptr || ld_acquire_gpu_u64(f.tok_ready_all) >= epoch;
   // start pulling this worker's token rows of every chunk into L2
-  if constexpr (NT > 0) {
+  if (NT > 0 && resident) {
     const int row_bytes = f.rp.hidden * (int)sizeof(T);
     for (int c = 0; c < C; ++c) {
       const int t0 = s_coff[c], t1 = s_coff[c + 1];
@@ -339,22 +342,68 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     unsigned long long early_v = 0;
     if (threadIdx.x == 0 && !f.delayed && next < n_desc) early_v = ld_relaxed_gpu_u64(&f.desc_ready[next]);
     for (int e = threadIdx.x; e < E; e += blockDim.x) run[e] = 0;  // per-chunk expert counts
+    if (!resident) {
+      // streamed: wait for this chunk's rows; early arm: dispatch every
+      // descriptor the control warp releases meanwhile
+      const unsigned long long deadline = globaltimer_ns() + f.timeout_ns;
+      for (;;) {
+        if (threadIdx.x == 0) {
+          int st = 0;
+          while (st == 0) {
+            if (ld_acquire_sys_u64(reinterpret_cast<const uint64_t*>(&f.tok_ready[c])) >= epoch ||
+                ld_acquire_sys_u64(reinterpret_cast<const uint64_t*>(f.tok_ready_all)) >= epoch) {
+              st = 1;
+            } else if (!f.delayed && next < n_desc && ld_relaxed_gpu_u64(&f.desc_ready[next]) == epoch) {
+              __threadfence();  // acquire the release seen by the relaxed poll
+              st = 2;
+            } else if (globaltimer_ns() > deadline) {
+              record_status(f.dp.status, kTimeoutInput, kFrontKernelId, c, (long long)epoch);
+              st = 1;  // route what is there; the status fails the call
+            } else {
+              __nanosleep(100);
+            }
+          }
+          s_flag = st;
+        }
+        __syncthreads();
+        const int st = s_flag;
+        __syncthreads();
+        if (st == 1) break;
+        worker_dispatch<T>(f, next, w, W, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, true);
+        ++next;
+      }
+      if (threadIdx.x == 0 && !f.delayed && next < n_desc) early_v = ld_relaxed_gpu_u64(&f.desc_ready[next]);
+      for (int e = threadIdx.x; e < E; e += blockDim.x) run[e] = 0;  // worker_dispatch used it
+    }
     __syncthreads();
     const float* cbias = f.rp.chunk_bias ? s_cbias + (long long)c * E : nullptr;
     const int t0 = s_coff[c], t1 = s_coff[c + 1];
+    // streamed batches: the workers digest the rows they route (feature digest
+    // + checksum base); a resident batch had them computed when it was loaded
+    const bool digest = !resident && f.digest_out != nullptr;
+    DigestSink dsink{f.digest_out, f.csbase_out, f.dp.token_ids, f.dp.dims.rank, c, t0, s_dred};
     if constexpr (NT > 0) {
       const int ngroups = (t1 - t0 + NT - 1) / NT;
       for (int g = w; g < ngroups; g += W) {
         const int tf = t0 + g * NT;
         router_group<T, NT, EP>(f.rp, s_rbias, cbias, f.rp.block_mask ? s_rmask : nullptr, tf, min(NT, t1 - tf),
-                                red, run, use_wpre ? wpre : nullptr);
+                                red, run, use_wpre ? wpre : nullptr, digest ? &dsink : nullptr);
       }
     } else {
+      const int nvec_tok = f.rp.hidden * (int)sizeof(T) / 16;
       for (int t = t0 + w * nwarps + warp; t < t1; t += W * nwarps) {
         int sel[8];
         router_token<T, EMAX, false>(f.rp, cbias, t, wts, sel);
         if (lane == 0)
           for (int j = 0; j < f.rp.top_k; ++j) atomicAdd(&run[sel[j]], 1);
+        if (digest) {
+          const long long dg = warp_row_digest((const uint4*)((const T*)f.rp.tokens + (long long)t * f.rp.hidden),
+                                               nvec_tok);
+          if (lane == 0) {
+            f.digest_out[t] = dg;
+            f.csbase_out[t] = token_checksum_base(f.dp.token_ids[t], f.dp.dims.rank, c, t - t0, t, dg);
+          }
+        }
       }
     }
     if (c < 8) cta_stamp(f, 52 + c);
@@ -379,7 +428,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       bool ready = s_flag == 1;
       __syncthreads();
       while (next < n_desc && ready) {
-        worker_dispatch<T>(f, next, w, W, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag);
+        worker_dispatch<T>(f, next, w, W, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident);
         ++next;
         ready = next < n_desc && wait_released(f, next, epoch, &s_flag, false) == 1;
       }
@@ -388,7 +437,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   if (f.delayed && wait_released(f, n_desc - 1, epoch, &s_flag, true) != 1) return;
   while (next < n_desc) {
     if (wait_released(f, next, epoch, &s_flag, true) != 1) return;
-    worker_dispatch<T>(f, next, w, W, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag);
+    worker_dispatch<T>(f, next, w, W, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident);
     ++next;
   }
 }

@@ -152,6 +152,15 @@ class MoELayerRunner {
     ck(cudaEventCreateWithFlags(&ev_disp_done_, cudaEventDisableTiming), "cudaEventCreate");
     ck(cudaEventCreateWithFlags(&ev_plan_, cudaEventDisableTiming), "cudaEventCreate");
     ck(cudaEventCreateWithFlags(&ev_retmeta_, cudaEventDisableTiming), "cudaEventCreate");
+    ck(cudaEventCreateWithFlags(&ev_call_done_, cudaEventDisableTiming), "cudaEventCreate");
+    ev_tok_.resize(d.chunks);
+    for (auto& e : ev_tok_) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+    ck(cudaStreamCreateWithFlags(&sig_, cudaStreamNonBlocking), "cudaStreamCreate");
+    if (tensors.contains("tok_ready")) {
+      tok_ready_ = ptr<unsigned long long>(tensors, "tok_ready");
+      tok_ready_all_ = tok_ready_ + d.chunks;
+      stream_pending_ = tok_ready_ + d.chunks + 1;
+    }
     // dispatch chain: its own stream, so trigger q+1's control overlaps dispatch q
     ck(cudaStreamCreateWithFlags(&disp_, cudaStreamNonBlocking), "cudaStreamCreate");
   }
@@ -166,6 +175,9 @@ class MoELayerRunner {
     if (ev_disp_done_) cudaEventDestroy(ev_disp_done_);
     if (ev_plan_) cudaEventDestroy(ev_plan_);
     if (ev_retmeta_) cudaEventDestroy(ev_retmeta_);
+    if (ev_call_done_) cudaEventDestroy(ev_call_done_);
+    for (auto& e : ev_tok_) cudaEventDestroy(e);
+    if (sig_) cudaStreamDestroy(sig_);
     if (ev_start_) cudaEventDestroy(ev_start_);
     if (disp_) cudaStreamDestroy(disp_);
   }
@@ -189,7 +201,7 @@ class MoELayerRunner {
     trace_labels_.clear();
     raiccl::TraceSlot* reset_slot = trace_slot("layer_reset", -1);
     raiccl::launch_layer_reset(sent_base, d.experts, desc_counts, d.n_desc, done_counter, epoch, trace_,
-                               trace_cap_, chunk_words_, n_chunk_words_, comm_);
+                               trace_cap_, chunk_words_, n_chunk_words_, tok_ready_all_, stream_pending_, comm_);
     (void)reset_slot;
     ++launches;
 
@@ -339,6 +351,11 @@ class MoELayerRunner {
       fp.fault_skip_desc = fault_skip_signal_desc_;
       fp.timeout_ns = timeout_ns_;
       fp.cta_clock = opt_ptr<unsigned long long>(t, "fe_clock");
+      // streamed calls: the workers wait for each chunk and digest the rows they route
+      fp.digest_out = ptr<long long>(t, "feat_digest");
+      fp.csbase_out = ptr<long long>(t, "checksum_base");
+      fp.tok_ready = tok_ready_;
+      fp.tok_ready_all = tok_ready_all_;
       const size_t mark = trace_labels_.size();
       fp.trace = trace_slot("frontend", -1);
       raiccl::TraceSlot* first = nullptr;
@@ -479,7 +496,80 @@ class MoELayerRunner {
     // join the dispatch stream (the metadata grid finished long before)
     ck(cudaStreamWaitEvent(comm_, ev_retmeta_, 0), "cudaStreamWaitEvent");
     ck(cudaGetLastError(), "MoE layer launch");
+    if (!capturing()) call_done();
     return launches;
+  }
+
+  // Every executed call (eager or replayed) advances the device epoch by one;
+  // the host mirror names the epoch of the next call for streamed inputs.
+  bool capturing() const {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    ck(cudaStreamIsCapturing(comm_, &st), "cudaStreamIsCapturing");
+    return st != cudaStreamCaptureStatusNone;
+  }
+  void call_done() {
+    ++calls_;
+    ck(cudaEventRecord(ev_call_done_, comm_), "cudaEventRecord");
+  }
+
+  // One layer call whose token batch is streamed from pinned host memory:
+  // chunk c's rows are copied on `copy_stream` and published by a
+  // stream-ordered write of this call's epoch into tok_ready[c], which the
+  // front end's workers wait for before routing the chunk (so the copy of
+  // later chunks overlaps the routing, control and dispatch of earlier ones).
+  // The copies start once the previous call has finished with the token
+  // buffer; the caller orders copy_stream and the comm stream after its work.
+  int stream_call(int64_t host_ptr, int64_t copy_stream, bool delayed) {
+    c10::cuda::CUDAGuard guard(device_);
+    if (!use_frontend_ || tok_ready_ == nullptr)
+      throw std::runtime_error("streamed inputs need the persistent front end");
+    auto* copy = reinterpret_cast<cudaStream_t>(copy_stream);
+    const auto& d = dims_;
+    const unsigned long long e_next = calls_ + 1;
+    const size_t row_bytes = (size_t)d.hidden * d.feat_bytes;
+    auto* dst = ptr<uint8_t>(tensors_, "tokens");
+    const auto* src = reinterpret_cast<const uint8_t*>(host_ptr);
+    ck(write_value(comm_, stream_pending_, 1), "stream write (pending)");
+    ck(cudaStreamWaitEvent(copy, ev_call_done_, 0), "cudaStreamWaitEvent");
+    // The copies run back to back on the copy stream; a second stream turns
+    // each copy's completion event into its arrival word, so no stream write
+    // sits between two copies (each would hold the next copy until it ran).
+    ck(cudaStreamWaitEvent(sig_, ev_call_done_, 0), "cudaStreamWaitEvent");
+    for (int c = 0; c < d.chunks; ++c) {
+      const size_t off = (size_t)chunk_offsets_[c] * row_bytes;
+      const size_t n = (size_t)(chunk_offsets_[c + 1] - chunk_offsets_[c]) * row_bytes;
+      if (n) ck(cudaMemcpyAsync(dst + off, src + off, n, cudaMemcpyHostToDevice, copy), "cudaMemcpyAsync");
+      ck(cudaEventRecord(ev_tok_[c], copy), "cudaEventRecord");
+      ck(cudaStreamWaitEvent(sig_, ev_tok_[c], 0), "cudaStreamWaitEvent");
+      ck(write_value(sig_, tok_ready_ + c, e_next), "stream write (chunk)");
+    }
+    // the caller's streams see the copies through the copy stream
+    ck(cudaStreamWaitEvent(copy, ev_tok_[d.chunks - 1], 0), "cudaStreamWaitEvent");
+    const int a = delayed ? 1 : 0;
+    if (exec_[a]) {
+      ck(cudaGraphLaunch(exec_[a], comm_), "cudaGraphLaunch");
+      call_done();
+      return graph_launches_[a];
+    }
+    return forward(delayed);
+  }
+
+  // cuStreamWriteValue64 through the runtime's driver entry point: a word
+  // written by the stream's front end in stream order, no kernel (a kernel
+  // could not start while the cooperative front end holds every SM).
+  static cudaError_t write_value(cudaStream_t s, unsigned long long* addr, unsigned long long v) {
+    static PFN_cuStreamWriteValue64_v11070 fn = nullptr;
+    if (fn == nullptr) {
+      void* p = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuStreamWriteValue64", &p, cudaEnableDefault, &q) != cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || p == nullptr)
+        return cudaErrorNotSupported;
+      fn = reinterpret_cast<PFN_cuStreamWriteValue64_v11070>(p);
+    }
+    return fn((CUstream)s, (CUdeviceptr)addr, (cuuint64_t)v, CU_STREAM_WRITE_VALUE_DEFAULT) == CUDA_SUCCESS
+               ? cudaSuccess
+               : cudaErrorUnknown;
   }
 
   // Record one layer call of the given arm into that arm's CUDA graph slot.
@@ -511,6 +601,7 @@ class MoELayerRunner {
     const int a = delayed ? 1 : 0;
     if (!exec_[a]) throw std::runtime_error("no captured graph for this arm");
     ck(cudaGraphLaunch(exec_[a], comm_), "cudaGraphLaunch");
+    call_done();
     return graph_launches_[a];
   }
 
@@ -529,6 +620,7 @@ class MoELayerRunner {
   }
 
   long long sym_bytes() const { return layout_.total; }
+  unsigned long long calls() const { return calls_; }
 
   // Fault injection for failure-detection tests: the dispatch of descriptor
   // `desc` moves its rows but publishes no ready flag, so every receiver's
@@ -596,6 +688,13 @@ class MoELayerRunner {
     return trace_ + (trace_labels_.size() - 1);
   }
   cudaEvent_t ev_start_ = nullptr, ev_disp_done_ = nullptr, ev_plan_ = nullptr, ev_retmeta_ = nullptr;
+  cudaEvent_t ev_call_done_ = nullptr;  // end of the last executed call on the comm stream
+  std::vector<cudaEvent_t> ev_tok_;     // streamed chunk c copied
+  cudaStream_t sig_ = nullptr;          // publishes streamed-chunk arrival words
+  unsigned long long calls_ = 0;        // executed calls (== the device epoch after them)
+  unsigned long long* tok_ready_ = nullptr;       // [C] streamed-chunk arrival words
+  unsigned long long* tok_ready_all_ = nullptr;   // resident-batch word
+  unsigned long long* stream_pending_ = nullptr;  // the next reset leaves arrival to the copy stream
   std::vector<cudaEvent_t> ev_chunk_, ev_ctl_;
   cudaGraph_t graph_[2] = {nullptr, nullptr};
   cudaGraphExec_t exec_[2] = {nullptr, nullptr};
@@ -730,6 +829,9 @@ void register_moe(py::module_& m) {
       .def("forward", &MoELayerRunner::forward, py::arg("delayed"))
       .def("capture", &MoELayerRunner::capture, py::arg("delayed"))
       .def("replay", &MoELayerRunner::replay, py::arg("delayed"))
+      .def("stream_call", &MoELayerRunner::stream_call, py::arg("host_ptr"), py::arg("copy_stream"),
+           py::arg("delayed"))
+      .def("calls", &MoELayerRunner::calls)
       .def("has_graph", &MoELayerRunner::has_graph, py::arg("delayed"))
       .def("device_barrier", &MoELayerRunner::device_barrier)
       .def("sym_bytes", &MoELayerRunner::sym_bytes)

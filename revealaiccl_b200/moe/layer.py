@@ -184,6 +184,8 @@ class ProgressiveMoELayer:
             "bar_counter": torch.zeros(1, dtype=torch.int64, device=dev),
             # return-signal handoff: [elected epoch, parts reported, metadata CTAs done, pad]
             "ret_sync": torch.zeros(4, dtype=torch.int64, device=dev),
+            # streamed inputs: per-chunk arrival words [C], resident-batch word, streamed-call flag
+            "tok_ready": torch.zeros(cfg.chunks + 2, dtype=torch.int64, device=dev),
             "segs": self.segs, "rows_out": self.rows_out,
             "prefix1": torch.zeros(nseg + 1, dtype=torch.int32, device=dev),
             "prefix2": torch.zeros(nseg + 1, dtype=torch.int32, device=dev),
@@ -207,6 +209,7 @@ class ProgressiveMoELayer:
             self.tensors["trace"] = torch.zeros(TRACE_SLOTS * 4, dtype=torch.int64, device=dev)
         self.router_stream = torch.cuda.Stream(device=dev)
         self.comm_stream = torch.cuda.Stream(device=dev)
+        self.copy_stream = torch.cuda.Stream(device=dev)  # streamed token chunks (H2D)
         torch.cuda.synchronize(dev)
         self.runner = self._k.MoELayerRunner(
             ints, self.tensors, [int(b) for b in self.channel.bases], list(cfg.chunk_offsets),
@@ -288,12 +291,28 @@ class ProgressiveMoELayer:
     def __call__(self, host_tokens: torch.Tensor, host_out: torch.Tensor | None = None,
                  arm: str = "early") -> torch.Tensor:
         """End-to-end call: pinned host tokens in, combined output back in host
-        memory (the captured graph of ``arm`` is used when one exists)."""
-        self.load_tokens_(host_tokens)
-        if self.runner.has_graph(arm == "delayed"):
-            self.launches_per_call = self.runner.replay(arm == "delayed") + 2
+        memory (the captured graph of ``arm`` is used when one exists).
+
+        With the persistent front end the batch is streamed: each router
+        chunk's rows are copied on the copy stream and published to the
+        running front end, whose workers route a chunk as soon as it lands and
+        digest its rows on the way, so the host-to-device copy of later chunks
+        overlaps the routing, control and dispatch of earlier ones."""
+        cur = torch.cuda.current_stream(self.device)
+        streamed = (self.runner.persistent_frontend() and host_tokens.is_pinned() and host_tokens.is_contiguous()
+                    and host_tokens.dtype == self.inputs.tokens.dtype and host_tokens.shape == self.inputs.tokens.shape)
+        if streamed:
+            self.copy_stream.wait_stream(cur)
+            self.comm_stream.wait_stream(cur)
+            # copies and stream writes only: no kernels beyond the layer's own
+            self.launches_per_call = self.runner.stream_call(host_tokens.data_ptr(), self.copy_stream.cuda_stream,
+                                                             arm == "delayed")
         else:
-            self.launches_per_call = self.runner.forward(arm == "delayed") + 2
+            self.load_tokens_(host_tokens)
+            if self.runner.has_graph(arm == "delayed"):
+                self.launches_per_call = self.runner.replay(arm == "delayed") + 2
+            else:
+                self.launches_per_call = self.runner.forward(arm == "delayed") + 2
         if host_out is None:
             host_out = torch.empty(self.out.shape, dtype=self.out.dtype, pin_memory=True)
         with torch.cuda.stream(self.comm_stream):

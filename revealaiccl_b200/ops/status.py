@@ -22,6 +22,7 @@ CODES = {
     5: "bad launch configuration",
     6: "descriptor permit wait timed out",
     7: "signal sequence mismatch",
+    8: "streamed input chunk never landed",
 }
 
 

@@ -252,3 +252,42 @@ def test_programmatic_dependent_launch_matches_plain_launches():
         finally:
             layer.close()
     assert torch.equal(outs[True], outs[False])
+
+
+@pytest.mark.gpu
+def test_streamed_inputs_match_resident_calls():
+    """The end-to-end call streams the token batch chunk by chunk into the running
+    front end (the workers digest the rows they route); outputs, verification and
+    digests equal the resident path's, eagerly and through the captured graph."""
+    from revealaiccl_b200.moe.config import preset
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    layer = ProgressiveMoELayer(preset("full_tf32").with_overrides(tokens_per_rank=2048, chunk_sizes=(256,) * 8),
+                                timeout_s=5.0)
+    try:
+        layer.forward("early")
+        torch.cuda.synchronize()
+        assert layer.runner.persistent_frontend()
+        ref_out = layer.out.clone()
+        ref_digest = layer.feat_digest.clone()
+        host_in = torch.empty(layer.inputs.tokens.shape, dtype=layer.inputs.tokens.dtype, pin_memory=True)
+        host_in.copy_(layer.inputs.tokens.cpu())
+        host_out = torch.empty(layer.out.shape, dtype=layer.out.dtype, pin_memory=True)
+        for i in range(3):
+            layer.inputs.tokens.zero_()  # the call must bring its own rows
+            layer(host_in, host_out, arm="early")
+            torch.cuda.synchronize()
+            rep = layer.verify()
+            assert rep["pass"], (i, rep["violations"])
+            assert torch.equal(host_out, ref_out.cpu())
+            assert torch.equal(layer.feat_digest, ref_digest)
+        layer.capture("early")
+        layer.inputs.tokens.zero_()
+        layer(host_in, host_out, arm="early")  # graph replay with streamed inputs
+        torch.cuda.synchronize()
+        assert layer.verify()["pass"] and torch.equal(host_out, ref_out.cpu())
+        layer.forward("delayed")  # a resident call after streamed ones
+        assert layer.verify()["pass"]
+        assert layer.runner.calls() == int(layer.tensors["epoch"].item())
+    finally:
+        layer.close()
