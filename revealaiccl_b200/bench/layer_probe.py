@@ -1,11 +1,17 @@
 """Small-case driver of one MoE layer for kernel profiling.
 
     python -m revealaiccl_b200.bench.layer_probe --config r4_reference --calls 4 [--graph] [--trace t.json]
+        [--control-clocks] [--streamed]
 
 Builds one layer on cuda:0, runs ``--calls`` layer calls (eager launches, or
 replays of a captured graph with ``--graph``), verifies the last one and
 prints the per-call device time.  Meant to be wrapped by ``ncu -k ... -c ...``
 so that a capture sees only a handful of launches of the kernel of interest.
+``--control-clocks`` adds, per scheduler trigger of the last call, the SM
+clock (cumulative cycles) at the end of each control phase (stage, reveal,
+enumerate, select, guard, apply, log) from the control log rows.
+``--streamed`` times end-to-end calls instead (pinned host batch streamed in
+chunk by chunk, combined output copied back).
 """
 
 from __future__ import annotations
@@ -29,6 +35,8 @@ def main() -> None:
     ap.add_argument("--trace", default=None, help="write a Chrome trace of the last call to this path")
     ap.add_argument("--frontend", default="persistent", choices=("persistent", "steps"),
                     help="one cooperative front-end launch, or one launch per router chunk / trigger / descriptor")
+    ap.add_argument("--control-clocks", action="store_true", help="per-trigger control phase clocks")
+    ap.add_argument("--streamed", action="store_true", help="end-to-end calls with a streamed host batch")
     args = ap.parse_args()
     cfg = preset(args.config)
     if args.tokens:
@@ -41,16 +49,32 @@ def main() -> None:
         if args.graph:
             layer.capture(args.arm)
         times = []
+        if args.streamed:
+            host_in = torch.empty(layer.inputs.tokens.shape, dtype=layer.inputs.tokens.dtype, pin_memory=True)
+            host_in.copy_(layer.inputs.tokens.cpu())
+            host_out = torch.empty(layer.out.shape, dtype=layer.out.dtype, pin_memory=True)
         for _ in range(args.calls):
+            cur = torch.cuda.current_stream()
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record(layer.comm_stream)
-            layer.replay(args.arm) if args.graph else layer.forward(args.arm)
-            e.record(layer.comm_stream)
+            if args.streamed:
+                s.record(cur)
+                layer(host_in, host_out, arm=args.arm)
+                e.record(cur)
+            else:
+                s.record(layer.comm_stream)
+                layer.replay(args.arm) if args.graph else layer.forward(args.arm)
+                e.record(layer.comm_stream)
             torch.cuda.synchronize()
             times.append(s.elapsed_time(e))
         rep = layer.verify()
         rec = {"config": cfg.name, "arm": args.arm, "graph": args.graph, "ms": times,
                "pass": rep["pass"], "launches_per_call": layer.launches_per_call}
+        if args.control_clocks:
+            from ..moe.layer import LOG_HEADER  # noqa: F401  (log row layout lives with the layer)
+            log = layer.tensors["ctl_log"].cpu().view(layer.cfg.n_desc, layer.log_stride)
+            rec["control_clocks"] = [{"trigger": q, "candidates": int(log[q, 0]), "kept": int(log[q, 1]),
+                                      "revealed": int(log[q, 6]), "cycles": [int(x) for x in log[q, 8:15]]}
+                                     for q in range(layer.cfg.n_desc)]
         if args.trace:
             from .trace import summarize, write_chrome
 
