@@ -76,6 +76,25 @@ struct NoHooks {
 // Called by one full warp.  csm holds the staged control blob; s_dst
 // (kCtlStageMax >= chunks x ctl_per_chunk), s_coff (kCtlMaxChunks + 1) and
 // s_egmask (kWarpMaxE) are shared scratch.  reset: start a layer call (fresh scheduler state).
+// Rare paths, kept out of line: the warp executes its hot path once per
+// trigger, so every instruction line of it is fetched once per trigger, and
+// inlined fallbacks would spread that path over more lines.
+static __device__ __noinline__ void cold_status(DeviceStatus* st, int code, int id, long long index, long long bound) {
+  record_status(st, code, id, index, bound);
+}
+static __device__ __noinline__ int cold_select(const sched::PlanView& plan, sched::StateView& st, const sched::Cand* cand,
+                                        int n, int revealed, int* keep) {
+  return sched::select(plan, st, cand, n, revealed, keep, true);
+}
+static __device__ __noinline__ int cold_check(const sched::PlanView& plan, sched::StateView& st, const int64_t* actions,
+                                       int kept, int revealed) {
+  return sched::check(plan, st, actions, kept, revealed, true, true);
+}
+static __device__ __noinline__ void cold_apply(const sched::PlanView& plan, sched::StateView& st, const int64_t* actions,
+                                        int kept) {
+  sched::apply(plan, st, actions, kept, true);
+}
+
 template <class Hooks>
 __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims, uint8_t* csm, int* s_dst,
                                  int* s_coff, uint32_t* s_egmask, int q0, int q1, bool reset, Hooks& hooks) {
@@ -203,7 +222,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     const long long room = T - start > 0 ? T - start : 0;
     const int n = nk <= room ? nk : (int)room;
     if (nk > room) {
-      if (lane == 0) record_status(p.status, kBoundsViolation, 60, start + n, T);
+      if (lane == 0) cold_status(p.status, kBoundsViolation, 60, start + n, T);
       gate_ok = false;
     }
     const int rank = __popc(bal & lanemask_lt());
@@ -288,7 +307,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   }
   int n = carry;
   if (n > p.max_cands) {
-    if (lane == 0) record_status(p.status, kBoundsViolation, 61, n, p.max_cands);
+    if (lane == 0) cold_status(p.status, kBoundsViolation, 61, n, p.max_cands);
     n = p.max_cands;
     gate_ok = false;
   }
@@ -341,7 +360,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     for (int e = lane; e < E; e += 32) st.link_credits[e] = s_cap[e];
     for (int g = lane; g < G; g += 32) st.group_credits[g] = s_glim[g];
     __syncwarp();
-    if (lane == 0) kept = sched::select(plan, st, cand, n, revealed, keep, true);
+    if (lane == 0) kept = cold_select(plan, st, cand, n, revealed, keep);
     kept = __shfl_sync(FULL, kept, 0);
   }
   __syncwarp();
@@ -403,7 +422,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
       }
     }
   } else {
-    if (lane == 0) code = sched::check(plan, st, actions, kept, revealed, true, true);
+    if (lane == 0) code = cold_check(plan, st, actions, kept, revealed);
     code = __shfl_sync(FULL, code, 0);
   }
   const bool accepted = code == sched::kAccept;
@@ -442,7 +461,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     for (int e = lane; e < E; e += 32) st.link_credits[e] = s_cap[e];
     for (int g = lane; g < G; g += 32) st.group_credits[g] = s_glim[g];
     __syncwarp();
-    if (accepted && kept > 0 && lane == 0) sched::apply(plan, st, actions, kept, true);
+    if (accepted && kept > 0 && lane == 0) cold_apply(plan, st, actions, kept);
   }
   for (int t = lane; t < T; t += 32) st.scratch_selected[t] = 0;
   if (accepted && kept > 0) version += 1;
@@ -458,7 +477,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   int* L = p.log + (long long)desc * p.log_stride;
   if (lane == 0) {
     p.permit[desc] = (accepted && gate_ok) ? epoch_v : 0ULL;
-    if (!(accepted && gate_ok)) record_status(p.status, kTimeoutPermit, 62, desc, code);
+    if (!(accepted && gate_ok)) cold_status(p.status, kTimeoutPermit, 62, desc, code);
     S[kCompleted] = completed; S[kRevealedBits] = revealed_bits; S[kPending] = pending;
     S[kDispatched] = dispatched; S[kStaged] = staged; S[kRevealedCount] = revealed_count;
     S[kVersion] = version; S[kFuture] = future; S[kUnrevealed] = unrevealed; S[kStale] = stale;
