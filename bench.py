@@ -109,6 +109,9 @@ def run_product(args) -> dict | None:
     rank, world, local = _env_world()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if local >= torch.cuda.device_count():
+        # one rank per GPU: ranks that wait on each other must never share a GPU
+        raise SystemExit(f"LOCAL_RANK={local} but only {torch.cuda.device_count()} GPU(s) on this node")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:

@@ -35,6 +35,9 @@ def run(configs: list[str], timeout_s: float, tokens: int) -> bool:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if local >= torch.cuda.device_count():
+        # one rank per GPU: ranks that wait on each other must never share a GPU
+        raise SystemExit(f"LOCAL_RANK={local} but only {torch.cuda.device_count()} GPU(s) on this node")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -65,7 +68,19 @@ def run(configs: list[str], timeout_s: float, tokens: int) -> bool:
                 ok &= bool(layer.verify()["pass"])
                 graph_same = torch.equal(early, layer.out)
                 ok &= same and graph_same
-                rec.update(early_delayed_identical=same, graph_identical=graph_same,
+                # end-to-end calls: the pinned batch streamed into the running front end
+                host_in = torch.empty(layer.inputs.tokens.shape, dtype=layer.inputs.tokens.dtype, pin_memory=True)
+                host_in.copy_(layer.inputs.tokens.cpu())
+                host_out = torch.empty(layer.out.shape, dtype=layer.out.dtype, pin_memory=True)
+                stream_same = True
+                for _ in range(2):
+                    layer.device_barrier()
+                    layer(host_in, host_out, arm="early")
+                    torch.cuda.synchronize(dev)
+                    ok &= bool(layer.verify()["pass"])
+                    stream_same &= torch.equal(host_out, early.cpu())
+                ok &= stream_same
+                rec.update(early_delayed_identical=same, graph_identical=graph_same, streamed_identical=stream_same,
                            launches_per_call=layer.launches_per_call)
             except Exception as exc:  # reported, then the collective error path below
                 ok = False

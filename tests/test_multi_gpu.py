@@ -35,4 +35,5 @@ def test_two_rank_layer_selftest(configs):
     recs = [json.loads(line) for line in p.stdout.splitlines() if line.startswith("{")]
     assert p.returncode == 0, (p.stdout[-3000:], p.stderr[-3000:])
     assert [r["config"] for r in recs] == configs
-    assert all(r["pass"] and r["early_delayed_identical"] and r["graph_identical"] for r in recs), recs
+    assert all(r["pass"] and r["early_delayed_identical"] and r["graph_identical"] and r["streamed_identical"]
+               for r in recs), recs
