@@ -44,6 +44,7 @@ constexpr int kWarpMaxPerChunk = 32;
 
 // 16-byte vector copy, four loads in flight per thread before the stores.
 __device__ __forceinline__ void copy16(uint4* dst, const uint4* src, long long n) {
+  #pragma unroll 1
   for (long long i0 = threadIdx.x; i0 < n; i0 += 4LL * blockDim.x) {
     uint4 r[4];
 #pragma unroll
@@ -105,6 +106,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   const int P = p.partial_chunks;
   const int cpc = p.ctl_per_chunk;
   const unsigned long long epoch_v = *p.epoch;
+  #pragma unroll 1
   for (int c = lane; c <= C; c += 32) s_coff[c] = p.chunk_offsets[c];
   auto at = [&](int a) { return csm + Lt.off[a]; };
   sched::PlanView plan = p.plan;
@@ -151,22 +153,31 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   int* cbase = reinterpret_cast<int*>(actions) + T;
   __syncwarp();
   if (reset) {
+    #pragma unroll 1
     for (int i = lane; i < T; i += 32) {
       st.sources[i] = -1; st.destinations[i] = -1; st.ready[i] = 0; st.residual[i] = 0;
       st.remaining_hops[i] = sched::kInf; st.scratch_selected[i] = 0; st.scratch_seen[i] = 0;
     }
+    #pragma unroll 1
     for (long long i = lane; i < (long long)T * V; i += 32) st.holders[i] = 0;
+    #pragma unroll 1
     for (long long i = lane; i < (long long)T * E; i += 32) st.committed[i] = 0;
+    #pragma unroll 1
     for (int i = lane; i < V * V; i += 32) st.residual_demand[i] = 0;
+    #pragma unroll 1
     for (int i = lane; i < E; i += 32) { st.link_credits[i] = s_cap[i]; st.scratch_edge_load[i] = 0; }
+    #pragma unroll 1
     for (int i = lane; i < G; i += 32) st.group_credits[i] = s_glim[i];
+    #pragma unroll 1
     for (int i = lane; i < kChunkStarts + 2 * C; i += 32)
       S[i] = (i >= kChunkStarts && i < kChunkStarts + C) ? -1 : 0;
   }
   // edge -> group bitmask (a repeated group falls back to the serial selection)
   int dup_local = 0;
+  #pragma unroll 1
   for (int e = lane; e < E; e += 32) {
     uint32_t m = 0;
+    #pragma unroll 1
     for (int k = egptr[e]; k < egptr[e + 1]; ++k) {
       const uint32_t b = 1u << egmem[k];
       dup_local |= (m & b) ? 1 : 0;
@@ -176,6 +187,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   }
   const bool dup_groups = __any_sync(FULL, dup_local) != 0;
   __syncwarp();
+  #pragma unroll 1
   for (int desc = q0; desc < q1; ++desc) {
   if (!hooks.before(desc)) break;
   const long long clk0 = clock64();
@@ -187,6 +199,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   // by absolute chunk: s_dst[c * cpc + j]
   if constexpr (!Hooks::kFetchesTokens) {
     const int n_stage = (c_hi - c_lo + 1) * cpc;
+    #pragma unroll 1
     for (int i = lane; i < n_stage; i += 32) {
       const int c = c_lo + i / cpc, j = i % cpc;
       const int off = s_coff[c];
@@ -205,6 +218,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   if (lane == 0) clk[0] = (int)(clock64() - clk0);
 
   // ---- complete: stage the control tokens of the trigger's chunks
+  #pragma unroll 1
   for (int c = c_lo; c <= c_hi; ++c) {
     const long long bit = 1LL << c;
     if (completed & bit) { gate_ok = false; continue; }  // completed-chunk replay
@@ -231,6 +245,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
       st.sources[o] = src;
       st.destinations[o] = dst;
       uint8_t* h = st.holders + (long long)o * V;
+      #pragma unroll 1
       for (int v = 0; v < V; ++v) h[v] = 0;
       h[src] = 1;
     }
@@ -240,6 +255,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     __syncwarp();
   }
   // ---- reveal pending chunks strictly in ordinal order
+  #pragma unroll 1
   for (int c = c_lo; c <= c_hi; ++c) {
     const long long bit = 1LL << c;
     if (!(completed & bit)) { future += 1; gate_ok = false; continue; }
@@ -247,6 +263,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     const long long s0 = starts[c], cn = counts[c];
     if (!(pending & bit) || s0 != revealed_count) { gate_ok = false; continue; }
     revealed_bits |= bit;
+    #pragma unroll 1
     for (long long o = s0 + lane; o < s0 + cn; o += 32) {
       const int s = st.sources[o], d = st.destinations[o];
       st.ready[o] = 1;
@@ -255,6 +272,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
       st.residual[o] = residual ? 1 : 0;
       if (residual) atomicAdd(reinterpret_cast<unsigned long long*>(&st.residual_demand[(long long)s * V + d]), 1ULL);
       int best = sched::kInf;
+      #pragma unroll 1
       for (int v = 0; v < V; ++v)
         if (h[v] && dist[(long long)v * V + d] < best) best = dist[(long long)v * V + d];
       st.remaining_hops[o] = best;
@@ -267,8 +285,10 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   if (lane == 0) clk[1] = (int)(clock64() - clk0);
 
   // ---- enumerate: per-ordinal template bitmask and candidate prefix
+  #pragma unroll 1
   for (int t = lane; t < T; t += 32) st.scratch_selected[t] = 0;
   int carry = 0;
+  #pragma unroll 1
   for (int o0 = 0; o0 < revealed; o0 += 32) {
     const int o = o0 + lane;
     uint32_t vm = 0;
@@ -278,6 +298,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
       if (before > 0 && before < sched::kInf) {
         const uint8_t* h = st.holders + (long long)o * V;
         const int k0 = tptr[d], nt = tptr[d + 1] - k0;
+        #pragma unroll 1
         for (int j = 0; j < nt; ++j) {
           const int k = k0 + j;
           if (h[tsrc[k]] && !h[ttgt[k]] && ttd[k] == before - 1) vm |= 1u << j;
@@ -299,6 +320,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
         const int before = st.remaining_hops[o];
         const int k0 = tptr[d];
         int i = base;
+        #pragma unroll 1
         for (uint32_t m = vm; m; m &= m - 1, ++i)
           if (i < p.max_cands) cand[i] = sched::Cand{o, tedge[k0 + __ffs(m) - 1], before, before - 1};
       }
@@ -322,12 +344,14 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     unsigned long long lack_link = (unsigned long long)__ballot_sync(FULL, lane < E && cred_lo < 1) |
                                    ((unsigned long long)__ballot_sync(FULL, lane + 32 < E && cred_hi < 1) << 32);
     uint32_t lack_grp = __ballot_sync(FULL, lane < G && gcred < 1);
+    #pragma unroll 1
     for (int o0 = 0; o0 < revealed; o0 += 32) {
       const int my_o = o0 + lane;
       const uint32_t my_vm = my_o < revealed ? vmask[my_o] : 0u;
       const int my_base = my_o < revealed ? cbase[my_o] : 0;
       const int my_k0 = (my_o < revealed && my_vm) ? tptr[st.destinations[my_o]] : 0;
       uint32_t todo = __ballot_sync(FULL, my_vm != 0 && my_base < n);
+      #pragma unroll 1
       while (todo) {
         const int src_lane = __ffs(todo) - 1;
         todo &= todo - 1;
@@ -357,13 +381,16 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     if (lane < G) st.group_credits[lane] = gcred;
     __syncwarp();
   } else {
+    #pragma unroll 1
     for (int e = lane; e < E; e += 32) st.link_credits[e] = s_cap[e];
+    #pragma unroll 1
     for (int g = lane; g < G; g += 32) st.group_credits[g] = s_glim[g];
     __syncwarp();
     if (lane == 0) kept = cold_select(plan, st, cand, n, revealed, keep);
     kept = __shfl_sync(FULL, kept, 0);
   }
   __syncwarp();
+  #pragma unroll 1
   for (int i = lane; i < kept; i += 32) {
     const sched::Cand cc = cand[keep[i]];
     actions[2 * i] = cc.ordinal;
@@ -373,7 +400,9 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   if (lane == 0) clk[3] = (int)(clock64() - clk0);
 
   // ---- guard check
+  #pragma unroll 1
   for (int t = lane; t < T; t += 32) st.scratch_seen[t] = 0;
+  #pragma unroll 1
   for (int e = lane; e < E; e += 32) st.scratch_edge_load[e] = 0;
   __syncwarp();
   int code = sched::kAccept;
@@ -417,6 +446,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
       } else {
         long long load = 0;
         if (lane < G)
+          #pragma unroll 1
           for (int k = gptr[lane]; k < gptr[lane + 1]; ++k) load += st.scratch_edge_load[gmem[k]];
         if (__ballot_sync(FULL, lane < G && load > s_glim[lane])) code = sched::kGroup;
       }
@@ -436,6 +466,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     if (lane + 32 < E) st.link_credits[lane + 32] = s_cap[lane + 32] - st.scratch_edge_load[lane + 32];
     if (lane < G) {
       long long used = 0;
+      #pragma unroll 1
       for (int e = 0; e < E; ++e)
         if ((s_egmask[e] >> lane) & 1u) used += st.scratch_edge_load[e];
       st.group_credits[lane] = s_glim[lane] - used;
@@ -453,18 +484,23 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
         st.residual[o] = 0;
       }
       int best = sched::kInf;
+      #pragma unroll 1
       for (int v = 0; v < V; ++v)
         if (h[v] && dist[(long long)v * V + d] < best) best = dist[(long long)v * V + d];
       st.remaining_hops[o] = best;
     }
   } else {
+    #pragma unroll 1
     for (int e = lane; e < E; e += 32) st.link_credits[e] = s_cap[e];
+    #pragma unroll 1
     for (int g = lane; g < G; g += 32) st.group_credits[g] = s_glim[g];
     __syncwarp();
     if (accepted && kept > 0 && lane == 0) cold_apply(plan, st, actions, kept);
   }
+  #pragma unroll 1
   for (int t = lane; t < T; t += 32) st.scratch_selected[t] = 0;
   if (accepted && kept > 0) version += 1;
+  #pragma unroll 1
   for (int c = c_lo; c <= c_hi; ++c) {
     const long long bit = 1LL << c;
     if (!(completed & bit)) { future += 1; gate_ok = false; }
@@ -472,6 +508,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     else if (dispatched & bit) { stale += 1; gate_ok = false; }
   }
   if (gate_ok)
+    #pragma unroll 1
     for (int c = c_lo; c <= c_hi; ++c) dispatched |= 1LL << c;
   __syncwarp();
   int* L = p.log + (long long)desc * p.log_stride;
@@ -487,11 +524,13 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   }
   // ---- log and state write-back
   int* sel = L + kLogHeader;
+  #pragma unroll 1
   for (int i = lane; i < kept; i += 32) {
     sel[2 * i] = (int)actions[2 * i];
     sel[2 * i + 1] = (int)actions[2 * i + 1];
   }
   int* cl = L + kLogHeader + 2 * T;
+  #pragma unroll 1
   for (int i = lane; i < n; i += 32) {
     cl[4 * i] = cand[i].ordinal; cl[4 * i + 1] = cand[i].edge;
     cl[4 * i + 2] = cand[i].before; cl[4 * i + 3] = cand[i].after;

@@ -169,6 +169,67 @@ __device__ __forceinline__ void gemm_epilogue_row(const GroupedGemmParams& p, co
   }
 }
 
+// Staged epilogue (CTA-pair kernel): per 32-column chunk the warp writes its
+// 32 rows x 32 columns into a padded shared-memory tile (row pitch
+// 32 * sizeof(OutT) + 16 bytes, so both the row-wise writes and the column-wise
+// reads below are bank-conflict free), then reads it back so that each store
+// instruction covers 32 / CH whole 128- or 64-byte row pieces instead of 32
+// scattered 16-byte pieces (CH = 16-byte chunks per row piece).  Rows keep
+// their own mapped output row and validity (shuffled from the row's lane).
+template <typename OutT>
+struct EpiTile {
+  static constexpr int ROW_BYTES = 32 * (int)sizeof(OutT);
+  static constexpr int PITCH = ROW_BYTES + 16;
+  static constexpr int BYTES = 32 * PITCH;  // per epilogue warp
+  static constexpr int CH = ROW_BYTES / 16;
+  static constexpr int ROWS_PER_PASS = 32 / CH;
+};
+
+template <int BN, Act ACT, typename OutT>
+__device__ __forceinline__ void gemm_epilogue_staged(const GroupedGemmParams& p, const GemmSegment& seg, int nb,
+                                                     int r_local, uint32_t t_row, int c0, int c1, uint8_t* tile) {
+  using TL = EpiTile<OutT>;
+  const int lane = threadIdx.x & 31;
+  const bool valid = r_local < seg.rows;
+  const int arow = seg.a_row0 + r_local;
+  long long orow = 0;
+  float scale = 1.f;
+  if (valid) {
+    orow = p.row_map ? (long long)__ldg(p.row_map + arow) : (long long)(seg.out_row0 + r_local);
+    if (p.row_scale) scale = __ldg(p.row_scale + arow);
+  }
+  OutT* out = (OutT*)p.out_ptrs[seg.out_slot];
+  const float* bias = p.bias ? p.bias + (long long)seg.expert * p.N + nb * BN : nullptr;
+  uint8_t* my_row = tile + lane * TL::PITCH;
+#pragma unroll 1
+  for (int c = c0; c < c1; c += 32) {
+    uint32_t r0[16], r1[16];
+    tmem_ld16(t_row + c, r0);
+    tmem_ld16(t_row + c + 16, r1);
+    tmem_ld_wait();
+    float b[16], v[16];
+    load_bias16(bias ? bias + c : nullptr, b);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = apply_act(__uint_as_float(r0[j]) + b[j], ACT) * scale;
+    store16((OutT*)my_row, v);
+    load_bias16(bias ? bias + c + 16 : nullptr, b);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = apply_act(__uint_as_float(r1[j]) + b[j], ACT) * scale;
+    store16((OutT*)my_row + 16, v);
+    __syncwarp();
+#pragma unroll
+    for (int pass = 0; pass < TL::CH; ++pass) {
+      const int row = pass * TL::ROWS_PER_PASS + lane / TL::CH;  // tile row this lane stores
+      const int k = lane % TL::CH;                                 // its 16-byte chunk
+      const long long orow_r = __shfl_sync(0xffffffffu, orow, row);
+      const int valid_r = __shfl_sync(0xffffffffu, (int)valid, row);
+      const uint4 q = *(const uint4*)(tile + row * TL::PITCH + k * 16);
+      if (valid_r) *(uint4*)((uint8_t*)(out + orow_r * p.ldo + nb * BN + c) + k * 16) = q;
+    }
+    __syncwarp();
+  }
+}
+
 // Column range [c0, c1) of epilogue warp `ew` (0..kEpiWarps-1) in a tile
 // whose epilogue covers `cols` columns: warps ew and ew + 4 split the range
 // at a 16-column boundary.

@@ -25,7 +25,7 @@
 
 namespace raiccl {
 
-template <int BN, bool TF32>
+template <int BN, bool TF32, typename OutT = float>
 struct PairCfg {
   static constexpr int BM = 128;                  // rows per CTA; the pair's tile has 256
   static constexpr int BNH = BN / 2;              // B rows staged per CTA
@@ -35,12 +35,14 @@ struct PairCfg {
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BNH * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int SMEM_BUDGET = 200 * 1024;
+  // staging tiles of the eight epilogue warps (coalesced stores), behind the ring
+  static constexpr int EPI_BYTES = kEpiWarps * EpiTile<OutT>::BYTES;
+  static constexpr int SMEM_BUDGET = 224 * 1024 - EPI_BYTES;
   static constexpr int STAGES_RAW = SMEM_BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int TMEM_COLS = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128 : (2 * BN) <= 256 ? 256 : 512;
   static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, 256, BN);
-  static constexpr int SMEM_TOTAL = 1024 + STAGES * STAGE_BYTES + 256;
+  static constexpr int SMEM_TOTAL = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + 256;
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair tile: BN/2 rows of B per CTA, N <= 256");
   static_assert(STAGES >= 2, "pipeline needs two stages");
 };
@@ -49,12 +51,13 @@ template <int BN, bool TF32, Act ACT, typename OutT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
 grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                          GroupedGemmParams p) {
-  using C = PairCfg<BN, TF32>;
+  using C = PairCfg<BN, TF32, OutT>;
   constexpr int kKernelId = 300 + BN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* stage_base = smem;
-  uint64_t* bars = (uint64_t*)(smem + C::STAGES * C::STAGE_BYTES);
+  uint8_t* epi_base = smem + C::STAGES * C::STAGE_BYTES;  // epilogue staging tiles
+  uint64_t* bars = (uint64_t*)(epi_base + C::EPI_BYTES);
   uint64_t* full_bar = bars;                   // used in the leader only
   uint64_t* empty_bar = bars + C::STAGES;      // per CTA: stage free again
   uint64_t* tfull_bar = bars + 2 * C::STAGES;  // per CTA: accumulator ready
@@ -170,8 +173,12 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.status, kKernelId, lim)) break;
       tc_fence_after_sync();
       const int r_local = mb * 2 * C::BM + (int)rank * C::BM + row_in_tile;
-      gemm_epilogue_row<BN, ACT, OutT>(p, seg, nb, r_local, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
-                                       c0, c1);
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      if constexpr (ACT == Act::kSwiGLU)
+        gemm_epilogue_row<BN, ACT, OutT>(p, seg, nb, r_local, t_row, c0, c1);
+      else
+        gemm_epilogue_staged<BN, ACT, OutT>(p, seg, nb, r_local, t_row, c0, c1,
+                                            epi_base + (warp - 2) * EpiTile<OutT>::BYTES);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));
@@ -191,7 +198,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
 template <int BN, bool TF32, Act ACT, typename OutT>
 inline void launch_one_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GroupedGemmParams& p, int grid,
                             cudaStream_t stream) {
-  using C = PairCfg<BN, TF32>;
+  using C = PairCfg<BN, TF32, OutT>;
   auto kern = grouped_gemm_pair_kernel<BN, TF32, ACT, OutT>;
   static bool configured = false;
   if (!configured) {

@@ -19,8 +19,9 @@
 //       experts), add the per-expert counts, and release
 //       chunk_done[c].  In the early arm, a worker dispatches every descriptor
 //       already released between chunks (a non-blocking poll, so routing never
-//       waits on the control plane).  After the last chunk it dispatches the
-//       rest, waiting (bounded) for each release.  In the delayed arm nothing is
+//       waits on the control plane), and while it waits for a streamed chunk.
+//       After the last chunk it dispatches the rest, waiting (bounded) for
+//       each release.  In the delayed arm nothing is
 //       dispatched before the final trigger.  Each worker packs and stores its
 //       token share of a descriptor (dispatch_rows).  The last worker to finish
 //       a descriptor publishes the counts and the per-destination ready words.
@@ -111,7 +112,9 @@ struct FrontHooks {
     int ok = 1;
     if (lane == 0) {
       const unsigned long long deadline = globaltimer_ns() + f->timeout_ns;
+      #pragma unroll 1
       for (int c = chunks_ready; c < need && ok; ++c) {
+        #pragma unroll 1
         while (ld_acquire_gpu_s32(&f->chunk_done[c]) < workers) {
           if (globaltimer_ns() > deadline) {
             record_status(f->dp.status, kTimeoutChunkFlag, kFrontKernelId, c, workers);
@@ -125,6 +128,7 @@ struct FrontHooks {
     if (!ok) return false;
     // every further chunk that is already complete (one parallel poll)
     int hi = need;
+    #pragma unroll 1
     for (int base = need; base < C; base += 32) {
       const int c = base + lane;
       const bool done = c < C && ld_acquire_gpu_s32(&f->chunk_done[c]) >= workers;
@@ -137,12 +141,14 @@ struct FrontHooks {
     __threadfence();
     __syncwarp();
     const int lo = chunks_ready;
+    #pragma unroll 1
     for (int i = lane; i < (hi - lo) * cpc; i += 32) {
       const int c = lo + i / cpc, j = i % cpc;
       const int off = s_coff[c];
       const int size = s_coff[c + 1] - off;
       s_dst[c * cpc + j] = j < size ? f->cp.expert_ids[(long long)(off + j) * f->cp.top_k] % f->cp.ctl_nodes : -1;
     }
+    #pragma unroll 1
     for (int i = lane; i < (hi - lo) * E; i += 32) s_ccount[lo * E + i] = f->chunk_counts[(long long)lo * E + i];
     chunks_ready = hi;
     __syncwarp();
@@ -154,8 +160,10 @@ struct FrontHooks {
   __device__ void after(int q, bool permitted) {
     const int lane = threadIdx.x & 31;
     const int c_lo = trigger_first_chunk(q, P), c_hi = trigger_last_chunk(q, P, C);
+    #pragma unroll 1
     for (int e = lane; e < E; e += 32) {
       int cnt = 0;
+      #pragma unroll 1
       for (int c = c_lo; c <= c_hi; ++c) cnt += s_ccount[c * E + e];
       const int base = s_sent[e];
       f->disp_base[(long long)q * E + e] = base;
