@@ -17,11 +17,11 @@
 //   CTAs 1..W — workers.  For each router chunk: route a share of its tokens
 //       (groups of tokens per CTA, or one warp per token for more than 32
 //       experts), add the per-expert counts, and release
-//       chunk_done[c].  In the early arm, a worker dispatches every descriptor
-//       already released between chunks (a non-blocking poll, so routing never
-//       waits on the control plane), and while it waits for a streamed chunk.
-//       After the last chunk it dispatches the rest, waiting (bounded) for
-//       each release.  In the delayed arm nothing is
+//       chunk_done[c].  A resident batch is routed chunk after chunk without
+//       interruption; a streamed batch is routed as its chunks land, and while
+//       a worker waits for the next chunk (early arm) it dispatches every
+//       descriptor already released.  After the last chunk a worker dispatches
+//       the rest, waiting (bounded) for each release.  In the delayed arm nothing is
 //       dispatched before the final trigger.  Each worker packs and stores its
 //       token share of a descriptor (dispatch_rows).  The last worker to finish
 //       a descriptor publishes the counts and the per-destination ready words.
@@ -426,8 +426,11 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       trace_end(rslot);
     }
     if (c < 8) cta_stamp(f, 3 + 2 * c);
-    // early arm: dispatch every descriptor already released (never waits)
-    if (!f.delayed) {
+    // early arm, streamed batch: dispatch every descriptor already released
+    // (never waits).  A resident batch routes every chunk first: routing is
+    // then a few microseconds per chunk and the scheduler chain, which needs
+    // each chunk, is not held back by dispatch work queued between chunks.
+    if (!f.delayed && !resident) {
       if (threadIdx.x == 0) {
         if (early_v == epoch) __threadfence();
         s_flag = early_v == epoch ? 1 : 0;
