@@ -382,15 +382,29 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
   // same expert elect one leader that adds the group's size (one shared-memory
   // atomic per distinct expert per warp instead of one per item)
   {
+    // UH independent loads in flight per lane before the matches (the scan is
+    // latency-bound: one round trip per UH x 32 items per warp)
+    // warps 1.. scan while warp 0 ranks the share's own items below
+    constexpr int UH = 8;
     const long long i_end = (long long)a * k;
-    for (long long i0 = (long long)t0 * k + (long long)warp * 32; i0 < i_end; i0 += (long long)nwarps * 32) {
-      const long long i = i0 + lane;
-      const int e = i < i_end ? p.expert_ids[i] : E;  // sentinel groups the tail lanes
-      const unsigned peers = __match_any_sync(0xffffffffu, e);
-      if (e < E && lane == __ffs(peers) - 1) atomicAdd(&hist[e], __popc(peers));
+    const int hw = nwarps > 1 ? nwarps - 1 : 1, hwarp = nwarps > 1 ? warp - 1 : warp;
+    const long long stride = (long long)hw * 32;
+    for (long long i0 = (long long)t0 * k + (long long)hwarp * 32; hwarp >= 0 && i0 < i_end; i0 += stride * UH) {
+      int ev[UH];
+#pragma unroll
+      for (int u = 0; u < UH; ++u) {
+        const long long i = i0 + u * stride + lane;
+        ev[u] = i < i_end ? p.expert_ids[i] : E;  // sentinel groups the tail lanes
+      }
+#pragma unroll
+      for (int u = 0; u < UH; ++u) {
+        const unsigned peers = __match_any_sync(0xffffffffu, ev[u]);
+        if (ev[u] < E && lane == __ffs(peers) - 1) atomicAdd(&hist[ev[u]], __popc(peers));
+      }
     }
   }
-  // in-order rank of every item of this share within its expert
+  // in-order rank of every item of this share within its expert (run is
+  // this share's own counter, so it does not race with the scan above)
   if (warp == 0) {
     const long long i0 = (long long)a * k, i1 = (long long)b * k;
     for (long long base = i0; base < i1; base += 32) {
@@ -400,7 +414,7 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
       const unsigned peers = __match_any_sync(0xffffffffu, e);
       const int rank_in = __popc(peers & ((1u << lane) - 1u));
       const int prev = valid ? run[e] : 0;
-      if (valid) item_pos[i - i0] = prev + rank_in;
+      if (valid) item_pos[i - i0] = (prev + rank_in) | (e << 24);  // rank (< 2^24 rows) and expert (< 256)
       __syncwarp();
       if (valid && lane == __ffs(peers) - 1) run[e] = prev + __popc(peers);
       __syncwarp();
@@ -413,9 +427,17 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
   for (long long li = warp; li < nitems; li += nwarps) {
     const long long i = (long long)a * k + li;
     const int t = (int)(i / k), j = (int)(i % k);
-    const int e = p.expert_ids[i];
+    const int packed = item_pos[li];
+    const int e = (int)((unsigned)packed >> 24);
     const int r = expert_owner(d, e), le = expert_slot(d, e);
-    const long long row = (long long)base_e[e] + hist[e] + item_pos[li];
+    const long long row = (long long)base_e[e] + hist[e] + (packed & 0xFFFFFF);
+    // the identity fields' global loads go out before the row copy
+    long long pre = 0;
+    float gate = 1.f;
+    if (lane == 0) pre = p.token_ids[t];
+    else if (lane == 7) pre = p.feat_digest[t];
+    else if (lane == 8) pre = p.checksum_base[t];
+    else if (lane == 17 && d.gate_mode) gate = p.gates[i];
     if (row >= d.cap || r >= d.world || le >= d.expert_slots) {
       if (lane == 0) record_status(p.status, kBoundsViolation, 21, row, d.cap);
       continue;
@@ -446,16 +468,16 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
       while (c + 1 < d.chunks && p.chunk_offsets[c + 1] <= t) ++c;  // beyond the staged table
       long long val;
       switch (lane) {
-        case 0: val = p.token_ids[t]; break;
+        case 0: val = pre; break;
         case 1: val = d.rank; break;
         case 2: val = r; break;
         case 3: val = e; break;
         case 4: val = c; break;
         case 5: val = t - (c <= nc ? s_coff[c] : p.chunk_offsets[c]); break;
         case 6: val = t; break;
-        case 7: val = p.feat_digest[t]; break;
+        case 7: val = pre; break;
         default: {
-          uint64_t cs = (uint64_t)p.checksum_base[t];
+          uint64_t cs = (uint64_t)pre;
           cs = addmod(cs, mulmod_coeff((uint64_t)r, c_checksum_coeff[2]));
           cs = addmod(cs, mulmod_coeff((uint64_t)e, c_checksum_coeff[3]));
           val = (long long)cs;
@@ -465,7 +487,7 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
     } else if (lane == 16) {
       ((int*)(base + p.layout.recv_retrow))[grow] = t * k + j;
     } else if (lane == 17) {
-      ((float*)(base + p.layout.recv_gate))[grow] = d.gate_mode ? p.gates[i] : 1.f;
+      ((float*)(base + p.layout.recv_gate))[grow] = gate;
     }
   }
 }

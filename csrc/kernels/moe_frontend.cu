@@ -109,6 +109,11 @@ struct FrontHooks {
   __device__ bool before(int q) {
     const int lane = threadIdx.x & 31;
     const int need = trigger_last_chunk(q, P, C) + 1;
+    if (chunks_ready >= need) {  // fetched with an earlier trigger: no global traffic
+      if (lane == 0 && f->phase_trace) trace_begin(&f->phase_trace[C + q]);
+      if (q < 16) cta_stamp(*f, 2 + 2 * q);
+      return true;
+    }
     int ok = 1;
     if (lane == 0) {
       const unsigned long long deadline = globaltimer_ns() + f->timeout_ns;
@@ -141,15 +146,18 @@ struct FrontHooks {
     __threadfence();
     __syncwarp();
     const int lo = chunks_ready;
+    const int nd = (hi - lo) * cpc, nt = nd + (hi - lo) * E;
     #pragma unroll 1
-    for (int i = lane; i < (hi - lo) * cpc; i += 32) {
-      const int c = lo + i / cpc, j = i % cpc;
-      const int off = s_coff[c];
-      const int size = s_coff[c + 1] - off;
-      s_dst[c * cpc + j] = j < size ? f->cp.expert_ids[(long long)(off + j) * f->cp.top_k] % f->cp.ctl_nodes : -1;
+    for (int i = lane; i < nt; i += 32) {  // destinations and counts in one pass (loads overlap)
+      if (i < nd) {
+        const int c = lo + i / cpc, j = i % cpc;
+        const int off = s_coff[c];
+        const int size = s_coff[c + 1] - off;
+        s_dst[c * cpc + j] = j < size ? f->cp.expert_ids[(long long)(off + j) * f->cp.top_k] % f->cp.ctl_nodes : -1;
+      } else {
+        s_ccount[lo * E + (i - nd)] = f->chunk_counts[(long long)lo * E + (i - nd)];
+      }
     }
-    #pragma unroll 1
-    for (int i = lane; i < (hi - lo) * E; i += 32) s_ccount[lo * E + i] = f->chunk_counts[(long long)lo * E + i];
     chunks_ready = hi;
     __syncwarp();
     if (lane == 0 && f->phase_trace) trace_begin(&f->phase_trace[C + q]);
@@ -174,7 +182,8 @@ struct FrontHooks {
     if (q < 16) cta_stamp(*f, 3 + 2 * q);
     if (lane == 0) {
       if (f->phase_trace) trace_end(&f->phase_trace[C + q]);
-      __threadfence();
+      // the warp barrier above orders every lane's stores (bases, counts,
+      // permit, log) before this release, which publishes them at gpu scope
       st_release_gpu_u64(&f->desc_ready[q], epoch);
     }
     __syncwarp();
