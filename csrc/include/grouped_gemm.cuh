@@ -169,16 +169,18 @@ __device__ __forceinline__ void gemm_epilogue_row(const GroupedGemmParams& p, co
   }
 }
 
-// Staged epilogue (CTA-pair kernel): per 32-column chunk the warp writes its
-// 32 rows x 32 columns into a padded shared-memory tile (row pitch
-// 32 * sizeof(OutT) + 16 bytes, so both the row-wise writes and the column-wise
-// reads below are bank-conflict free), then reads it back so that each store
-// instruction covers 32 / CH whole 128- or 64-byte row pieces instead of 32
-// scattered 16-byte pieces (CH = 16-byte chunks per row piece).  Rows keep
-// their own mapped output row and validity (shuffled from the row's lane).
+// Staged epilogue (CTA-pair kernel): per 64-byte row piece (16 fp32 or 32
+// bf16 columns) the warp writes its 32 rows into a padded shared-memory tile
+// (row pitch 80 bytes: the row-wise 16-byte writes of eight lanes hit eight
+// distinct bank quads), then reads it back so that each store instruction
+// covers eight whole 64-byte row pieces instead of 32 scattered 16-byte
+// pieces.  Rows keep their own mapped output row and validity (shuffled from
+// the row's lane).  A 2.5 KB tile per warp leaves room for a sixth 32 KB
+// operand stage at BN = 256.
 template <typename OutT>
 struct EpiTile {
-  static constexpr int ROW_BYTES = 32 * (int)sizeof(OutT);
+  static constexpr int ROW_BYTES = 64;
+  static constexpr int COLS = ROW_BYTES / (int)sizeof(OutT);
   static constexpr int PITCH = ROW_BYTES + 16;
   static constexpr int BYTES = 32 * PITCH;  // per epilogue warp
   static constexpr int CH = ROW_BYTES / 16;
@@ -189,6 +191,7 @@ template <int BN, Act ACT, typename OutT>
 __device__ __forceinline__ void gemm_epilogue_staged(const GroupedGemmParams& p, const GemmSegment& seg, int nb,
                                                      int r_local, uint32_t t_row, int c0, int c1, uint8_t* tile) {
   using TL = EpiTile<OutT>;
+  static_assert(TL::COLS == 16 || TL::COLS == 32, "a row piece holds one or two 16-column TMEM loads");
   const int lane = threadIdx.x & 31;
   const bool valid = r_local < seg.rows;
   const int arow = seg.a_row0 + r_local;
@@ -201,6 +204,20 @@ __device__ __forceinline__ void gemm_epilogue_staged(const GroupedGemmParams& p,
   OutT* out = (OutT*)p.out_ptrs[seg.out_slot];
   const float* bias = p.bias ? p.bias + (long long)seg.expert * p.N + nb * BN : nullptr;
   uint8_t* my_row = tile + lane * TL::PITCH;
+  // store the staged row pieces of columns [col, col + COLS)
+  auto flush = [&](int col) {
+    __syncwarp();
+#pragma unroll
+    for (int pass = 0; pass < TL::CH; ++pass) {
+      const int row = pass * TL::ROWS_PER_PASS + lane / TL::CH;  // tile row this lane stores
+      const int k = lane % TL::CH;                                 // its 16-byte chunk
+      const long long orow_r = __shfl_sync(0xffffffffu, orow, row);
+      const int valid_r = __shfl_sync(0xffffffffu, (int)valid, row);
+      const uint4 q = *(const uint4*)(tile + row * TL::PITCH + k * 16);
+      if (valid_r) *(uint4*)((uint8_t*)(out + orow_r * p.ldo + nb * BN + col) + k * 16) = q;
+    }
+    __syncwarp();
+  };
 #pragma unroll 1
   for (int c = c0; c < c1; c += 32) {
     uint32_t r0[16], r1[16];
@@ -212,21 +229,17 @@ __device__ __forceinline__ void gemm_epilogue_staged(const GroupedGemmParams& p,
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = apply_act(__uint_as_float(r0[j]) + b[j], ACT) * scale;
     store16((OutT*)my_row, v);
+    if constexpr (TL::COLS == 16) flush(c);
     load_bias16(bias ? bias + c + 16 : nullptr, b);
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = apply_act(__uint_as_float(r1[j]) + b[j], ACT) * scale;
-    store16((OutT*)my_row + 16, v);
-    __syncwarp();
-#pragma unroll
-    for (int pass = 0; pass < TL::CH; ++pass) {
-      const int row = pass * TL::ROWS_PER_PASS + lane / TL::CH;  // tile row this lane stores
-      const int k = lane % TL::CH;                                 // its 16-byte chunk
-      const long long orow_r = __shfl_sync(0xffffffffu, orow, row);
-      const int valid_r = __shfl_sync(0xffffffffu, (int)valid, row);
-      const uint4 q = *(const uint4*)(tile + row * TL::PITCH + k * 16);
-      if (valid_r) *(uint4*)((uint8_t*)(out + orow_r * p.ldo + nb * BN + c) + k * 16) = q;
+    if constexpr (TL::COLS == 16) {
+      store16((OutT*)my_row, v);
+      flush(c + 16);
+    } else {
+      store16((OutT*)my_row + 16, v);
+      flush(c);
     }
-    __syncwarp();
   }
 }
 

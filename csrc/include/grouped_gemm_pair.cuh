@@ -25,6 +25,74 @@
 
 namespace raiccl {
 
+// Tile t of the pair kernel.  Full tiles come first, in segment order, then
+// the swapped tail tiles (GroupedGemmParams::tail_prefix); nsw is 0 for a full
+// tile and the tail's row count rounded up to 16 for a swapped one.
+struct PairTile {
+  int s, mb, nb, nsw;
+};
+
+__device__ __forceinline__ PairTile pair_tile(const GroupedGemmParams& p, int t, int total_full, int nblocks) {
+  PairTile r;
+  if (t < total_full) {
+    r.s = find_segment(p.tile_prefix, p.num_segs, t);
+    const int local = t - p.tile_prefix[r.s];
+    r.mb = local / nblocks;
+    r.nb = local % nblocks;
+    r.nsw = 0;
+  } else {
+    const int u = t - total_full;
+    r.s = find_segment(p.tail_prefix, p.num_segs, u);
+    r.nb = u - p.tail_prefix[r.s];
+    const int rows = p.segs[r.s].rows;
+    r.mb = (rows - 1) / 256;
+    r.nsw = (rows - r.mb * 256 + 15) & ~15;
+  }
+  return r;
+}
+
+__device__ __forceinline__ void store1(float* dst, float v) { *dst = v; }
+__device__ __forceinline__ void store1(__nv_bfloat16* dst, float v) { *dst = __float2bfloat16_rn(v); }
+
+// Epilogue of a swapped tail tile.  The accumulator holds output features in
+// TMEM lanes (this CTA's 128 of the tile's 256: column nb * BN + feat for the
+// calling thread) and the tail's tokens in TMEM columns [0, nsw).  Warps ew
+// and ew + 4 split the token columns; for each token the warp's 32 lanes store
+// 32 consecutive features of that token's output row.
+template <int BN, Act ACT, typename OutT>
+__device__ __forceinline__ void gemm_epilogue_swapped(const GroupedGemmParams& p, const GemmSegment& seg,
+                                                      const PairTile& pt, int feat, uint32_t t_row, int ew) {
+  const int lane = threadIdx.x & 31;
+  int c0, c1;
+  epi_columns(ew, pt.nsw, c0, c1);
+  const int row0 = pt.mb * 256;       // first segment row of the tail tile
+  const int rem = seg.rows - row0;    // its valid tokens
+  OutT* out = (OutT*)p.out_ptrs[seg.out_slot];
+  const int col = pt.nb * BN + feat;
+  const float b = p.bias ? __ldg(p.bias + (long long)seg.expert * p.N + col) : 0.f;
+#pragma unroll 1
+  for (int c = c0; c < c1; c += 16) {
+    uint32_t r[16];
+    tmem_ld16(t_row + c, r);
+    // lanes 0..15 fetch the output row and scale of tokens c .. c + 15
+    const int tok = c + (lane & 15);
+    long long orow = 0;
+    float sc = 1.f;
+    if (tok < rem) {
+      const int arow = seg.a_row0 + row0 + tok;
+      orow = p.row_map ? (long long)__ldg(p.row_map + arow) : (long long)(seg.out_row0 + row0 + tok);
+      if (p.row_scale) sc = __ldg(p.row_scale + arow);
+    }
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const long long o = __shfl_sync(0xffffffffu, orow, j);
+      const float sj = __shfl_sync(0xffffffffu, sc, j);
+      if (c + j < rem) store1(out + o * p.ldo + col, apply_act(__uint_as_float(r[j]) + b, ACT) * sj);
+    }
+  }
+}
+
 template <int BN, bool TF32, typename OutT = float>
 struct PairCfg {
   static constexpr int BM = 128;                  // rows per CTA; the pair's tile has 256
@@ -89,7 +157,10 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
   griddep_launch_dependents();
   if (p.trace != nullptr && threadIdx.x == 0) atomicMin(&p.trace->t_start, (unsigned long long)globaltimer_ns());
 
-  const int total_tiles = p.tile_prefix[p.num_segs];
+  // Swapped tail tiles need the weights to fill the 256-row operand: BN = 256.
+  const bool swapping = BN == 256 && ACT != Act::kSwiGLU && p.tail_prefix != nullptr;
+  const int total_full = p.tile_prefix[p.num_segs];
+  const int total_tiles = total_full + (swapping ? p.tail_prefix[p.num_segs] : 0);
   const int nblocks = p.N / BN;
   const int kblocks = (p.K + C::BK - 1) / C::BK;
   const uint64_t lim = p.timeout_ns;
@@ -99,12 +170,11 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     if (elect_one_sync()) {
       int stage = 0; uint32_t phase = 0;
       for (int t = pair; t < total_tiles; t += npairs) {
-        const int s = find_segment(p.tile_prefix, p.num_segs, t);
-        const GemmSegment seg = p.segs[s];
-        const int local = t - p.tile_prefix[s];
-        const int mb = local / nblocks, nb = local % nblocks;
-        const int arow = seg.a_row0 + mb * 2 * C::BM + (int)rank * C::BM;
-        const int brow = seg.expert * p.N + nb * BN + (int)rank * C::BNH;
+        const PairTile pt = pair_tile(p, t, total_full, nblocks);
+        const GemmSegment seg = p.segs[pt.s];
+        // a swapped tile's tokens are the N operand: each CTA stages half of them
+        const int arow = seg.a_row0 + pt.mb * 2 * C::BM + (int)rank * (pt.nsw ? pt.nsw / 2 : C::BM);
+        const int brow = seg.expert * p.N + pt.nb * BN + (int)rank * C::BNH;
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, p.status, kKernelId, lim)) { ok = false; break; }
@@ -128,19 +198,24 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
         if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1u, p.status, kKernelId, lim)) break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * BN;
+        // swapped tail: weights (the B stage) are the M = 256 operand, tokens N = nsw
+        const int nsw = t < total_full ? 0 : pair_tile(p, t, total_full, nblocks).nsw;
+        const uint32_t idesc = nsw ? umma_idesc(TF32 ? 2u : 1u, 256, (uint32_t)nsw) : C::IDESC;
+        const uint32_t swap_off = nsw ? (uint32_t)C::A_BYTES : 0u;
         bool ok = true;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait_bounded(&full_bar[stage], phase, p.status, kKernelId, lim)) { ok = false; break; }
           tc_fence_after_sync();
-          const uint32_t a_addr = smem_u32(stage_base + stage * C::STAGE_BYTES);
-          const uint32_t b_addr = a_addr + C::A_BYTES;
+          const uint32_t stage_addr = smem_u32(stage_base + stage * C::STAGE_BYTES);
+          const uint32_t a_addr = stage_addr + swap_off;
+          const uint32_t b_addr = stage_addr + (C::A_BYTES - swap_off);
 #pragma unroll
           for (int k = 0; k < C::BK / C::UK; ++k) {
             const uint64_t ad = umma_desc_k_sw128(a_addr + k * 32);
             const uint64_t bd = umma_desc_k_sw128(b_addr + k * 32);
             const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
-            if (TF32) umma_tf32_pair(d_tmem, ad, bd, C::IDESC, accum);
-            else umma_f16_pair(d_tmem, ad, bd, C::IDESC, accum);
+            if (TF32) umma_tf32_pair(d_tmem, ad, bd, idesc, accum);
+            else umma_f16_pair(d_tmem, ad, bd, idesc, accum);
           }
           const uint32_t eb = smem_u32(&empty_bar[stage]);
           umma_commit_pair(mapa_shared(eb, 0));
@@ -166,19 +241,21 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     for (int t = pair; t < total_tiles; t += npairs, ++iter) {
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
-      const int s = find_segment(p.tile_prefix, p.num_segs, t);
-      const GemmSegment seg = p.segs[s];
-      const int local = t - p.tile_prefix[s];
-      const int mb = local / nblocks, nb = local % nblocks;
+      const PairTile pt = pair_tile(p, t, total_full, nblocks);
+      const GemmSegment seg = p.segs[pt.s];
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.status, kKernelId, lim)) break;
       tc_fence_after_sync();
-      const int r_local = mb * 2 * C::BM + (int)rank * C::BM + row_in_tile;
+      const int r_local = pt.mb * 2 * C::BM + (int)rank * C::BM + row_in_tile;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      if constexpr (ACT == Act::kSwiGLU)
-        gemm_epilogue_row<BN, ACT, OutT>(p, seg, nb, r_local, t_row, c0, c1);
-      else
-        gemm_epilogue_staged<BN, ACT, OutT>(p, seg, nb, r_local, t_row, c0, c1,
-                                            epi_base + (warp - 2) * EpiTile<OutT>::BYTES);
+      if constexpr (ACT == Act::kSwiGLU) {
+        gemm_epilogue_row<BN, ACT, OutT>(p, seg, pt.nb, r_local, t_row, c0, c1);
+      } else {
+        if (pt.nsw)
+          gemm_epilogue_swapped<BN, ACT, OutT>(p, seg, pt, (int)rank * C::BNH + row_in_tile, t_row, warp - 2);
+        else
+          gemm_epilogue_staged<BN, ACT, OutT>(p, seg, pt.nb, r_local, t_row, c0, c1,
+                                              epi_base + (warp - 2) * EpiTile<OutT>::BYTES);
+      }
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[acc]), 0));

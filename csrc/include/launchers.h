@@ -12,9 +12,12 @@
 namespace raiccl {
 
 // prefix[s] = sum over segments j < s of ceil(rows_j / bm) * nblocks (bm = 128 for
-// the one-CTA kernel, 256 for the CTA-pair kernel).
+// the one-CTA kernel, 256 for the CTA-pair kernel).  With tail != nullptr and
+// swap > 0, a segment's last row tile of at most swap rows is counted in
+// tail[] instead of prefix[] (GroupedGemmParams::tail_prefix).
 void launch_tile_plan(const GemmSegment* segs, int num_segs, int nblocks, int* prefix,
-                      cudaStream_t stream, TraceSlot* trace = nullptr, int bm = 128);
+                      cudaStream_t stream, TraceSlot* trace = nullptr, int bm = 128,
+                      int* tail = nullptr, int swap = 0);
 
 // in_tf32: A/B hold fp32 (tf32 math) else bf16; out_bf16 selects the output dtype.
 void launch_gg_tf32_f32(int act, int bn, const CUtensorMap& ta, const CUtensorMap& tb,

@@ -64,6 +64,12 @@ struct PlanParams {
   int32_t* prefix2;
   int nblocks1, nblocks2;
   int bm1, bm2;
+  // Swapped tail tiles (CTA-pair GEMMs at BN = 256): when swap1 > 0, a
+  // segment's last 256-row tile of at most swap1 rows is left out of prefix1
+  // and counted in tail1 instead (nblocks1 tiles); likewise swap2 / tail2.
+  int32_t* tail1;
+  int32_t* tail2;
+  int swap1, swap2;
 };
 
 struct ReturnMetaParams {

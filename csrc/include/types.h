@@ -67,6 +67,14 @@ struct GroupedGemmParams {
   TraceSlot* trace;          // launch trace slot or nullptr
   int pair;                  // 1: CTA-pair kernel (256-row tiles in tile_prefix), 0: one CTA per 128-row tile
   int pdl;                   // 1: launch as a programmatic dependent of the previous kernel in the stream
+  // CTA-pair kernel at BN = 256 only: [num_segs + 1] cumulative counts of
+  // swapped tail tiles, or nullptr.  When given, tile_prefix counts every
+  // segment's 256-row tiles except a last tile of at most swap_max rows; that
+  // tail tile is computed with the operands swapped (weights as the 256-row
+  // operand, the tail's tokens as N = rows rounded up to 16) and is ordered
+  // after all full tiles.
+  const int* tail_prefix;
+  int swap_max;
 };
 
 }  // namespace raiccl

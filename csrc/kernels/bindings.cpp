@@ -23,7 +23,7 @@ void grouped_gemm(torch::Tensor A, torch::Tensor B, torch::Tensor segs, torch::T
                   int64_t N, int64_t bn, int64_t act, c10::optional<torch::Tensor> bias,
                   c10::optional<torch::Tensor> row_map, c10::optional<torch::Tensor> row_scale,
                   torch::Tensor out_ptrs, int64_t ldo, bool out_bf16, torch::Tensor status,
-                  int64_t grid, int64_t timeout_ns, bool pair) {
+                  int64_t grid, int64_t timeout_ns, bool pair, int64_t swap_max) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && segs.is_cuda() && prefix.is_cuda() &&
                   out_ptrs.is_cuda() && status.is_cuda(),
               "grouped_gemm: CUDA tensors required");
@@ -64,8 +64,18 @@ void grouped_gemm(torch::Tensor A, torch::Tensor B, torch::Tensor segs, torch::T
                                               B.stride(0), (uint32_t)(pair ? bn / 2 : bn), bk);
   const int S = (int)segs.size(0);
   const int nblocks = (int)(N / bn);
+  // swapped tail tiles: CTA-pair kernel at BN = 256 without SwiGLU; their
+  // table follows the full-tile table in `prefix`
+  const bool swapping = swap_max > 0;
+  if (swapping) {
+    TORCH_CHECK(pair && bn == 256 && act != (int64_t)raiccl::Act::kSwiGLU && swap_max <= 256,
+                "grouped_gemm: swap_max needs the CTA-pair kernel at BN 256 without SwiGLU, swap_max <= 256");
+    TORCH_CHECK(prefix.numel() >= 2 * (segs.size(0) + 1), "grouped_gemm: prefix int32 [2 (S+1)] with swap_max");
+  }
+  int* tail = swapping ? prefix.data_ptr<int>() + S + 1 : nullptr;
   raiccl::launch_tile_plan((const raiccl::GemmSegment*)segs.data_ptr<int>(), S, nblocks,
-                           prefix.data_ptr<int>(), cur_stream(), nullptr, pair ? 256 : 128);
+                           prefix.data_ptr<int>(), cur_stream(), nullptr, pair ? 256 : 128,
+                           tail, (int)swap_max);
   raiccl::GroupedGemmParams p{};  // value-initialised: fields this call does not set (trace, ...) are null
   p.segs = (const raiccl::GemmSegment*)segs.data_ptr<int>();
   p.tile_prefix = prefix.data_ptr<int>();
@@ -80,6 +90,8 @@ void grouped_gemm(torch::Tensor A, torch::Tensor B, torch::Tensor segs, torch::T
   p.status = (raiccl::DeviceStatus*)status.data_ptr();
   p.timeout_ns = (unsigned long long)timeout_ns;
   p.pair = pair ? 1 : 0;
+  p.tail_prefix = tail;
+  p.swap_max = (int)swap_max;
   raiccl::launch_grouped_gemm(tf32, out_bf16, (int)act, (int)bn, ta, tb, p, (int)grid,
                               cur_stream());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -95,6 +107,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("A"), py::arg("B"), py::arg("segs"), py::arg("prefix"), py::arg("N"),
         py::arg("bn"), py::arg("act"), py::arg("bias"), py::arg("row_map"), py::arg("row_scale"),
         py::arg("out_ptrs"), py::arg("ldo"), py::arg("out_bf16"), py::arg("status"),
-        py::arg("grid"), py::arg("timeout_ns"), py::arg("pair") = false);
+        py::arg("grid"), py::arg("timeout_ns"), py::arg("pair") = false, py::arg("swap_max") = 0);
   register_moe(m);
 }

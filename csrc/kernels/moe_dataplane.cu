@@ -155,6 +155,16 @@ __global__ void __launch_bounds__(kDispatchThreads) moe_dispatch_kernel(Dispatch
 // Expert plan: wait (bounded) for every (source, descriptor) ready signal,
 // then emit one grouped-GEMM segment per (local expert slot, source).
 // ---------------------------------------------------------------------------
+// Tiles of one segment in a GEMM tile table: ceil(rows / bm) row tiles times
+// nblocks column tiles.  With swap > 0 a last row tile of at most swap rows
+// is counted apart (tail = nblocks) for the swapped-operand tail pass.
+__device__ __forceinline__ void plan_tiles(int rows, int bm, int nblocks, int swap, int& full, int& tail) {
+  const int mt = (rows + bm - 1) / bm;
+  const bool sw = swap > 0 && mt > 0 && rows - (mt - 1) * bm <= swap;
+  full = (mt - (sw ? 1 : 0)) * nblocks;
+  tail = sw ? nblocks : 0;
+}
+
 __global__ void moe_expert_plan_kernel(PlanParams p) {
   griddep_wait();  // programmatic dependent of the front end (no-op otherwise)
   griddep_launch_dependents();
@@ -173,13 +183,13 @@ __global__ void moe_expert_plan_kernel(PlanParams p) {
   __syncthreads();
   const int* counts = (const int*)(mine + p.layout.recv_count);
   // Each thread owns a contiguous run of segments, so the GEMM tile tables
-  // (exclusive prefix of ceil(rows / bm) * nblocks per segment, for both
-  // GEMMs) come out of one block scan in this same launch.
+  // (exclusive prefixes of plan_tiles counts per segment, for both GEMMs)
+  // come out of one block scan in this same launch.
   const int S = d.expert_slots * d.world;
   const int per = (S + blockDim.x - 1) / blockDim.x;
   const int s0 = threadIdx.x * per;
   const int s1 = min(S, s0 + per);
-  int local1 = 0, local2 = 0;
+  int local[4] = {0, 0, 0, 0};  // full tiles of GEMM 1, its swapped tails, and the same for GEMM 2
   for (int s = s0; s < s1; ++s) {
     int rows = 0;
     if (s_ok) {
@@ -196,34 +206,46 @@ __global__ void moe_expert_plan_kernel(PlanParams p) {
     p.segs[s] = seg;
     p.rows_out[s] = rows;
     if (p.prefix1 != nullptr) {
-      local1 += ((rows + p.bm1 - 1) / p.bm1) * p.nblocks1;
-      local2 += ((rows + p.bm2 - 1) / p.bm2) * p.nblocks2;
+      int f, tl;
+      plan_tiles(rows, p.bm1, p.nblocks1, p.swap1, f, tl);
+      local[0] += f; local[1] += tl;
+      plan_tiles(rows, p.bm2, p.nblocks2, p.swap2, f, tl);
+      local[2] += f; local[3] += tl;
     }
   }
   if (p.prefix1 == nullptr) return;
-  __shared__ int s_scan1[256], s_scan2[256];
-  s_scan1[threadIdx.x] = local1;
-  s_scan2[threadIdx.x] = local2;
+  __shared__ int s_scan[4][256];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) s_scan[a][threadIdx.x] = local[a];
   __syncthreads();
   for (int off = 1; off < (int)blockDim.x; off <<= 1) {
-    const int v1 = threadIdx.x >= off ? s_scan1[threadIdx.x - off] : 0;
-    const int v2 = threadIdx.x >= off ? s_scan2[threadIdx.x - off] : 0;
+    int v[4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) v[a] = threadIdx.x >= off ? s_scan[a][threadIdx.x - off] : 0;
     __syncthreads();
-    s_scan1[threadIdx.x] += v1;
-    s_scan2[threadIdx.x] += v2;
+#pragma unroll
+    for (int a = 0; a < 4; ++a) s_scan[a][threadIdx.x] += v[a];
     __syncthreads();
   }
-  int run1 = s_scan1[threadIdx.x] - local1, run2 = s_scan2[threadIdx.x] - local2;
+  int run[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) run[a] = s_scan[a][threadIdx.x] - local[a];
+  int32_t* out[4] = {p.prefix1, p.tail1, p.prefix2, p.tail2};
   for (int s = s0; s < s1; ++s) {
-    p.prefix1[s] = run1;
-    p.prefix2[s] = run2;
     const int rows = p.rows_out[s];
-    run1 += ((rows + p.bm1 - 1) / p.bm1) * p.nblocks1;
-    run2 += ((rows + p.bm2 - 1) / p.bm2) * p.nblocks2;
+    int c[4];
+    plan_tiles(rows, p.bm1, p.nblocks1, p.swap1, c[0], c[1]);
+    plan_tiles(rows, p.bm2, p.nblocks2, p.swap2, c[2], c[3]);
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      if (out[a] != nullptr) out[a][s] = run[a];
+      run[a] += c[a];
+    }
   }
   if (threadIdx.x == blockDim.x - 1) {
-    p.prefix1[S] = s_scan1[threadIdx.x];
-    p.prefix2[S] = s_scan2[threadIdx.x];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+      if (out[a] != nullptr) out[a][S] = s_scan[a][threadIdx.x];
   }
 }
 

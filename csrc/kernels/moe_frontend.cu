@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   // inputs resident at launch (not streamed in by the copy engine during this call)
   const bool resident = f.tok_ready == nullptr || ld_acquire_gpu_u64(f.tok_ready_all) >= epoch;
   // start pulling this worker's token rows of every chunk into L2
-  if (NT > 0 && resident) {
+  if constexpr (NT > 0) if (resident) {
     const int row_bytes = f.rp.hidden * (int)sizeof(T);
     for (int c = 0; c < C; ++c) {
       const int t0 = s_coff[c], t1 = s_coff[c + 1];

@@ -108,6 +108,12 @@ class MoELayerRunner {
       const bool allow = !ints.contains("gemm_pair") || geti(ints, "gemm_pair") != 0;
       pair1_ = allow && bn1_ >= 64;
       pair2_ = allow && bn2_ >= 64;
+      // swapped tail tiles: CTA-pair kernel at BN = 256, not for SwiGLU (its
+      // tile interleaves gate and up columns)
+      const int swap = ints.contains("gemm_swap_max") ? geti(ints, "gemm_swap_max") : 128;
+      if (swap < 0 || swap > 256) throw std::invalid_argument("gemm_swap_max must be in [0, 256]");
+      swap1_ = pair1_ && bn1_ == 256 && act1_ != (int)raiccl::Act::kSwiGLU ? swap : 0;
+      swap2_ = pair2_ && bn2_ == 256 ? swap : 0;
     }
     timeout_ns_ = (unsigned long long)ints["timeout_ns"].cast<int64_t>();
     max_cands_ = geti(ints, "max_cands");
@@ -421,6 +427,12 @@ class MoELayerRunner {
     pp.nblocks2 = d.out_dim / bn2_;
     pp.bm1 = pair1_ ? 256 : 128;
     pp.bm2 = pair2_ ? 256 : 128;
+    int* tail1 = swap1_ ? ptr<int>(t, "tail1") : nullptr;
+    int* tail2 = swap2_ ? ptr<int>(t, "tail2") : nullptr;
+    pp.tail1 = tail1;
+    pp.tail2 = tail2;
+    pp.swap1 = swap1_;
+    pp.swap2 = swap2_;
     raiccl::launch_expert_plan(pp, comm_, pdl_);
     ++launches;
 
@@ -446,6 +458,8 @@ class MoELayerRunner {
     raiccl::GroupedGemmParams g1{};
     g1.segs = segs;
     g1.tile_prefix = prefix1;
+    g1.tail_prefix = tail1;
+    g1.swap_max = swap1_;
     g1.num_segs = S;
     g1.N = n1_;
     g1.K = d.hidden;
@@ -465,6 +479,8 @@ class MoELayerRunner {
     raiccl::GroupedGemmParams g2{};
     g2.segs = segs;
     g2.tile_prefix = prefix2;
+    g2.tail_prefix = tail2;
+    g2.swap_max = swap2_;
     g2.num_segs = S;
     g2.N = d.out_dim;
     g2.K = ffn_;
@@ -665,6 +681,7 @@ class MoELayerRunner {
   raiccl::PeerBases peers_{};
   int partial_ = 0, ffn_ = 0, n1_ = 0, act1_ = 0, bn1_ = 0, bn2_ = 0;
   bool pair1_ = false, pair2_ = false;  // GEMM 1 / 2 on the CTA-pair kernel
+  int swap1_ = 0, swap2_ = 0;            // GEMM 1 / 2 swapped-tail row limit (0: off)
   bool pdl_ = true;  // plan, GEMMs and combine as programmatic dependents of their predecessors
   int max_cands_ = 0, log_stride_ = 0, max_ctl_tokens_ = 0, grid_sms_ = 148;
   bool control_serial_ = false;  // run the CTA control kernel even where the single-warp one fits

@@ -37,13 +37,15 @@ def main() -> None:
                     help="one cooperative front-end launch, or one launch per router chunk / trigger / descriptor")
     ap.add_argument("--control-clocks", action="store_true", help="per-trigger control phase clocks")
     ap.add_argument("--streamed", action="store_true", help="end-to-end calls with a streamed host batch")
+    ap.add_argument("--gemm-swap-max", type=int, default=128,
+                    help="swapped-operand tail tiles of at most this many rows (0: off)")
     args = ap.parse_args()
     cfg = preset(args.config)
     if args.tokens:
         n = cfg.chunks
         cfg = cfg.with_overrides(tokens_per_rank=args.tokens, chunk_sizes=(args.tokens // n,) * n)
     layer = ProgressiveMoELayer(cfg, device=torch.device("cuda", 0), timeout_s=10.0, trace=bool(args.trace),
-                                frontend=args.frontend)
+                                frontend=args.frontend, gemm_swap_max=args.gemm_swap_max)
     try:
         layer.forward(args.arm)
         if args.graph:

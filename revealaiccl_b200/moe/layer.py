@@ -55,7 +55,7 @@ class ProgressiveMoELayer:
                  world: int | None = None, rank: int | None = None, group=None,
                  timeout_s: float = 10.0, seed: int = 0, control_topology=None,
                  control_path: str = "auto", trace: bool = False, frontend: str = "persistent",
-                 gemm_pair: bool = True, pdl: bool = True) -> None:
+                 gemm_pair: bool = True, pdl: bool = True, gemm_swap_max: int = 128) -> None:
         self.cfg = cfg
         if world is None:
             world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -140,6 +140,9 @@ class ProgressiveMoELayer:
             "frontend": {"steps": 0, "persistent": 1}[frontend],
             "gemm_pair": int(bool(gemm_pair)),
             "pdl": int(bool(pdl)),
+            # CTA-pair GEMMs at BN = 256: a segment's last row tile of at most this
+            # many rows runs with swapped operands (0 disables)
+            "gemm_swap_max": int(gemm_swap_max),
         }
         self.layout = self._k.sym_layout(ints)
         self.channel = PeerChannel(self.layout["total"], dev, group=group)
@@ -189,6 +192,8 @@ class ProgressiveMoELayer:
             "segs": self.segs, "rows_out": self.rows_out,
             "prefix1": torch.zeros(nseg + 1, dtype=torch.int32, device=dev),
             "prefix2": torch.zeros(nseg + 1, dtype=torch.int32, device=dev),
+            "tail1": torch.zeros(nseg + 1, dtype=torch.int32, device=dev),
+            "tail2": torch.zeros(nseg + 1, dtype=torch.int32, device=dev),
             "w1": w1l.reshape(self.slots * cfg.gemm1_n, D).contiguous(),
             "b1": b1l.reshape(-1).contiguous() if has_b1 else None,
             "w2": w2l.reshape(self.slots * O, F_).contiguous(),

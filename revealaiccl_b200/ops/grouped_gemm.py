@@ -87,12 +87,17 @@ def grouped_gemm(
     timeout_ns: int = DEFAULT_TIMEOUT_NS,
     check: bool = False,
     pair: bool = False,
+    swap_max: int = 0,
 ) -> torch.Tensor | None:
     """Launch the grouped GEMM on the current stream.
 
     Either ``out`` (a local tensor, slot 0) or ``out_ptrs`` (int64 device
     pointers, one per ``out_slot``) must be given.  ``pair=True`` runs the
-    CTA-pair kernel (256 x bn tiles on clusters of two SMs; bn >= 64).  With ``check=True`` the
+    CTA-pair kernel (256 x bn tiles on clusters of two SMs; bn >= 64).
+    ``swap_max > 0`` (pair kernel, bn = 256, no SwiGLU) computes a segment's
+    last 256-row tile of at most ``swap_max`` rows with swapped operands: the
+    weights fill the 256-row side and the tail's tokens the narrow N side, so
+    a short tail costs a fraction of a full tile.  With ``check=True`` the
     call synchronises and raises on a recorded device status.
     """
     mod = kernels()
@@ -109,12 +114,14 @@ def grouped_gemm(
     if status is None:
         status = _status.new_status(A.device)
     if prefix is None:
-        prefix = torch.empty(segs.shape[0] + 1, dtype=torch.int32, device=A.device)
+        tables = 2 if swap_max > 0 else 1  # full-tile table, then the swapped-tail table
+        prefix = torch.empty(tables * (segs.shape[0] + 1), dtype=torch.int32, device=A.device)
     if grid is None:
         grid = num_sms(A.device)
     mod.grouped_gemm(
         A, B, segs, prefix, int(n), int(bn), ACT_IDS[act], bias, row_map, row_scale,
         out_ptrs, int(ldo), bool(out_bf16), status, int(grid), int(timeout_ns), bool(pair),
+        int(swap_max),
     )
     if check:
         torch.cuda.synchronize(A.device)

@@ -168,3 +168,44 @@ def test_cta_pair_kernel_matches_fp32_reference_and_single_cta(dtype, act, bn):
     torch.testing.assert_close(outs[True][valid], ref[valid], atol=tol, rtol=tol)
     assert torch.equal(outs[True][valid], outs[False][valid])
     assert torch.isnan(outs[True][~valid]).all()  # rows outside every segment are never written
+
+
+@pytest.mark.parametrize("dtype,act,out_dtype", [("tf32", "gelu", torch.float32), ("bf16", "none", torch.bfloat16),
+                                                 ("bf16", "silu", torch.float32)])
+def test_cta_pair_swapped_tail_tiles(dtype, act, out_dtype):
+    """Swapped tail tiles (weights as the 256-row operand, a short tail's tokens
+    as N) against the fp32 reference, with a row map and row scales, on tails
+    of 1..129 rows, an expert of one row and an empty segment."""
+    gg = _gg()
+    torch.manual_seed(11)
+    dev = torch.device("cuda")
+    k, n, E = 384, 512, 4
+    seg_rows = [(0, 300, 2), (300, 0, 1), (300, 1, 0), (301, 513, 3), (814, 257, 1), (1071, 16, 2),
+                (1087, 17, 0), (1104, 384, 3), (1488, 385, 1)]
+    total = 1873
+    dt = torch.float32 if dtype == "tf32" else torch.bfloat16
+    A = torch.randn(total, k, device=dev).to(dt)
+    B = (torch.randn(E * n, k, device=dev) / k ** 0.5).to(dt)
+    bias = torch.randn(E * n, device=dev) * 0.1
+    perm = torch.randperm(total, device=dev).to(torch.int32)
+    scale = torch.rand(total, device=dev) + 0.5
+    segs_list = [(a0, r, e, 0, a0) for (a0, r, e) in seg_rows]
+    segs = gg.make_segments(segs_list, dev)
+    valid = torch.zeros(total, dtype=torch.bool, device=dev)
+    for (a0, r, e) in seg_rows:
+        valid[a0:a0 + r] = True
+    outs = {}
+    for swap in (128, 0):
+        out = torch.full((total, n), float("nan"), device=dev, dtype=out_dtype)
+        gg.grouped_gemm(A, B, segs, n=n, act=act, bias=bias, row_map=perm, row_scale=scale, out=out, bn=256,
+                        check=True, pair=True, swap_max=swap)
+        outs[swap] = out.float()
+    ref_rows = _ref(A, B, segs_list, n, act, bias=bias, row_scale=scale, out_rows=total)
+    ref = torch.full((total, n), float("nan"), device=dev)
+    ref[perm.long()[valid]] = ref_rows[valid]
+    written = torch.zeros(total, dtype=torch.bool, device=dev)
+    written[perm.long()[valid]] = True
+    tol = 5e-3 if dtype == "tf32" else 3e-2
+    torch.testing.assert_close(outs[128][written], ref[written], atol=tol, rtol=tol)
+    torch.testing.assert_close(outs[128][written], outs[0][written], atol=tol, rtol=tol)
+    assert torch.isnan(outs[128][~written]).all()  # rows outside every segment are never written
