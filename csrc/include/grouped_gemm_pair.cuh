@@ -117,8 +117,8 @@ struct PairCfg {
 
 template <int BN, bool TF32, Act ACT, typename OutT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
-grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                         GroupedGemmParams p) {
+grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_a8,
+                         const __grid_constant__ CUtensorMap tmap_b, GroupedGemmParams p) {
   using C = PairCfg<BN, TF32, OutT>;
   constexpr int kKernelId = 300 + BN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -145,6 +145,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     fence_mbarrier_init();
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    if (p.tail_prefix != nullptr) tma_prefetch_desc(&tmap_a8);
   }
   if (warp == 1) { tmem_alloc_pair(tmem_slot, C::TMEM_COLS); tmem_relinquish_pair(); }
   tc_fence_before_sync();
@@ -179,9 +180,17 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, p.status, kKernelId, lim)) { ok = false; break; }
           uint8_t* sa = stage_base + stage * C::STAGE_BYTES;
-          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * C::STAGE_BYTES);
+          // a swapped tile stages only its nsw / 2 token rows per CTA (8-row boxes,
+          // each one 1024-byte swizzle atom)
+          if (rank == 0)
+            mbar_arrive_expect_tx(&full_bar[stage], pt.nsw ? 2 * C::B_BYTES + pt.nsw * 128 : 2 * C::STAGE_BYTES);
           const uint32_t leader_full = mapa_shared(smem_u32(&full_bar[stage]), 0);
-          tma_load_2d_pair(sa, &tmap_a, leader_full, kb * C::BK, arow);
+          if (pt.nsw) {
+            for (int j = 0; j < pt.nsw / 16; ++j)
+              tma_load_2d_pair(sa + j * 1024, &tmap_a8, leader_full, kb * C::BK, arow + j * 8);
+          } else {
+            tma_load_2d_pair(sa, &tmap_a, leader_full, kb * C::BK, arow);
+          }
           tma_load_2d_pair(sa + C::A_BYTES, &tmap_b, leader_full, kb * C::BK, brow);
           if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -273,8 +282,8 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
 }
 
 template <int BN, bool TF32, Act ACT, typename OutT>
-inline void launch_one_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GroupedGemmParams& p, int grid,
-                            cudaStream_t stream) {
+inline void launch_one_pair(const CUtensorMap& ta, const CUtensorMap& ta8, const CUtensorMap& tb,
+                            const GroupedGemmParams& p, int grid, cudaStream_t stream) {
   using C = PairCfg<BN, TF32, OutT>;
   auto kern = grouped_gemm_pair_kernel<BN, TF32, ACT, OutT>;
   static bool configured = false;
@@ -283,30 +292,30 @@ inline void launch_one_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
     configured = true;
   }
   const int g = grid & ~1;  // whole pairs
-  launch_with_pdl(kern, dim3(g < 2 ? 2 : g), dim3(kGemmThreads), C::SMEM_TOTAL, stream, p.pdl != 0, ta, tb, p);
+  launch_with_pdl(kern, dim3(g < 2 ? 2 : g), dim3(kGemmThreads), C::SMEM_TOTAL, stream, p.pdl != 0, ta, ta8, tb, p);
 }
 
 template <bool TF32, Act ACT, typename OutT>
-inline void dispatch_bn_pair(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GroupedGemmParams& p,
-                             int grid, cudaStream_t stream) {
+inline void dispatch_bn_pair(int bn, const CUtensorMap& ta, const CUtensorMap& ta8, const CUtensorMap& tb,
+                             const GroupedGemmParams& p, int grid, cudaStream_t stream) {
   switch (bn) {
-    case 64: launch_one_pair<64, TF32, ACT, OutT>(ta, tb, p, grid, stream); return;
-    case 128: launch_one_pair<128, TF32, ACT, OutT>(ta, tb, p, grid, stream); return;
-    case 256: launch_one_pair<256, TF32, ACT, OutT>(ta, tb, p, grid, stream); return;
+    case 64: launch_one_pair<64, TF32, ACT, OutT>(ta, ta8, tb, p, grid, stream); return;
+    case 128: launch_one_pair<128, TF32, ACT, OutT>(ta, ta8, tb, p, grid, stream); return;
+    case 256: launch_one_pair<256, TF32, ACT, OutT>(ta, ta8, tb, p, grid, stream); return;
     default: break;
   }
   throw std::runtime_error("grouped_gemm (pair): unsupported BN " + std::to_string(bn));
 }
 
 template <bool TF32, typename OutT>
-inline void dispatch_act_pair(int act, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
+inline void dispatch_act_pair(int act, int bn, const CUtensorMap& ta, const CUtensorMap& ta8, const CUtensorMap& tb,
                               const GroupedGemmParams& p, int grid, cudaStream_t stream) {
   switch ((Act)act) {
-    case Act::kNone: dispatch_bn_pair<TF32, Act::kNone, OutT>(bn, ta, tb, p, grid, stream); return;
-    case Act::kRelu: dispatch_bn_pair<TF32, Act::kRelu, OutT>(bn, ta, tb, p, grid, stream); return;
-    case Act::kGelu: dispatch_bn_pair<TF32, Act::kGelu, OutT>(bn, ta, tb, p, grid, stream); return;
-    case Act::kSilu: dispatch_bn_pair<TF32, Act::kSilu, OutT>(bn, ta, tb, p, grid, stream); return;
-    case Act::kSwiGLU: dispatch_bn_pair<TF32, Act::kSwiGLU, OutT>(bn, ta, tb, p, grid, stream); return;
+    case Act::kNone: dispatch_bn_pair<TF32, Act::kNone, OutT>(bn, ta, ta8, tb, p, grid, stream); return;
+    case Act::kRelu: dispatch_bn_pair<TF32, Act::kRelu, OutT>(bn, ta, ta8, tb, p, grid, stream); return;
+    case Act::kGelu: dispatch_bn_pair<TF32, Act::kGelu, OutT>(bn, ta, ta8, tb, p, grid, stream); return;
+    case Act::kSilu: dispatch_bn_pair<TF32, Act::kSilu, OutT>(bn, ta, ta8, tb, p, grid, stream); return;
+    case Act::kSwiGLU: dispatch_bn_pair<TF32, Act::kSwiGLU, OutT>(bn, ta, ta8, tb, p, grid, stream); return;
   }
   throw std::runtime_error("grouped_gemm (pair): unknown activation");
 }

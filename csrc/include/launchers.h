@@ -26,16 +26,21 @@ void launch_gg_bf16_bf16(int act, int bn, const CUtensorMap& ta, const CUtensorM
                          const GroupedGemmParams& p, int grid, cudaStream_t stream);
 void launch_gg_bf16_f32(int act, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
                         const GroupedGemmParams& p, int grid, cudaStream_t stream);
-void launch_gg_pair_tf32_f32(int act, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
-                             const GroupedGemmParams& p, int grid, cudaStream_t stream);
-void launch_gg_pair_bf16_bf16(int act, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
-                              const GroupedGemmParams& p, int grid, cudaStream_t stream);
-void launch_gg_pair_bf16_f32(int act, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
-                             const GroupedGemmParams& p, int grid, cudaStream_t stream);
+void launch_gg_pair_tf32_f32(int act, int bn, const CUtensorMap& ta, const CUtensorMap& ta8,
+                             const CUtensorMap& tb, const GroupedGemmParams& p, int grid,
+                             cudaStream_t stream);
+void launch_gg_pair_bf16_bf16(int act, int bn, const CUtensorMap& ta, const CUtensorMap& ta8,
+                              const CUtensorMap& tb, const GroupedGemmParams& p, int grid,
+                              cudaStream_t stream);
+void launch_gg_pair_bf16_f32(int act, int bn, const CUtensorMap& ta, const CUtensorMap& ta8,
+                             const CUtensorMap& tb, const GroupedGemmParams& p, int grid,
+                             cudaStream_t stream);
 // p.pair selects the CTA-pair kernel (BN in {64, 128, 256}; A tensor map box of
-// 128 rows, B box of bn / 2 rows; tile_prefix counted in 256-row tiles).
+// 128 rows, B box of bn / 2 rows; tile_prefix counted in 256-row tiles).  With
+// swapped tail tiles (p.tail_prefix) the pair kernel also needs ta8: the A
+// tensor with a box of 8 rows, so a tail tile stages only the rows it uses.
 void launch_grouped_gemm(bool in_tf32, bool out_bf16, int act, int bn, const CUtensorMap& ta,
                          const CUtensorMap& tb, const GroupedGemmParams& p, int grid,
-                         cudaStream_t stream);
+                         cudaStream_t stream, const CUtensorMap* ta8 = nullptr);
 
 }  // namespace raiccl

@@ -62,6 +62,8 @@ void grouped_gemm(torch::Tensor A, torch::Tensor B, torch::Tensor segs, torch::T
                                               A.stride(0), 128, bk);
   CUtensorMap tb = raiccl::make_tmap_2d_sw128(B.data_ptr(), dt, elem, B.size(0), B.size(1),
                                               B.stride(0), (uint32_t)(pair ? bn / 2 : bn), bk);
+  CUtensorMap ta8 = raiccl::make_tmap_2d_sw128(A.data_ptr(), dt, elem, A.size(0), A.size(1),
+                                               A.stride(0), 8, bk);
   const int S = (int)segs.size(0);
   const int nblocks = (int)(N / bn);
   // swapped tail tiles: CTA-pair kernel at BN = 256 without SwiGLU; their
@@ -93,7 +95,7 @@ void grouped_gemm(torch::Tensor A, torch::Tensor B, torch::Tensor segs, torch::T
   p.tail_prefix = tail;
   p.swap_max = (int)swap_max;
   raiccl::launch_grouped_gemm(tf32, out_bf16, (int)act, (int)bn, ta, tb, p, (int)grid,
-                              cur_stream());
+                              cur_stream(), &ta8);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -74,15 +74,18 @@ void launch_tile_plan(const GemmSegment* segs, int num_segs, int nblocks, int* p
 // SwiGLU at BN=16 (a SwiGLU tile holds gate and up halves of >=16 columns).
 void launch_grouped_gemm(bool in_tf32, bool out_bf16, int act, int bn, const CUtensorMap& ta,
                          const CUtensorMap& tb, const GroupedGemmParams& p, int grid,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, const CUtensorMap* ta8) {
   if (p.pair) {
+    if (p.tail_prefix != nullptr && ta8 == nullptr)
+      throw std::runtime_error("grouped_gemm: swapped tail tiles need the 8-row A tensor map");
+    const CUtensorMap& a8 = ta8 != nullptr ? *ta8 : ta;  // unused without swapped tiles
     if (in_tf32) {
       if (out_bf16) throw std::runtime_error("grouped_gemm: tf32 inputs produce fp32 outputs");
-      launch_gg_pair_tf32_f32(act, bn, ta, tb, p, grid, stream);
+      launch_gg_pair_tf32_f32(act, bn, ta, a8, tb, p, grid, stream);
     } else if (out_bf16) {
-      launch_gg_pair_bf16_bf16(act, bn, ta, tb, p, grid, stream);
+      launch_gg_pair_bf16_bf16(act, bn, ta, a8, tb, p, grid, stream);
     } else {
-      launch_gg_pair_bf16_f32(act, bn, ta, tb, p, grid, stream);
+      launch_gg_pair_bf16_f32(act, bn, ta, a8, tb, p, grid, stream);
     }
     return;
   }

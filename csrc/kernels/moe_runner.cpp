@@ -137,6 +137,9 @@ class MoELayerRunner {
     ta1_ = raiccl::make_tmap_2d_sw128(recv_feat, dt, eb, rows, d.hidden, d.hidden, 128, bk);
     tb1_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "w1"), dt, eb, (uint64_t)d.expert_slots * n1_, d.hidden, d.hidden, pair1_ ? bn1_ / 2 : bn1_, bk);
     ta2_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "h"), dt, eb, rows, ffn_, ffn_, 128, bk);
+    // 8-row boxes of the same A tensors: swapped tail tiles stage only the rows they use
+    ta1n_ = raiccl::make_tmap_2d_sw128(recv_feat, dt, eb, rows, d.hidden, d.hidden, 8, bk);
+    ta2n_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "h"), dt, eb, rows, ffn_, ffn_, 8, bk);
     tb2_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "w2"), dt, eb, (uint64_t)d.expert_slots * d.out_dim, ffn_, ffn_, pair2_ ? bn2_ / 2 : bn2_, bk);
 
     {
@@ -473,7 +476,7 @@ class MoELayerRunner {
     g1.pair = pair1_ ? 1 : 0;
     g1.pdl = pdl_ ? 1 : 0;
     g1.trace = trace_slot("gemm1", -1);
-    raiccl::launch_grouped_gemm(!feat_bf16_, feat_bf16_, act1_, bn1_, ta1_, tb1_, g1, grid_sms_, comm_);
+    raiccl::launch_grouped_gemm(!feat_bf16_, feat_bf16_, act1_, bn1_, ta1_, tb1_, g1, grid_sms_, comm_, &ta1n_);
     ++launches;
 
     raiccl::GroupedGemmParams g2{};
@@ -494,7 +497,7 @@ class MoELayerRunner {
     g2.pair = pair2_ ? 1 : 0;
     g2.pdl = pdl_ ? 1 : 0;
     g2.trace = trace_slot("gemm2_return", -1);
-    raiccl::launch_grouped_gemm(!feat_bf16_, out_bf16_, 0, bn2_, ta2_, tb2_, g2, grid_sms_, comm_);
+    raiccl::launch_grouped_gemm(!feat_bf16_, out_bf16_, 0, bn2_, ta2_, tb2_, g2, grid_sms_, comm_, &ta2n_);
     ++launches;
 
     raiccl::CombineParams cb{};
@@ -687,7 +690,7 @@ class MoELayerRunner {
   bool control_serial_ = false;  // run the CTA control kernel even where the single-warp one fits
   bool feat_bf16_ = false, out_bf16_ = false;
   unsigned long long timeout_ns_ = 0;
-  CUtensorMap ta1_{}, tb1_{}, ta2_{}, tb2_{};
+  CUtensorMap ta1_{}, tb1_{}, ta2_{}, tb2_{}, ta1n_{}, ta2n_{};
   cudaStream_t router_ = nullptr, comm_ = nullptr;
   cudaStream_t disp_ = nullptr;
   int device_ = 0;
