@@ -371,9 +371,11 @@ __device__ void router_group(const RouterParams& p, const float* bias, const flo
 // return run[e] holds this share's item count per expert.  Collective over the
 // CTA (contains __syncthreads); the caller checks (b - a) * k <= kDispatchMaxItems.
 // ---------------------------------------------------------------------------
-template <typename T>
-__device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, const int* base_e, int* hist, int* run,
-                              int* item_pos, const int* s_coff, int nc, bool streamed = false) {
+// Index part of dispatch_rows: hist[e] = items of expert e in [t0, a), and
+// item_pos[i - a k] = (in-order rank within its expert in [a, b)) | expert << 24.
+// Reads only the routed expert ids, so it may run before the descriptor is
+// released once its chunks are complete.  hist / run zero on entry.
+__device__ inline void dispatch_index(const DispatchParams& p, int t0, int a, int b, int* hist, int* run, int* item_pos) {
   const MoEDims& d = p.dims;
   const int k = d.top_k;
   const int E = d.experts;
@@ -421,6 +423,16 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
     }
   }
   __syncthreads();
+}
+
+// indexed: hist / run / item_pos already hold dispatch_index's result.
+template <typename T>
+__device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, const int* base_e, int* hist, int* run,
+                              int* item_pos, const int* s_coff, int nc, bool streamed = false, bool indexed = false) {
+  const MoEDims& d = p.dims;
+  const int k = d.top_k;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  if (!indexed) dispatch_index(p, t0, a, b, hist, run, item_pos);
   // copy features + identity rows, one warp per item
   const long long nitems = (long long)(b - a) * k;
   const int vec_per_row = d.hidden * d.feat_bytes / 16;

@@ -194,7 +194,7 @@ struct FrontHooks {
 template <typename T>
 __device__ void worker_dispatch(const FrontendParams& f, int q, int w, int W, unsigned long long epoch,
                                 int* hist, int* run, int* item_pos, int* s_base, const int* s_coff, int nc,
-                                int* s_flag, bool streamed) {
+                                int* s_flag, bool streamed, bool indexed = false) {
   const MoEDims& d = f.dp.dims;
   const int P = f.cp.partial_chunks, C = d.chunks, E = d.experts, k = d.top_k;
   const int t0 = s_coff[trigger_first_chunk(q, P)];
@@ -207,8 +207,10 @@ __device__ void worker_dispatch(const FrontendParams& f, int q, int w, int W, un
   const int a = t0 + min(ntok, w * per);
   const int b = t0 + min(ntok, (w + 1) * per);
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    hist[e] = 0;
-    run[e] = 0;
+    if (!indexed) {
+      hist[e] = 0;
+      run[e] = 0;
+    }
     s_base[e] = f.disp_base[(long long)q * E + e];
   }
   if (threadIdx.x == 0) *s_flag = (f.dp.permit[q] == epoch) ? 1 : 0;
@@ -218,7 +220,7 @@ __device__ void worker_dispatch(const FrontendParams& f, int q, int w, int W, un
   if (permitted && (long long)(b - a) * k > kDispatchMaxItems) {
     if (threadIdx.x == 0) record_status(f.dp.status, kBadConfig, 22, (long long)(b - a) * k, kDispatchMaxItems);
   } else if (permitted && a < b) {
-    dispatch_rows<T>(f.dp, t0, a, b, s_base, hist, run, item_pos, s_coff, nc, streamed);
+    dispatch_rows<T>(f.dp, t0, a, b, s_base, hist, run, item_pos, s_coff, nc, streamed, indexed);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -231,6 +233,45 @@ __device__ void worker_dispatch(const FrontendParams& f, int q, int w, int W, un
   if (threadIdx.x == 0) trace_end(slot);
   cta_stamp(f, 25 + 2 * q);
   __syncthreads();
+}
+
+// This worker's index part of descriptor q (dispatch_index), computed while
+// the release is still pending; worker_dispatch(..., indexed = true) then
+// only loads the bases and copies.  Collective over the CTA.
+__device__ void worker_index(const FrontendParams& f, int q, int w, int W, int* hist, int* run, int* item_pos,
+                             const int* s_coff) {
+  const MoEDims& d = f.dp.dims;
+  const int P = f.cp.partial_chunks, C = d.chunks, E = d.experts;
+  const int t0 = s_coff[trigger_first_chunk(q, P)];
+  const int t1 = s_coff[trigger_last_chunk(q, P, C) + 1];
+  const int ntok = t1 - t0;
+  const int per = (ntok + W - 1) / W;
+  const int a = t0 + min(ntok, w * per);
+  const int b = t0 + min(ntok, (w + 1) * per);
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    hist[e] = 0;
+    run[e] = 0;
+  }
+  __syncthreads();
+  if (a < b && (long long)(b - a) * d.top_k <= kDispatchMaxItems) dispatch_index(f.dp, t0, a, b, hist, run, item_pos);
+  __syncthreads();
+}
+
+// Whether every router chunk of descriptor q is complete (all W workers
+// reported it); a non-blocking poll, collective over the CTA.
+__device__ bool chunks_complete(const FrontendParams& f, int q, int W, int* s_flag) {
+  const int P = f.cp.partial_chunks, C = f.dp.dims.chunks;
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    for (int c = trigger_first_chunk(q, P); c <= trigger_last_chunk(q, P, C) && ok; ++c)
+      ok = ld_acquire_gpu_s32(&f.chunk_done[c]) >= W ? 1 : 0;
+    if (ok) __threadfence();
+    *s_flag = ok;
+  }
+  __syncthreads();
+  const bool v = *s_flag != 0;
+  __syncthreads();
+  return v;
 }
 
 // Whether descriptor q was released: 1 yes, 0 not yet (non-blocking poll),
@@ -456,8 +497,17 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   }
   if (f.delayed && wait_released(f, n_desc - 1, epoch, &s_flag, true) != 1) return;
   while (next < n_desc) {
-    if (wait_released(f, next, epoch, &s_flag, true) != 1) return;
-    worker_dispatch<T>(f, next, w, W, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident);
+    // a descriptor not yet released whose chunks are routed: compute its
+    // index part (prefix counts and ranks, from the expert ids only) while
+    // the control warp works, so the release is followed by the copy alone
+    const int rel = wait_released(f, next, epoch, &s_flag, false);
+    bool indexed = false;
+    if (rel == 0 && chunks_complete(f, next, W, &s_flag)) {
+      worker_index(f, next, w, W, hist, run, item_pos, s_coff);
+      indexed = true;
+    }
+    if (rel != 1 && wait_released(f, next, epoch, &s_flag, true) != 1) return;
+    worker_dispatch<T>(f, next, w, W, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident, indexed);
     ++next;
   }
 }
