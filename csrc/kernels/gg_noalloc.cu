@@ -43,6 +43,7 @@
 #include <exception>
 #include <mutex>
 
+#include "gg_noalloc.h"
 #include "launchers.h"
 #include "sm100_ptx.cuh"
 #include "tma_host.h"
@@ -63,9 +64,21 @@ constexpr int kPlanKernelId = 40;
 
 static __device__ __align__(256) unsigned char g_gg_noalloc_scratch[kNoAllocScratchBytes];
 
-// Clears the status record, stores the output pointer, checks the segments and
-// writes the cumulative tile table (prefix[s] = tiles of segments < s).
+// Clears the status record, stores the output pointer, checks every segment
+// against the caller's extents and writes the cumulative tile table
+// (prefix[s] = tiles of segments < s).  Any failed check records a status and
+// turns the whole call into a no-op (prefix[num_segs] = 0): the GEMM kernel
+// then runs no tile, so no out-of-range row, expert or output is touched.
+__device__ __forceinline__ bool gg_noalloc_seg_ok(const GemmSegment& g, long long rows_a, int experts,
+                                                  long long out_rows, bool mapped) {
+  if (g.rows < 0 || g.a_row0 < 0 || (long long)g.a_row0 + g.rows > rows_a) return false;
+  if (g.expert < 0 || g.expert >= experts) return false;
+  if (!mapped && (g.out_row0 < 0 || (long long)g.out_row0 + g.rows > out_rows)) return false;
+  return true;
+}
+
 __global__ void gg_noalloc_plan_kernel(const GemmSegment* segs, int num_segs, int nblocks, void* out,
+                                       long long rows_a, int experts, long long out_rows, const int* row_map,
                                        unsigned char* scratch) {
   __shared__ int partial[1024];
   DeviceStatus* st = reinterpret_cast<DeviceStatus*>(scratch + kOffStatus);
@@ -78,12 +91,25 @@ __global__ void gg_noalloc_plan_kernel(const GemmSegment* segs, int num_segs, in
   const int tid = threadIdx.x;
   const int per = (num_segs + blockDim.x - 1) / blockDim.x;
   const int s0 = tid * per;
+  const bool mapped = row_map != nullptr;
   int local = 0;
   for (int s = s0; s < s0 + per && s < num_segs; ++s) {
     const GemmSegment g = segs[s];
     if (g.out_slot != 0) record_status(st, kBadConfig, kPlanKernelId, s, 0);
+    if (!gg_noalloc_seg_ok(g, rows_a, experts, out_rows, mapped)) record_status(st, kBoundsViolation, kPlanKernelId, s, rows_a);
     const int rows = g.rows > 0 ? g.rows : 0;
     local += ((rows + 127) / 128) * nblocks;
+  }
+  if (mapped) {
+    // every mapped output row of an in-range segment must exist
+    for (int s = 0; s < num_segs; ++s) {
+      const GemmSegment g = segs[s];
+      if (!gg_noalloc_seg_ok(g, rows_a, experts, out_rows, true)) continue;
+      for (int r = tid; r < g.rows; r += blockDim.x) {
+        const int o = row_map[g.a_row0 + r];
+        if (o < 0 || (long long)o >= out_rows) record_status(st, kBoundsViolation, kPlanKernelId, g.a_row0 + r, out_rows);
+      }
+    }
   }
   partial[tid] = local;
   __syncthreads();
@@ -100,7 +126,7 @@ __global__ void gg_noalloc_plan_kernel(const GemmSegment* segs, int num_segs, in
     run += ((rows + 127) / 128) * nblocks;
   }
   if (tid == blockDim.x - 1) {
-    // a segment with out_slot != 0 turns the whole call into a no-op
+    // a rejected segment turns the whole call into a no-op
     prefix[num_segs] = st->code == 0 ? partial[tid] : 0;
   }
 }
@@ -130,11 +156,7 @@ int scratch_for_current_device(unsigned char** out) {
 
 extern "C" {
 
-// Return codes: 0 = launched; > 0 = a cudaError_t value; < 0 = rejected arguments.
-#define RAICCL_NOALLOC_TOO_MANY_SEGMENTS (-1)
-#define RAICCL_NOALLOC_BAD_ARGUMENT (-2)
-#define RAICCL_NOALLOC_LAUNCH_FAILED (-3)
-#define RAICCL_NOALLOC_BAD_DEVICE (-4)
+// Declared, with the return codes, in csrc/include/gg_noalloc.h.
 
 __attribute__((visibility("default"))) int raiccl_grouped_gemm_noalloc_max_segments(void) {
   return raiccl::kNoAllocMaxSegs;
@@ -151,23 +173,15 @@ __attribute__((visibility("default"))) const char* raiccl_grouped_gemm_noalloc_e
   }
 }
 
-// out[out_row0 + r, :] (or out[row_map[a_row0 + r], :]) =
-//     act(A[a_row0 + r] @ B[expert * N : (expert + 1) * N].T + bias[expert]) * row_scale[a_row0 + r]
-// for every segment (int32[8] records: a_row0, rows, expert, out_slot (must be 0),
-// out_row0, 3 unused).  All pointers are device pointers on the current device.
-//   in_fp32:   0 = A and B are bf16; 1 = fp32 (tf32 tensor-core math)
-//   A:         [rows_a, K], row stride lda elements;  B: [rows_b, K], row stride ldb (rows_b = E * N)
-//   bn:        tile width 16/32/64/128/256 dividing N; act: 0 none 1 relu 2 gelu 3 silu 4 swiglu
-//   bias:      fp32 [rows_b] or NULL; row_map int32 / row_scale fp32 [rows_a] or NULL
-//   out:       fp32 (out_bf16 = 0) or bf16 (out_bf16 = 1), row stride ldo elements
-//   grid:      persistent CTAs (0 = one per SM)
-// The call only enqueues work on `stream`; read the device status afterwards
-// with raiccl_grouped_gemm_noalloc_status.
+// The contract (shapes, alignment, segment checks) is written out beside the
+// declaration in csrc/include/gg_noalloc.h.  The call only enqueues work on
+// `stream`; read the device status afterwards with
+// raiccl_grouped_gemm_noalloc_status.
 __attribute__((visibility("default"))) int raiccl_grouped_gemm_noalloc(
     int in_fp32, const void* A, long long rows_a, long long K, long long lda, const void* B,
     long long rows_b, long long ldb, const void* segs, int num_segs, int N, int bn, int act,
-    const float* bias, const int* row_map, const float* row_scale, void* out, long long ldo, int out_bf16,
-    int grid, unsigned long long timeout_ns, cudaStream_t stream) {
+    const float* bias, const int* row_map, const float* row_scale, void* out, long long out_rows, long long ldo,
+    int out_bf16, int grid, unsigned long long timeout_ns, cudaStream_t stream) {
   using namespace raiccl;
   if (num_segs > kNoAllocMaxSegs) return RAICCL_NOALLOC_TOO_MANY_SEGMENTS;
   if (num_segs < 1 || A == nullptr || B == nullptr || segs == nullptr || out == nullptr) return RAICCL_NOALLOC_BAD_ARGUMENT;
@@ -176,7 +190,20 @@ __attribute__((visibility("default"))) int raiccl_grouped_gemm_noalloc(
     return RAICCL_NOALLOC_BAD_ARGUMENT;
   if (act < 0 || act > 4 || (act == 4 && bn < 32)) return RAICCL_NOALLOC_BAD_ARGUMENT;
   if (in_fp32 && out_bf16) return RAICCL_NOALLOC_BAD_ARGUMENT;
-  if ((reinterpret_cast<uintptr_t>(segs) & 15) != 0) return RAICCL_NOALLOC_BAD_ARGUMENT;
+  // 16-byte vector accesses: segment records, bias loads, output row stores,
+  // TMA operand rows; 4-byte loads of row_map / row_scale
+  auto misaligned = [](const void* q, uintptr_t a) { return (reinterpret_cast<uintptr_t>(q) & (a - 1)) != 0; };
+  if (misaligned(segs, 16) || misaligned(A, 16) || misaligned(B, 16) || misaligned(out, 16)) return RAICCL_NOALLOC_BAD_ARGUMENT;
+  if ((bias != nullptr && misaligned(bias, 16)) || (row_map != nullptr && misaligned(row_map, 4)) ||
+      (row_scale != nullptr && misaligned(row_scale, 4)))
+    return RAICCL_NOALLOC_BAD_ARGUMENT;
+  {
+    const long long in_elem = in_fp32 ? 4 : 2, out_elem = out_bf16 ? 2 : 4;
+    const long long out_width = act == 4 ? N / 2 : N;
+    if ((lda * in_elem) % 16 != 0 || (ldb * in_elem) % 16 != 0) return RAICCL_NOALLOC_BAD_ARGUMENT;
+    if (out_rows < 1 || ldo < out_width || (ldo * out_elem) % 16 != 0) return RAICCL_NOALLOC_BAD_ARGUMENT;
+    if (rows_a > 0x7fffffffLL || rows_b / N > 0x7fffffffLL || out_rows > 0x7fffffffLL) return RAICCL_NOALLOC_BAD_ARGUMENT;
+  }
   unsigned char* scratch = nullptr;
   const int rc = scratch_for_current_device(&scratch);
   if (rc != 0) return rc;
@@ -192,7 +219,8 @@ __attribute__((visibility("default"))) int raiccl_grouped_gemm_noalloc(
     const CUtensorMap ta = make_tmap_2d_sw128(A, dt, elem, rows_a, K, lda, 128, 128 / elem);
     const CUtensorMap tb = make_tmap_2d_sw128(B, dt, elem, rows_b, K, ldb, (uint32_t)bn, 128 / elem);
     const GemmSegment* sg = static_cast<const GemmSegment*>(segs);
-    gg_noalloc_plan_kernel<<<1, 1024, 0, stream>>>(sg, num_segs, N / bn, out, scratch);
+    gg_noalloc_plan_kernel<<<1, 1024, 0, stream>>>(sg, num_segs, N / bn, out, rows_a, (int)(rows_b / N), out_rows,
+                                                    row_map, scratch);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
     GroupedGemmParams p{};  // value-initialised: fields this call does not set (trace, ...) are null
