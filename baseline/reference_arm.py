@@ -12,7 +12,15 @@ reference's own full-MoE primary makespan (first Router launch -> combined
 output, ``timing.primary_makespan_us``), max over ranks.
 
 The reference driver hard-codes a world size of two (``main`` raises on any
-other size), so every other GPU count prints an ``unavailable`` line.
+other size, and ``_run_arm`` builds its packing state with ``world_size=2``),
+so every other GPU count prints an ``unavailable`` line.
+
+End to end: before each early-arm call the case's tokens are copied from
+pinned host memory into the device tensor the reference reads
+(``tokens_device``), on the current stream, which ``_run_arm`` synchronises
+before its first Router launch.  The reference's combined output is a host
+array when ``primary_done_host_ns`` is taken, so the end-to-end time is that
+stamp minus the host clock read just before the copy (same monotonic clock).
 """
 
 from __future__ import annotations
@@ -22,6 +30,7 @@ import os
 from pathlib import Path
 import statistics
 import sys
+import time
 
 REF_ROOT = Path(__file__).resolve().parent / "_ref"
 
@@ -30,7 +39,7 @@ def _unavailable(why: str) -> dict:
     return {"impl": "reference", "unavailable": why}
 
 
-def run_reference(args) -> dict | None:
+def run_reference(args, clock_sampler=None) -> dict | None:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if not (REF_ROOT / "scripts" / "run_r4_a0_c0_full_moe.py").exists():
@@ -81,25 +90,45 @@ def run_reference(args) -> dict | None:
         masks = tuple(mask.narrow(0, case_data["chunk_offsets"][i], case_data["chunk_sizes"][i])
                       for i in range(r4.CHUNKS))
 
-        def arm(name: str) -> float:
+        host_tokens = torch.from_numpy(case_data["tokens"]).pin_memory()
+
+        def arm(name: str, copy_in: bool = False) -> tuple[float, float]:
             dist.barrier()
+            t0 = time.monotonic_ns()
+            if copy_in:
+                tokens.copy_(host_tokens, non_blocking=True)
             res = r4._run_arm(
                 arm=name, case_name=case, rank=rank, topology=topology, plan=plan, bridge=bridge,
                 case_data=case_data, tokens_device=tokens, token_chunks=chunks, mask_chunks=masks,
                 router_weight=router_weight, router_bias=bias, expert_weights=expert_weights,
                 router_stream=router_stream, comm_stream=comm_stream)
-            return float(res["timing"]["primary_makespan_us"]) / 1e3
+            timing = res["timing"]
+            return (float(timing["primary_makespan_us"]) / 1e3,
+                    (int(timing["primary_done_host_ns"]) - t0) / 1e6)
 
         for _ in range(args.warmup):
-            arm("C")
+            arm("C", copy_in=True)
             arm("D")
-        early, delayed = [], []
+        bus = None
+        props = torch.cuda.get_device_properties(device)
+        if hasattr(props, "pci_bus_id") and hasattr(props, "pci_device_id"):
+            bus = f"{int(props.pci_bus_id):02X}:{int(props.pci_device_id):02X}.0"
+        gathered = [None] * world
+        dist.all_gather_object(gathered, bus)
+        sampler = clock_sampler([b for b in gathered if b]) if (clock_sampler and rank == 0) else None
+        if sampler:
+            sampler.__enter__()
+        early, delayed, e2e = [], [], []
         for _ in range(args.steps):
-            early.append(arm("C"))
-            delayed.append(arm("D"))
-        t = torch.tensor([early, delayed], dtype=torch.float64, device=device)
+            ms, e2e_ms = arm("C", copy_in=True)
+            early.append(ms)
+            e2e.append(e2e_ms)
+            delayed.append(arm("D")[0])
+        if sampler:
+            sampler.__exit__(None, None, None)
+        t = torch.tensor([early, delayed, e2e], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        early, delayed = t[0].tolist(), t[1].tolist()
+        early, delayed, e2e = t[0].tolist(), t[1].tolist(), t[2].tolist()
         bridge.stop()
     finally:
         dist.barrier()
@@ -111,13 +140,21 @@ def run_reference(args) -> dict | None:
         "impl": "reference", "metric": "full MoE layer p50 ms + Delta=T_delayed-T_early", "value": round(p50, 4),
         "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(statistics.fmean(early), 4), "higher_is_better": False, "scaling": "weak",
-        "vs_baseline": round(p50 / 480.265, 6), "dtype": "fp32",
+        "vs_baseline": round(p50 / 480.265, 6),
+        "vs_baseline_note": "reference published p50 of the same R4 config on 2x V100 (other hardware)",
+        "dtype": "fp32",
         "data": "synthetic (reference balanced case; seeded reference weights)",
         "config": {"model": "r4_reference: 4 experts top-1, D=2048, expert 2048->32 relu->16",
                    "global_batch": r4.TOTAL_TOKENS * world, "seq_len": r4.TOTAL_TOKENS, "parallelism": f"ep{world}",
                    "timing": "reference primary makespan (host monotonic ns), max over ranks"},
         "p50_early_ms": round(p50, 4), "p50_delayed_ms": round(statistics.median(delayed), 4),
         "delta_ms": round(statistics.median([d - e for e, d in zip(early, delayed)]), 4),
+        "e2e": {"value": round(statistics.median(e2e), 4), "unit": "ms",
+                "h2d_bytes_per_step": int(host_tokens.numel() * host_tokens.element_size()),
+                "d2h_bytes_per_step": int(r4.TOTAL_TOKENS * r4.EXPERT_OUTPUT * 4),
+                "timing": "pinned H2D of the case tokens + the reference primary path, whose combined "
+                          "output is a host array (host monotonic ns), max over ranks"},
+        "clocks": sampler.summary() if sampler else None,
     }
 
 

@@ -162,6 +162,7 @@ class MoELayerRunner {
     ck(cudaEventCreateWithFlags(&ev_plan_, cudaEventDisableTiming), "cudaEventCreate");
     ck(cudaEventCreateWithFlags(&ev_retmeta_, cudaEventDisableTiming), "cudaEventCreate");
     ck(cudaEventCreateWithFlags(&ev_call_done_, cudaEventDisableTiming), "cudaEventCreate");
+    ck(cudaEventCreateWithFlags(&ev_entry_, cudaEventDisableTiming), "cudaEventCreate");
     ev_tok_.resize(d.chunks);
     for (auto& e : ev_tok_) ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
     ck(cudaStreamCreateWithFlags(&sig_, cudaStreamNonBlocking), "cudaStreamCreate");
@@ -185,6 +186,7 @@ class MoELayerRunner {
     if (ev_plan_) cudaEventDestroy(ev_plan_);
     if (ev_retmeta_) cudaEventDestroy(ev_retmeta_);
     if (ev_call_done_) cudaEventDestroy(ev_call_done_);
+    if (ev_entry_) cudaEventDestroy(ev_entry_);
     for (auto& e : ev_tok_) cudaEventDestroy(e);
     if (sig_) cudaStreamDestroy(sig_);
     if (ev_start_) cudaEventDestroy(ev_start_);
@@ -536,8 +538,11 @@ class MoELayerRunner {
   // stream-ordered write of this call's epoch into tok_ready[c], which the
   // front end's workers wait for before routing the chunk (so the copy of
   // later chunks overlaps the routing, control and dispatch of earlier ones).
-  // The copies start once the previous call has finished with the token
-  // buffer; the caller orders copy_stream and the comm stream after its work.
+  // The copies start once everything already enqueued on the comm stream has
+  // run (the previous call, which reads the token buffer, and any work the
+  // caller put there, such as the start event of a timed region), so a call's
+  // host-to-device traffic lies inside any window that the caller opens on
+  // the comm stream before the call.
   int stream_call(int64_t host_ptr, int64_t copy_stream, bool delayed) {
     c10::cuda::CUDAGuard guard(device_);
     if (!use_frontend_ || tok_ready_ == nullptr)
@@ -549,11 +554,12 @@ class MoELayerRunner {
     auto* dst = ptr<uint8_t>(tensors_, "tokens");
     const auto* src = reinterpret_cast<const uint8_t*>(host_ptr);
     ck(write_value(comm_, stream_pending_, 1), "stream write (pending)");
-    ck(cudaStreamWaitEvent(copy, ev_call_done_, 0), "cudaStreamWaitEvent");
+    ck(cudaEventRecord(ev_entry_, comm_), "cudaEventRecord");
+    ck(cudaStreamWaitEvent(copy, ev_entry_, 0), "cudaStreamWaitEvent");
     // The copies run back to back on the copy stream; a second stream turns
     // each copy's completion event into its arrival word, so no stream write
     // sits between two copies (each would hold the next copy until it ran).
-    ck(cudaStreamWaitEvent(sig_, ev_call_done_, 0), "cudaStreamWaitEvent");
+    ck(cudaStreamWaitEvent(sig_, ev_entry_, 0), "cudaStreamWaitEvent");
     for (int c = 0; c < d.chunks; ++c) {
       const size_t off = (size_t)chunk_offsets_[c] * row_bytes;
       const size_t n = (size_t)(chunk_offsets_[c + 1] - chunk_offsets_[c]) * row_bytes;
@@ -709,6 +715,7 @@ class MoELayerRunner {
   }
   cudaEvent_t ev_start_ = nullptr, ev_disp_done_ = nullptr, ev_plan_ = nullptr, ev_retmeta_ = nullptr;
   cudaEvent_t ev_call_done_ = nullptr;  // end of the last executed call on the comm stream
+  cudaEvent_t ev_entry_ = nullptr;      // comm stream at the entry of a streamed call
   std::vector<cudaEvent_t> ev_tok_;     // streamed chunk c copied
   cudaStream_t sig_ = nullptr;          // publishes streamed-chunk arrival words
   unsigned long long calls_ = 0;        // executed calls (== the device epoch after them)

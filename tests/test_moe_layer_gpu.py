@@ -291,3 +291,39 @@ def test_streamed_inputs_match_resident_calls():
         assert layer.runner.calls() == int(layer.tensors["epoch"].item())
     finally:
         layer.close()
+
+
+@pytest.mark.gpu
+def test_streamed_copies_start_inside_the_callers_window():
+    """A timed end-to-end region opened on the comm stream must contain the
+    call's host-to-device copies: the copy stream waits for everything already
+    enqueued on the comm stream.  A 5 ms device sleep sits on the comm stream
+    before the start event; copies that did not wait for it would finish
+    before the start event."""
+    from revealaiccl_b200.moe.config import preset
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    layer = ProgressiveMoELayer(preset("full_tf32").with_overrides(tokens_per_rank=2048, chunk_sizes=(256,) * 8),
+                                timeout_s=5.0)
+    try:
+        layer.forward("early")
+        torch.cuda.synchronize()
+        host_in = torch.empty(layer.inputs.tokens.shape, dtype=layer.inputs.tokens.dtype, pin_memory=True)
+        host_in.copy_(layer.inputs.tokens.cpu())
+        host_out = torch.empty(layer.out.shape, dtype=layer.out.dtype, pin_memory=True)
+        cs = layer.comm_stream
+        for graph in (False, True):
+            if graph:
+                layer.capture("early")
+            s = torch.cuda.Event(enable_timing=True)
+            copied = torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(cs):
+                torch.cuda._sleep(int(5e-3 * 1.9e9))  # ~5 ms at the maximum SM clock
+            s.record(cs)
+            layer(host_in, host_out, arm="early")
+            copied.record(layer.copy_stream)  # after the call's last chunk copy
+            torch.cuda.synchronize()
+            assert s.elapsed_time(copied) > 0.0, graph
+            assert layer.verify()["pass"]
+    finally:
+        layer.close()
