@@ -583,6 +583,51 @@ class DynamicGuard:
             rows.append((-1 if o is None else int(o), int(a.edge_index)))
         return np.asarray(rows, dtype=np.int64).reshape(-1, 2)
 
+    def _first_refusal(self, state: IncrementalState, proposal: Proposal, semantics: bool) -> str | None:
+        """NumPy form of the guard: every action's checks are evaluated as
+        columns of one table, and the verdict is the first failing check of
+        the first failing action (the order the trusted checker uses), then
+        the slot's edge and group budgets."""
+        plan = self.plan
+        E = len(plan.edges)
+        n = len(proposal.actions)
+        ords = np.fromiter((state.token_ordinals.get(a.token_id, -1) for a in proposal.actions), np.int64, n)
+        edges = np.fromiter((int(a.edge_index) for a in proposal.actions), np.int64, n)
+        o = np.clip(ords, 0, max(state.revealed_count - 1, 0))
+        revealed = (ords >= 0) & (ords < state.revealed_count)
+        revealed &= np.asarray(state.ready, dtype=bool)[o] if state.revealed_count else False
+        # an ordinal that an earlier action of the slot already named
+        _, first = np.unique(ords, return_index=True)
+        earlier = np.ones(n, dtype=bool)
+        earlier[first] = False
+        in_range = (edges >= 0) & (edges < E)
+        e = np.where(in_range, edges, 0)
+        src, tgt = np.asarray(plan.edge_sources)[e], np.asarray(plan.edge_targets)[e]
+        held = np.asarray(state.holders, dtype=bool)
+        columns = [
+            ("unrevealed", ~revealed),
+            ("duplicate_in_slot", earlier),
+            ("edge_range", ~in_range),
+            ("source_holder", ~held[o, src]),
+            ("duplicate_commit", held[o, tgt] | np.asarray(state.committed_bitmap, dtype=bool)[o, e]),
+        ]
+        if semantics:
+            hops = np.asarray(state.remaining_hops, dtype=np.int64)[o]
+            to_dst = np.asarray(plan.distances)[tgt, np.asarray(state.destinations, dtype=np.int64)[o]]
+            columns.append(("residual_demand", ~np.asarray(state.residual_token, dtype=bool)[o] | (hops <= 0)
+                            | (to_dst != hops - 1)))
+        fails = np.stack([bad for _, bad in columns], axis=1)
+        if fails.any():
+            i = int(np.flatnonzero(fails.any(axis=1))[0])
+            return columns[int(np.flatnonzero(fails[i])[0])][0]
+        load = np.bincount(edges, minlength=E)
+        if np.any(load > np.asarray(plan.capacity_units)):
+            return "edge_capacity"
+        for g, members in enumerate(plan.group_edges):
+            if int(load[np.asarray(members, dtype=np.int64)].sum()) > int(plan.group_limits[g]):
+                return "bandwidth_group"
+        return None
+
     def check(self, state: IncrementalState, proposal: Proposal, *,
               require_scheduler_semantics: bool = False,
               expected_state_version: int | None = None) -> GuardDecision:
@@ -602,36 +647,9 @@ class DynamicGuard:
                 if code != 0:
                     raise ValueError(GUARD_REASONS[code])
                 return GuardDecision(True, None, len(proposal.actions), state.state_version + 1)
-            state._scratch_seen_tokens.fill(False)
-            state._scratch_edge_load.fill(0)
-            E = len(self.plan.edges)
-            for a in proposal.actions:
-                o = state.token_ordinals.get(a.token_id)
-                if o is None or o >= state.revealed_count or not state.ready[o]:
-                    raise ValueError("unrevealed")
-                if state._scratch_seen_tokens[o]:
-                    raise ValueError("duplicate_in_slot")
-                state._scratch_seen_tokens[o] = True
-                e = int(a.edge_index)
-                if e < 0 or e >= E:
-                    raise ValueError("edge_range")
-                s, t = int(self.plan.edge_sources[e]), int(self.plan.edge_targets[e])
-                if not state.holders[o, s]:
-                    raise ValueError("source_holder")
-                if state.holders[o, t] or state.committed_bitmap[o, e]:
-                    raise ValueError("duplicate_commit")
-                if require_scheduler_semantics:
-                    d = int(state.destinations[o])
-                    before = int(state.remaining_hops[o])
-                    if (not state.residual_token[o] or before <= 0
-                            or int(self.plan.distances[t, d]) != before - 1):
-                        raise ValueError("residual_demand")
-                state._scratch_edge_load[e] += 1
-            if np.any(state._scratch_edge_load > self.plan.capacity_units):
-                raise ValueError("edge_capacity")
-            for g, members in enumerate(self.plan.group_edges):
-                if sum(int(state._scratch_edge_load[e]) for e in members) > int(self.plan.group_limits[g]):
-                    raise ValueError("bandwidth_group")
+            reason = self._first_refusal(state, proposal, bool(require_scheduler_semantics))
+            if reason is not None:
+                raise ValueError(reason)
             return GuardDecision(True, None, len(proposal.actions), state.state_version + 1)
         except Exception as error:  # fail closed
             return GuardDecision(False, str(error), 0, state.state_version)

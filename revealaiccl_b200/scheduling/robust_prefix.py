@@ -1,23 +1,36 @@
-"""Reference (uncompiled) planner primitives — the oracle of the compiled scheduler.
+"""Uncompiled planner primitives: the oracle of the compiled scheduler, and the
+robust-prefix planner of the recourse study.
 
-Behaviour of rlccl/scheduling/robust_prefix.py:63-452:
+Semantics of rlccl/scheduling/robust_prefix.py:63-452 (kept, because the
+compiled scheduler, the device control plane and the recourse runner must
+reproduce them exactly):
 
-* ``canonical_shortest_path``: BFS over *usable* edges (unit capacity >= 1 and
-  every group containing the edge has limit >= 1), expanding each node's
-  out-edges in (target node, edge index) order, so ties go to the smaller
-  destination id first ("destination-first tie").  It runs a BFS per call.
-* ``enumerate_candidates``: for every revealed token with 0 < d(holders, dst)
-  < inf, every usable edge from a holder to a non-holder that reduces the
-  global distance by exactly one; sorted by (token ordinal, edge index).
-* ``pack_candidate_batch``: greedy, one hop per token, edge and group unit
-  budgets.
-* robust scoring (criticality, utility, robust score) and
-  ``RobustPrefixPlanner`` for the research arm (H/P allowlist, lambda in
-  {0, .5, 1}, K in {1, 8}).
+* routes use *usable* edges only (capacity units >= 1 and every shared group
+  containing the edge has limit units >= 1); a shortest route is found by BFS
+  that expands each node's out-edges in (target node, edge index) order, so
+  ties go to the smaller target id first ("destination-first");
+* a candidate is one hop of a revealed token from a holder to a non-holder
+  over a usable edge that lowers the token's distance to its destination by
+  exactly one; candidates are ordered by (token ordinal, edge index);
+* a batch is packed greedily from an ordered candidate list: at most one hop
+  per token, within every edge's and every group's unit budget;
+* the robust score of a hop is the weighted mean minus lambda times the
+  weighted standard deviation, over scenarios, of
+  1 + 0.25 * criticality - 0.05 * distance-after, where criticality sums the
+  scenario's residual load over capacity units of the edge and of each group
+  containing it.
+
+Mechanics of this module: every topology gets one cached ``_Routes`` table,
+built by a BFS from each source (V BFS runs in total, instead of one per
+query): the all-pairs distance matrix and each source's BFS parent edges,
+from which a canonical route is read back.  Candidate enumeration is then a
+vectorised edge mask per token, batch packing keeps running edge and group
+loads, and a residual projection adds whole route incidence vectors.
 """
 
 from __future__ import annotations
 
+from collections import OrderedDict
 from dataclasses import dataclass, replace
 import hashlib
 import math
@@ -30,6 +43,8 @@ from ..uncertainty.observation import PublicTopologyView, readonly_array
 SCORE_TIE_TOLERANCE = 1e-12
 LEGAL_HORIZON_PREFIX = frozenset({(2, 1), (4, 1), (4, 2), (8, 1), (8, 2), (8, 4),
                                   (16, 1), (16, 2), (16, 4), (16, 8)})
+RISK_LAMBDAS = (0.0, 0.5, 1.0)
+REQUESTED_K = (1, 8)
 
 
 class UnreachableScenarioError(ValueError):
@@ -44,56 +59,154 @@ class StaleSupportError(ValueError):
     pass
 
 
-def canonical_digest(value: Any) -> str:
-    """sha256 over a typed, length-prefixed encoding (floats by their hex form)."""
-    out = bytearray()
-
-    def enc(item: Any) -> None:
-        if item is None:
-            out.extend(b"N|")
-        elif isinstance(item, (bool, np.bool_)):
-            out.extend(b"B1|" if bool(item) else b"B0|")
-        elif isinstance(item, (int, np.integer)):
-            out.extend(f"I{int(item)}|".encode())
-        elif isinstance(item, (float, np.floating)):
-            f = float(item)
+# --------------------------------------------------------------------- digest
+def _digest_parts(item: Any, out: bytearray) -> None:
+    """Typed, length-prefixed encoding (floats by their exact hex form)."""
+    stack = [item]
+    while stack:
+        x = stack.pop()
+        if x is None:
+            out += b"N|"
+        elif isinstance(x, (bool, np.bool_)):
+            out += b"B1|" if x else b"B0|"
+        elif isinstance(x, (int, np.integer)):
+            out += b"I%d|" % int(x)
+        elif isinstance(x, (float, np.floating)):
+            f = float(x)
             if not math.isfinite(f):
                 raise ValueError("digest values must be finite")
-            out.extend(f"F{f.hex()}|".encode())
-        elif isinstance(item, str):
-            raw = item.encode()
-            out.extend(f"S{len(raw)}:".encode() + raw + b"|")
-        elif isinstance(item, np.ndarray):
-            enc({"dtype": item.dtype.str, "shape": list(item.shape), "data": item.reshape(-1).tolist()})
-        elif hasattr(item, "__dataclass_fields__"):
-            enc({k: getattr(item, k) for k in item.__dataclass_fields__})
-        elif isinstance(item, dict):
-            keys = sorted(item, key=lambda k: str(k).encode())
-            out.extend(f"M{len(keys)}:".encode())
-            for k in keys:
-                enc(str(k))
-                enc(item[k])
-        elif isinstance(item, (list, tuple)):
-            out.extend(f"L{len(item)}:".encode())
-            for v in item:
-                enc(v)
-        elif isinstance(item, np.generic):
-            enc(item.item())
+            out += b"F" + f.hex().encode() + b"|"
+        elif isinstance(x, str):
+            raw = x.encode()
+            out += b"S%d:" % len(raw) + raw + b"|"
+        elif isinstance(x, np.ndarray):
+            stack.append({"dtype": x.dtype.str, "shape": list(x.shape), "data": x.reshape(-1).tolist()})
+        elif hasattr(x, "__dataclass_fields__"):
+            stack.append({k: getattr(x, k) for k in x.__dataclass_fields__})
+        elif isinstance(x, dict):
+            keys = sorted(x, key=lambda k: str(k).encode())
+            out += b"M%d:" % len(keys)
+            for k in reversed(keys):  # the stack pops them back in key order
+                stack.append(x[k])
+                stack.append(str(k))
+        elif isinstance(x, (list, tuple)):
+            out += b"L%d:" % len(x)
+            stack.extend(reversed(x))
+        elif isinstance(x, np.generic):
+            stack.append(x.item())
         else:
-            raise TypeError(f"unsupported digest type: {type(item).__name__}")
+            raise TypeError(f"unsupported digest type: {type(x).__name__}")
 
-    enc(value)
+
+def canonical_digest(value: Any) -> str:
+    """sha256 of the typed encoding of ``value`` (nested containers, dataclasses, arrays)."""
+    out = bytearray()
+    _digest_parts(value, out)
     return hashlib.sha256(bytes(out)).hexdigest()
 
 
+# ------------------------------------------------------------------- topology
 def _topology(topology: Any) -> tuple[int, np.ndarray, np.ndarray, tuple[Any, ...]]:
     nodes = int(getattr(topology, "num_nodes", getattr(topology, "V", 0)))
-    edges = np.asarray(getattr(topology, "edges"), dtype=np.int64)
-    caps = np.asarray(getattr(topology, "capacities"), dtype=np.float64)
+    edges = np.asarray(topology.edges, dtype=np.int64).reshape(-1, 2)
+    caps = np.asarray(topology.capacities, dtype=np.float64)
     groups = tuple(getattr(topology, "shared_constraints", ()))
     return nodes, edges, caps, groups
 
 
+def atomic_units(raw: float) -> int:
+    """Whole transfer units a capacity allows per slot."""
+    v = float(raw)
+    if not (math.isfinite(v) and v >= 0):
+        raise ValueError("a capacity is finite and nonnegative")
+    return int(math.floor(v))
+
+
+class _Routes:
+    """Usable edges, all-pairs BFS distances and canonical parent edges of one topology."""
+
+    def __init__(self, topology: Any) -> None:
+        nodes, edges, caps, groups = _topology(topology)
+        self.nodes, self.edges = nodes, edges
+        self.edge_units = np.asarray([atomic_units(c) for c in caps], dtype=np.int64)
+        self.groups = tuple((np.asarray(list(m), dtype=np.int64), lim) for m, lim in groups)
+        self.group_units = np.asarray([atomic_units(lim) if len(m) else 0 for m, lim in self.groups],
+                                      dtype=np.int64)
+        usable = self.edge_units >= 1
+        for (members, _), units in zip(self.groups, self.group_units):
+            if len(members) and units < 1:
+                usable[members] = False
+        self.usable = usable
+        # groups containing each edge, in group order, and how many times each
+        # lists the edge (a group's load counts an edge once per listing)
+        self.edge_groups: list[list[int]] = [[] for _ in range(len(edges))]
+        self.edge_group_mult: list[dict[int, int]] = [{} for _ in range(len(edges))]
+        for g, (members, _) in enumerate(self.groups):
+            for e in members.tolist():
+                if g not in self.edge_group_mult[e]:
+                    self.edge_groups[e].append(g)
+                self.edge_group_mult[e][g] = self.edge_group_mult[e].get(g, 0) + 1
+        ids = np.flatnonzero(usable)
+        ids = ids[np.lexsort((ids, edges[ids, 1], edges[ids, 0]))]  # by source, then target, then edge
+        starts = np.searchsorted(edges[ids, 0], np.arange(nodes + 1))
+        self.dist = np.full((nodes, nodes), np.inf)
+        self.parent = np.full((nodes, nodes), -1, dtype=np.int64)
+        for s in range(nodes):
+            self.dist[s, s] = 0.0
+            queue = [s]
+            for u in queue:
+                for e in ids[starts[u]:starts[u + 1]].tolist():
+                    t = int(edges[e, 1])
+                    if self.dist[s, t] == np.inf:
+                        self.dist[s, t] = self.dist[s, u] + 1.0
+                        self.parent[s, t] = e
+                        queue.append(t)
+
+    def path(self, source: int, destination: int) -> tuple[int, ...]:
+        if source == destination:
+            return ()
+        if self.dist[source, destination] == np.inf:
+            raise UnreachableScenarioError(f"unreachable OD {source}->{destination}")
+        hops = []
+        node = destination
+        while node != source:
+            e = int(self.parent[source, node])
+            hops.append(e)
+            node = int(self.edges[e, 0])
+        return tuple(reversed(hops))
+
+
+_ROUTE_CACHE: "OrderedDict[tuple, _Routes]" = OrderedDict()
+
+
+def _routes(topology: Any) -> _Routes:
+    nodes, edges, caps, groups = _topology(topology)
+    key = (nodes, edges.tobytes(), caps.tobytes(),
+           tuple((tuple(int(e) for e in m), float(lim)) for m, lim in groups))
+    hit = _ROUTE_CACHE.get(key)
+    if hit is None:
+        hit = _Routes(topology)
+        _ROUTE_CACHE[key] = hit
+        if len(_ROUTE_CACHE) > 64:
+            _ROUTE_CACHE.popitem(last=False)
+    else:
+        _ROUTE_CACHE.move_to_end(key)
+    return hit
+
+
+def edge_usable(topology: Any, edge: int) -> bool:
+    return bool(_routes(topology).usable[int(edge)])
+
+
+def canonical_shortest_path(topology: Any, source: int, destination: int) -> tuple[int, ...]:
+    return _routes(topology).path(int(source), int(destination))
+
+
+def _distance(topology: Any, source: int, destination: int) -> float:
+    return float(_routes(topology).dist[int(source), int(destination)])
+
+
+# ---------------------------------------------------------------- public view
 @dataclass(frozen=True, slots=True)
 class PublicRevealedToken:
     local_ordinal: int
@@ -117,91 +230,39 @@ class SchedulingObservationView:
     residual_state_digest: str
 
     def __post_init__(self) -> None:
-        object.__setattr__(self, "observed_matrix", readonly_array(self.observed_matrix, dtype=np.int64))
-        object.__setattr__(self, "entry_mask", readonly_array(self.entry_mask, dtype=bool))
-        if self.source_totals is not None:
-            object.__setattr__(self, "source_totals", readonly_array(self.source_totals, dtype=np.int64))
-        if self.destination_totals is not None:
-            object.__setattr__(self, "destination_totals", readonly_array(self.destination_totals, dtype=np.int64))
+        for name, dtype in (("observed_matrix", np.int64), ("entry_mask", bool),
+                            ("source_totals", np.int64), ("destination_totals", np.int64)):
+            value = getattr(self, name)
+            if value is not None:
+                object.__setattr__(self, name, readonly_array(value, dtype=dtype))
         t = self.topology
         object.__setattr__(self, "topology", PublicTopologyView(
             t.num_nodes, t.num_edges, t.edges, t.capacities, t.shared_constraints, t.name))
 
 
+def _residual_key(tokens: Sequence[PublicRevealedToken]) -> tuple:
+    return tuple((t.local_ordinal, t.holders) for t in tokens)
+
+
 def build_scheduling_view(observation: Any) -> SchedulingObservationView:
+    """The planner's view of an observation, with digests of its demand part
+    and of its demand plus current holders."""
+    o = observation
     tokens = tuple(PublicRevealedToken(i, int(t.source), int(t.destination), tuple(t.holders))
-                   for i, t in enumerate(observation.revealed_tokens))
-    o = observation.topology
-    topo = PublicTopologyView(o.num_nodes, o.num_edges, o.edges, o.capacities,
-                              o.shared_constraints, o.name)
-    demand_key = (int(observation.stage), float(observation.ratio),
-                  np.asarray(observation.observed_matrix), np.asarray(observation.entry_mask),
-                  observation.source_totals, observation.destination_totals,
-                  tuple((t.source, t.destination) for t in tokens), topo)
-    residual_key = (demand_key, tuple((t.local_ordinal, t.holders) for t in tokens))
+                   for i, t in enumerate(o.revealed_tokens))
+    topo = PublicTopologyView(o.topology.num_nodes, o.topology.num_edges, o.topology.edges,
+                              o.topology.capacities, o.topology.shared_constraints, o.topology.name)
+    demand = (int(o.stage), float(o.ratio), np.asarray(o.observed_matrix), np.asarray(o.entry_mask),
+              o.source_totals, o.destination_totals, tuple((t.source, t.destination) for t in tokens), topo)
     return SchedulingObservationView(
-        int(observation.stage), float(observation.ratio), int(observation.state_version),
-        observation.observed_matrix, observation.entry_mask, observation.source_totals,
-        observation.destination_totals, tokens, topo, canonical_digest(demand_key),
-        canonical_digest(residual_key))
+        stage=int(o.stage), ratio=float(o.ratio), state_version=int(o.state_version),
+        observed_matrix=o.observed_matrix, entry_mask=o.entry_mask, source_totals=o.source_totals,
+        destination_totals=o.destination_totals, revealed_tokens=tokens, topology=topo,
+        observation_digest=canonical_digest(demand),
+        residual_state_digest=canonical_digest((demand, _residual_key(tokens))))
 
 
-def atomic_units(raw: float) -> int:
-    v = float(raw)
-    if not math.isfinite(v) or v < 0:
-        raise ValueError("capacity must be finite and nonnegative")
-    return int(math.floor(v))
-
-
-def edge_usable(topology: Any, edge: int) -> bool:
-    _, _, caps, groups = _topology(topology)
-    if atomic_units(caps[edge]) < 1:
-        return False
-    return all(atomic_units(limit) >= 1 for members, limit in groups if edge in members)
-
-
-_usable = edge_usable
-
-
-def canonical_shortest_path(topology: Any, source: int, destination: int) -> tuple[int, ...]:
-    nodes, edges, _, _ = _topology(topology)
-    source, destination = int(source), int(destination)
-    if source == destination:
-        return ()
-    out: list[list[int]] = [[] for _ in range(nodes)]
-    for e, (u, _v) in enumerate(edges):
-        if edge_usable(topology, e):
-            out[int(u)].append(e)
-    for row in out:
-        row.sort(key=lambda e: (int(edges[e, 1]), e))
-    parent: dict[int, tuple[int, int]] = {}
-    seen = {source}
-    frontier = [source]
-    for node in frontier:
-        for e in out[node]:
-            t = int(edges[e, 1])
-            if t in seen:
-                continue
-            seen.add(t)
-            parent[t] = (node, e)
-            if t == destination:
-                path = []
-                cur = t
-                while cur != source:
-                    cur, pe = parent[cur]
-                    path.append(pe)
-                return tuple(reversed(path))
-            frontier.append(t)
-    raise UnreachableScenarioError(f"unreachable OD {source}->{destination}")
-
-
-def _distance(topology: Any, source: int, destination: int) -> float:
-    try:
-        return float(len(canonical_shortest_path(topology, source, destination)))
-    except UnreachableScenarioError:
-        return math.inf
-
-
+# ----------------------------------------------------------------- candidates
 @dataclass(frozen=True, slots=True)
 class CandidateDistances:
     source_distance: float
@@ -212,11 +273,11 @@ class CandidateDistances:
 
 def candidate_distances(topology: Any, *, holders: Sequence[int], destination: int,
                         edge_index: int) -> CandidateDistances:
-    _, edges, _, _ = _topology(topology)
-    s, t = map(int, edges[int(edge_index)])
-    before = min(_distance(topology, h, destination) for h in holders)
-    td = _distance(topology, t, destination)
-    return CandidateDistances(_distance(topology, s, destination), td, before, min(before, td))
+    r = _routes(topology)
+    src, tgt = (int(x) for x in r.edges[int(edge_index)])
+    before = float(min(r.dist[int(h), int(destination)] for h in holders))
+    target = float(r.dist[tgt, int(destination)])
+    return CandidateDistances(float(r.dist[src, int(destination)]), target, before, min(before, target))
 
 
 def is_strict_global_progress(topology: Any, *, holders: Sequence[int], destination: int,
@@ -234,21 +295,25 @@ class CandidateAction:
 
 
 def enumerate_candidates(view: SchedulingObservationView) -> tuple[CandidateAction, ...]:
+    """Every distance-lowering hop of every revealed token, by (ordinal, edge)."""
     if view.ratio == 0 or not view.revealed_tokens:
         return ()
-    _, edges, _, _ = _topology(view.topology)
-    found: list[CandidateAction] = []
-    for tok in view.revealed_tokens:
-        before = min(_distance(view.topology, h, tok.destination) for h in tok.holders)
-        if not math.isfinite(before) or before <= 0:
+    r = _routes(view.topology)
+    src, tgt = r.edges[:, 0], r.edges[:, 1]
+    out: list[CandidateAction] = []
+    for token in view.revealed_tokens:
+        held = np.zeros(r.nodes, dtype=bool)
+        held[list(token.holders)] = True
+        to_dst = r.dist[:, token.destination]
+        before = float(to_dst[held].min()) if held.any() else math.inf
+        if not (math.isfinite(before) and before > 0):
             continue
-        for e, (s, t) in enumerate(edges):
-            if int(s) not in tok.holders or int(t) in tok.holders or not edge_usable(view.topology, e):
-                continue
-            after = min(before, _distance(view.topology, int(t), tok.destination))
-            if after == before - 1:
-                found.append(CandidateAction(tok.local_ordinal, e, int(before), int(after)))
-    return tuple(sorted(found, key=lambda c: (c.local_token_ordinal, c.edge_index)))
+        # a usable hop from a holder to a non-holder whose target is one step closer
+        hop = r.usable & held[src] & ~held[tgt] & (to_dst[tgt] == before - 1)
+        out.extend(CandidateAction(token.local_ordinal, int(e), int(before), int(before) - 1)
+                   for e in np.flatnonzero(hop).tolist())
+    out.sort(key=lambda c: (c.local_token_ordinal, c.edge_index))
+    return tuple(out)
 
 
 @dataclass(frozen=True, slots=True)
@@ -258,32 +323,59 @@ class BatchLoads:
 
 
 def batch_loads(batch: Sequence[CandidateAction], topology: Any) -> BatchLoads:
+    """Units a batch puts on every edge and on every shared group."""
     _, edges, _, groups = _topology(topology)
-    edge = np.zeros(len(edges), dtype=np.int64)
-    for c in batch:
-        edge[c.edge_index] += 1
-    group = np.asarray([sum(edge[i] for i in members) for members, _ in groups], dtype=np.int64)
-    return BatchLoads(edge, group)
+    per_edge = np.bincount(np.asarray([c.edge_index for c in batch], dtype=np.int64),
+                           minlength=len(edges)).astype(np.int64)
+    per_group = np.asarray([int(per_edge[np.asarray(list(m), dtype=np.int64)].sum()) for m, _ in groups],
+                           dtype=np.int64)
+    return BatchLoads(per_edge, per_group)
+
+
+class _Packer:
+    """Running edge and group loads of a batch under construction."""
+
+    def __init__(self, topology: Any) -> None:
+        r = _routes(topology)
+        self.r = r
+        self.edge_load = np.zeros(len(r.edges), dtype=np.int64)
+        self.group_load = np.zeros(len(r.groups), dtype=np.int64)
+        self.tokens: set[int] = set()
+
+    def fits(self, c: CandidateAction) -> bool:
+        if c.local_token_ordinal in self.tokens:
+            return False
+        e = c.edge_index
+        if self.edge_load[e] + 1 > self.r.edge_units[e]:
+            return False
+        return all(self.group_load[g] + k <= self.r.group_units[g] for g, k in self.r.edge_group_mult[e].items())
+
+    def add(self, c: CandidateAction) -> None:
+        self.tokens.add(c.local_token_ordinal)
+        self.edge_load[c.edge_index] += 1
+        for g, k in self.r.edge_group_mult[c.edge_index].items():
+            self.group_load[g] += k
 
 
 def can_add_candidate(batch: Sequence[CandidateAction], candidate: CandidateAction, topology: Any) -> bool:
-    if any(c.local_token_ordinal == candidate.local_token_ordinal for c in batch):
-        return False
-    _, _, caps, groups = _topology(topology)
-    loads = batch_loads((*batch, candidate), topology)
-    if any(loads.edge_units[i] > atomic_units(caps[i]) for i in range(len(caps))):
-        return False
-    return all(loads.group_units[i] <= atomic_units(lim) for i, (_, lim) in enumerate(groups))
+    packer = _Packer(topology)
+    for c in batch:
+        packer.add(c)
+    return packer.fits(candidate)
 
 
 def pack_candidate_batch(candidates: Sequence[CandidateAction], topology: Any) -> tuple[CandidateAction, ...]:
-    batch: list[CandidateAction] = []
+    """Greedy batch in the given candidate order."""
+    packer = _Packer(topology)
+    chosen = []
     for c in candidates:
-        if can_add_candidate(batch, c, topology):
-            batch.append(c)
-    return tuple(batch)
+        if packer.fits(c):
+            packer.add(c)
+            chosen.append(c)
+    return tuple(chosen)
 
 
+# ------------------------------------------------------- residual projections
 @dataclass(frozen=True, slots=True)
 class ResidualProjection:
     edge_loads: np.ndarray
@@ -292,74 +384,77 @@ class ResidualProjection:
 
 
 def project_residual_scenario(scenario: Any, view: SchedulingObservationView) -> ResidualProjection:
+    """Edge and group loads a scenario still needs on canonical routes, given
+    what the revealed tokens already carry (each revealed token's own route is
+    replaced by the route from its closest holder, or by nothing once it has
+    arrived)."""
     m = np.asarray(scenario)
     if m.shape != view.observed_matrix.shape or not np.issubdtype(m.dtype, np.number):
         raise ValueError("scenario shape/type mismatch")
     if not np.all(np.isfinite(m)) or np.any(m < 0) or np.any(m != np.floor(m)):
-        raise InconsistentResidualError("negative or noninteger scenario")
+        raise InconsistentResidualError("a scenario holds negative or noninteger demand")
     m = m.astype(np.int64)
-    nodes, edges, _, groups = _topology(view.topology)
-    revealed = np.zeros_like(m)
+    r = _routes(view.topology)
+    seen = np.zeros_like(m)
     for t in view.revealed_tokens:
-        revealed[t.source, t.destination] += 1
-    if np.any(m < revealed):
-        raise InconsistentResidualError("insufficient scenario load for revealed tokens")
-    loads = np.zeros(len(edges), dtype=np.float64)
-    for s in range(nodes):
-        for d in range(nodes):
-            amount = int(m[s, d])
-            if amount <= 0 or s == d:
-                continue
-            try:
-                path = canonical_shortest_path(view.topology, s, d)
-            except UnreachableScenarioError:
-                raise UnreachableScenarioError("positive unreachable scenario demand")
-            loads[list(path)] += amount
+        seen[t.source, t.destination] += 1
+    if np.any(m < seen):
+        raise InconsistentResidualError("the scenario has fewer units than the revealed tokens on a pair")
+    loads = np.zeros(len(r.edges), dtype=np.float64)
+    pairs = np.argwhere(m > 0)
+    for s, d in pairs.tolist():  # row-major, so the first unreachable pair is reported
+        if s == d:
+            continue
+        if r.dist[s, d] == np.inf:
+            raise UnreachableScenarioError("a scenario has positive demand on an unreachable pair")
+        loads[list(r.path(s, d))] += float(m[s, d])
     for t in view.revealed_tokens:
-        try:
-            origin = canonical_shortest_path(view.topology, t.source, t.destination)
-        except UnreachableScenarioError as exc:
-            raise InconsistentResidualError("revealed token unreachable") from exc
-        loads[list(origin)] -= 1
+        if r.dist[t.source, t.destination] == np.inf:
+            raise InconsistentResidualError("a revealed token's pair is unreachable")
+        loads[list(r.path(t.source, t.destination))] -= 1.0
         if t.destination not in t.holders:
-            holder = min(t.holders, key=lambda n: (_distance(view.topology, n, t.destination), n))
-            loads[list(canonical_shortest_path(view.topology, holder, t.destination))] += 1
+            best = min(t.holders, key=lambda h: (r.dist[h, t.destination], h))
+            loads[list(r.path(best, t.destination))] += 1.0
     if np.any(loads < -1e-12):
-        raise InconsistentResidualError("insufficient revealed scenario load")
-    loads = np.maximum(loads, 0)
-    group = np.asarray([sum(loads[i] for i in members) for members, _ in groups], dtype=np.float64)
+        raise InconsistentResidualError("the scenario does not cover the revealed tokens' loads")
+    loads = np.maximum(loads, 0.0)
+    group = np.asarray([sum(loads[i] for i in members.tolist()) for members, _ in r.groups], dtype=np.float64)
     loads.setflags(write=False)
     group.setflags(write=False)
     return ResidualProjection(loads, group, canonical_digest((loads, group)))
 
 
+# -------------------------------------------------------------------- scoring
 def criticality_for_edge(*, residual_edge_load: float, edge_units: int,
                          incident_group_loads: Sequence[float], incident_group_units: Sequence[int]) -> float:
-    values = [float(residual_edge_load), *map(float, incident_group_loads)]
-    if not all(math.isfinite(v) and v >= 0 for v in values):
-        raise ValueError("loads must be finite nonnegative")
-    out = values[0] / max(int(edge_units), 1)
-    out += sum(load / max(int(u), 1) for load, u in zip(values[1:], incident_group_units))
-    return float(out)
+    """Residual load over capacity units, summed over the edge and its groups."""
+    loads = [float(residual_edge_load)] + [float(v) for v in incident_group_loads]
+    if not all(math.isfinite(v) and v >= 0 for v in loads):
+        raise ValueError("residual loads must be finite and nonnegative")
+    edge_part = loads[0] / max(int(edge_units), 1)
+    group_part = sum(load / max(int(u), 1) for load, u in zip(loads[1:], incident_group_units))
+    return float(edge_part + group_part)
 
 
 def candidate_utility(*, criticality: float, after_distance: float) -> float:
-    if not math.isfinite(float(criticality)) or not math.isfinite(float(after_distance)):
-        raise ValueError("Q inputs must be finite")
-    return 1.0 + 0.25 * float(criticality) - 0.05 * float(after_distance)
+    c, a = float(criticality), float(after_distance)
+    if not (math.isfinite(c) and math.isfinite(a)):
+        raise ValueError("utility inputs must be finite")
+    return 1.0 + 0.25 * c - 0.05 * a
 
 
 def robust_score(q: Any, weights: Any, *, risk_lambda: float) -> float:
-    v = np.asarray(q, dtype=np.float64)
+    """Weighted mean minus lambda times weighted standard deviation of q."""
+    qv = np.asarray(q, dtype=np.float64)
     w = np.asarray(weights, dtype=np.float64)
-    if v.ndim != 1 or w.shape != v.shape or not np.all(np.isfinite(v)):
-        raise ValueError("Q must be finite vector")
+    if qv.ndim != 1 or w.shape != qv.shape or not np.all(np.isfinite(qv)):
+        raise ValueError("utilities must be a finite vector")
     if not np.all(np.isfinite(w)) or np.any(w < 0) or w.sum() <= 0:
-        raise ValueError("weights must be finite nonnegative with positive sum")
+        raise ValueError("weights must be finite, nonnegative and not all zero")
     p = w / w.sum()
-    mean = float(p @ v)
-    var = float(p @ ((v - mean) ** 2))
-    return mean - float(risk_lambda) * math.sqrt(max(var, 0.0))
+    mean = float(p @ qv)
+    spread = float(p @ ((qv - mean) ** 2))
+    return mean - float(risk_lambda) * math.sqrt(max(spread, 0.0))
 
 
 @dataclass(frozen=True, slots=True)
@@ -372,25 +467,26 @@ class CandidateScore:
 def score_candidates(candidates: Sequence[CandidateAction], support: Any, *,
                      risk_lambda: float) -> tuple[CandidateScore, ...]:
     projections = [project_residual_scenario(m, support.observation) for m in support.matrices]
-    _, _, caps, groups = _topology(support.observation.topology)
+    r = _routes(support.observation.topology)
     p = np.asarray(support.weights, dtype=float)
     p = p / p.sum()
-    out = []
+    scored = []
     for c in candidates:
-        incident = [i for i, (members, _) in enumerate(groups) if c.edge_index in members]
+        e = c.edge_index
+        groups = r.edge_groups[e]
         q = np.asarray([candidate_utility(
             criticality=criticality_for_edge(
-                residual_edge_load=pr.edge_loads[c.edge_index],
-                edge_units=atomic_units(caps[c.edge_index]),
-                incident_group_loads=tuple(pr.group_loads[i] for i in incident),
-                incident_group_units=tuple(atomic_units(groups[i][1]) for i in incident)),
+                residual_edge_load=pr.edge_loads[e], edge_units=int(r.edge_units[e]),
+                incident_group_loads=[pr.group_loads[g] for g in groups],
+                incident_group_units=[int(r.group_units[g]) for g in groups]),
             after_distance=c.after_distance) for pr in projections])
         mean = float(p @ q)
-        std = float(np.sqrt(p @ ((q - mean) ** 2)))
-        out.append(CandidateScore(c, robust_score(q, p, risk_lambda=risk_lambda), std))
-    return tuple(out)
+        scored.append(CandidateScore(c, robust_score(q, p, risk_lambda=risk_lambda),
+                                     float(np.sqrt(p @ ((q - mean) ** 2)))))
+    return tuple(scored)
 
 
+# -------------------------------------------------------------------- planner
 @dataclass(frozen=True, slots=True)
 class RobustPrefixConfig:
     horizon: int
@@ -400,10 +496,10 @@ class RobustPrefixConfig:
 
     def __post_init__(self) -> None:
         if (int(self.horizon), int(self.prefix)) not in LEGAL_HORIZON_PREFIX:
-            raise ValueError("nonallowlisted H/P")
-        if float(self.risk_lambda) not in (0.0, 0.5, 1.0):
-            raise ValueError("risk lambda")
-        if int(self.requested_k) not in (1, 8):
+            raise ValueError(f"(horizon, prefix) must be one of {sorted(LEGAL_HORIZON_PREFIX)}")
+        if float(self.risk_lambda) not in RISK_LAMBDAS:
+            raise ValueError(f"risk lambda must be one of {RISK_LAMBDAS}")
+        if int(self.requested_k) not in REQUESTED_K:
             raise ValueError("requested K must be point K1 or robust K8")
 
 
@@ -425,45 +521,42 @@ class PrefixPlan:
 
 
 class RobustPrefixPlanner:
-    """Plan H simulated slots with robust scores and keep the first P batches."""
+    """Simulate up to ``horizon`` slots of robust-score batches on the public
+    view, and keep the first ``prefix`` batches as the plan."""
 
     def __init__(self, config: RobustPrefixConfig) -> None:
         self.config = config
 
     def plan(self, observation: SchedulingObservationView, support: Any) -> PrefixPlan:
         if support.stage != observation.stage:
-            raise StaleSupportError("support stage mismatch")
+            raise StaleSupportError("the support was built at another reveal stage")
         if support.observation_digest != observation.observation_digest:
-            raise StaleSupportError("support observation digest mismatch")
-        static = canonical_digest(tuple(project_residual_scenario(m, observation).digest
-                                        for m in support.matrices))
-        sim = observation
-        planned: list[tuple[CandidateAction, ...]] = []
-        trace: list[SimulationStep] = []
-        _, edges, _, _ = _topology(observation.topology)
+            raise StaleSupportError("the support was built for another observation")
+        projected = canonical_digest(tuple(project_residual_scenario(m, observation).digest
+                                           for m in support.matrices))
+        dst_of = np.asarray(observation.topology.edges, dtype=np.int64)[:, 1]
+        view, batches = observation, []
         for _ in range(self.config.horizon):
-            cands = enumerate_candidates(sim)
-            if not cands:
+            candidates = enumerate_candidates(view)
+            if not candidates:
                 break
-            scores = score_candidates(cands, support, risk_lambda=self.config.risk_lambda)
-            ordered = [s.candidate for s in sorted(
-                scores, key=lambda s: (-s.robust_score, s.candidate.local_token_ordinal, s.candidate.edge_index))]
-            batch = pack_candidate_batch(ordered, sim.topology)
+            scores = score_candidates(candidates, support, risk_lambda=self.config.risk_lambda)
+            ranked = sorted(scores, key=lambda s: (-s.robust_score, s.candidate.local_token_ordinal,
+                                                   s.candidate.edge_index))
+            batch = pack_candidate_batch([s.candidate for s in ranked], view.topology)
             if not batch:
                 break
-            planned.append(batch)
-            trace.append(SimulationStep(static))
-            holders = [set(t.holders) for t in sim.revealed_tokens]
-            for a in batch:
-                holders[a.local_token_ordinal].add(int(edges[a.edge_index, 1]))
-            toks = tuple(replace(t, holders=tuple(sorted(holders[t.local_ordinal]))) for t in sim.revealed_tokens)
-            sim = replace(sim, revealed_tokens=toks, residual_state_digest=canonical_digest(
-                tuple((t.local_ordinal, t.holders) for t in toks)))
-        batches = tuple(planned[: self.config.prefix])
-        structural = tuple((a.local_token_ordinal, a.edge_index) for b in batches for a in b)
-        return PrefixPlan(observation.stage, observation.state_version, 0, support.digest,
-                          canonical_digest(self.config), batches, structural,
-                          tuple(trace[: self.config.prefix]))
+            batches.append(batch)
+            grown = {c.local_token_ordinal: {int(dst_of[c.edge_index])} for c in batch}
+            tokens = tuple(replace(t, holders=tuple(sorted(set(t.holders) | grown.get(t.local_ordinal, set()))))
+                           for t in view.revealed_tokens)
+            view = replace(view, revealed_tokens=tokens, residual_state_digest=canonical_digest(_residual_key(tokens)))
+        kept = tuple(batches[: self.config.prefix])
+        return PrefixPlan(
+            origin_stage=observation.stage, origin_state_version=observation.state_version, revision=0,
+            support_digest=support.digest, config_digest=canonical_digest(self.config), batches=kept,
+            structural_actions=tuple((c.local_token_ordinal, c.edge_index) for b in kept for c in b),
+            simulation_trace=tuple(SimulationStep(projected) for _ in kept))
 
 
 __all__ = [

@@ -1,20 +1,30 @@
-"""Proposals and the trusted deterministic checker (rlccl/uncertainty/execution.py:18-161).
+"""Proposals and the trusted, deterministic slot checker.
 
-``commit_proposal`` validates a whole slot before applying anything and
-rejects, in this order: scenario-only proposals, an observation of another
-problem stage, a stale state version, a token acted on twice, an unrevealed
-token, an out-of-range edge, a source that does not hold the token, a
-destination that already holds it, edge capacity, and every shared
-bandwidth group.  It then applies all transfers atomically; because sources
-were checked against the pre-slot state, a token received in this slot
-cannot be forwarded in the same slot.
+Interface of rlccl/uncertainty/execution.py:18-161 (``TransferAction``,
+``Proposal``, ``CommitResult``, ``commit_proposal``,
+``validate_legacy_schedule_matrix``) and its verdicts, in its order:
+
+1. envelope: the observation and proposal types, no scenario tokens, the
+   observation belongs to this problem stage, its state version is current
+   (a wait is then legal and changes nothing);
+2. per action, in proposal order: a token acted on twice, a token not
+   revealed (not executable), an edge index out of range, an edge whose
+   source does not hold the token, an edge whose destination already does;
+3. bandwidth of the whole slot: per-edge capacity, then every shared group.
+
+The slot is applied only after all three pass, atomically: possession is
+read from the pre-slot state, so a token received in this slot cannot be
+forwarded in the same slot.  Here the per-action stage resolves each action
+to (token row, destination, edge) and the bandwidth stage works on the edge
+column of that table (``np.bincount``) instead of accumulating loads
+action by action.
 """
 
 from __future__ import annotations
 
 from dataclasses import dataclass
 from types import MappingProxyType
-from typing import TYPE_CHECKING, Any, Mapping
+from typing import TYPE_CHECKING, Any, Mapping, Sequence
 
 import numpy as np
 
@@ -24,6 +34,16 @@ from .scenarios import ScenarioSet
 if TYPE_CHECKING:
     from .problem import UncertainProblemInstance
 
+_SLACK = 1e-12  # capacities are compared with this tolerance
+
+
+class StaleObservationError(ValueError):
+    """The observation's state version is no longer the world's."""
+
+
+def _is_index(value: Any) -> bool:
+    return isinstance(value, (int, np.integer)) and not isinstance(value, (bool, np.bool_))
+
 
 @dataclass(frozen=True, slots=True)
 class TransferAction:
@@ -32,9 +52,9 @@ class TransferAction:
 
     def __post_init__(self) -> None:
         if not isinstance(self.token_id, TruthTokenId):
-            raise TypeError("TransferAction requires TruthTokenId; scenario tokens are not executable")
-        if isinstance(self.edge_index, (bool, np.bool_)) or not isinstance(self.edge_index, (int, np.integer)):
-            raise TypeError("edge_index must be an integer")
+            raise TypeError("only a TruthTokenId can be transferred (scenario tokens never execute)")
+        if not _is_index(self.edge_index):
+            raise TypeError("edge_index is an integer")
         object.__setattr__(self, "edge_index", int(self.edge_index))
 
 
@@ -45,10 +65,10 @@ class Proposal:
 
     def __post_init__(self) -> None:
         actions = tuple(self.actions)
-        if any(not isinstance(a, TransferAction) for a in actions):
-            raise TypeError("Proposal actions must be TransferAction objects")
-        if self.scenario_set is not None and actions:
-            raise ValueError("A scenario-only proposal cannot contain executable actions")
+        if not all(isinstance(a, TransferAction) for a in actions):
+            raise TypeError("every proposal action is a TransferAction")
+        if actions and self.scenario_set is not None:
+            raise ValueError("a scenario-only proposal carries no executable action")
         object.__setattr__(self, "actions", actions)
 
     @classmethod
@@ -56,26 +76,22 @@ class Proposal:
         return cls()
 
     @classmethod
-    def from_transfers(cls, actions: tuple[TransferAction, ...]) -> "Proposal":
+    def from_transfers(cls, actions: Sequence[TransferAction]) -> "Proposal":
         return cls(actions=tuple(actions))
 
     @classmethod
     def scenario_only(cls, scenario_set: ScenarioSet) -> "Proposal":
         if not isinstance(scenario_set, ScenarioSet):
-            raise TypeError("scenario_only requires ScenarioSet")
+            raise TypeError("scenario_only takes a ScenarioSet")
         return cls(scenario_set=scenario_set)
 
     @property
     def is_wait(self) -> bool:
-        return not self.actions and self.scenario_set is None
+        return self.scenario_set is None and len(self.actions) == 0
 
     def to_public_payload(self) -> Mapping[str, Any]:
-        return MappingProxyType({
-            "actions": tuple(MappingProxyType({"token_id": a.token_id, "edge_index": a.edge_index})
-                             for a in self.actions),
-            "is_wait": self.is_wait,
-            "scenario_set": self.scenario_set,
-        })
+        rows = tuple(MappingProxyType({"token_id": a.token_id, "edge_index": a.edge_index}) for a in self.actions)
+        return MappingProxyType({"actions": rows, "is_wait": self.is_wait, "scenario_set": self.scenario_set})
 
 
 @dataclass(frozen=True, slots=True)
@@ -86,74 +102,88 @@ class CommitResult:
 
 
 def validate_legacy_schedule_matrix(matrix: Any, *, expected_shape: tuple[int, int]) -> np.ndarray:
+    """A 0/1 schedule matrix of the legacy format as a read-only int8 copy."""
     m = np.asarray(matrix)
     if m.ndim != 2:
-        raise ValueError("Legacy schedule matrix must be 2-D")
+        raise ValueError("a legacy schedule matrix is 2-D")
     if tuple(m.shape) != tuple(expected_shape):
-        raise ValueError(f"Legacy schedule matrix shape must be {expected_shape}")
+        raise ValueError(f"a legacy schedule matrix here has shape {expected_shape}")
     if not np.issubdtype(m.dtype, np.number):
-        raise ValueError("Legacy schedule matrix must contain numeric binary values")
-    f = m.astype(np.float64, copy=False)
-    if not np.all(np.isfinite(f)):
-        raise ValueError("Legacy schedule matrix must contain finite values, not NaN/Inf")
-    if np.any(f < 0):
-        raise ValueError("Legacy schedule matrix must be nonnegative")
-    if np.any((f != 0) & (f != 1)):
-        raise ValueError("Legacy schedule matrix must be binary")
-    out = np.array(f, dtype=np.int8, copy=True)
+        raise ValueError("a legacy schedule matrix holds numeric binary values")
+    values = m.astype(np.float64, copy=False)
+    for bad, why in ((~np.isfinite(values), "finite values (no NaN/Inf)"),
+                     (values < 0, "nonnegative values"),
+                     ((values != 0) & (values != 1), "binary values (0 or 1)")):
+        if np.any(bad):
+            raise ValueError(f"a legacy schedule matrix holds {why}")
+    out = values.astype(np.int8)
     out.setflags(write=False)
     return out
 
 
-_EPS = 1e-12
+def _check_envelope(world: "UncertainProblemInstance", observation: Any, proposal: Any) -> None:
+    if not isinstance(observation, PartialObservationState):
+        raise TypeError("commit takes a PartialObservationState")
+    if not isinstance(proposal, Proposal):
+        raise TypeError("commit takes a Proposal")
+    if proposal.scenario_set is not None:
+        raise ValueError("scenario tokens are for planning only and never execute")
+    if (observation.sequence_id, observation.sequence_step) != (world.sequence_id, world.sequence_step):
+        raise ValueError("the observation belongs to another problem stage")
+    if observation.state_version != world._state_version:
+        raise StaleObservationError("stale observation: its state version is not the world's current one")
+
+
+def _resolve_actions(world: "UncertainProblemInstance", observation: PartialObservationState,
+                     actions: tuple[TransferAction, ...]) -> np.ndarray:
+    """[n, 3] int64 rows (token row, destination node, edge) or a ValueError
+    naming the first action, in proposal order, that may not run."""
+    topo = world.topology_info
+    src_of, dst_of = np.asarray(topo.edge_src), np.asarray(topo.edge_dst)
+    revealed = frozenset(observation.executable_token_ids)
+    held = world._possession
+    table = np.empty((len(actions), 3), dtype=np.int64)
+    taken: set[TruthTokenId] = set()
+    for i, action in enumerate(actions):
+        tid, edge = action.token_id, action.edge_index
+        if tid in taken:
+            raise ValueError("duplicate token action conflict: one token acted on twice in a slot")
+        taken.add(tid)
+        row = world._public_to_private.get(tid) if tid in revealed else None
+        if row is None:
+            raise ValueError("the token is unrevealed and not executable at this stage")
+        if not 0 <= edge < topo.E:
+            raise ValueError(f"edge_index {edge} is outside 0..{topo.E - 1}")
+        src, dst = int(src_of[edge]), int(dst_of[edge])
+        if not held[row, src]:
+            raise ValueError("the edge's source does not hold the token (source possession required)")
+        if held[row, dst]:
+            raise ValueError("the edge's destination already holds the token")
+        table[i] = (row, dst, edge)
+    return table
+
+
+def _check_bandwidth(topology: Any, edges: np.ndarray) -> None:
+    load = np.bincount(edges, minlength=int(topology.E)).astype(np.float64)
+    if np.any(load > np.asarray(topology.capacities, dtype=np.float64) + _SLACK):
+        raise ValueError("an edge's capacity (bandwidth) is exceeded")
+    for members, limit in topology.shared_constraints:
+        if load[np.asarray(members, dtype=np.int64)].sum() > float(limit) + _SLACK:
+            raise ValueError("a shared group's bandwidth limit is exceeded")
 
 
 def commit_proposal(world: "UncertainProblemInstance", observation: PartialObservationState,
                     proposal: Proposal) -> CommitResult:
-    if not isinstance(observation, PartialObservationState):
-        raise TypeError("commit requires PartialObservationState")
-    if not isinstance(proposal, Proposal):
-        raise TypeError("commit requires Proposal")
-    if proposal.scenario_set is not None:
-        raise ValueError("Scenario tokens are planning-only and not executable")
-    if observation.sequence_id != world.sequence_id or observation.sequence_step != world.sequence_step:
-        raise ValueError("Observation belongs to a different problem stage")
-    if observation.state_version != world._state_version:
-        raise ValueError("stale observation cannot be committed")
+    """Check a whole slot against the truth world, then apply it atomically."""
+    _check_envelope(world, observation, proposal)
     if proposal.is_wait:
         return CommitResult(True, 0, world._state_version)
-    topo = world.topology_info
-    executable = set(observation.executable_token_ids)
-    seen: set[TruthTokenId] = set()
-    load = np.zeros(topo.E, dtype=np.float64)
-    resolved: list[tuple[int, int]] = []
-    for action in proposal.actions:
-        if action.token_id in seen:
-            raise ValueError("Duplicate token action conflict in one slot")
-        seen.add(action.token_id)
-        if action.token_id not in executable or action.token_id not in world._public_to_private:
-            raise ValueError("Token is unrevealed and not executable at this stage")
-        edge = int(action.edge_index)
-        if edge < 0 or edge >= topo.E:
-            raise ValueError("edge_index is outside valid edge range")
-        token = world._public_to_private[action.token_id]
-        src, dst = int(topo.edge_src[edge]), int(topo.edge_dst[edge])
-        if not world._possession[token, src]:
-            raise ValueError("Edge source is not a current token holder; source possession required")
-        if world._possession[token, dst]:
-            raise ValueError("Edge destination already holds this token")
-        load[edge] += 1.0
-        resolved.append((token, dst))
-    if np.any(load > np.asarray(topo.capacities, dtype=float) + _EPS):
-        raise ValueError("Edge capacity/bandwidth exceeded")
-    for members, limit in topo.shared_constraints:
-        if float(load[np.asarray(members, dtype=np.int64)].sum()) > float(limit) + _EPS:
-            raise ValueError("Shared group bandwidth limit exceeded")
-    for token, dst in resolved:
-        world._possession[token, dst] = True
+    table = _resolve_actions(world, observation, proposal.actions)
+    _check_bandwidth(world.topology_info, table[:, 2])
+    world._possession[table[:, 0], table[:, 1]] = True
     world._state_version += 1
-    return CommitResult(True, len(resolved), world._state_version)
+    return CommitResult(True, int(table.shape[0]), world._state_version)
 
 
-__all__ = ["CommitResult", "Proposal", "TransferAction", "commit_proposal",
+__all__ = ["CommitResult", "Proposal", "StaleObservationError", "TransferAction", "commit_proposal",
            "validate_legacy_schedule_matrix"]

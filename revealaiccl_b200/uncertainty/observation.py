@@ -1,21 +1,27 @@
-"""Planner-facing, read-only views of the reveal-aware world.
+"""What an ordinary planner is allowed to see of the reveal-aware world.
 
-Mirrors the public boundary of rlccl/uncertainty/observation.py:25-250:
+The public boundary of rlccl/uncertainty/observation.py:25-250 (class and
+field names, the opaque token identity, the rule that only revealed tokens
+are listed and that history stops strictly before the current step) with
+its own mechanics:
 
+* every array field is frozen by one table-driven pass (``_FROZEN``): an
+  owned copy in the field's dtype with the write flag cleared;
+* ``to_policy_payload`` is generated from the dataclass fields, so it always
+  carries exactly the observation's fields (arrays re-copied read-only, the
+  topology as a nested read-only mapping) and nothing evaluator-private.
+
+Types:
 * ``TruthTokenId`` — opaque identity issued only when a real token is revealed;
 * ``RevealedDemandToken(token_id, source, destination, holders)``;
 * ``PublicTopologyView`` — deep-copied, read-only static topology;
-* ``PartialObservationState`` — the only current-demand object an ordinary
-  planner may receive (entry/unknown masks, observed matrix, revealed tokens,
-  optional totals, state version);
+* ``PartialObservationState`` — the only current-demand object a planner gets;
 * ``SanitizedHistoryView`` — completed matrices of strictly earlier steps.
-
-All arrays are owned copies with the write flag cleared.
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass
+from dataclasses import dataclass, fields
 from types import MappingProxyType
 from typing import Any, Mapping, Sequence
 
@@ -25,13 +31,26 @@ from ..traffic.matrix_utils import validate_traffic_matrix
 
 
 def readonly_array(value: Any, *, dtype: Any | None = None) -> np.ndarray:
+    """An owned copy of ``value`` that cannot be written through."""
     out = np.array(value, dtype=dtype, copy=True)
     out.setflags(write=False)
     return out
 
 
-def _freeze(values: Mapping[str, Any]) -> Mapping[str, Any]:
-    return MappingProxyType(dict(values))
+def _freeze_fields(obj: Any, spec: Mapping[str, Any]) -> None:
+    """Replace each named array field (None stays None) by a frozen copy."""
+    for name, dtype in spec.items():
+        value = getattr(obj, name)
+        object.__setattr__(obj, name, None if value is None else readonly_array(value, dtype=dtype))
+
+
+def _publish(value: Any) -> Any:
+    """The policy-payload form of one field value."""
+    if isinstance(value, np.ndarray):
+        return readonly_array(value)
+    if isinstance(value, PublicTopologyView):
+        return MappingProxyType({f.name: _publish(getattr(value, f.name)) for f in fields(value)})
+    return value
 
 
 @dataclass(frozen=True, slots=True)
@@ -39,8 +58,8 @@ class TruthTokenId:
     opaque_value: str
 
     def __post_init__(self) -> None:
-        if not isinstance(self.opaque_value, str) or not self.opaque_value:
-            raise ValueError("TruthTokenId requires a non-empty opaque string")
+        if not (isinstance(self.opaque_value, str) and self.opaque_value):
+            raise ValueError("a truth token id is a non-empty opaque string")
 
     def __str__(self) -> str:
         return self.opaque_value
@@ -55,12 +74,12 @@ class RevealedDemandToken:
 
     def __post_init__(self) -> None:
         if not isinstance(self.token_id, TruthTokenId):
-            raise TypeError("RevealedDemandToken requires a TruthTokenId")
-        if self.source < 0 or self.destination < 0 or self.source == self.destination:
-            raise ValueError("Invalid revealed demand endpoints")
-        holders = tuple(int(h) for h in self.holders)
-        if any(h < 0 for h in holders):
-            raise ValueError("Holder indices must be nonnegative")
+            raise TypeError("a revealed token carries a TruthTokenId")
+        if min(self.source, self.destination) < 0 or self.source == self.destination:
+            raise ValueError("revealed token endpoints must be two distinct nonnegative nodes")
+        holders = tuple(map(int, self.holders))
+        if holders and min(holders) < 0:
+            raise ValueError("holder node indices are nonnegative")
         object.__setattr__(self, "holders", holders)
 
 
@@ -74,23 +93,20 @@ class PublicTopologyView:
     name: str | None = None
 
     def __post_init__(self) -> None:
-        edges = readonly_array(self.edges, dtype=np.int64)
-        caps = readonly_array(self.capacities, dtype=np.float64)
-        if edges.shape != (self.num_edges, 2):
-            raise ValueError("Public topology edge shape mismatch")
-        if caps.shape != (self.num_edges,):
-            raise ValueError("Public topology capacity shape mismatch")
-        groups = tuple((tuple(int(e) for e in idx), float(limit))
-                       for idx, limit in self.shared_constraints)
-        object.__setattr__(self, "edges", edges)
-        object.__setattr__(self, "capacities", caps)
-        object.__setattr__(self, "shared_constraints", groups)
+        _freeze_fields(self, {"edges": np.int64, "capacities": np.float64})
+        if self.edges.shape != (self.num_edges, 2):
+            raise ValueError(f"public topology edges must be [{self.num_edges}, 2]")
+        if self.capacities.shape != (self.num_edges,):
+            raise ValueError(f"public topology capacities must be [{self.num_edges}]")
+        object.__setattr__(self, "shared_constraints",
+                           tuple((tuple(map(int, members)), float(limit))
+                                 for members, limit in self.shared_constraints))
 
     @classmethod
     def from_topology_info(cls, topology: Any) -> "PublicTopologyView":
-        return cls(int(topology.V), int(topology.E), np.asarray(topology.edges),
-                   np.asarray(topology.capacities), tuple(topology.shared_constraints),
-                   getattr(topology, "name", None))
+        return cls(num_nodes=int(topology.V), num_edges=int(topology.E), edges=np.asarray(topology.edges),
+                   capacities=np.asarray(topology.capacities),
+                   shared_constraints=tuple(topology.shared_constraints), name=getattr(topology, "name", None))
 
     @property
     def edge_src(self) -> np.ndarray:
@@ -99,6 +115,10 @@ class PublicTopologyView:
     @property
     def edge_dst(self) -> np.ndarray:
         return readonly_array(self.edges[:, 1], dtype=np.int64)
+
+
+_OBSERVATION_ARRAYS = {"entry_mask": bool, "observed_matrix": np.int64, "unknown_mask": bool,
+                       "source_totals": np.int64, "destination_totals": np.int64}
 
 
 @dataclass(frozen=True, slots=True)
@@ -119,54 +139,33 @@ class PartialObservationState:
     state_version: int
 
     def __post_init__(self) -> None:
-        entry = readonly_array(self.entry_mask, dtype=bool)
-        observed = readonly_array(self.observed_matrix, dtype=np.int64)
-        unknown = readonly_array(self.unknown_mask, dtype=bool)
-        if observed.ndim != 2 or observed.shape[0] != observed.shape[1]:
-            raise ValueError("Observed matrix must be square")
-        if entry.shape != observed.shape or unknown.shape != observed.shape:
-            raise ValueError("Observation masks must match observed matrix")
-        if not np.array_equal(unknown, ~entry):
-            raise ValueError("unknown_mask must be the complement of entry_mask")
-        if np.any(np.diag(observed) != 0):
-            raise ValueError("Observed matrix diagonal must be zero")
-        tokens = tuple(self.revealed_tokens)
-        if len({t.token_id for t in tokens}) != len(tokens):
-            raise ValueError("Revealed token IDs must be unique")
-        st = None if self.source_totals is None else readonly_array(self.source_totals, dtype=np.int64)
-        dt = None if self.destination_totals is None else readonly_array(self.destination_totals, dtype=np.int64)
-        n = observed.shape[0]
-        if st is not None and st.shape != (n,):
-            raise ValueError("source_totals shape mismatch")
-        if dt is not None and dt.shape != (n,):
-            raise ValueError("destination_totals shape mismatch")
-        for name, value in (("entry_mask", entry), ("observed_matrix", observed),
-                            ("unknown_mask", unknown), ("revealed_tokens", tokens),
-                            ("source_totals", st), ("destination_totals", dt)):
-            object.__setattr__(self, name, value)
+        _freeze_fields(self, _OBSERVATION_ARRAYS)
+        object.__setattr__(self, "revealed_tokens", tuple(self.revealed_tokens))
+        obs = self.observed_matrix
+        if obs.ndim != 2 or obs.shape[0] != obs.shape[1]:
+            raise ValueError("the observed matrix is square")
+        n = obs.shape[0]
+        if self.entry_mask.shape != obs.shape or self.unknown_mask.shape != obs.shape:
+            raise ValueError("entry and unknown masks have the observed matrix's shape")
+        if np.any(self.unknown_mask == self.entry_mask):
+            raise ValueError("unknown_mask must be exactly the entries entry_mask leaves out")
+        if np.diagonal(obs).any():
+            raise ValueError("the observed matrix has a zero diagonal")
+        ids = [t.token_id for t in self.revealed_tokens]
+        if len(set(ids)) != len(ids):
+            raise ValueError("a revealed token id is listed twice")
+        for name in ("source_totals", "destination_totals"):
+            totals = getattr(self, name)
+            if totals is not None and totals.shape != (n,):
+                raise ValueError(f"{name} must have one entry per node")
 
     @property
     def executable_token_ids(self) -> tuple[TruthTokenId, ...]:
         return tuple(t.token_id for t in self.revealed_tokens)
 
     def to_policy_payload(self) -> Mapping[str, Any]:
-        topo = _freeze({
-            "num_nodes": self.topology.num_nodes, "num_edges": self.topology.num_edges,
-            "edges": readonly_array(self.topology.edges),
-            "capacities": readonly_array(self.topology.capacities),
-            "shared_constraints": self.topology.shared_constraints, "name": self.topology.name,
-        })
-        return _freeze({
-            "sequence_id": self.sequence_id, "sequence_step": self.sequence_step,
-            "family": self.family, "mode": self.mode, "stage": self.stage, "ratio": self.ratio,
-            "entry_mask": readonly_array(self.entry_mask),
-            "observed_matrix": readonly_array(self.observed_matrix),
-            "unknown_mask": readonly_array(self.unknown_mask),
-            "revealed_tokens": self.revealed_tokens,
-            "source_totals": None if self.source_totals is None else readonly_array(self.source_totals),
-            "destination_totals": None if self.destination_totals is None else readonly_array(self.destination_totals),
-            "topology": topo, "state_version": self.state_version,
-        })
+        """A fresh read-only mapping of this observation's fields."""
+        return MappingProxyType({f.name: _publish(getattr(self, f.name)) for f in fields(self)})
 
 
 @dataclass(frozen=True, slots=True)
@@ -177,24 +176,24 @@ class SanitizedHistoryView:
     current_step: int
 
     def __post_init__(self) -> None:
-        raw = tuple(np.asarray(m) for m in self.matrices)
-        for m in raw:
+        given = [np.asarray(m) for m in self.matrices]
+        for m in given:
             validate_traffic_matrix(m)
-        mats = tuple(readonly_array(m, dtype=np.int64) for m in raw)
-        steps = tuple(int(s) for s in self.steps)
-        if len(mats) != len(steps):
-            raise ValueError("History matrices and steps must have equal lengths")
-        if tuple(sorted(steps)) != steps or len(set(steps)) != len(steps):
-            raise ValueError("History steps must be strictly increasing")
-        if any(s >= self.current_step for s in steps):
-            raise ValueError("History steps must be < current step; current/future X is forbidden")
-        object.__setattr__(self, "matrices", mats)
-        object.__setattr__(self, "steps", steps)
+        steps = np.asarray([int(s) for s in self.steps], dtype=np.int64)
+        if len(given) != steps.size:
+            raise ValueError("history needs one step number per matrix")
+        if steps.size > 1 and np.any(np.diff(steps) <= 0):
+            raise ValueError("history step numbers must strictly increase")
+        if steps.size and int(steps.max()) >= self.current_step:
+            raise ValueError("history may only hold steps before the current one (no current or future matrix)")
+        object.__setattr__(self, "matrices", tuple(readonly_array(m, dtype=np.int64) for m in given))
+        object.__setattr__(self, "steps", tuple(steps.tolist()))
 
     @classmethod
     def from_completed_matrices(cls, *, matrices: Sequence[np.ndarray], steps: Sequence[int],
                                 sequence_id: str, current_step: int) -> "SanitizedHistoryView":
-        return cls(tuple(matrices), tuple(steps), str(sequence_id), int(current_step))
+        return cls(matrices=tuple(matrices), steps=tuple(steps), sequence_id=str(sequence_id),
+                   current_step=int(current_step))
 
 
 __all__ = ["PartialObservationState", "PublicTopologyView", "RevealedDemandToken",
