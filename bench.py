@@ -5,6 +5,7 @@
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
         --master-port P bench.py --gpus N --steps K --warmup W
     python bench.py --impl reference ...     (the unmodified reference build)
+    python bench.py --impl nccl ...          (PyTorch + NCCL baseline layer, same preset and N)
 
 Metric: full MoE layer p50 latency (first Router launch -> combined output),
 device-timed with CUDA events on the layer's stream, max over ranks per step,
@@ -252,6 +253,100 @@ def run_product(args) -> dict | None:
             dist.destroy_process_group()
 
 
+def run_nccl(args) -> dict | None:
+    """The PyTorch + NCCL baseline layer (transport/nccl_baseline.py) at the
+    same preset and GPU count: router per chunk, per-descriptor count exchange
+    and uneven all_to_all_single, PyTorch experts, NCCL return, scatter-add
+    combine.  Device-timed with CUDA events around each call (which synchronises
+    with the host inside, as the reference's driver does), max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from revealaiccl_b200.bench.paired import bootstrap_median
+    from revealaiccl_b200.moe.config import preset
+    from revealaiccl_b200.moe.oracle import layer_reference
+    from revealaiccl_b200.transport.nccl_baseline import NcclMoELayer
+
+    rank, world, local = _env_world()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    cfg = preset(args.config)
+    try:
+        layer = NcclMoELayer(cfg, device=dev)
+        out_e = layer.forward("early").clone()
+        ref, _ = layer_reference(cfg, layer.inputs.tokens, layer.weights, layer.ids.int(), layer.gates)
+        tol = 2e-2 if cfg.dtype == "bf16" else 5e-3
+        if not torch.allclose(out_e, ref, atol=tol, rtol=tol):
+            raise RuntimeError("NCCL baseline output differs from the fp32 oracle")
+        if not torch.equal(out_e, layer.forward("delayed")):
+            raise RuntimeError("NCCL baseline early and delayed arms differ")
+        flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+        cur = torch.cuda.current_stream(dev)
+
+        def step(arm, host_in=None, host_out=None):
+            flush.zero_()
+            torch.cuda.synchronize(dev)
+            if world > 1:
+                dist.barrier()
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record(cur)
+            if host_in is not None:
+                layer.inputs.tokens.copy_(host_in, non_blocking=True)
+            out = layer.forward(arm)
+            if host_out is not None:
+                host_out.copy_(out, non_blocking=True)
+            e.record(cur)
+            torch.cuda.synchronize(dev)
+            return s.elapsed_time(e)
+
+        for _ in range(args.warmup):
+            step("early")
+            step("delayed")
+        early, delayed = [], []
+        for _ in range(args.steps):
+            early.append(step("early"))
+            delayed.append(step("delayed"))
+        host_in = torch.empty(layer.inputs.tokens.shape, dtype=layer.inputs.tokens.dtype, pin_memory=True)
+        host_in.copy_(layer.inputs.tokens.cpu())
+        host_out = torch.empty(layer.out.shape, dtype=layer.out.dtype, pin_memory=True)
+        e2e = [step("early", host_in, host_out) for _ in range(args.steps)]
+        early = _max_over_ranks(early, world, dev)
+        delayed = _max_over_ranks(delayed, world, dev)
+        e2e = _max_over_ranks(e2e, world, dev)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+    if rank != 0:
+        return None
+    p50 = statistics.median(early)
+    deltas = [d - e for e, d in zip(early, delayed)]
+    ci = bootstrap_median(deltas)
+    return {
+        "impl": "nccl", "metric": METRIC, "value": round(p50, 4), "unit": "ms", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(statistics.fmean(early), 4),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": vs_baseline(args.config, p50),
+        "dtype": "fp32-tf32" if cfg.dtype == "fp32" else "bf16",
+        "data": "synthetic (the product layer's seeded inputs and weights)",
+        "config": {"model": f"{cfg.name}: {cfg.experts} experts top-{cfg.top_k}, D={cfg.hidden}, "
+                            f"expert {cfg.hidden}->{cfg.ffn_hidden} {cfg.activation}->{cfg.out_dim}",
+                   "global_batch": cfg.tokens_per_rank * world, "seq_len": cfg.tokens_per_rank,
+                   "parallelism": f"ep{world}", "l2": "256 MiB flush before every timed step",
+                   "path": "PyTorch router/experts + NCCL all_to_all_single per descriptor"},
+        "p50_early_ms": round(p50, 4), "p50_delayed_ms": round(statistics.median(delayed), 4),
+        "delta_ms": round(statistics.median(deltas), 4),
+        "delta_ci95_ms": [round(ci["ci95_lower"], 4), round(ci["ci95_upper"], 4)],
+        "e2e": {"value": round(statistics.median(e2e), 4), "unit": "ms",
+                "h2d_bytes_per_step": int(host_in.numel() * host_in.element_size()),
+                "d2h_bytes_per_step": int(host_out.numel() * host_out.element_size())},
+    }
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -262,7 +357,7 @@ def main() -> None:
     # D=2048, 4 experts top-1, 2048->32 ReLU->16, fp32, 8 x 512 chunks).  full_tf32,
     # skewed_bf16, mixtral_8x7b and deepseek_v2_lite are explicit runs.
     ap.add_argument("--config", default=DEFAULT_CONFIG)
-    ap.add_argument("--impl", choices=("product", "reference"), default="product")
+    ap.add_argument("--impl", choices=("product", "reference", "nccl"), default="product")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -270,6 +365,8 @@ def main() -> None:
         from baseline.reference_arm import run_reference
 
         out = run_reference(args, ClockSampler)
+    elif args.impl == "nccl":
+        out = run_nccl(args)
     else:
         out = run_product(args)
     if out is not None:

@@ -515,12 +515,16 @@ __device__ __forceinline__ void dispatch_publish(const DispatchParams& p, int de
                                                  unsigned long long epoch, bool update_sent_base) {
   const MoEDims& d = p.dims;
   const int E = d.experts;
+  // bytes one forward row moves: features, identity row, return-row index, gate
+  const unsigned long long row_bytes = (unsigned long long)d.hidden * d.feat_bytes + kFwdMetaFields * 8 + 4 + 4;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     const int cnt = atomicAdd(&p.desc_counts[(long long)desc * E + e], 0);
     const int r = expert_owner(d, e), le = expert_slot(d, e);
     uint8_t* base = (uint8_t*)p.peers.base[r];
     ((int*)(base + p.layout.recv_count))[((long long)le * d.world + d.rank) * d.n_desc + desc] = cnt;
     if (update_sent_base) p.sent_base[e] += cnt;
+    if (p.peer_counters != nullptr)
+      atomicAdd(p.peer_counters + (long long)r * kPeerCounterFields + kPcBytes, (unsigned long long)cnt * row_bytes + 4);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -528,6 +532,12 @@ __device__ __forceinline__ void dispatch_publish(const DispatchParams& p, int de
       uint8_t* base = (uint8_t*)p.peers.base[r];
       st_release_sys_u64((uint64_t*)(base + p.layout.recv_flag) + (long long)d.rank * d.n_desc + desc, epoch);
     }
+    if (p.peer_counters != nullptr)
+      for (int r = 0; r < d.world; ++r) {
+        unsigned long long* pc = p.peer_counters + (long long)r * kPeerCounterFields;
+        atomicAdd(pc + kPcPutCalls, 1ULL);
+        if (!skip_signal) atomicAdd(pc + kPcSignals, 1ULL);
+      }
     p.done_counter[desc] = 0;
   }
 }

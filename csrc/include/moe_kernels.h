@@ -45,6 +45,7 @@ struct DispatchParams {
   const unsigned long long* epoch;   // device word holding this call's sequence number
   DeviceStatus* status;
   TraceSlot* trace;
+  unsigned long long* peer_counters;  // [world][kPeerCounterFields] or nullptr
 };
 
 struct PlanParams {
@@ -70,6 +71,7 @@ struct PlanParams {
   int32_t* tail1;
   int32_t* tail2;
   int swap1, swap2;
+  unsigned long long* peer_counters;  // [world][kPeerCounterFields] or nullptr
 };
 
 struct ReturnMetaParams {

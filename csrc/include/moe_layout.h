@@ -21,6 +21,16 @@
 namespace raiccl {
 
 constexpr int kMaxRanks = 8;
+
+// Per-peer traffic counters of one rank (int64 words, [world][kPeerCounterFields],
+// monotonic across calls): forward descriptors put to the peer, forward bytes
+// (feature rows, identity rows, return-row and gate words, count header),
+// ready signals sent to it, ready words waited for from it, return bytes sent
+// to it (output rows + return identity rows) and return signals sent to it.
+enum PeerCounter : int {
+  kPcPutCalls = 0, kPcBytes = 1, kPcSignals = 2, kPcWaits = 3, kPcReturnBytes = 4, kPcReturnSignals = 5,
+  kPeerCounterFields = 8
+};
 constexpr int kFwdMetaFields = 9;
 constexpr int kRetMetaFields = 8;
 

@@ -165,6 +165,23 @@ __device__ __forceinline__ void plan_tiles(int rows, int bm, int nblocks, int sw
   tail = sw ? nblocks : 0;
 }
 
+// Traffic counters of the expert side: one ready word waited for per (source,
+// descriptor), and per source rank the return bytes (output rows and return
+// identity rows of every row received from it) and one return signal.
+__device__ __forceinline__ void plan_count_traffic(const PlanParams& p) {
+  if (p.peer_counters == nullptr || threadIdx.x != 0) return;
+  const MoEDims& d = p.dims;
+  const unsigned long long row_bytes = (unsigned long long)d.out_dim * d.out_bytes + kRetMetaFields * 8;
+  for (int src = 0; src < d.world; ++src) {
+    unsigned long long rows = 0;
+    for (int s = 0; s < d.expert_slots; ++s) rows += (unsigned long long)p.rows_out[s * d.world + src];
+    unsigned long long* pc = p.peer_counters + (long long)src * kPeerCounterFields;
+    atomicAdd(pc + kPcWaits, (unsigned long long)d.n_desc);
+    atomicAdd(pc + kPcReturnBytes, rows * row_bytes);
+    atomicAdd(pc + kPcReturnSignals, 1ULL);
+  }
+}
+
 __global__ void moe_expert_plan_kernel(PlanParams p) {
   griddep_wait();  // programmatic dependent of the front end (no-op otherwise)
   griddep_launch_dependents();
@@ -213,6 +230,8 @@ __global__ void moe_expert_plan_kernel(PlanParams p) {
       local[2] += f; local[3] += tl;
     }
   }
+  __syncthreads();  // rows_out of every segment written
+  plan_count_traffic(p);
   if (p.prefix1 == nullptr) return;
   __shared__ int s_scan[4][256];
 #pragma unroll

@@ -86,6 +86,17 @@ __device__ __forceinline__ void cta_stamp(const FrontendParams& f, int k) {
   if (f.cta_clock != nullptr && threadIdx.x == 0) f.cta_clock[(long long)blockIdx.x * 64 + k] = globaltimer_ns();
 }
 
+// Routing work is dealt out over the workers as one sequence across chunks:
+// unit u of chunk c (a token group, or a token for the warp-per-token router)
+// goes to worker (units of chunks before c + u) mod n.  A chunk with fewer
+// units than workers therefore leaves the next workers free for the next
+// chunk, so consecutive chunks are routed side by side.  Returns this
+// worker's first unit index in the chunk.
+__device__ __forceinline__ int first_share(int worker, int units_before, int n) {
+  const int g = worker - units_before % n;
+  return g < 0 ? g + n : g;
+}
+
 __device__ __forceinline__ int trigger_first_chunk(int q, int P) { return q < P ? q : P; }
 __device__ __forceinline__ int trigger_last_chunk(int q, int P, int C) { return q < P ? q : C - 1; }
 
@@ -375,21 +386,24 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   // start pulling this worker's token rows of every chunk into L2
   if constexpr (NT > 0) if (resident) {
     const int row_bytes = f.rp.hidden * (int)sizeof(T);
+    int cum = 0;  // token groups of the chunks before c (the assignment below)
     for (int c = 0; c < C; ++c) {
       const int t0 = s_coff[c], t1 = s_coff[c + 1];
       const int ngroups = (t1 - t0 + NT - 1) / NT;
-      for (int g = w; g < ngroups; g += W) {
+      for (int g = first_share(w, cum, W); g < ngroups; g += W) {
         const int tf = t0 + g * NT, nt = min(NT, t1 - tf);
         const char* base = (const char*)f.rp.tokens + (long long)tf * row_bytes;
         for (int off = threadIdx.x * 128; off < nt * row_bytes; off += blockDim.x * 128)
           asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
       }
+      cum += ngroups;
     }
   }
   cta_stamp(f, 0);
   __syncthreads();
   cta_stamp(f, 1);
   int next = 0;
+  int cum_units = 0;  // routing units (token groups, or tokens) of the chunks before c
   for (int c = 0; c < C; ++c) {
     TraceSlot* rslot = f.phase_trace ? &f.phase_trace[c] : nullptr;
     if (threadIdx.x == 0) trace_begin(rslot);
@@ -442,14 +456,16 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     DigestSink dsink{f.digest_out, f.csbase_out, f.dp.token_ids, f.dp.dims.rank, c, t0, s_dred};
     if constexpr (NT > 0) {
       const int ngroups = (t1 - t0 + NT - 1) / NT;
-      for (int g = w; g < ngroups; g += W) {
+      for (int g = first_share(w, cum_units, W); g < ngroups; g += W) {
         const int tf = t0 + g * NT;
         router_group<T, NT, EP>(f.rp, s_rbias, cbias, f.rp.block_mask ? s_rmask : nullptr, tf, min(NT, t1 - tf),
                                 red, run, use_wpre ? wpre : nullptr, digest ? &dsink : nullptr);
       }
+      cum_units += ngroups;
     } else {
       const int nvec_tok = f.rp.hidden * (int)sizeof(T) / 16;
-      for (int t = t0 + w * nwarps + warp; t < t1; t += W * nwarps) {
+      const int slots = W * nwarps;
+      for (int t = t0 + first_share(w * nwarps + warp, cum_units, slots); t < t1; t += slots) {
         int sel[8];
         router_token<T, EMAX, false>(f.rp, cbias, t, wts, sel);
         if (lane == 0)
@@ -463,6 +479,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
           }
         }
       }
+      cum_units += t1 - t0;
     }
     if (c < 8) cta_stamp(f, 52 + c);
     __syncthreads();

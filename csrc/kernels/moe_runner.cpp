@@ -331,6 +331,7 @@ class MoELayerRunner {
     dp.permit = permit;
     dp.epoch = epoch;
     dp.status = status;
+    dp.peer_counters = opt_ptr<unsigned long long>(t, "peer_counters");
 
     auto dispatch = [&](int q) {
       const int c_lo = q < partial_ ? q : partial_;
@@ -436,6 +437,7 @@ class MoELayerRunner {
     int* tail2 = swap2_ ? ptr<int>(t, "tail2") : nullptr;
     pp.tail1 = tail1;
     pp.tail2 = tail2;
+    pp.peer_counters = dp.peer_counters;
     pp.swap1 = swap1_;
     pp.swap2 = swap2_;
     raiccl::launch_expert_plan(pp, comm_, pdl_);

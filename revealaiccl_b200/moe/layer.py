@@ -207,8 +207,11 @@ class ProgressiveMoELayer:
             "plan_MT": int(max_tmpl),
             "ctl_blob": self._control_blob(flat, Ep, G, V, Tc, dev),
             "ctl_log": torch.zeros(cfg.n_desc * self.log_stride, dtype=torch.int32, device=dev),
+            # per-peer traffic counters, updated by the dispatch and expert-plan kernels
+            "peer_counters": torch.zeros(W * PeerChannel.COUNTER_STRIDE, dtype=torch.int64, device=dev),
         }
         self.tensors = {kk: v for kk, v in self.tensors.items() if v is not None}
+        self.channel.bind_counters(self.tensors["peer_counters"])
         self.tensors.update(self._ctl_views)
         if trace:  # device trace ring: 32-byte slots, one per launch of a call
             self.tensors["trace"] = torch.zeros(TRACE_SLOTS * 4, dtype=torch.int64, device=dev)

@@ -67,7 +67,35 @@ class PeerChannel:
                     self._opened.append(p)
                     bases.append(p)
             self.bases = bases
-        self.counters = {"put_calls": 0, "bytes_transferred": 0, "signals": 0, "waits": 0}
+        self._device_counters: torch.Tensor | None = None
+
+    COUNTER_FIELDS = ("put_calls", "bytes_transferred", "signals", "waits", "return_bytes", "return_signals")
+    COUNTER_STRIDE = 8  # int64 words per peer in the device counter array
+
+    def bind_counters(self, counters: torch.Tensor) -> None:
+        """Attach the device counter array the data-plane kernels update:
+        [world][8] int64 words per peer (descriptors put, forward bytes, ready
+        signals sent, ready words waited for, return bytes, return signals)."""
+        if counters.dtype != torch.int64 or counters.numel() != self.world * self.COUNTER_STRIDE:
+            raise ValueError("peer counters must be int64 [world * 8]")
+        self._device_counters = counters
+
+    def peer_counters(self) -> list[dict[str, int]]:
+        """Per-peer counts (index = peer rank, own rank included) since the layer was built."""
+        if self._device_counters is None:
+            return [dict.fromkeys(self.COUNTER_FIELDS, 0) for _ in range(self.world)]
+        rows = self._device_counters.view(self.world, self.COUNTER_STRIDE).cpu().tolist()
+        return [dict(zip(self.COUNTER_FIELDS, row)) for row in rows]
+
+    @property
+    def counters(self) -> dict[str, int]:
+        """Totals over all peers of the device counters (the MSCCL++ runtime's
+        put_calls / bytes_transferred / signals / waits, plus the return side)."""
+        total = dict.fromkeys(self.COUNTER_FIELDS, 0)
+        for row in self.peer_counters():
+            for k, v in row.items():
+                total[k] += int(v)
+        return total
 
     def view(self, offset: int, shape: tuple[int, ...], dtype: torch.dtype, rank: int | None = None) -> torch.Tensor:
         base = self.bases[self.rank if rank is None else rank]

@@ -90,6 +90,15 @@ def load_topology_info(name: str, root: str | os.PathLike | None = None,
                         cache_dir=str(path.parent) if cache else None, name=name)
 
 
+def node_roles(name: str, root: str | os.PathLike | None = None) -> list[str]:
+    """The ``role`` of every node of a topology file, in node order ("gpu",
+    "switch", "nic", ...); nodes without one count as GPUs."""
+    path = topology_path(name, root)
+    with open(path, "r", encoding="utf-8") as f:
+        data = json.load(f)
+    return [str(n.get("role", "gpu")).lower() for n in data.get("nodes", [])]
+
+
 def file_sha256(path: str | os.PathLike) -> str:
     return hashlib.sha256(Path(path).read_bytes()).hexdigest()
 

@@ -327,3 +327,121 @@ def test_streamed_copies_start_inside_the_callers_window():
             assert layer.verify()["pass"]
     finally:
         layer.close()
+
+
+# The bf16 benchmark shapes with their full expert widths, expert counts,
+# top-k, chunk counts and gate modes, on fewer tokens per rank.
+BASELINE_SHAPES = {
+    "skewed_bf16": dict(tokens_per_rank=2048, chunk_sizes=(128,) * 16),
+    "mixtral_8x7b": dict(tokens_per_rank=2048, chunk_sizes=(64,) * 32),
+    "deepseek_v2_lite": dict(tokens_per_rank=2048, chunk_sizes=(128,) * 16),
+}
+
+
+@pytest.mark.parametrize("name", sorted(BASELINE_SHAPES))
+def test_baseline_shapes_world1_verified(name):
+    """SwiGLU experts at the benchmark widths (Mixtral 4096->14336->4096,
+    DeepSeek-V2-Lite 64 experts top-6 2048->1408->2048, skewed 16 experts with
+    Zipf bias and a hot phase) pass the fail-closed checker against the fp32
+    oracle, and the early and delayed arms give identical outputs."""
+    from revealaiccl_b200.moe.config import preset
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    cfg = preset(name, **BASELINE_SHAPES[name])
+    layer = ProgressiveMoELayer(cfg, timeout_s=10.0)
+    try:
+        layer.forward("early")
+        rep = layer.verify()
+        assert rep["pass"], rep["violations"]
+        assert rep["forward"]["tokens"] == cfg.tokens_per_rank * cfg.top_k
+        out_e = layer.out.clone()
+        layer.forward("delayed")
+        assert layer.verify()["pass"]
+        assert torch.equal(out_e, layer.out)
+    finally:
+        layer.close()
+
+
+def _revealed_prefix(layer, c):
+    """Everything the layer produced for router chunks 0..c and descriptors
+    0..c: expert ids and gates of those rows, the control-log decision rows
+    (without their phase clocks) and the forward identity rows and features
+    each (local expert, source) region received from those descriptors."""
+    cfg = layer.cfg
+    off = cfg.chunk_offsets
+    T, W, S = cfg.tokens_per_rank, layer.world, layer.slots
+    torch.cuda.synchronize()
+    log = layer.tensors["ctl_log"].view(cfg.n_desc, layer.log_stride).cpu()
+    counts = layer._region("recv_count", (S, W, cfg.n_desc), torch.int32).cpu()
+    meta = layer._region("recv_meta", (S, W, T, 9), torch.int64).cpu()
+    dt = torch.bfloat16 if cfg.dtype == "bf16" else torch.float32
+    feat = layer._region("recv_feat", (S, W, T, cfg.hidden), dt).cpu()
+    rows = []
+    for s in range(S):
+        for src in range(W):
+            n = int(counts[s, src, :c + 1].sum())
+            rows.append((meta[s, src, :n].clone(), feat[s, src, :n].clone()))
+    return {
+        "ids": layer.expert_ids[:off[c + 1]].cpu(), "gates": layer.gates[:off[c + 1]].cpu(),
+        "log": torch.cat([log[:c + 1, :8], log[:c + 1, 16:]], dim=1),
+        "rows": rows,
+    }
+
+
+def test_hidden_future_perturbation_leaves_revealed_prefix_unchanged():
+    """Revealed-only on the device path: changing the token rows and the
+    router logit bias of every chunk after chunk c between two calls must not
+    change anything the layer decided or sent for chunks (descriptors) 0..c:
+    routing, control-plane decisions and dispatched identity rows are equal,
+    while the later chunks' routing does change."""
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    c = 2
+    layer = ProgressiveMoELayer(_small("fp32", "gelu", 2, case_bias=(0.0, 0.0, 0.0, 0.0)), timeout_s=5.0)
+    try:
+        assert c < layer.cfg.progressive_chunks - 1 and layer.inputs.chunk_bias is not None
+        layer.forward("early")
+        assert layer.verify()["pass"]
+        first = _revealed_prefix(layer, c)
+        ids_before = layer.expert_ids.clone()
+        cut = layer.cfg.chunk_offsets[c + 1]
+        g = torch.Generator(device="cpu").manual_seed(99)
+        host = layer.inputs.tokens.cpu().clone()
+        host[cut:] = torch.randn(host[cut:].shape, generator=g).to(host.dtype)
+        layer.inputs.chunk_bias[c + 1:] += (torch.randn(layer.inputs.chunk_bias[c + 1:].shape, generator=g) * 3.0
+                                            ).to(layer.inputs.chunk_bias.device)
+        layer.load_tokens_(host.pin_memory())
+        layer.forward("early")
+        assert layer.verify()["pass"]
+        second = _revealed_prefix(layer, c)
+        assert torch.equal(first["ids"], second["ids"]) and torch.equal(first["gates"], second["gates"])
+        assert torch.equal(first["log"], second["log"])
+        for (m1, f1), (m2, f2) in zip(first["rows"], second["rows"]):
+            assert torch.equal(m1, m2) and torch.equal(f1, f2)
+        assert not torch.equal(ids_before[cut:], layer.expert_ids[cut:])  # the future did change
+    finally:
+        layer.close()
+
+
+def test_peer_counters_count_one_call():
+    """The device traffic counters behind PeerChannel.counters: one call on
+    one rank puts every descriptor to itself once, with its rows' bytes, one
+    ready signal per descriptor, one wait per descriptor, and returns every
+    (token, choice) row once."""
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    layer = ProgressiveMoELayer(_small("fp32", "gelu", 2), timeout_s=5.0)
+    try:
+        layer.forward("early")
+        torch.cuda.synchronize()
+        cfg = layer.cfg
+        c = layer.channel.peer_counters()[0]
+        rows = cfg.tokens_per_rank * cfg.top_k
+        fwd_row = cfg.hidden * 4 + 9 * 8 + 4 + 4
+        assert c["put_calls"] == cfg.n_desc and c["signals"] == cfg.n_desc and c["waits"] == cfg.n_desc
+        assert c["bytes_transferred"] == rows * fwd_row + 4 * cfg.experts * cfg.n_desc
+        assert c["return_bytes"] == rows * (cfg.out_dim * 4 + 8 * 8) and c["return_signals"] == 1
+        layer.forward("early")
+        assert layer.channel.counters["put_calls"] == 2 * cfg.n_desc
+    finally:
+        layer.close()
