@@ -128,7 +128,8 @@ def run_product(args) -> dict | None:
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     cfg = preset(args.config)
-    layer = ProgressiveMoELayer(cfg, device=dev, timeout_s=10.0)
+    layer = ProgressiveMoELayer(cfg, device=dev, timeout_s=10.0, progressive=bool(args.progressive),
+                                dispatch_ctas=args.dispatch_ctas)
     try:
         # correctness gate (untimed): both arms verified, outputs identical
         layer.forward("early")
@@ -231,7 +232,9 @@ def run_product(args) -> dict | None:
                                 f"expert {cfg.hidden}->{cfg.ffn_hidden} {cfg.activation}->{cfg.out_dim}",
                        "global_batch": tokens_total, "seq_len": cfg.tokens_per_rank,
                        "tokens_per_rank": cfg.tokens_per_rank, "chunks": cfg.chunks,
-                       "parallelism": f"ep{world}", "l2": "256 MiB flush before every timed step"},
+                       "parallelism": f"ep{world}", "l2": "256 MiB flush before every timed step",
+                       "progressive_gemm1": bool(layer.runner.progressive()),
+                       "dispatch_ctas": args.dispatch_ctas},
             "p50_early_ms": round(p50, 4), "p50_delayed_ms": round(statistics.median(delayed), 4),
             "delta_ms": round(statistics.median(deltas), 4),
             "delta_ci95_ms": [round(ci["ci95_lower"], 4), round(ci["ci95_upper"], 4)],
@@ -358,6 +361,10 @@ def main() -> None:
     # skewed_bf16, mixtral_8x7b and deepseek_v2_lite are explicit runs.
     ap.add_argument("--config", default=DEFAULT_CONFIG)
     ap.add_argument("--impl", choices=("product", "reference", "nccl"), default="product")
+    # expert side: GEMM-1 takes 256-row tiles as descriptors arrive (1) or after the
+    # whole batch (0); front-end workers that keep dispatching (0: all of them)
+    ap.add_argument("--progressive", type=int, default=1, choices=(0, 1))
+    ap.add_argument("--dispatch-ctas", type=int, default=0)
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

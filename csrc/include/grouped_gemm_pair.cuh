@@ -51,6 +51,73 @@ __device__ __forceinline__ PairTile pair_tile(const GroupedGemmParams& p, int t,
   return r;
 }
 
+// ---------------------------------------------------------------------------
+// Progressive tile source (GroupedGemmParams::progressive).  Iteration k of
+// pair `pair`: the leader's producer draws a ticket T from the per-call
+// counter and posts it in the pair's ring slot k % kPairTicketRing, tagged
+// with the call epoch and k; every other role of both CTAs reads it there.
+// Then each role waits (bounded) until the planner's published tile count
+// passes T, and reads tile T from the list; a final count at or below T
+// means the pair has no more tiles.  Returns 1 (tile in pt), 0 (no more
+// tiles) or -1 (a wait ran out; status recorded).  One thread per call.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64_gg(const unsigned long long* a) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ int progressive_next(const GroupedGemmParams& p, int pair, int k, bool draw,
+                                                unsigned long long epoch, PairTile& pt, int kernel_id) {
+  unsigned long long* slot = p.pair_tickets + (long long)pair * kPairTicketRing + (k & (kPairTicketRing - 1));
+  const unsigned long long tag = ((epoch & 0xffffffULL) << 40) | ((unsigned long long)(k & 0xfffff) << 20);
+  unsigned int T = 0;
+  if (draw) {
+    T = atomicAdd(p.ticket_counter, 1u) & 0xfffffu;
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(slot), "l"(tag | T) : "memory");
+  } else {
+    const uint64_t start = globaltimer_ns();
+    for (uint32_t polls = 1;; ++polls) {
+      const unsigned long long v = ld_acquire_gpu_u64_gg(slot);
+      if ((v & ~0xfffffULL) == tag) {
+        T = (unsigned int)(v & 0xfffffULL);
+        break;
+      }
+      __nanosleep(32);
+      if ((polls & 63u) == 0) {
+        if (globaltimer_ns() - start > p.timeout_ns) {
+          record_status(p.status, kTimeoutPipeline, kernel_id, k, pair);
+          return -1;
+        }
+        if (status_failed(p.status)) return -1;
+      }
+    }
+  }
+  const unsigned long long want = (epoch & 0xffffffffULL) << 32;
+  const uint64_t start = globaltimer_ns();
+  for (uint32_t polls = 1;; ++polls) {
+    const unsigned long long w = ld_acquire_gpu_u64_gg(p.tile_word);
+    if ((w & 0xffffffff00000000ULL) == want) {
+      if (T < (unsigned int)(w & 0x7fffffffULL)) break;
+      if (w & 0x80000000ULL) return 0;
+    }
+    __nanosleep(64);
+    if ((polls & 63u) == 0) {
+      if (globaltimer_ns() - start > p.timeout_ns) {
+        record_status(p.status, kTimeoutPeerSignal, kernel_id, (long long)T, pair);
+        return -1;
+      }
+      if (status_failed(p.status)) return -1;
+    }
+  }
+  const int4 e = reinterpret_cast<const int4*>(p.tile_list)[T];
+  pt.s = e.x;
+  pt.mb = e.y;
+  pt.nb = e.z;
+  pt.nsw = e.w;
+  return 1;
+}
+
 __device__ __forceinline__ void store1(float* dst, float v) { *dst = v; }
 __device__ __forceinline__ void store1(__nv_bfloat16* dst, float v) { *dst = __float2bfloat16_rn(v); }
 
@@ -153,15 +220,19 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
   // Prologue: shared memory, TMEM and the partner only; the tile table,
-  // segments and A rows come from the previous launch.
-  griddep_wait();
+  // segments and A rows come from the previous launch.  A progressive GEMM
+  // does not wait for the planner to finish: it takes tiles as they are
+  // published (progressive_next).
+  const bool progressive = p.progressive != 0;
+  if (!progressive) griddep_wait();
   griddep_launch_dependents();
   if (p.trace != nullptr && threadIdx.x == 0) atomicMin(&p.trace->t_start, (unsigned long long)globaltimer_ns());
+  const unsigned long long epoch = progressive ? *p.epoch : 0ULL;
 
   // Swapped tail tiles need the weights to fill the 256-row operand: BN = 256.
-  const bool swapping = BN == 256 && ACT != Act::kSwiGLU && p.tail_prefix != nullptr;
-  const int total_full = p.tile_prefix[p.num_segs];
-  const int total_tiles = total_full + (swapping ? p.tail_prefix[p.num_segs] : 0);
+  const bool swapping = BN == 256 && ACT != Act::kSwiGLU && (p.tail_prefix != nullptr || progressive);
+  const int total_full = progressive ? 0 : p.tile_prefix[p.num_segs];
+  const int total_tiles = progressive ? 0 : total_full + (swapping ? p.tail_prefix[p.num_segs] : 0);
   const int nblocks = p.N / BN;
   const int kblocks = (p.K + C::BK - 1) / C::BK;
   const uint64_t lim = p.timeout_ns;
@@ -170,8 +241,15 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     // ------------------------------------------------------------ producer (both CTAs)
     if (elect_one_sync()) {
       int stage = 0; uint32_t phase = 0;
-      for (int t = pair; t < total_tiles; t += npairs) {
-        const PairTile pt = pair_tile(p, t, total_full, nblocks);
+      for (int t = pair, k = 0;; t += npairs, ++k) {
+        PairTile pt;
+        if (progressive) {
+          if (progressive_next(p, pair, k, rank == 0, epoch, pt, kKernelId) <= 0) break;
+          asm volatile("fence.proxy.async.global;" ::: "memory");  // rows landed by generic stores, read by TMA
+        } else {
+          if (t >= total_tiles) break;
+          pt = pair_tile(p, t, total_full, nblocks);
+        }
         const GemmSegment seg = p.segs[pt.s];
         // a swapped tile's tokens are the N operand: each CTA stages half of them
         const int arow = seg.a_row0 + pt.mb * 2 * C::BM + (int)rank * (pt.nsw ? pt.nsw / 2 : C::BM);
@@ -201,14 +279,22 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     // ------------------------------------------------------------ MMA issuer (leader)
     if (rank == 0 && elect_one_sync()) {
       int stage = 0; uint32_t phase = 0; int iter = 0;
-      for (int t = pair; t < total_tiles; t += npairs, ++iter) {
+      for (int t = pair;; t += npairs, ++iter) {
+        int nsw = 0;
+        if (progressive) {
+          PairTile pt;
+          if (progressive_next(p, pair, iter, false, epoch, pt, kKernelId) <= 0) break;
+          nsw = pt.nsw;
+        } else {
+          if (t >= total_tiles) break;
+          nsw = t < total_full ? 0 : pair_tile(p, t, total_full, nblocks).nsw;
+        }
         const int acc = iter & 1;
         const uint32_t acc_phase = (iter >> 1) & 1;
         if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1u, p.status, kKernelId, lim)) break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * BN;
         // swapped tail: weights (the B stage) are the M = 256 operand, tokens N = nsw
-        const int nsw = t < total_full ? 0 : pair_tile(p, t, total_full, nblocks).nsw;
         const uint32_t idesc = nsw ? umma_idesc(TF32 ? 2u : 1u, 256, (uint32_t)nsw) : C::IDESC;
         const uint32_t swap_off = nsw ? (uint32_t)C::A_BYTES : 0u;
         bool ok = true;
@@ -247,10 +333,24 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     int c0, c1;
     epi_columns(warp - 2, ACT == Act::kSwiGLU ? BN / 2 : BN, c0, c1);
     int iter = 0;
-    for (int t = pair; t < total_tiles; t += npairs, ++iter) {
+    for (int t = pair;; t += npairs, ++iter) {
+      PairTile pt;
+      if (progressive) {
+        int r = 0;
+        if (lane == 0) r = progressive_next(p, pair, iter, false, epoch, pt, kKernelId);
+        r = __shfl_sync(0xffffffffu, r, 0);
+        if (r <= 0) break;
+        pt.s = __shfl_sync(0xffffffffu, pt.s, 0);
+        pt.mb = __shfl_sync(0xffffffffu, pt.mb, 0);
+        pt.nb = __shfl_sync(0xffffffffu, pt.nb, 0);
+        pt.nsw = __shfl_sync(0xffffffffu, pt.nsw, 0);
+        __syncwarp();  // orders lane 0's acquire before every lane's reads of the segment
+      } else {
+        if (t >= total_tiles) break;
+        pt = pair_tile(p, t, total_full, nblocks);
+      }
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
-      const PairTile pt = pair_tile(p, t, total_full, nblocks);
       const GemmSegment seg = p.segs[pt.s];
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.status, kKernelId, lim)) break;
       tc_fence_after_sync();

@@ -43,4 +43,14 @@ void launch_grouped_gemm(bool in_tf32, bool out_bf16, int act, int bn, const CUt
                          const CUtensorMap& tb, const GroupedGemmParams& p, int grid,
                          cudaStream_t stream, const CUtensorMap* ta8 = nullptr);
 
+// Peer primitives (csrc/kernels/peer_ops.cu).  src / dst: 16-byte aligned,
+// bytes a multiple of 16; dst and flag may be another GPU's mapped memory;
+// done_counter: a zeroed device int of this GPU, one per concurrent put.
+void launch_peer_put_signal(const void* src, void* dst, long long bytes, unsigned long long* flag,
+                            unsigned long long seq, int* done_counter, int grid, cudaStream_t s);
+// Waits (bounded) until *flag >= seq; waited_ns (optional) receives the wait
+// time, or ~0 after a timeout (the status then holds kTimeoutPeerSignal).
+void launch_peer_wait(const unsigned long long* flag, unsigned long long seq, unsigned long long timeout_ns,
+                      DeviceStatus* status, unsigned long long* waited_ns, cudaStream_t s);
+
 }  // namespace raiccl

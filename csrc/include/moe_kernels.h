@@ -72,6 +72,11 @@ struct PlanParams {
   int32_t* tail2;
   int swap1, swap2;
   unsigned long long* peer_counters;  // [world][kPeerCounterFields] or nullptr
+  // Progressive planning (launch_expert_plan_progressive): GEMM-1's tiles in
+  // arrival order, published descriptor by descriptor in tile_word.
+  int32_t* tile_list;               // [max_tiles1][4]
+  unsigned long long* tile_word;
+  int max_tiles1;
 };
 
 struct ReturnMetaParams {
@@ -172,6 +177,12 @@ struct FrontendParams {
   // tok_ready_all has reached this call's epoch (null: tokens resident).
   const unsigned long long* tok_ready;      // [C], written by the copy stream after chunk c's rows
   const unsigned long long* tok_ready_all;  // set by the layer reset when the batch was resident
+  // Progressive expert side: the next launch (the expert planner) may start
+  // as soon as this grid is resident, and only the first dispatch_ctas
+  // workers dispatch; the others leave after routing, so their SMs take
+  // GEMM-1 tiles while the scheduler chain runs (0: every worker dispatches).
+  int early_dependents;
+  int dispatch_ctas;
 };
 
 // Returns false (nothing launched) when the device cannot co-schedule the grid.
@@ -187,6 +198,12 @@ void launch_checksum_base(const long long* token_ids, const long long* digest, c
 void launch_router(const RouterParams& p, bool bf16, cudaStream_t s);
 void launch_dispatch(const DispatchParams& p, bool bf16, int grid, cudaStream_t s);
 void launch_expert_plan(const PlanParams& p, cudaStream_t s, bool pdl = false);
+// One-warp planner of the progressive expert side (a programmatic dependent
+// of the front end that starts at once): per descriptor, waits for every
+// source's ready word, appends the newly complete 256-row GEMM-1 tiles to
+// p.tile_list and publishes their count; after the last, the remaining and
+// swapped tail tiles, the segments, rows_out and GEMM-2's tile tables.
+void launch_expert_plan_progressive(const PlanParams& p, cudaStream_t s);
 void launch_return_meta(const ReturnMetaParams& p, int grid, cudaStream_t s);
 void launch_combine(const CombineParams& p, bool bf16, int grid, cudaStream_t s, bool pdl = false);
 void launch_host_flag_signal(unsigned long long* flag, unsigned long long value, unsigned long long delay_ns,
@@ -194,7 +211,7 @@ void launch_host_flag_signal(unsigned long long* flag, unsigned long long value,
 void launch_layer_reset(int* sent_base, int experts, int* desc_counts, int n_desc, int* done_counter,
                         unsigned long long* epoch, TraceSlot* trace, int n_trace, int* chunk_words,
                         int n_chunk_words, unsigned long long* tok_ready_all, unsigned long long* stream_pending,
-                        cudaStream_t s);
+                        cudaStream_t s, unsigned int* ticket_counter = nullptr);
 void launch_control(const ControlParams& p, cudaStream_t s);
 void launch_device_barrier(const BarrierParams& p, cudaStream_t s);
 

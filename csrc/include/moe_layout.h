@@ -56,9 +56,17 @@ struct MoEDims {
   long long cap;      // rows per (slot, source) region
 };
 
+// Every array of the region is followed by a guard band of kGuardBytes that
+// no kernel writes: the host fills the bands with a canary pattern when the
+// region is created and the checker verifies them after a call, so a store
+// past the end of any receive or return array is caught.
+constexpr int kSymArrays = 10;
+constexpr long long kGuardBytes = 256;
+
 struct SymLayout {
   long long recv_feat, recv_meta, recv_retrow, recv_gate, recv_count, recv_flag;
   long long ret_out, ret_meta, ret_flag, bar_flag;
+  long long guard[kSymArrays];  // offset of the guard band after each array, in the order above
   long long total;
 };
 
@@ -67,18 +75,25 @@ inline long long align256(long long x) { return (x + 255) / 256 * 256; }
 inline SymLayout make_sym_layout(const MoEDims& d) {
   SymLayout L;
   long long off = 0;
+  int g = 0;
+  auto place = [&](long long& at, long long bytes) {
+    at = off;
+    off = align256(off + bytes);
+    L.guard[g++] = off;
+    off += kGuardBytes;
+  };
   const long long rows = (long long)d.expert_slots * d.world * d.cap;
-  L.recv_feat = off;   off = align256(off + rows * d.hidden * d.feat_bytes);
-  L.recv_meta = off;   off = align256(off + rows * kFwdMetaFields * 8);
-  L.recv_retrow = off; off = align256(off + rows * 4);
-  L.recv_gate = off;   off = align256(off + rows * 4);
-  L.recv_count = off;  off = align256(off + (long long)d.expert_slots * d.world * d.n_desc * 4);
-  L.recv_flag = off;   off = align256(off + (long long)d.world * d.n_desc * 8);
   const long long ret_rows = (long long)d.tokens * d.top_k;
-  L.ret_out = off;     off = align256(off + ret_rows * d.out_dim * d.out_bytes);
-  L.ret_meta = off;    off = align256(off + ret_rows * kRetMetaFields * 8);
-  L.ret_flag = off;    off = align256(off + (long long)d.world * 8);
-  L.bar_flag = off;    off = align256(off + (long long)d.world * 8);
+  place(L.recv_feat, rows * d.hidden * d.feat_bytes);
+  place(L.recv_meta, rows * kFwdMetaFields * 8);
+  place(L.recv_retrow, rows * 4);
+  place(L.recv_gate, rows * 4);
+  place(L.recv_count, (long long)d.expert_slots * d.world * d.n_desc * 4);
+  place(L.recv_flag, (long long)d.world * d.n_desc * 8);
+  place(L.ret_out, ret_rows * d.out_dim * d.out_bytes);
+  place(L.ret_meta, ret_rows * kRetMetaFields * 8);
+  place(L.ret_flag, (long long)d.world * 8);
+  place(L.bar_flag, (long long)d.world * 8);
   L.total = off;
   return L;
 }

@@ -75,6 +75,20 @@ struct GroupedGemmParams {
   // after all full tiles.
   const int* tail_prefix;
   int swap_max;
+  // Progressive tile source (CTA-pair kernel, progressive != 0): tiles are
+  // taken in arrival order from tile_list as the expert planner publishes
+  // them in tile_word ((call epoch low 32 bits) << 32 | final << 31 | count);
+  // each pair's leader draws tickets from ticket_counter (zeroed per call) and
+  // passes them to its partner and its other roles through its
+  // kPairTicketRing slots of pair_tickets.  tile_prefix / tail_prefix unused.
+  int progressive;
+  const int* tile_list;                 // [max] 4 ints per tile: segment, row tile, column block, nsw
+  const unsigned long long* tile_word;
+  unsigned int* ticket_counter;
+  unsigned long long* pair_tickets;     // [pairs][kPairTicketRing]
+  const unsigned long long* epoch;      // this call's sequence number
 };
+
+constexpr int kPairTicketRing = 32;
 
 }  // namespace raiccl

@@ -103,6 +103,39 @@ void grouped_gemm(torch::Tensor A, torch::Tensor B, torch::Tensor segs, torch::T
 
 void register_moe(py::module_& m);
 
+// Peer put + signal: copies src (a CUDA tensor, 16-byte aligned, bytes a
+// multiple of 16) to the device address dst_ptr (own or peer mapping), then
+// releases seq at flag_ptr.  counter: zeroed int32 CUDA tensor [1].
+void peer_put_signal(torch::Tensor src, int64_t dst_ptr, int64_t flag_ptr, int64_t seq, torch::Tensor counter,
+                     int64_t grid) {
+  TORCH_CHECK(src.is_cuda() && src.is_contiguous(), "peer_put_signal: contiguous CUDA source");
+  const long long bytes = src.numel() * src.element_size();
+  TORCH_CHECK(bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(src.data_ptr()) & 15) == 0 && (dst_ptr & 15) == 0,
+              "peer_put_signal: 16-byte aligned buffers and a multiple of 16 bytes");
+  TORCH_CHECK(flag_ptr != 0 && (flag_ptr & 7) == 0, "peer_put_signal: 8-byte aligned flag");
+  TORCH_CHECK(counter.is_cuda() && counter.scalar_type() == torch::kInt32, "peer_put_signal: int32 counter");
+  TORCH_CHECK(grid >= 1 && grid <= 65535, "peer_put_signal: grid");
+  c10::cuda::CUDAGuard guard(src.device());
+  raiccl::launch_peer_put_signal(src.data_ptr(), reinterpret_cast<void*>(dst_ptr), bytes,
+                                 reinterpret_cast<unsigned long long*>(flag_ptr), (unsigned long long)seq,
+                                 counter.data_ptr<int>(), (int)grid, cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Bounded wait until the 64-bit word at flag_ptr (this GPU) is >= seq; the
+// waited time (ns, or -1 after a timeout) goes to waited[0].
+void peer_wait(int64_t flag_ptr, int64_t seq, int64_t timeout_ns, torch::Tensor status, torch::Tensor waited) {
+  TORCH_CHECK(flag_ptr != 0 && (flag_ptr & 7) == 0, "peer_wait: 8-byte aligned flag");
+  TORCH_CHECK(status.is_cuda() && status.numel() * status.element_size() >= (int64_t)sizeof(raiccl::DeviceStatus),
+              "peer_wait: status buffer");
+  TORCH_CHECK(waited.is_cuda() && waited.scalar_type() == torch::kInt64, "peer_wait: int64 waited");
+  c10::cuda::CUDAGuard guard(status.device());
+  raiccl::launch_peer_wait(reinterpret_cast<const unsigned long long*>(flag_ptr), (unsigned long long)seq,
+                           (unsigned long long)timeout_ns, reinterpret_cast<raiccl::DeviceStatus*>(status.data_ptr()),
+                           reinterpret_cast<unsigned long long*>(waited.data_ptr<int64_t>()), cur_stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "revealaiccl_b200 sm_100a kernels (tcgen05/TMEM/TMA, NVLink peer stores)";
   m.def("grouped_gemm", &grouped_gemm, "tcgen05 grouped GEMM with fused epilogue",
@@ -111,4 +144,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out_ptrs"), py::arg("ldo"), py::arg("out_bf16"), py::arg("status"),
         py::arg("grid"), py::arg("timeout_ns"), py::arg("pair") = false, py::arg("swap_max") = 0);
   register_moe(m);
+  m.def("peer_put_signal", &peer_put_signal, py::arg("src"), py::arg("dst_ptr"), py::arg("flag_ptr"), py::arg("seq"),
+        py::arg("counter"), py::arg("grid") = 64);
+  m.def("peer_wait", &peer_wait, py::arg("flag_ptr"), py::arg("seq"), py::arg("timeout_ns"), py::arg("status"),
+        py::arg("waited"));
 }

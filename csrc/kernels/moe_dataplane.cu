@@ -268,6 +268,159 @@ __global__ void moe_expert_plan_kernel(PlanParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Progressive expert plan: one warp, a programmatic dependent of the front
+// end that lets it start as soon as the front end is resident.  Descriptor
+// by descriptor (in order), it waits (bounded) for every source's ready
+// word, adds the descriptor's rows to each (local expert slot, source)
+// segment, appends the 256-row GEMM-1 tiles that are now complete (all
+// column blocks of each) to the tile list and publishes the list's length
+// with a release store; the GEMM-1 CTA pairs take tiles as they appear.
+// After the last descriptor it appends each segment's remaining tiles and
+// then the swapped tail tiles (the order of the non-progressive plan), and
+// writes the segments, rows_out and GEMM-2's tile tables before the final
+// publish.  Segment row counts only grow, so a tile never reads a row count
+// below its own rows.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void publish_tiles(unsigned long long* word, unsigned long long epoch, int count,
+                                              bool final) {
+  __threadfence();
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(word),
+               "l"(((epoch & 0xffffffffULL) << 32) | (final ? 0x80000000ULL : 0ULL) | (unsigned long long)count)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(32) moe_expert_plan_progressive_kernel(PlanParams p) {
+  griddep_launch_dependents();  // the progressive GEMM-1 may launch now
+  TraceScope trace_scope(p.trace);
+  const unsigned FULL = 0xffffffffu;
+  const MoEDims& d = p.dims;
+  const int lane = threadIdx.x;
+  const uint8_t* mine = (const uint8_t*)p.peers.base[d.rank];
+  const uint64_t* flags = (const uint64_t*)(mine + p.layout.recv_flag);
+  const int* counts = (const int*)(mine + p.layout.recv_count);
+  const unsigned long long epoch = *p.epoch;
+  const int S = d.expert_slots * d.world;
+  extern __shared__ int psm[];
+  int* cum = psm;       // [S] rows received so far
+  int* done = psm + S;  // [S] row tiles already listed
+  for (int s = lane; s < S; s += 32) {
+    cum[s] = 0;
+    done[s] = 0;
+    GemmSegment seg;
+    seg.a_row0 = (int)((long long)s * d.cap);
+    seg.rows = 0;
+    seg.expert = s / d.world;
+    seg.out_slot = s % d.world;
+    seg.out_row0 = seg.a_row0;
+    seg.pad0 = seg.pad1 = seg.pad2 = 0;
+    p.segs[s] = seg;
+  }
+  __syncwarp();
+  const int bm = 256, nb1 = p.nblocks1;
+  int listed = 0;
+  bool ok = true;
+  for (int q = 0; q < d.n_desc; ++q) {
+    const bool final = q == d.n_desc - 1;
+    bool got = true;
+    for (int src = lane; src < d.world && ok; src += 32)
+      got = wait_flag_geq_sys(flags + (long long)src * d.n_desc + q, epoch, p.status, kTimeoutPeerSignal, 33,
+                              (long long)src * d.n_desc + q, p.timeout_ns) && got;
+    ok = __all_sync(FULL, got) && ok;  // (the warp barrier orders every lane's acquire before the reads below)
+    for (int s = lane; s < S && ok; s += 32) {
+      int v = cum[s] + counts[(long long)s * d.n_desc + q];
+      if (v > d.cap) {
+        record_status(p.status, kBoundsViolation, 31, v, d.cap);
+        v = cum[s];
+      }
+      cum[s] = v;
+      p.segs[s].rows = v;
+    }
+    __syncwarp();
+    // pass 0: complete row tiles (every remaining one after the last
+    // descriptor); pass 1 (last descriptor): swapped tail tiles
+    for (int pass = 0; pass < (final ? 2 : 1) && ok; ++pass) {
+      for (int s0 = 0; s0 < S; s0 += 32) {
+        const int s = s0 + lane;
+        int first = 0, n = 0, nsw = 0;
+        if (s < S) {
+          const int rows = cum[s];
+          if (!final) {
+            first = done[s];
+            n = rows / bm - first;
+          } else {
+            const int mt = (rows + bm - 1) / bm;
+            const bool sw = p.swap1 > 0 && mt > 0 && rows - (mt - 1) * bm <= p.swap1;
+            if (pass == 0) {
+              first = done[s];
+              n = mt - (sw ? 1 : 0) - first;
+            } else if (sw) {
+              first = mt - 1;
+              n = 1;
+              nsw = (rows - first * bm + 15) & ~15;
+            }
+          }
+          if (n < 0) n = 0;
+        }
+        const int cnt = n * nb1;
+        int incl = cnt;
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(FULL, incl, o);
+          if (lane >= o) incl += v;
+        }
+        const int base = listed + incl - cnt;
+        if (cnt > 0 && base + cnt <= p.max_tiles1) {
+          for (int i = 0; i < cnt; ++i) {
+            int4 e;
+            e.x = s; e.y = first + i / nb1; e.z = i % nb1; e.w = nsw;
+            reinterpret_cast<int4*>(p.tile_list)[base + i] = e;
+          }
+        } else if (cnt > 0) {
+          record_status(p.status, kBoundsViolation, 34, base + cnt, p.max_tiles1);
+        }
+        if (s < S && pass == 0) done[s] = first + n;
+        listed += __shfl_sync(FULL, incl, 31);
+      }
+    }
+    if (listed > p.max_tiles1) listed = p.max_tiles1;
+    if (final || !ok) break;
+    __syncwarp();
+    if (lane == 0) publish_tiles(p.tile_word, epoch, listed, false);
+  }
+  // final segment rows (all zero rows after a failed wait), rows_out and GEMM-2's tile tables
+  const int S2 = S;
+  int run2 = 0, runt = 0;
+  for (int s0 = 0; s0 < S2; s0 += 32) {
+    const int s = s0 + lane;
+    int f = 0, tl = 0;
+    if (s < S2) {
+      const int rows = ok ? cum[s] : 0;
+      p.segs[s].rows = rows;
+      p.rows_out[s] = rows;
+      plan_tiles(rows, p.bm2, p.nblocks2, p.swap2, f, tl);
+    }
+    int a = f, b = tl;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int va = __shfl_up_sync(FULL, a, o), vb = __shfl_up_sync(FULL, b, o);
+      if (lane >= o) { a += va; b += vb; }
+    }
+    if (s < S2) {
+      if (p.prefix2 != nullptr) p.prefix2[s] = run2 + a - f;
+      if (p.tail2 != nullptr) p.tail2[s] = runt + b - tl;
+    }
+    run2 += __shfl_sync(FULL, a, 31);
+    runt += __shfl_sync(FULL, b, 31);
+  }
+  if (lane == 0) {
+    if (p.prefix2 != nullptr) p.prefix2[S2] = run2;
+    if (p.tail2 != nullptr) p.tail2[S2] = runt;
+  }
+  __syncwarp();
+  plan_count_traffic(p);
+  __syncwarp();
+  if (lane == 0) publish_tiles(p.tile_word, epoch, listed, true);
+}
+
 // Publish this rank's return sequence number at every source rank.
 __device__ void publish_return_signal(const MoEDims& d, const SymLayout& L, const PeerBases& P,
                                       unsigned long long epoch) {
@@ -455,8 +608,10 @@ void launch_device_barrier(const BarrierParams& p, cudaStream_t s) {
 __global__ void moe_layer_reset_kernel(int* sent_base, int experts, int* desc_counts, int n_desc,
                                        int* done_counter, unsigned long long* epoch, TraceSlot* trace,
                                        int n_trace, int* chunk_words, int n_chunk_words,
-                                       unsigned long long* tok_ready_all, unsigned long long* stream_pending) {
+                                       unsigned long long* tok_ready_all, unsigned long long* stream_pending,
+                                       unsigned int* ticket_counter) {
   if (threadIdx.x == 0) {
+    if (ticket_counter != nullptr) *ticket_counter = 0;
     const unsigned long long e = *epoch + 1;
     *epoch = e;
     if (tok_ready_all != nullptr) {
@@ -560,6 +715,11 @@ void launch_expert_plan(const PlanParams& p, cudaStream_t s, bool pdl) {
   launch_with_pdl(moe_expert_plan_kernel, dim3(1), dim3(256), 0, s, pdl, p);
 }
 
+void launch_expert_plan_progressive(const PlanParams& p, cudaStream_t s) {
+  const size_t smem = 2 * sizeof(int) * (size_t)p.dims.expert_slots * p.dims.world;
+  launch_with_pdl(moe_expert_plan_progressive_kernel, dim3(1), dim3(32), smem, s, true, p);
+}
+
 void launch_return_meta(const ReturnMetaParams& p, int grid, cudaStream_t s) {
   moe_return_meta_kernel<<<grid, 256, 0, s>>>(p);
 }
@@ -580,10 +740,10 @@ void launch_host_flag_signal(unsigned long long* flag, unsigned long long value,
 void launch_layer_reset(int* sent_base, int experts, int* desc_counts, int n_desc, int* done_counter,
                         unsigned long long* epoch, TraceSlot* trace, int n_trace, int* chunk_words,
                         int n_chunk_words, unsigned long long* tok_ready_all, unsigned long long* stream_pending,
-                        cudaStream_t s) {
+                        cudaStream_t s, unsigned int* ticket_counter) {
   moe_layer_reset_kernel<<<1, 256, 0, s>>>(sent_base, experts, desc_counts, n_desc, done_counter, epoch, trace,
                                            trace ? n_trace : 0, chunk_words, chunk_words ? n_chunk_words : 0,
-                                           tok_ready_all, stream_pending);
+                                           tok_ready_all, stream_pending, ticket_counter);
 }
 
 }  // namespace raiccl

@@ -331,6 +331,9 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   const unsigned long long epoch = *f.dp.epoch;
   const int nc = min(C, kDispatchMaxChunks);
   for (int c = threadIdx.x; c <= nc; c += blockDim.x) s_coff[c] = f.dp.chunk_offsets[c];
+  // the progressive expert planner (next launch) may start now: it waits on
+  // the ready words itself
+  if (f.early_dependents) griddep_launch_dependents();
 
   if (blockIdx.x == 0) {
     // ---------------- control CTA
@@ -359,6 +362,9 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
 
   // ---------------- worker CTAs
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  // workers [0, Wd) dispatch; the others only route and then leave
+  const int Wd = f.dispatch_ctas > 0 ? min(W, f.dispatch_ctas) : W;
+  const bool dispatcher = w < Wd;
   const T* wts = (const T*)f.rp.weight;
   // router tables in shared memory for the whole launch: bias, block mask and
   // (behind the blob area) the per-chunk bias rows
@@ -383,11 +389,15 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   }
   // inputs resident at launch (not streamed in by the copy engine during this call)
   const bool resident = f.tok_ready == nullptr || ld_acquire_gpu_u64(f.tok_ready_all) >= epoch;
-  // start pulling this worker's token rows of every chunk into L2
-  if constexpr (NT > 0) if (resident) {
-    const int row_bytes = f.rp.hidden * (int)sizeof(T);
-    int cum = 0;  // token groups of the chunks before c (the assignment below)
-    for (int c = 0; c < C; ++c) {
+  // pull this worker's token rows into L2 a little ahead of routing them:
+  // chunks 0 and 1 now, chunk c + 2 when chunk c starts (pulling every chunk
+  // at once would queue chunk 0's rows behind the whole batch)
+  const int row_bytes = f.rp.hidden * (int)sizeof(T);
+  auto prefetch_chunk = [&](int c) {
+    if constexpr (NT > 0) {
+      if (!resident || c >= C) return;
+      int cum = 0;  // token groups of the chunks before c (the assignment below)
+      for (int cc = 0; cc < c; ++cc) cum += (s_coff[cc + 1] - s_coff[cc] + NT - 1) / NT;
       const int t0 = s_coff[c], t1 = s_coff[c + 1];
       const int ngroups = (t1 - t0 + NT - 1) / NT;
       for (int g = first_share(w, cum, W); g < ngroups; g += W) {
@@ -396,9 +406,10 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
         for (int off = threadIdx.x * 128; off < nt * row_bytes; off += blockDim.x * 128)
           asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
       }
-      cum += ngroups;
     }
-  }
+  };
+  prefetch_chunk(0);
+  prefetch_chunk(1);
   cta_stamp(f, 0);
   __syncthreads();
   cta_stamp(f, 1);
@@ -407,6 +418,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   for (int c = 0; c < C; ++c) {
     TraceSlot* rslot = f.phase_trace ? &f.phase_trace[c] : nullptr;
     if (threadIdx.x == 0) trace_begin(rslot);
+    prefetch_chunk(c + 2);
     if (c < 8) cta_stamp(f, 2 + 2 * c);
     // early arm: this chunk's poll of the next release is a relaxed load issued
     // before the routing work and read after it (a fence makes it an acquire
@@ -425,7 +437,8 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
             if (ld_acquire_sys_u64(reinterpret_cast<const uint64_t*>(&f.tok_ready[c])) >= epoch ||
                 ld_acquire_sys_u64(reinterpret_cast<const uint64_t*>(f.tok_ready_all)) >= epoch) {
               st = 1;
-            } else if (!f.delayed && next < n_desc && ld_relaxed_gpu_u64(&f.desc_ready[next]) == epoch) {
+            } else if (dispatcher && !f.delayed && next < n_desc &&
+                       ld_relaxed_gpu_u64(&f.desc_ready[next]) == epoch) {
               __threadfence();  // acquire the release seen by the relaxed poll
               st = 2;
             } else if (globaltimer_ns() > deadline) {
@@ -441,7 +454,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
         const int st = s_flag;
         __syncthreads();
         if (st == 1) break;
-        worker_dispatch<T>(f, next, w, W, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, true);
+        worker_dispatch<T>(f, next, w, Wd, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, true);
         ++next;
       }
       if (threadIdx.x == 0 && !f.delayed && next < n_desc) early_v = ld_relaxed_gpu_u64(&f.desc_ready[next]);
@@ -497,7 +510,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     // (never waits).  A resident batch routes every chunk first: routing is
     // then a few microseconds per chunk and the scheduler chain, which needs
     // each chunk, is not held back by dispatch work queued between chunks.
-    if (!f.delayed && !resident) {
+    if (dispatcher && !f.delayed && !resident) {
       if (threadIdx.x == 0) {
         if (early_v == epoch) __threadfence();
         s_flag = early_v == epoch ? 1 : 0;
@@ -506,12 +519,13 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       bool ready = s_flag == 1;
       __syncthreads();
       while (next < n_desc && ready) {
-        worker_dispatch<T>(f, next, w, W, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident);
+        worker_dispatch<T>(f, next, w, Wd, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident);
         ++next;
         ready = next < n_desc && wait_released(f, next, epoch, &s_flag, false) == 1;
       }
     }
   }
+  if (!dispatcher) return;  // routing done: this SM is free for the expert side
   if (f.delayed && wait_released(f, n_desc - 1, epoch, &s_flag, true) != 1) return;
   while (next < n_desc) {
     // a descriptor not yet released whose chunks are routed: compute its
@@ -520,11 +534,11 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     const int rel = wait_released(f, next, epoch, &s_flag, false);
     bool indexed = false;
     if (rel == 0 && chunks_complete(f, next, W, &s_flag)) {
-      worker_index(f, next, w, W, hist, run, item_pos, s_coff);
+      worker_index(f, next, w, Wd, hist, run, item_pos, s_coff);
       indexed = true;
     }
     if (rel != 1 && wait_released(f, next, epoch, &s_flag, true) != 1) return;
-    worker_dispatch<T>(f, next, w, W, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident, indexed);
+    worker_dispatch<T>(f, next, w, Wd, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident, indexed);
     ++next;
   }
 }

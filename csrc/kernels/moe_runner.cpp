@@ -116,6 +116,12 @@ class MoELayerRunner {
       swap2_ = pair2_ && bn2_ == 256 ? swap : 0;
     }
     timeout_ns_ = (unsigned long long)ints["timeout_ns"].cast<int64_t>();
+    // Progressive expert side: GEMM-1 (CTA pairs) takes tiles as descriptors
+    // arrive; needs the persistent front end (decided below) and its tensors.
+    progressive_req_ = pair1_ && (!ints.contains("progressive") || geti(ints, "progressive") != 0) &&
+                       tensors.contains("tile_list") && tensors.contains("tile_word") &&
+                       tensors.contains("ticket_counter") && tensors.contains("pair_tickets");
+    dispatch_ctas_ = ints.contains("dispatch_ctas") ? geti(ints, "dispatch_ctas") : 0;
     max_cands_ = geti(ints, "max_cands");
     log_stride_ = geti(ints, "log_stride");
     max_ctl_tokens_ = geti(ints, "max_ctl_tokens");
@@ -211,8 +217,10 @@ class MoELayerRunner {
 
     trace_labels_.clear();
     raiccl::TraceSlot* reset_slot = trace_slot("layer_reset", -1);
+    const bool progressive = progressive_req_ && use_frontend_;
     raiccl::launch_layer_reset(sent_base, d.experts, desc_counts, d.n_desc, done_counter, epoch, trace_,
-                               trace_cap_, chunk_words_, n_chunk_words_, tok_ready_all_, stream_pending_, comm_);
+                               trace_cap_, chunk_words_, n_chunk_words_, tok_ready_all_, stream_pending_, comm_,
+                               progressive ? ptr<unsigned int>(t, "ticket_counter") : nullptr);
     (void)reset_slot;
     ++launches;
 
@@ -368,6 +376,8 @@ class MoELayerRunner {
       fp.csbase_out = ptr<long long>(t, "checksum_base");
       fp.tok_ready = tok_ready_;
       fp.tok_ready_all = tok_ready_all_;
+      fp.early_dependents = progressive ? 1 : 0;
+      fp.dispatch_ctas = progressive ? dispatch_ctas_ : 0;
       const size_t mark = trace_labels_.size();
       fp.trace = trace_slot("frontend", -1);
       raiccl::TraceSlot* first = nullptr;
@@ -384,6 +394,8 @@ class MoELayerRunner {
       } else {
         trace_labels_.resize(mark);
         use_frontend_ = front = false;  // not co-schedulable here: step pipeline from now on
+        if (progressive) throw std::runtime_error("progressive expert side needs the persistent front end; "
+                                                  "rebuild the layer with progressive=0");
       }
     }
     if (!front) launch_routers();
@@ -440,12 +452,22 @@ class MoELayerRunner {
     pp.peer_counters = dp.peer_counters;
     pp.swap1 = swap1_;
     pp.swap2 = swap2_;
-    raiccl::launch_expert_plan(pp, comm_, pdl_);
+    if (progressive) {
+      auto tl = t["tile_list"].cast<torch::Tensor>();
+      pp.tile_list = reinterpret_cast<int32_t*>(tl.data_ptr());
+      pp.max_tiles1 = (int)(tl.numel() / 4);
+      pp.tile_word = ptr<unsigned long long>(t, "tile_word");
+      raiccl::launch_expert_plan_progressive(pp, comm_);
+    } else {
+      raiccl::launch_expert_plan(pp, comm_, pdl_);
+    }
     ++launches;
 
+    auto launch_return_meta_side = [&]() {
     // Return metadata depends only on the plan: it runs on the dispatch
-    // stream beside the two GEMMs; whichever of it and the combine reports
-    // last publishes the return signal.
+    // stream beside the GEMMs; whichever of it and the combine reports last
+    // publishes the return signal.  (A progressive GEMM-1 is launched right
+    // behind its planner, so that nothing stands between the two launches.)
     ck(cudaEventRecord(ev_plan_, comm_), "cudaEventRecord");
     ck(cudaStreamWaitEvent(disp_, ev_plan_, 0), "cudaStreamWaitEvent");
     raiccl::ReturnMetaParams rm{};
@@ -461,6 +483,9 @@ class MoELayerRunner {
     raiccl::launch_return_meta(rm, grid_sms_, disp_);
     ck(cudaEventRecord(ev_retmeta_, disp_), "cudaEventRecord");
     ++launches;
+    };
+    auto* ret_sync = reinterpret_cast<unsigned long long*>(ptr<int64_t>(t, "ret_sync"));
+    if (!progressive) launch_return_meta_side();
 
     raiccl::GroupedGemmParams g1{};
     g1.segs = segs;
@@ -480,8 +505,20 @@ class MoELayerRunner {
     g1.pair = pair1_ ? 1 : 0;
     g1.pdl = pdl_ ? 1 : 0;
     g1.trace = trace_slot("gemm1", -1);
+    if (progressive) {
+      g1.progressive = 1;
+      g1.pdl = 1;
+      g1.tile_list = ptr<int32_t>(t, "tile_list");
+      g1.tile_word = ptr<unsigned long long>(t, "tile_word");
+      g1.ticket_counter = ptr<unsigned int>(t, "ticket_counter");
+      g1.pair_tickets = ptr<unsigned long long>(t, "pair_tickets");
+      g1.epoch = epoch;
+      if (t["pair_tickets"].cast<torch::Tensor>().numel() < (int64_t)(grid_sms_ / 2) * raiccl::kPairTicketRing)
+        throw std::invalid_argument("pair_tickets holds fewer than (sms / 2) * kPairTicketRing words");
+    }
     raiccl::launch_grouped_gemm(!feat_bf16_, feat_bf16_, act1_, bn1_, ta1_, tb1_, g1, grid_sms_, comm_, &ta1n_);
     ++launches;
+    if (progressive) launch_return_meta_side();
 
     raiccl::GroupedGemmParams g2{};
     g2.segs = segs;
@@ -655,6 +692,7 @@ class MoELayerRunner {
   // Takes effect at the next forward() / capture().
   void inject_skip_signal(int desc) { fault_skip_signal_desc_ = desc; }
   bool persistent_frontend() const { return use_frontend_; }
+  bool progressive() const { return progressive_req_ && use_frontend_; }
 
   py::list trace_labels() const {
     py::list out;
@@ -693,6 +731,8 @@ class MoELayerRunner {
   int partial_ = 0, ffn_ = 0, n1_ = 0, act1_ = 0, bn1_ = 0, bn2_ = 0;
   bool pair1_ = false, pair2_ = false;  // GEMM 1 / 2 on the CTA-pair kernel
   int swap1_ = 0, swap2_ = 0;            // GEMM 1 / 2 swapped-tail row limit (0: off)
+  bool progressive_req_ = false;         // progressive GEMM-1 requested and possible with the pair kernel
+  int dispatch_ctas_ = 0;                // front-end workers that dispatch in progressive mode (0: all)
   bool pdl_ = true;  // plan, GEMMs and combine as programmatic dependents of their predecessors
   int max_cands_ = 0, log_stride_ = 0, max_ctl_tokens_ = 0, grid_sms_ = 148;
   bool control_serial_ = false;  // run the CTA control kernel even where the single-warp one fits
@@ -814,6 +854,10 @@ py::dict sym_layout(py::dict ints) {
   o["recv_gate"] = L.recv_gate; o["recv_count"] = L.recv_count; o["recv_flag"] = L.recv_flag;
   o["ret_out"] = L.ret_out; o["ret_meta"] = L.ret_meta; o["ret_flag"] = L.ret_flag;
   o["bar_flag"] = L.bar_flag; o["total"] = L.total;
+  py::list guards;
+  for (int i = 0; i < raiccl::kSymArrays; ++i) guards.append(L.guard[i]);
+  o["guards"] = guards;
+  o["guard_bytes"] = raiccl::kGuardBytes;
   return o;
 }
 
@@ -867,6 +911,7 @@ void register_moe(py::module_& m) {
       .def("trace_labels", &MoELayerRunner::trace_labels)
       .def("inject_skip_signal", &MoELayerRunner::inject_skip_signal, py::arg("desc"))
       .def("persistent_frontend", &MoELayerRunner::persistent_frontend)
+      .def("progressive", &MoELayerRunner::progressive)
       .def("layout", &MoELayerRunner::layout);
   m.def("router_topk", &router_topk, py::arg("tokens"), py::arg("weight"), py::arg("bias"),
         py::arg("chunk_bias"), py::arg("block_mask"), py::arg("row0"), py::arg("row1"), py::arg("top_k"),

@@ -3,15 +3,23 @@
     python -m revealaiccl_b200.bench.layer_probe --config r4_reference --calls 4 [--graph] [--trace t.json]
         [--control-clocks] [--streamed]
 
-Builds one layer on cuda:0, runs ``--calls`` layer calls (eager launches, or
-replays of a captured graph with ``--graph``), verifies the last one and
-prints the per-call device time.  Meant to be wrapped by ``ncu -k ... -c ...``
+Builds one layer per rank (run it under ``torch.distributed.run`` for
+several GPUs; one GPU otherwise), runs ``--calls`` layer calls (eager
+launches, or replays of a captured graph with ``--graph``), verifies the
+last one and prints, on rank 0, the per-call device time (max over ranks).  Meant to be wrapped by ``ncu -k ... -c ...``
 so that a capture sees only a handful of launches of the kernel of interest.
 ``--control-clocks`` adds, per scheduler trigger of the last call, the SM
 clock (cumulative cycles) at the end of each control phase (stage, reveal,
 enumerate, select, guard, apply, log) from the control log rows.
 ``--streamed`` times end-to-end calls instead (pinned host batch streamed in
 chunk by chunk, combined output copied back).
+``--roofline`` (with ``--trace``) adds, per rank, achieved fractions of the
+fused paths against their rooflines: the front end's dispatch (the bytes this
+rank put to its peers, from the device traffic counters, over the dispatch
+span, against the measured peer-copy bandwidth per direction), each grouped
+GEMM (its FLOPs over its span against the measured tensor peak) and GEMM-2
+with its fused return (the slower of its FLOPs at the tensor peak and its
+return bytes at the link bandwidth, over its span).
 """
 
 from __future__ import annotations
@@ -41,12 +49,26 @@ def main() -> None:
     ap.add_argument("--streamed", action="store_true", help="end-to-end calls with a streamed host batch")
     ap.add_argument("--gemm-swap-max", type=int, default=128,
                     help="swapped-operand tail tiles of at most this many rows (0: off)")
+    ap.add_argument("--roofline", action="store_true", help="achieved fractions of the fused paths (needs --trace)")
     args = ap.parse_args()
+    import os
+
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    rank = dist.get_rank() if world > 1 else 0
     cfg = preset(args.config)
     if args.tokens:
         n = cfg.chunks
         cfg = cfg.with_overrides(tokens_per_rank=args.tokens, chunk_sizes=(args.tokens // n,) * n)
-    layer = ProgressiveMoELayer(cfg, device=torch.device("cuda", 0), timeout_s=10.0, trace=bool(args.trace),
+    layer = ProgressiveMoELayer(cfg, device=dev, timeout_s=10.0, trace=bool(args.trace or args.roofline),
                                 frontend=args.frontend, gemm_swap_max=args.gemm_swap_max)
     try:
         if args.cta_clocks:
@@ -60,7 +82,13 @@ def main() -> None:
             host_in = torch.empty(layer.inputs.tokens.shape, dtype=layer.inputs.tokens.dtype, pin_memory=True)
             host_in.copy_(layer.inputs.tokens.cpu())
             host_out = torch.empty(layer.out.shape, dtype=layer.out.dtype, pin_memory=True)
-        for _ in range(args.calls):
+        counters_before = None
+        for i in range(args.calls):
+            if i == args.calls - 1:
+                torch.cuda.synchronize()
+                counters_before = layer.channel.peer_counters()
+                if world > 1:
+                    layer.device_barrier()
             cur = torch.cuda.current_stream()
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             if args.streamed:
@@ -73,8 +101,13 @@ def main() -> None:
                 e.record(layer.comm_stream)
             torch.cuda.synchronize()
             times.append(s.elapsed_time(e))
+        counters_after = layer.channel.peer_counters()
         rep = layer.verify()
-        rec = {"config": cfg.name, "arm": args.arm, "graph": args.graph, "ms": times,
+        if world > 1:
+            t = torch.tensor(times, dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            times = t.tolist()
+        rec = {"config": cfg.name, "world": world, "arm": args.arm, "graph": args.graph, "ms": times,
                "pass": rep["pass"], "launches_per_call": layer.launches_per_call}
         if args.control_clocks:
             from ..moe.layer import LOG_HEADER  # noqa: F401  (log row layout lives with the layer)
@@ -84,15 +117,87 @@ def main() -> None:
                                      for q in range(layer.cfg.n_desc)]
         if args.cta_clocks:
             rec["cta_clocks"] = _cta_clocks(layer)
-        if args.trace:
+        if args.trace or args.roofline:
             from .trace import summarize, write_chrome
 
             evs = layer.trace_events()
-            write_chrome(evs, args.trace, arm=args.arm)
+            roof = _roofline(layer, evs, counters_before, counters_after) if args.roofline else None
+            if world > 1:
+                every = [None] * world
+                dist.all_gather_object(every, (evs, roof))
+                evs = [e for part, _ in every for e in part]
+                roofs = [r for _, r in every]
+            else:
+                roofs = [roof]
+            if args.trace and rank == 0:
+                write_chrome(evs, args.trace, arm=args.arm)
             rec["trace"] = summarize(evs)
-        print(json.dumps(rec))
+            if args.roofline:
+                rec["roofline"] = roofs
+        if rank == 0:
+            print(json.dumps(rec))
     finally:
         layer.close()
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _peaks() -> dict:
+    """Measured denominators: HBM copy bandwidth and bf16 tensor throughput
+    (MEASURED_PEAKS.json beside the repository when present, else an earlier
+    measurement on B200) and the measured NVLink peer-copy bandwidth per
+    direction.  tf32 tensor throughput is taken as half of bf16's."""
+    import os
+    from pathlib import Path
+
+    peaks = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "nvlink_gbs": 770.0, "source": "fallback"}
+    path = Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        peaks.update(hbm_gbs=float(d.get("hbm_gbs", peaks["hbm_gbs"])),
+                     bf16_tflops=float(d.get("bf16_tflops", peaks["bf16_tflops"])), source="measured")
+    peaks["nvlink_gbs"] = float(os.environ.get("RAICCL_NVLINK_GBS", peaks["nvlink_gbs"]))
+    return peaks
+
+
+def _roofline(layer, evs, before, after) -> dict:
+    """Achieved fraction of each fused path of this rank's last call."""
+    cfg, W, r = layer.cfg, layer.world, layer.rank
+    pk = _peaks()
+    tensor_tflops = pk["bf16_tflops"] * (0.5 if cfg.dtype == "fp32" else 1.0)
+    delta = [{k: after[p][k] - before[p][k] for k in after[p]} for p in range(W)]
+    out_bytes = sum(delta[p]["bytes_transferred"] for p in range(W) if p != r)
+    ret_bytes = sum(delta[p]["return_bytes"] for p in range(W) if p != r)
+    # per kind: the sum of its launches' (or phases') spans; descriptors are
+    # dispatched one after another, so for the dispatch this is its busy time,
+    # not the time it waits for the scheduler between descriptors
+    us: dict[str, float] = {}
+    for e in evs:
+        us[e["kind"]] = us.get(e["kind"], 0.0) + (e["end_ns"] - e["start_ns"]) / 1e3
+    rows = int(layer.rows_out.sum().item())
+    f1 = 2.0 * rows * cfg.hidden * cfg.gemm1_n
+    f2 = 2.0 * rows * cfg.ffn_hidden * cfg.out_dim
+
+    def frac(target_us, span):
+        return round(target_us / span, 3) if span and span > 0 else None
+
+    res = {"rank": r, "peaks": pk, "rows": rows}
+    if "dispatch" in us:
+        tgt = out_bytes / (pk["nvlink_gbs"] * 1e3)
+        res["dispatch"] = {"nvlink_bytes": out_bytes, "span_us": round(us["dispatch"], 2),
+                           "achieved_gbs": round(out_bytes / (us["dispatch"] * 1e3), 1) if us["dispatch"] else None,
+                           "roofline_us": round(tgt, 2), "fraction": frac(tgt, us["dispatch"])}
+    if "gemm1" in us:
+        tgt = f1 / (tensor_tflops * 1e6)
+        res["gemm1"] = {"gflop": round(f1 / 1e9, 2), "span_us": round(us["gemm1"], 2),
+                        "tflops": round(f1 / (us["gemm1"] * 1e6), 1), "roofline_us": round(tgt, 2),
+                        "fraction": frac(tgt, us["gemm1"])}
+    if "gemm2_return" in us:
+        tgt = max(f2 / (tensor_tflops * 1e6), ret_bytes / (pk["nvlink_gbs"] * 1e3))
+        res["gemm2_return"] = {"gflop": round(f2 / 1e9, 2), "nvlink_bytes": ret_bytes,
+                               "span_us": round(us["gemm2_return"], 2), "roofline_us": round(tgt, 2),
+                               "fraction": frac(tgt, us["gemm2_return"])}
+    return res
 
 
 def _cta_clocks(layer) -> dict:

@@ -235,6 +235,9 @@ def verify_layer(layer, *, atol: float | None = None, rtol: float | None = None,
             dig = torch.empty(n, dtype=torch.int64, device=dev)
             layer._k.feature_digest(feat[base:base + n].contiguous(), dig)
             fwd["corruption"] += int((dig.cpu().numpy() != m[:, 7]).sum())
+    # ---- canary words after every array of the symmetric region
+    broken = layer.guards_intact()
+    rep["guards_broken"] = broken
     rep["forward"] = fwd
 
     # ---- return side: every (token, choice) of this rank came back exactly once
@@ -284,6 +287,8 @@ def verify_layer(layer, *, atol: float | None = None, rtol: float | None = None,
         bad.append(f"final_combine max_abs_err={rep['max_abs_err']:.3g}")
     if not rep["permits_ok"] or not rep["guard_gate_ok"]:
         bad.append("control permits")
+    if rep["guards_broken"]:
+        bad.append(f"guard bands overwritten at offsets {rep['guards_broken']}")
     if replay_control:
         c = rep["control"]
         for name in ("device_candidate_divergences", "device_action_divergences", "candidate_divergences",

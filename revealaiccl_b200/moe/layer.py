@@ -42,6 +42,8 @@ FWD_META = 9
 RET_META = 8
 LOG_HEADER = 16  # 8-word decision record + 8 phase-clock words
 TRACE_SLOTS = 256
+GUARD_CANARY = 0x5CA1AB1E0DDC0FFE  # fills the guard band after every array of the symmetric region
+PAIR_TICKET_RING = 32  # ticket slots per GEMM CTA pair (kPairTicketRing in csrc/include/types.h)
 
 
 @dataclass
@@ -55,7 +57,8 @@ class ProgressiveMoELayer:
                  world: int | None = None, rank: int | None = None, group=None,
                  timeout_s: float = 10.0, seed: int = 0, control_topology=None,
                  control_path: str = "auto", trace: bool = False, frontend: str = "persistent",
-                 gemm_pair: bool = True, pdl: bool = True, gemm_swap_max: int = 128) -> None:
+                 gemm_pair: bool = True, pdl: bool = True, gemm_swap_max: int = 128,
+                 progressive: bool = True, dispatch_ctas: int = 0) -> None:
         self.cfg = cfg
         if world is None:
             world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -143,11 +146,17 @@ class ProgressiveMoELayer:
             # CTA-pair GEMMs at BN = 256: a segment's last row tile of at most this
             # many rows runs with swapped operands (0 disables)
             "gemm_swap_max": int(gemm_swap_max),
+            # progressive expert side: GEMM-1 CTA pairs take 256-row tiles as
+            # their descriptors arrive, on the SMs of front-end workers that
+            # leave after routing (dispatch_ctas workers stay to dispatch)
+            "progressive": int(bool(progressive)),
+            "dispatch_ctas": int(dispatch_ctas),
         }
         self.layout = self._k.sym_layout(ints)
         self.channel = PeerChannel(self.layout["total"], dev, group=group)
         if self.channel.world != W:
             raise RuntimeError("process group world size differs from the layer's world size")
+        self._fill_guards()
 
         # ---- per-token precompute (untimed): digests and checksum bases
         self.chunk_offsets_dev = dev_t(np.asarray(cfg.chunk_offsets, dtype=np.int32))
@@ -209,6 +218,12 @@ class ProgressiveMoELayer:
             "ctl_log": torch.zeros(cfg.n_desc * self.log_stride, dtype=torch.int32, device=dev),
             # per-peer traffic counters, updated by the dispatch and expert-plan kernels
             "peer_counters": torch.zeros(W * PeerChannel.COUNTER_STRIDE, dtype=torch.int64, device=dev),
+            # progressive GEMM-1: tile list in arrival order (4 ints per tile), its
+            # published length, the per-call ticket counter and each CTA pair's ticket ring
+            "tile_list": torch.zeros(4 * self._max_tiles1(nseg), dtype=torch.int32, device=dev),
+            "tile_word": torch.zeros(1, dtype=torch.int64, device=dev),
+            "ticket_counter": torch.zeros(1, dtype=torch.int32, device=dev),
+            "pair_tickets": torch.zeros((ints["sms"] // 2) * PAIR_TICKET_RING, dtype=torch.int64, device=dev),
         }
         self.tensors = {kk: v for kk, v in self.tensors.items() if v is not None}
         self.channel.bind_counters(self.tensors["peer_counters"])
@@ -226,6 +241,14 @@ class ProgressiveMoELayer:
         self.launches_per_call = 0
         if W > 1:
             dist.barrier(group=group)
+
+    def _max_tiles1(self, nseg: int) -> int:
+        """Upper bound of GEMM-1's 256-row tiles: every row this rank can
+        receive (all ranks' tokens x top-k) plus one partial tile per
+        segment, times the column blocks."""
+        cfg = self.cfg
+        rows = self.world * cfg.tokens_per_rank * cfg.top_k
+        return (rows // 256 + nseg + 1) * max(1, cfg.gemm1_n // self.bn1)
 
     def _control_blob(self, flat, Ep: int, G: int, V: int, Tc: int, dev) -> torch.Tensor:
         """One device buffer holding the compiled plan, the scheduler state, the
@@ -329,12 +352,28 @@ class ProgressiveMoELayer:
         return host_out
 
     def clear_returns(self) -> None:
-        """Zero this rank's return region (so a lost return row cannot hide behind
-        a previous call's row); collective-free, call between layer calls."""
+        """Zero this rank's return rows and return identity rows (so a lost
+        return row cannot hide behind a previous call's row); collective-free,
+        call between layer calls.  The guard bands stay as they are."""
         torch.cuda.synchronize(self.device)
-        n = self.layout["ret_flag"] - self.layout["ret_out"]
-        self._region("ret_out", (n,), torch.uint8).zero_()
+        guards = self.layout["guards"]
+        for name, guard in (("ret_out", guards[6]), ("ret_meta", guards[7])):
+            self._region(name, (guard - self.layout[name],), torch.uint8).zero_()
         torch.cuda.synchronize(self.device)
+
+    def _fill_guards(self) -> None:
+        """Write the canary pattern into every guard band of this rank's region."""
+        n = int(self.layout["guard_bytes"]) // 8
+        for off in self.layout["guards"]:
+            self.channel.view(int(off), (n,), torch.int64).fill_(GUARD_CANARY)
+        torch.cuda.synchronize(self.device)
+
+    def guards_intact(self) -> list[int]:
+        """Offsets of this rank's guard bands whose canary changed (empty: all intact)."""
+        torch.cuda.synchronize(self.device)
+        n = int(self.layout["guard_bytes"]) // 8
+        return [int(off) for off in self.layout["guards"]
+                if not bool((self.channel.view(int(off), (n,), torch.int64) == GUARD_CANARY).all().item())]
 
     def wait(self) -> None:
         torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)

@@ -445,3 +445,42 @@ def test_peer_counters_count_one_call():
         assert layer.channel.counters["put_calls"] == 2 * cfg.n_desc
     finally:
         layer.close()
+
+
+@pytest.mark.parametrize("name,over", [
+    ("full_tf32", dict(tokens_per_rank=2048, chunk_sizes=(256,) * 8)),
+    ("skewed_bf16", dict(tokens_per_rank=2048, chunk_sizes=(128,) * 16)),
+    ("deepseek_v2_lite", dict(tokens_per_rank=1024, chunk_sizes=(64,) * 16)),
+])
+def test_progressive_gemm1_matches_and_starts_early(name, over):
+    """GEMM-1 CTA pairs that take 256-row tiles as descriptors arrive compute
+    exactly the tiles of the whole-batch plan: the layer's output is
+    bit-identical with progressive planning on and off, in both arms, eagerly
+    and replayed from a graph; and GEMM-1's first tile starts before the
+    front end has finished."""
+    from revealaiccl_b200.moe.config import preset
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    cfg = preset(name, **over)
+    outs = {}
+    for prog in (False, True):
+        layer = ProgressiveMoELayer(cfg, timeout_s=10.0, progressive=prog, trace=True)
+        try:
+            for arm in ("early", "delayed"):
+                layer.forward(arm)
+                rep = layer.verify()
+                assert rep["pass"], (prog, arm, rep["violations"])
+                outs[(prog, arm)] = layer.out.clone()
+            layer.forward("early")
+            evs = {e["kind"]: e for e in layer.trace_events()}
+            if prog:
+                assert evs["gemm1"]["start_ns"] < evs["frontend"]["end_ns"], evs
+            layer.capture("early")
+            layer.replay("early")
+            torch.cuda.synchronize()
+            assert layer.verify()["pass"]
+            outs[(prog, "graph")] = layer.out.clone()
+        finally:
+            layer.close()
+    for key in ("early", "delayed", "graph"):
+        assert torch.equal(outs[(False, key)], outs[(True, key)]), key
