@@ -132,6 +132,15 @@ def main() -> None:
             if args.trace and rank == 0:
                 write_chrome(evs, args.trace, arm=args.arm)
             rec["trace"] = summarize(evs)
+            if layer.runner.persistent_frontend():
+                from .trace_analysis import TraceError, analyze
+
+                try:  # fail closed: an inconsistent trace reports its error, never numbers
+                    rep = analyze(evs, partial_chunks=cfg.progressive_chunks, chunks=cfg.chunks, slack_ns=1024)
+                    rec["control_chain"] = {r: {k: v for k, v in x.items() if k != "descriptors"}
+                                            for r, x in rep["ranks"].items()}
+                except TraceError as exc:
+                    rec["control_chain"] = {"error": str(exc)}
             if args.roofline:
                 rec["roofline"] = roofs
         if rank == 0:

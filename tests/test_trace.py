@@ -53,3 +53,37 @@ def test_device_trace_ring_spans():
             assert trace.summarize(evs)["makespan_ms"] > 0
     finally:
         layer.close()
+
+
+def _ev(kind, arg, s, e, rank=0):
+    return {"kind": kind, "arg": arg, "start_ns": s, "end_ns": e, "rank": rank, "ctas": 1}
+
+
+def _call(shift=0, rank=0):
+    evs = []
+    for c in range(8):
+        evs.append(_ev("router", c, 1000 * c + shift, 1000 * c + 900 + shift, rank))
+    for q in range(7):
+        last = q if q < 6 else 7
+        r_end = 1000 * last + 900 + shift
+        evs.append(_ev("control", q, r_end + 100, r_end + 600, rank))
+        evs.append(_ev("dispatch", q, r_end + 700, r_end + 1500, rank))
+    return evs
+
+
+def test_trace_analysis_latencies_overlap_and_fail_closed():
+    from revealaiccl_b200.bench.trace_analysis import TraceError, analyze
+
+    rep = analyze(_call() + _call(rank=1), partial_chunks=6, chunks=8)
+    r0 = rep["ranks"][0]
+    assert r0["ready_to_release_us_p50"] == 0.6 and r0["ready_to_dispatch_us_p50"] == 0.7
+    assert r0["dispatch_us_p50"] == 0.8 and len(r0["descriptors"]) == 7
+    assert r0["early_start_share"] == 1.0 and 0.0 < r0["coexist_share"] < 1.0
+    bad = _call()
+    for e in bad:
+        if e["kind"] == "dispatch" and e["arg"] == 3:
+            e["start_ns"] -= 1000  # starts before its release
+    with pytest.raises(TraceError, match="before its release"):
+        analyze(bad, partial_chunks=6, chunks=8)
+    with pytest.raises(TraceError, match="missing"):
+        analyze([e for e in _call() if not (e["kind"] == "control" and e["arg"] == 2)], partial_chunks=6, chunks=8)
