@@ -363,7 +363,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=("product", "reference", "nccl"), default="product")
     # expert side: GEMM-1 takes 256-row tiles as descriptors arrive (1) or after the
     # whole batch (0); front-end workers that keep dispatching (0: all of them)
-    ap.add_argument("--progressive", type=int, default=1, choices=(0, 1))
+    ap.add_argument("--progressive", type=int, default=0, choices=(0, 1))
     ap.add_argument("--dispatch-ctas", type=int, default=0)
     args = ap.parse_args()
     if args.warmup < 3:

@@ -77,28 +77,37 @@ struct NoHooks {
 // Called by one full warp.  csm holds the staged control blob; s_dst
 // (kCtlStageMax >= chunks x ctl_per_chunk), s_coff (kCtlMaxChunks + 1) and
 // s_egmask (kWarpMaxE) are shared scratch.  reset: start a layer call (fresh scheduler state).
+// s_vmc (kCtlStageMax, optional): per-ordinal template masks kept across the
+// triggers of this call.  An ordinal's mask depends only on its own state
+// (ready, residual, destination, remaining hops, holders), which changes only
+// when it is revealed or one of its actions is applied, so each trigger
+// recomputes just those ordinals; without it every trigger recomputes all.
 // Rare paths, kept out of line: the warp executes its hot path once per
 // trigger, so every instruction line of it is fetched once per trigger, and
 // inlined fallbacks would spread that path over more lines.
 static __device__ __noinline__ void cold_status(DeviceStatus* st, int code, int id, long long index, long long bound) {
   record_status(st, code, id, index, bound);
 }
-static __device__ __noinline__ int cold_select(const sched::PlanView& plan, sched::StateView& st, const sched::Cand* cand,
+// The views are taken by value: a reference would make the caller's views
+// address-taken, so they would live in local memory for the whole trigger loop
+// and every field use on the hot path would be a local load.
+static __device__ __noinline__ int cold_select(sched::PlanView plan, sched::StateView st, const sched::Cand* cand,
                                         int n, int revealed, int* keep) {
   return sched::select(plan, st, cand, n, revealed, keep, true);
 }
-static __device__ __noinline__ int cold_check(const sched::PlanView& plan, sched::StateView& st, const int64_t* actions,
+static __device__ __noinline__ int cold_check(sched::PlanView plan, sched::StateView st, const int64_t* actions,
                                        int kept, int revealed) {
   return sched::check(plan, st, actions, kept, revealed, true, true);
 }
-static __device__ __noinline__ void cold_apply(const sched::PlanView& plan, sched::StateView& st, const int64_t* actions,
+static __device__ __noinline__ void cold_apply(sched::PlanView plan, sched::StateView st, const int64_t* actions,
                                         int kept) {
   sched::apply(plan, st, actions, kept, true);
 }
 
 template <class Hooks>
 __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims, uint8_t* csm, int* s_dst,
-                                 int* s_coff, uint32_t* s_egmask, int q0, int q1, bool reset, Hooks& hooks) {
+                                 int* s_coff, uint32_t* s_egmask, int q0, int q1, bool reset, Hooks& hooks,
+                                 uint32_t* s_vmc = nullptr) {
   const unsigned FULL = 0xffffffffu;
   const int lane = threadIdx.x & 31;
   const ControlLayout Lt = control_layout(dims);
@@ -149,8 +158,28 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   int64_t* actions = reinterpret_cast<int64_t*>(at(kCtlActions));
   // per-ordinal template bitmask / first candidate index, in the action scratch
   // (free until the selection has been turned into actions)
-  uint32_t* vmask = reinterpret_cast<uint32_t*>(actions);
+  uint32_t* vmask = s_vmc ? s_vmc : reinterpret_cast<uint32_t*>(actions);
   int* cbase = reinterpret_cast<int*>(actions) + T;
+  // template bitmask of ordinal o: templates j of its destination that take it
+  // one hop closer, from a node holding it to one that does not
+  auto ordinal_vm = [&](int o) -> uint32_t {
+    uint32_t vm = 0;
+    if (st.ready[o] && st.residual[o]) {
+      const int d = st.destinations[o];
+      const int before = st.remaining_hops[o];
+      if (before > 0 && before < sched::kInf) {
+        const uint8_t* h = st.holders + (long long)o * V;
+        const int k0 = tptr[d], nt = tptr[d + 1] - k0;
+        #pragma unroll 1
+        for (int j = 0; j < nt; ++j) {
+          const int k = k0 + j;
+          if (h[tsrc[k]] && !h[ttgt[k]] && ttd[k] == before - 1) vm |= 1u << j;
+        }
+      }
+    }
+    return vm;
+  };
+  bool vm_valid = false;  // s_vmc holds the mask of every revealed ordinal
   __syncwarp();
   if (reset) {
     #pragma unroll 1
@@ -276,6 +305,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
       for (int v = 0; v < V; ++v)
         if (h[v] && dist[(long long)v * V + d] < best) best = dist[(long long)v * V + d];
       st.remaining_hops[o] = best;
+      if (vm_valid) s_vmc[o] = ordinal_vm((int)o);
     }
     revealed_count += cn;
     pending &= ~bit;
@@ -287,24 +317,13 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   // ---- enumerate: per-ordinal template bitmask and candidate prefix
   #pragma unroll 1
   for (int t = lane; t < T; t += 32) st.scratch_selected[t] = 0;
+  const bool cached = vm_valid;
   int carry = 0;
   #pragma unroll 1
   for (int o0 = 0; o0 < revealed; o0 += 32) {
     const int o = o0 + lane;
     uint32_t vm = 0;
-    if (o < revealed && st.ready[o] && st.residual[o]) {
-      const int d = st.destinations[o];
-      const int before = st.remaining_hops[o];
-      if (before > 0 && before < sched::kInf) {
-        const uint8_t* h = st.holders + (long long)o * V;
-        const int k0 = tptr[d], nt = tptr[d + 1] - k0;
-        #pragma unroll 1
-        for (int j = 0; j < nt; ++j) {
-          const int k = k0 + j;
-          if (h[tsrc[k]] && !h[ttgt[k]] && ttd[k] == before - 1) vm |= 1u << j;
-        }
-      }
-    }
+    if (o < revealed) vm = cached ? s_vmc[o] : ordinal_vm(o);
     const int cnt = __popc(vm);
     int incl = cnt;
     for (int s = 1; s < 32; s <<= 1) {
@@ -313,7 +332,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     }
     const int base = carry + incl - cnt;
     if (o < revealed) {
-      vmask[o] = vm;
+      if (!cached) vmask[o] = vm;
       cbase[o] = base;
       if (vm) {
         const int d = st.destinations[o];
@@ -327,6 +346,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     }
     carry += __shfl_sync(FULL, incl, 31);
   }
+  vm_valid = s_vmc != nullptr;
   int n = carry;
   if (n > p.max_cands) {
     if (lane == 0) cold_status(p.status, kBoundsViolation, 61, n, p.max_cands);
@@ -337,43 +357,59 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   if (lane == 0) clk[2] = (int)(clock64() - clk0);
 
   // ---- select: greedy over candidates in (ordinal, template) order
+  // An edge is usable while it has link credit and none of its groups is
+  // exhausted; a candidate is viable iff its edge is usable.  Each lane holds
+  // the edge set of its ordinal's candidates, so one ballot finds the next
+  // ordinal with a viable candidate and ordinals without one cost nothing;
+  // once no edge is usable nothing further can be taken.
   int kept = 0;
   if (!dup_groups) {
     long long cred_lo = lane < E ? s_cap[lane] : 0, cred_hi = lane + 32 < E ? s_cap[lane + 32] : 0;
     long long gcred = lane < G ? s_glim[lane] : 0;
-    unsigned long long lack_link = (unsigned long long)__ballot_sync(FULL, lane < E && cred_lo < 1) |
-                                   ((unsigned long long)__ballot_sync(FULL, lane + 32 < E && cred_hi < 1) << 32);
+    const uint32_t eg_lo = lane < E ? s_egmask[lane] : 0u, eg_hi = lane + 32 < E ? s_egmask[lane + 32] : 0u;
     uint32_t lack_grp = __ballot_sync(FULL, lane < G && gcred < 1);
+    auto usable_edges = [&]() -> unsigned long long {
+      const bool ulo = lane < E && cred_lo >= 1 && !(eg_lo & lack_grp);
+      const bool uhi = lane + 32 < E && cred_hi >= 1 && !(eg_hi & lack_grp);
+      return (unsigned long long)__ballot_sync(FULL, ulo) | ((unsigned long long)__ballot_sync(FULL, uhi) << 32);
+    };
+    unsigned long long usable = usable_edges();
     #pragma unroll 1
-    for (int o0 = 0; o0 < revealed; o0 += 32) {
+    for (int o0 = 0; o0 < revealed && usable != 0ull; o0 += 32) {
       const int my_o = o0 + lane;
       const uint32_t my_vm = my_o < revealed ? vmask[my_o] : 0u;
       const int my_base = my_o < revealed ? cbase[my_o] : 0;
       const int my_k0 = (my_o < revealed && my_vm) ? tptr[st.destinations[my_o]] : 0;
-      uint32_t todo = __ballot_sync(FULL, my_vm != 0 && my_base < n);
+      unsigned long long my_edges = 0;  // edges of this ordinal's candidates inside the bound n
+      {
+        int i = my_base;
+        #pragma unroll 1
+        for (uint32_t m = my_vm; m && i < n; m &= m - 1, ++i) my_edges |= 1ull << tedge[my_k0 + __ffs(m) - 1];
+      }
+      uint32_t todo = __ballot_sync(FULL, (my_edges & usable) != 0ull);
       #pragma unroll 1
       while (todo) {
         const int src_lane = __ffs(todo) - 1;
-        todo &= todo - 1;
         const uint32_t vm = __shfl_sync(FULL, my_vm, src_lane);
         const int b = __shfl_sync(FULL, my_base, src_lane);
         const int k0 = __shfl_sync(FULL, my_k0, src_lane);
         const int ci = b + __popc(vm & lanemask_lt());
         const bool valid = ((vm >> lane) & 1u) && ci < n;
         const int e = valid ? tedge[k0 + lane] : 0;
-        const bool viable = valid && !((lack_link >> e) & 1ull) && !(s_egmask[e] & lack_grp);
-        const unsigned vb = __ballot_sync(FULL, viable);
-        if (!vb) continue;
+        const unsigned vb = __ballot_sync(FULL, valid && ((usable >> e) & 1ull));
+        const uint32_t later = ~((2u << src_lane) - 1u);  // lanes after src_lane
+        if (!vb) { todo &= later; continue; }
         const int jl = __ffs(vb) - 1;
         const int es = __shfl_sync(FULL, e, jl);
         const int cs = __shfl_sync(FULL, ci, jl);
         if (lane == 0) { keep[kept] = cs; st.scratch_selected[o0 + src_lane] = 1; }
         ++kept;
         if (lane == (es & 31)) { if (es < 32) cred_lo -= 1; else cred_hi -= 1; }
-        if (lane < G && ((s_egmask[es] >> lane) & 1u)) gcred -= 1;
-        lack_link = (unsigned long long)__ballot_sync(FULL, lane < E && cred_lo < 1) |
-                    ((unsigned long long)__ballot_sync(FULL, lane + 32 < E && cred_hi < 1) << 32);
+        const uint32_t egs = __shfl_sync(FULL, es < 32 ? eg_lo : eg_hi, es & 31);
+        if (lane < G && ((egs >> lane) & 1u)) gcred -= 1;
         lack_grp = __ballot_sync(FULL, lane < G && gcred < 1);
+        usable = usable_edges();
+        todo = __ballot_sync(FULL, (my_edges & usable) != 0ull) & later;
       }
     }
     if (lane < E) st.link_credits[lane] = cred_lo;
@@ -459,7 +495,27 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
   __syncwarp();
   if (lane == 0) clk[4] = (int)(clock64() - clk0);
 
-  // ---- apply (accepted actions), packing gate, permit
+  // ---- packing gate and permit, then the release: the descriptor's dispatch
+  // does not depend on the state update below, so it starts while it runs
+  if (accepted && kept > 0) version += 1;
+  #pragma unroll 1
+  for (int c = c_lo; c <= c_hi; ++c) {
+    const long long bit = 1LL << c;
+    if (!(completed & bit)) { future += 1; gate_ok = false; }
+    else if (!(revealed_bits & bit)) { unrevealed += 1; gate_ok = false; }
+    else if (dispatched & bit) { stale += 1; gate_ok = false; }
+  }
+  if (gate_ok)
+    #pragma unroll 1
+    for (int c = c_lo; c <= c_hi; ++c) dispatched |= 1LL << c;
+  if (lane == 0) {
+    p.permit[desc] = (accepted && gate_ok) ? epoch_v : 0ULL;
+    if (!(accepted && gate_ok)) cold_status(p.status, kTimeoutPermit, 62, desc, code);
+  }
+  __syncwarp();
+  hooks.after(desc, accepted && gate_ok);
+
+  // ---- apply (accepted actions)
   if (accepted && kept > 0 && fast_actions) {
     // credits after the slot = reset credits minus the committed usage
     if (lane < E) st.link_credits[lane] = s_cap[lane] - st.scratch_edge_load[lane];
@@ -488,6 +544,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
       for (int v = 0; v < V; ++v)
         if (h[v] && dist[(long long)v * V + d] < best) best = dist[(long long)v * V + d];
       st.remaining_hops[o] = best;
+      if (vm_valid) s_vmc[o] = ordinal_vm(o);  // the actions of one slot have distinct ordinals
     }
   } else {
     #pragma unroll 1
@@ -495,26 +552,16 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     #pragma unroll 1
     for (int g = lane; g < G; g += 32) st.group_credits[g] = s_glim[g];
     __syncwarp();
-    if (accepted && kept > 0 && lane == 0) cold_apply(plan, st, actions, kept);
+    if (accepted && kept > 0) {
+      if (lane == 0) cold_apply(plan, st, actions, kept);
+      vm_valid = false;  // recompute every mask next trigger
+    }
   }
   #pragma unroll 1
   for (int t = lane; t < T; t += 32) st.scratch_selected[t] = 0;
-  if (accepted && kept > 0) version += 1;
-  #pragma unroll 1
-  for (int c = c_lo; c <= c_hi; ++c) {
-    const long long bit = 1LL << c;
-    if (!(completed & bit)) { future += 1; gate_ok = false; }
-    else if (!(revealed_bits & bit)) { unrevealed += 1; gate_ok = false; }
-    else if (dispatched & bit) { stale += 1; gate_ok = false; }
-  }
-  if (gate_ok)
-    #pragma unroll 1
-    for (int c = c_lo; c <= c_hi; ++c) dispatched |= 1LL << c;
   __syncwarp();
   int* L = p.log + (long long)desc * p.log_stride;
   if (lane == 0) {
-    p.permit[desc] = (accepted && gate_ok) ? epoch_v : 0ULL;
-    if (!(accepted && gate_ok)) cold_status(p.status, kTimeoutPermit, 62, desc, code);
     S[kCompleted] = completed; S[kRevealedBits] = revealed_bits; S[kPending] = pending;
     S[kDispatched] = dispatched; S[kStaged] = staged; S[kRevealedCount] = revealed_count;
     S[kVersion] = version; S[kFuture] = future; S[kUnrevealed] = unrevealed; S[kStale] = stale;
@@ -542,7 +589,6 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     L[15] = 1;  // warp-path marker
   }
   __syncwarp();
-  hooks.after(desc, accepted && gate_ok);
   }  // trigger loop
 }
 

@@ -52,47 +52,51 @@ __device__ __forceinline__ PairTile pair_tile(const GroupedGemmParams& p, int t,
 }
 
 // ---------------------------------------------------------------------------
-// Progressive tile source (GroupedGemmParams::progressive).  Iteration k of
-// pair `pair`: the leader's producer draws a ticket T from the per-call
-// counter and posts it in the pair's ring slot k % kPairTicketRing, tagged
-// with the call epoch and k; every other role of both CTAs reads it there.
-// Then each role waits (bounded) until the planner's published tile count
-// passes T, and reads tile T from the list; a final count at or below T
-// means the pair has no more tiles.  Returns 1 (tile in pt), 0 (no more
-// tiles) or -1 (a wait ran out; status recorded).  One thread per call.
+// Progressive tile source (GroupedGemmParams::progressive).
+//
+// The pair leader's producer owns the schedule.  It draws ticket T for its
+// next tile from the per-call counter one tile ahead (the atomic's latency
+// hides behind the current tile's loads), waits (bounded) until the
+// planner's published tile count passes T, reads the tile from the list and
+// posts it, fully resolved, in the pair's ring slot for that iteration
+// (two 64-bit words: the packed tile, then a release store of the epoch /
+// iteration tag with T; T = kNoTicket ends the pair's loop).  The partner's
+// producer and both CTAs' epilogue warps read the ring (one acquire load
+// when the slot is already posted); the leader's MMA warp reads the tile
+// from a shared-memory slot the producer writes before the tile's first
+// stage barrier, so its scheduling costs no global round trip.
 // ---------------------------------------------------------------------------
+constexpr unsigned int kNoTicket = 0xfffffu;
+constexpr int kTileSlots = 16;  // shared-memory tile slots of the leader (>= stages + 1)
+
 __device__ __forceinline__ unsigned long long ld_acquire_gpu_u64_gg(const unsigned long long* a) {
   unsigned long long v;
   asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
   return v;
 }
 
-__device__ __forceinline__ int progressive_next(const GroupedGemmParams& p, int pair, int k, bool draw,
-                                                unsigned long long epoch, PairTile& pt, int kernel_id) {
-  unsigned long long* slot = p.pair_tickets + (long long)pair * kPairTicketRing + (k & (kPairTicketRing - 1));
-  const unsigned long long tag = ((epoch & 0xffffffULL) << 40) | ((unsigned long long)(k & 0xfffff) << 20);
-  unsigned int T = 0;
-  if (draw) {
-    T = atomicAdd(p.ticket_counter, 1u) & 0xfffffu;
-    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(slot), "l"(tag | T) : "memory");
-  } else {
-    const uint64_t start = globaltimer_ns();
-    for (uint32_t polls = 1;; ++polls) {
-      const unsigned long long v = ld_acquire_gpu_u64_gg(slot);
-      if ((v & ~0xfffffULL) == tag) {
-        T = (unsigned int)(v & 0xfffffULL);
-        break;
-      }
-      __nanosleep(32);
-      if ((polls & 63u) == 0) {
-        if (globaltimer_ns() - start > p.timeout_ns) {
-          record_status(p.status, kTimeoutPipeline, kernel_id, k, pair);
-          return -1;
-        }
-        if (status_failed(p.status)) return -1;
-      }
-    }
-  }
+__device__ __forceinline__ unsigned long long ring_tag(unsigned long long epoch, int k) {
+  return ((epoch & 0xffffffULL) << 40) | ((unsigned long long)(k & 0xfffff) << 20);
+}
+
+__device__ __forceinline__ unsigned long long pack_tile(const PairTile& t) {
+  return (unsigned long long)(t.s & 0xffff) | ((unsigned long long)(t.mb & 0xffff) << 16) |
+         ((unsigned long long)(t.nb & 0xffff) << 32) | ((unsigned long long)(t.nsw & 0xffff) << 48);
+}
+
+__device__ __forceinline__ PairTile unpack_tile(unsigned long long v) {
+  PairTile t;
+  t.s = (int)(v & 0xffff);
+  t.mb = (int)((v >> 16) & 0xffff);
+  t.nb = (int)((v >> 32) & 0xffff);
+  t.nsw = (int)((v >> 48) & 0xffff);
+  return t;
+}
+
+// Leader producer: the tile of ticket T once published.  1: tile in pt;
+// 0: the planner finished without it; -1: the wait ran out (status recorded).
+__device__ __forceinline__ int resolve_ticket(const GroupedGemmParams& p, unsigned int T, unsigned long long epoch,
+                                              PairTile& pt, int kernel_id, int pair) {
   const unsigned long long want = (epoch & 0xffffffffULL) << 32;
   const uint64_t start = globaltimer_ns();
   for (uint32_t polls = 1;; ++polls) {
@@ -111,11 +115,42 @@ __device__ __forceinline__ int progressive_next(const GroupedGemmParams& p, int 
     }
   }
   const int4 e = reinterpret_cast<const int4*>(p.tile_list)[T];
-  pt.s = e.x;
-  pt.mb = e.y;
-  pt.nb = e.z;
-  pt.nsw = e.w;
+  pt.s = e.x; pt.mb = e.y; pt.nb = e.z; pt.nsw = e.w;
   return 1;
+}
+
+__device__ __forceinline__ void post_ticket(const GroupedGemmParams& p, int pair, int k, unsigned long long epoch,
+                                            bool has_tile, const PairTile& pt) {
+  unsigned long long* slot = p.pair_tickets + 2LL * ((long long)pair * kPairTicketRing + (k & (kPairTicketRing - 1)));
+  if (has_tile) slot[1] = pack_tile(pt);
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(slot),
+               "l"(ring_tag(epoch, k) | (has_tile ? 0ULL : (unsigned long long)kNoTicket)) : "memory");
+}
+
+// Partner producer / epilogue: tile k of the pair from the ring.  1: tile in
+// pt; 0: no more tiles; -1: the wait ran out (status recorded).
+__device__ __forceinline__ int read_ticket(const GroupedGemmParams& p, int pair, int k, unsigned long long epoch,
+                                           PairTile& pt, int kernel_id) {
+  const unsigned long long* slot =
+      p.pair_tickets + 2LL * ((long long)pair * kPairTicketRing + (k & (kPairTicketRing - 1)));
+  const unsigned long long tag = ring_tag(epoch, k);
+  const uint64_t start = globaltimer_ns();
+  for (uint32_t polls = 1;; ++polls) {
+    const unsigned long long v = ld_acquire_gpu_u64_gg(slot);
+    if ((v & ~0xfffffULL) == tag) {
+      if ((unsigned int)(v & 0xfffffULL) == kNoTicket) return 0;
+      pt = unpack_tile(slot[1]);
+      return 1;
+    }
+    __nanosleep(32);
+    if ((polls & 63u) == 0) {
+      if (globaltimer_ns() - start > p.timeout_ns) {
+        record_status(p.status, kTimeoutPipeline, kernel_id, k, pair);
+        return -1;
+      }
+      if (status_failed(p.status)) return -1;
+    }
+  }
 }
 
 __device__ __forceinline__ void store1(float* dst, float v) { *dst = v; }
@@ -177,7 +212,7 @@ struct PairCfg {
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int TMEM_COLS = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128 : (2 * BN) <= 256 ? 256 : 512;
   static constexpr uint32_t IDESC = umma_idesc(TF32 ? 2u : 1u, 256, BN);
-  static constexpr int SMEM_TOTAL = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + 256;
+  static constexpr int SMEM_TOTAL = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + 256 + 256;
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair tile: BN/2 rows of B per CTA, N <= 256");
   static_assert(STAGES >= 2, "pipeline needs two stages");
 };
@@ -199,6 +234,8 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
   uint64_t* tempty_bar = tfull_bar + 2;        // leader: accumulator drained by both CTAs
   uint64_t* drain_bar = tempty_bar + 2;
   uint32_t* tmem_slot = (uint32_t*)(drain_bar + 1);
+  // progressive: the leader producer's tile slots for its MMA warp (16 bytes each, 256 bytes in all)
+  int4* tile_slot = (int4*)(epi_base + C::EPI_BYTES + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -222,7 +259,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
   // Prologue: shared memory, TMEM and the partner only; the tile table,
   // segments and A rows come from the previous launch.  A progressive GEMM
   // does not wait for the planner to finish: it takes tiles as they are
-  // published (progressive_next).
+  // published (the ticket protocol above).
   const bool progressive = p.progressive != 0;
   if (!progressive) griddep_wait();
   griddep_launch_dependents();
@@ -241,10 +278,32 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
     // ------------------------------------------------------------ producer (both CTAs)
     if (elect_one_sync()) {
       int stage = 0; uint32_t phase = 0;
+      // progressive leader: the current tile (resolved) and the ticket drawn for the next one
+      PairTile cur{0, 0, 0, 0};
+      int have = 0;
+      if (progressive && rank == 0) {
+        const unsigned int T0 = atomicAdd(p.ticket_counter, 1u) & 0xfffffu;
+        have = resolve_ticket(p, T0, epoch, cur, kKernelId, pair);
+        post_ticket(p, pair, 0, epoch, have > 0, cur);
+      }
       for (int t = pair, k = 0;; t += npairs, ++k) {
         PairTile pt;
+        unsigned int next_ticket = 0;
         if (progressive) {
-          if (progressive_next(p, pair, k, rank == 0, epoch, pt, kKernelId) <= 0) break;
+          if (rank == 0) {
+            if (have <= 0) {
+              // no more tiles: complete the next stage's phase without data so the
+              // MMA warp, which reads the tile slot behind that barrier, learns it
+              tile_slot[k & (kTileSlots - 1)] = make_int4(0, 0, 0, -1);
+              if (mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, p.status, kKernelId, lim))
+                mbar_arrive(&full_bar[stage]);
+              break;
+            }
+            pt = cur;
+            next_ticket = atomicAdd(p.ticket_counter, 1u) & 0xfffffu;  // drawn a tile ahead
+          } else if (read_ticket(p, pair, k, epoch, pt, kKernelId) <= 0) {
+            break;
+          }
           asm volatile("fence.proxy.async.global;" ::: "memory");  // rows landed by generic stores, read by TMA
         } else {
           if (t >= total_tiles) break;
@@ -260,8 +319,11 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
           uint8_t* sa = stage_base + stage * C::STAGE_BYTES;
           // a swapped tile stages only its nsw / 2 token rows per CTA (8-row boxes,
           // each one 1024-byte swizzle atom)
-          if (rank == 0)
+          if (rank == 0) {
+            // the MMA warp reads the tile behind the first stage's barrier (its arrive releases the slot)
+            if (progressive && kb == 0) tile_slot[k & (kTileSlots - 1)] = make_int4(pt.s, pt.mb, pt.nb, pt.nsw);
             mbar_arrive_expect_tx(&full_bar[stage], pt.nsw ? 2 * C::B_BYTES + pt.nsw * 128 : 2 * C::STAGE_BYTES);
+          }
           const uint32_t leader_full = mapa_shared(smem_u32(&full_bar[stage]), 0);
           if (pt.nsw) {
             for (int j = 0; j < pt.nsw / 16; ++j)
@@ -271,6 +333,11 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
           }
           tma_load_2d_pair(sa + C::A_BYTES, &tmap_b, leader_full, kb * C::BK, brow);
           if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (progressive && rank == 0) {
+          // resolve the ticket drawn above while this tile's loads are in flight
+          have = ok ? resolve_ticket(p, next_ticket, epoch, cur, kKernelId, pair) : -1;
+          post_ticket(p, pair, k + 1, epoch, have > 0, cur);
         }
         if (!ok) break;
       }
@@ -282,9 +349,11 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
       for (int t = pair;; t += npairs, ++iter) {
         int nsw = 0;
         if (progressive) {
-          PairTile pt;
-          if (progressive_next(p, pair, iter, false, epoch, pt, kKernelId) <= 0) break;
-          nsw = pt.nsw;
+          // the tile's first stage (or an empty phase at the end) carries its slot
+          if (!mbar_wait_bounded(&full_bar[stage], phase, p.status, kKernelId, lim)) break;
+          const int4 ts = tile_slot[iter & (kTileSlots - 1)];
+          if (ts.w < 0) break;
+          nsw = ts.w;
         } else {
           if (t >= total_tiles) break;
           nsw = t < total_full ? 0 : pair_tile(p, t, total_full, nblocks).nsw;
@@ -337,7 +406,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __gri
       PairTile pt;
       if (progressive) {
         int r = 0;
-        if (lane == 0) r = progressive_next(p, pair, iter, false, epoch, pt, kKernelId);
+        if (lane == 0) r = read_ticket(p, pair, iter, epoch, pt, kKernelId);
         r = __shfl_sync(0xffffffffu, r, 0);
         if (r <= 0) break;
         pt.s = __shfl_sync(0xffffffffu, pt.s, 0);

@@ -85,7 +85,7 @@ struct GroupedGemmParams {
   const int* tile_list;                 // [max] 4 ints per tile: segment, row tile, column block, nsw
   const unsigned long long* tile_word;
   unsigned int* ticket_counter;
-  unsigned long long* pair_tickets;     // [pairs][kPairTicketRing]
+  unsigned long long* pair_tickets;     // [pairs][kPairTicketRing][2]: tag | ticket, packed tile
   const unsigned long long* epoch;      // this call's sequence number
 };
 

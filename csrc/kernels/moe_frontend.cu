@@ -130,10 +130,12 @@ struct FrontHooks {
       const unsigned long long deadline = globaltimer_ns() + f->timeout_ns;
       #pragma unroll 1
       for (int c = chunks_ready; c < need && ok; ++c) {
+        int got;
         #pragma unroll 1
-        while (ld_acquire_gpu_s32(&f->chunk_done[c]) < workers) {
+        while ((got = ld_acquire_gpu_s32(&f->chunk_done[c])) < workers) {
           if (globaltimer_ns() > deadline) {
-            record_status(f->dp.status, kTimeoutChunkFlag, kFrontKernelId, c, workers);
+            // index: the chunk; bound: how many of the workers had finished it
+            record_status(f->dp.status, kTimeoutChunkFlag, kFrontKernelId, c, got);
             ok = 0;
             break;
           }
@@ -340,6 +342,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     __shared__ int s_dst[ctl::kCtlStageMax];
     __shared__ int s_ccoff[ctl::kCtlMaxChunks + 1];
     __shared__ uint32_t s_egmask[ctl::kWarpMaxE];
+    __shared__ uint32_t s_vmc[ctl::kCtlStageMax];
     const ControlDims dims{f.cp.plan.E, f.cp.plan.G, f.cp.plan.V, f.cp.st.max_tokens, f.cp.n_group_members,
                            f.cp.n_edge_group_members, f.cp.n_tmpl, f.cp.max_cands, f.cp.chunks};
     const ControlLayout Lt = control_layout(dims);
@@ -350,7 +353,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       int* s_ccount = reinterpret_cast<int*>(fsm + ((Lt.total + 15) & ~15LL));
       FrontHooks hooks{&f, W, f.cp.partial_chunks, C, E, epoch, hist, s_dst, s_ccoff, s_ccount,
                        f.cp.ctl_per_chunk, 0};
-      ctl::control_warp_run(f.cp, dims, fsm, s_dst, s_ccoff, s_egmask, 0, n_desc, true, hooks);
+      ctl::control_warp_run(f.cp, dims, fsm, s_dst, s_ccoff, s_egmask, 0, n_desc, true, hooks, s_vmc);
       __syncwarp();
       for (int e = threadIdx.x; e < E; e += 32) f.dp.sent_base[e] = hist[e];
     }

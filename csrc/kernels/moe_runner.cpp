@@ -513,8 +513,8 @@ class MoELayerRunner {
       g1.ticket_counter = ptr<unsigned int>(t, "ticket_counter");
       g1.pair_tickets = ptr<unsigned long long>(t, "pair_tickets");
       g1.epoch = epoch;
-      if (t["pair_tickets"].cast<torch::Tensor>().numel() < (int64_t)(grid_sms_ / 2) * raiccl::kPairTicketRing)
-        throw std::invalid_argument("pair_tickets holds fewer than (sms / 2) * kPairTicketRing words");
+      if (t["pair_tickets"].cast<torch::Tensor>().numel() < (int64_t)(grid_sms_ / 2) * raiccl::kPairTicketRing * 2)
+        throw std::invalid_argument("pair_tickets holds fewer than (sms / 2) * kPairTicketRing * 2 words");
     }
     raiccl::launch_grouped_gemm(!feat_bf16_, feat_bf16_, act1_, bn1_, ta1_, tb1_, g1, grid_sms_, comm_, &ta1n_);
     ++launches;

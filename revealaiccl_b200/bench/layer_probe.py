@@ -50,6 +50,9 @@ def main() -> None:
     ap.add_argument("--gemm-swap-max", type=int, default=128,
                     help="swapped-operand tail tiles of at most this many rows (0: off)")
     ap.add_argument("--roofline", action="store_true", help="achieved fractions of the fused paths (needs --trace)")
+    ap.add_argument("--progressive", type=int, default=0, choices=(0, 1),
+                    help="GEMM-1 takes tiles as descriptors arrive (1) or after the whole batch (0)")
+    ap.add_argument("--dispatch-ctas", type=int, default=0, help="front-end workers that dispatch (0: all)")
     args = ap.parse_args()
     import os
 
@@ -69,7 +72,8 @@ def main() -> None:
         n = cfg.chunks
         cfg = cfg.with_overrides(tokens_per_rank=args.tokens, chunk_sizes=(args.tokens // n,) * n)
     layer = ProgressiveMoELayer(cfg, device=dev, timeout_s=10.0, trace=bool(args.trace or args.roofline),
-                                frontend=args.frontend, gemm_swap_max=args.gemm_swap_max)
+                                frontend=args.frontend, gemm_swap_max=args.gemm_swap_max,
+                                progressive=bool(args.progressive), dispatch_ctas=args.dispatch_ctas)
     try:
         if args.cta_clocks:
             sms = torch.cuda.get_device_properties(layer.device).multi_processor_count

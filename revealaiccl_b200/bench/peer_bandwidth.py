@@ -30,6 +30,14 @@ def _size(text: str) -> int:
     return int(float(t[:-1]) * mult[t[-1]]) if t[-1] in mult else int(t)
 
 
+def _pattern(rank: int, nbytes: int, dev):
+    """The payload rank ``rank`` puts: int32 words (index * 2654435761 + rank) mod 2^31."""
+    import torch
+
+    i = torch.arange(nbytes // 4, dtype=torch.int64, device=dev)
+    return ((i * 2654435761 + rank) % (1 << 31)).to(torch.int32)
+
+
 def main(argv=None) -> None:
     import torch
     import torch.distributed as dist
@@ -64,7 +72,7 @@ def main(argv=None) -> None:
     rows = []
     try:
         for size in sizes:
-            src = torch.randn(size // 4, device=dev)
+            src = _pattern(rank, size, dev)
             times = []
             for it in range(args.warmup + args.iters):
                 torch.cuda.synchronize(dev)
@@ -99,7 +107,12 @@ def main(argv=None) -> None:
                 algbw = world * size / (ms * 1e6)
                 row["busbw_gbs"] = round(algbw * (world - 1) / world, 1)
             rows.append(row)
-        ok = bool((ops.slot(peers[0], 64).view(torch.float32)[:16].cpu() == src[:16].cpu()).all())
+        # every received slot holds its sender's pattern of the last size
+        ok = all(bool(torch.equal(ops.slot(p, size).view(torch.int32), _pattern(p, size, dev))) for p in peers)
+        if world > 1:
+            flag = torch.tensor([0 if ok else 1], device=dev)
+            dist.all_reduce(flag)
+            ok = int(flag.item()) == 0
     finally:
         ops.close()
         if world > 1 and dist.is_initialized():

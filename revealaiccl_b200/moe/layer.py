@@ -43,7 +43,7 @@ RET_META = 8
 LOG_HEADER = 16  # 8-word decision record + 8 phase-clock words
 TRACE_SLOTS = 256
 GUARD_CANARY = 0x5CA1AB1E0DDC0FFE  # fills the guard band after every array of the symmetric region
-PAIR_TICKET_RING = 32  # ticket slots per GEMM CTA pair (kPairTicketRing in csrc/include/types.h)
+PAIR_TICKET_RING = 32  # ticket slots (two words each) per GEMM CTA pair (kPairTicketRing in csrc/include/types.h)
 
 
 @dataclass
@@ -58,7 +58,7 @@ class ProgressiveMoELayer:
                  timeout_s: float = 10.0, seed: int = 0, control_topology=None,
                  control_path: str = "auto", trace: bool = False, frontend: str = "persistent",
                  gemm_pair: bool = True, pdl: bool = True, gemm_swap_max: int = 128,
-                 progressive: bool = True, dispatch_ctas: int = 0) -> None:
+                 progressive: bool = False, dispatch_ctas: int = 0) -> None:
         self.cfg = cfg
         if world is None:
             world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -223,7 +223,7 @@ class ProgressiveMoELayer:
             "tile_list": torch.zeros(4 * self._max_tiles1(nseg), dtype=torch.int32, device=dev),
             "tile_word": torch.zeros(1, dtype=torch.int64, device=dev),
             "ticket_counter": torch.zeros(1, dtype=torch.int32, device=dev),
-            "pair_tickets": torch.zeros((ints["sms"] // 2) * PAIR_TICKET_RING, dtype=torch.int64, device=dev),
+            "pair_tickets": torch.zeros((ints["sms"] // 2) * PAIR_TICKET_RING * 2, dtype=torch.int64, device=dev),
         }
         self.tensors = {kk: v for kk, v in self.tensors.items() if v is not None}
         self.channel.bind_counters(self.tensors["peer_counters"])
