@@ -104,6 +104,25 @@ static __device__ __noinline__ void cold_apply(sched::PlanView plan, sched::Stat
   sched::apply(plan, st, actions, kept, true);
 }
 
+// Edge -> group bitmasks of the plan (lanes over edges); returns whether an
+// edge lists a group twice (the selection then needs the serial core).
+// Called by one full warp.
+__device__ inline int edge_group_masks(const int32_t* egptr, const int32_t* egmem, int E, uint32_t* s_egmask) {
+  int dup_local = 0;
+  #pragma unroll 1
+  for (int e = threadIdx.x & 31; e < E; e += 32) {
+    uint32_t m = 0;
+    #pragma unroll 1
+    for (int k = egptr[e]; k < egptr[e + 1]; ++k) {
+      const uint32_t b = 1u << egmem[k];
+      dup_local |= (m & b) ? 1 : 0;
+      m |= b;
+    }
+    s_egmask[e] = m;
+  }
+  return __any_sync(0xffffffffu, dup_local) ? 1 : 0;
+}
+
 template <class Hooks>
 __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims, uint8_t* csm, int* s_dst,
                                  int* s_coff, uint32_t* s_egmask, int q0, int q1, bool reset, Hooks& hooks,
@@ -202,19 +221,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
       S[i] = (i >= kChunkStarts && i < kChunkStarts + C) ? -1 : 0;
   }
   // edge -> group bitmask (a repeated group falls back to the serial selection)
-  int dup_local = 0;
-  #pragma unroll 1
-  for (int e = lane; e < E; e += 32) {
-    uint32_t m = 0;
-    #pragma unroll 1
-    for (int k = egptr[e]; k < egptr[e + 1]; ++k) {
-      const uint32_t b = 1u << egmem[k];
-      dup_local |= (m & b) ? 1 : 0;
-      m |= b;
-    }
-    s_egmask[e] = m;
-  }
-  const bool dup_groups = __any_sync(FULL, dup_local) != 0;
+  const bool dup_groups = edge_group_masks(egptr, egmem, E, s_egmask) != 0;
   __syncwarp();
   #pragma unroll 1
   for (int desc = q0; desc < q1; ++desc) {

@@ -277,10 +277,15 @@ __host__ __device__ __forceinline__ bool router_group_ok(int experts, int hidden
 // wpre (optional): this lane's weight vectors wpre[e] = W_e[warp * 32 + lane]
 // when a row has exactly 8 x 32 vectors, held in registers across calls;
 // bias / block_mask: global or shared copies of the router tables.
+// srows (optional): the group's nt token rows already in shared memory
+// (landed there by a bulk copy), read instead of global memory.
+// Inlined into its callers so that wpre stays in registers (an array whose
+// address reaches a call lives in local memory).
 template <typename T, int NT, int EP>
-__device__ void router_group(const RouterParams& p, const float* bias, const float* chunk_bias,
-                             const uint8_t* block_mask, int t_first, int nt, float* red, int* sel_counts,
-                             const uint4* wpre, const DigestSink* dsink = nullptr) {
+__device__ __forceinline__ void router_group(const RouterParams& p, const float* bias, const float* chunk_bias,
+                                             const uint8_t* block_mask, int t_first, int nt, float* red,
+                                             int* sel_counts, const uint4 (&wpre)[EP], bool use_wpre,
+                                             const DigestSink* dsink = nullptr, const T* srows = nullptr) {
   static_assert(NT * EP == 32, "one (token, expert) sum per lane");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int D = p.hidden, E = p.experts;
@@ -298,7 +303,9 @@ __device__ void router_group(const RouterParams& p, const float* bias, const flo
     uint4 x[NT];
 #pragma unroll
     for (int j = 0; j < NT; ++j)
-      x[j] = j < nt ? __ldcg((const uint4*)(tok + (long long)(t_first + j) * D) + vi) : make_uint4(0, 0, 0, 0);
+      x[j] = j >= nt  ? make_uint4(0, 0, 0, 0)
+             : srows ? reinterpret_cast<const uint4*>(srows + (long long)j * D)[vi]
+                     : __ldcg((const uint4*)(tok + (long long)(t_first + j) * D) + vi);
     if (dsink != nullptr) {
 #pragma unroll
       for (int j = 0; j < NT; ++j)
@@ -307,7 +314,7 @@ __device__ void router_group(const RouterParams& p, const float* bias, const flo
 #pragma unroll
     for (int e = 0; e < EP; ++e) {
       if (e < E) {
-        const uint4 wr = wpre ? wpre[e] : __ldg((const uint4*)(w + (long long)e * D) + vi);
+        const uint4 wr = use_wpre ? wpre[e] : __ldg((const uint4*)(w + (long long)e * D) + vi);
         const T* wv = (const T*)&wr;
 #pragma unroll
         for (int j = 0; j < NT; ++j) {

@@ -159,7 +159,7 @@ struct FrontendParams {
   RouterParams rp;          // rp.chunk_bias: [C, E] base (row c per chunk) or nullptr
   ControlParams cp;
   DispatchParams dp;        // desc / t0 / t1 / fault_skip_signal are set per descriptor
-  int* chunk_done;          // [C] worker CTAs that finished router chunk c (zeroed per call)
+  int* chunk_done;          // [C] routing units (token groups or tokens) of chunk c routed so far (zeroed per call)
   int* chunk_counts;        // [C, E] router assignments per (chunk, expert) (zeroed per call)
   int* disp_base;           // [n_desc, E] first receive row of (descriptor, expert)
   unsigned long long* desc_ready;  // [n_desc] == epoch once the control warp released q
@@ -183,6 +183,17 @@ struct FrontendParams {
   // GEMM-1 tiles while the scheduler chain runs (0: every worker dispatches).
   int early_dependents;
   int dispatch_ctas;
+  // Resident batches: each worker streams its token groups into a ring of
+  // ring_slots group-sized slots at byte ring_off of its dynamic shared
+  // memory with bulk copies, issued ring_slots groups ahead of the routing
+  // (the caller passes ring_slots = 1 to ask for the ring, 0 to read every
+  // group from global memory; launch_frontend sizes it).
+  int ring_off;
+  int ring_slots;
+  // Control CTA: byte offset of the packed control path's tables and
+  // per-ordinal words in dynamic shared memory (set by launch_frontend when
+  // the plan fits that path; 0: the byte-per-entry path).
+  int ctl_packed_off;
 };
 
 // Returns false (nothing launched) when the device cannot co-schedule the grid.

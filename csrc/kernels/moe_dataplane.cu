@@ -91,7 +91,8 @@ __global__ void __launch_bounds__(256) moe_router_group_kernel(RouterParams p) {
   const int t_first = p.row0 + blockIdx.x * NT;
   const int nt = min(NT, p.row1 - t_first);
   if (nt <= 0) return;
-  router_group<T, NT, EP>(p, p.bias, p.chunk_bias, p.block_mask, t_first, nt, red, nullptr, nullptr);
+  const uint4 no_wpre[EP] = {};
+  router_group<T, NT, EP>(p, p.bias, p.chunk_bias, p.block_mask, t_first, nt, red, nullptr, no_wpre, false);
 }
 
 // ---------------------------------------------------------------------------

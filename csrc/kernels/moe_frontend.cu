@@ -16,9 +16,11 @@
 //       releases desc_ready[q] = epoch.
 //   CTAs 1..W — workers.  For each router chunk: route a share of its tokens
 //       (groups of tokens per CTA, or one warp per token for more than 32
-//       experts), add the per-expert counts, and release
-//       chunk_done[c].  A resident batch is routed chunk after chunk without
-//       interruption; a streamed batch is routed as its chunks land, and while
+//       experts), add the per-expert counts, and add the routed units to
+//       chunk_done[c] (a worker with no units in a chunk skips it).  A resident
+//       batch is streamed into shared memory by bulk copies ahead of the routing
+//       and routed chunk after chunk without interruption; a streamed batch is
+//       routed as its chunks land, and while
 //       a worker waits for the next chunk (early arm) it dispatches every
 //       descriptor already released.  After the last chunk a worker dispatches
 //       the rest, waiting (bounded) for each release.  In the delayed arm nothing is
@@ -38,6 +40,7 @@
 #include <cstdint>
 
 #include "control_warp.cuh"
+#include "control_warp_packed.cuh"
 #include "launchers.h"
 #include "moe_device.cuh"
 #include "moe_kernels.h"
@@ -97,6 +100,18 @@ __device__ __forceinline__ int first_share(int worker, int units_before, int n) 
   return g < 0 ? g + n : g;
 }
 
+// Units of a share that starts at unit `first` and takes every n-th of `units`.
+__device__ __forceinline__ int share_count(int first, int units, int n) {
+  return first < units ? (units - first + n - 1) / n : 0;
+}
+
+// Routing units of chunk c: token groups of `unit` tokens (1: single tokens).
+// chunk_done[c] counts the units routed so far; the chunk is complete when it
+// reaches this number.
+__device__ __forceinline__ int chunk_units(const int* s_coff, int c, int unit) {
+  return (s_coff[c + 1] - s_coff[c] + unit - 1) / unit;
+}
+
 __device__ __forceinline__ int trigger_first_chunk(int q, int P) { return q < P ? q : P; }
 __device__ __forceinline__ int trigger_last_chunk(int q, int P, int C) { return q < P ? q : C - 1; }
 
@@ -116,6 +131,7 @@ struct FrontHooks {
   int* s_ccount;       // [C * E] router counts per (chunk, expert) (shared)
   int cpc;
   int chunks_ready;    // chunks [0, chunks_ready) complete and fetched
+  int unit;            // tokens per routing unit
 
   __device__ bool before(int q) {
     const int lane = threadIdx.x & 31;
@@ -130,11 +146,12 @@ struct FrontHooks {
       const unsigned long long deadline = globaltimer_ns() + f->timeout_ns;
       #pragma unroll 1
       for (int c = chunks_ready; c < need && ok; ++c) {
+        const int need_units = chunk_units(s_coff, c, unit);
         int got;
         #pragma unroll 1
-        while ((got = ld_acquire_gpu_s32(&f->chunk_done[c])) < workers) {
+        while ((got = ld_acquire_gpu_s32(&f->chunk_done[c])) < need_units) {
           if (globaltimer_ns() > deadline) {
-            // index: the chunk; bound: how many of the workers had finished it
+            // index: the chunk; bound: how many of its routing units had been routed
             record_status(f->dp.status, kTimeoutChunkFlag, kFrontKernelId, c, got);
             ok = 0;
             break;
@@ -149,7 +166,7 @@ struct FrontHooks {
     #pragma unroll 1
     for (int base = need; base < C; base += 32) {
       const int c = base + lane;
-      const bool done = c < C && ld_acquire_gpu_s32(&f->chunk_done[c]) >= workers;
+      const bool done = c < C && ld_acquire_gpu_s32(&f->chunk_done[c]) >= chunk_units(s_coff, c, unit);
       const unsigned notdone = __ballot_sync(0xffffffffu, !done);
       const int run = notdone ? __ffs(notdone) - 1 : 32;
       hi = base + run;
@@ -270,14 +287,14 @@ __device__ void worker_index(const FrontendParams& f, int q, int w, int W, int* 
   __syncthreads();
 }
 
-// Whether every router chunk of descriptor q is complete (all W workers
-// reported it); a non-blocking poll, collective over the CTA.
-__device__ bool chunks_complete(const FrontendParams& f, int q, int W, int* s_flag) {
+// Whether every router chunk of descriptor q is complete (all its routing
+// units routed); a non-blocking poll, collective over the CTA.
+__device__ bool chunks_complete(const FrontendParams& f, int q, const int* s_coff, int unit, int* s_flag) {
   const int P = f.cp.partial_chunks, C = f.dp.dims.chunks;
   if (threadIdx.x == 0) {
     int ok = 1;
     for (int c = trigger_first_chunk(q, P); c <= trigger_last_chunk(q, P, C) && ok; ++c)
-      ok = ld_acquire_gpu_s32(&f.chunk_done[c]) >= W ? 1 : 0;
+      ok = ld_acquire_gpu_s32(&f.chunk_done[c]) >= chunk_units(s_coff, c, unit) ? 1 : 0;
     if (ok) __threadfence();
     *s_flag = ok;
   }
@@ -349,11 +366,27 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     ctl::copy16(reinterpret_cast<uint4*>(fsm), reinterpret_cast<const uint4*>(f.cp.blob), Lt.state_end / 16);
     for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;  // s_sent of the hooks
     __syncthreads();
+    // packed control path: template tables (whole CTA) and the edge -> group
+    // masks; an edge that lists a group twice keeps the byte-per-entry path
+    __shared__ int s_dup;
+    const bool packed = f.ctl_packed_off > 0;
+    ctl::PackedView pv = ctl::packed_view(fsm + f.ctl_packed_off, dims);
+    if (packed) {
+      ctl::build_packed_tables(fsm, dims, pv);
+      if (threadIdx.x < 32)
+        s_dup = ctl::edge_group_masks(reinterpret_cast<const int32_t*>(fsm + Lt.off[kCtlEdgeGroupPtr]),
+                                      reinterpret_cast<const int32_t*>(fsm + Lt.off[kCtlEdgeGroupMembers]),
+                                      dims.E, s_egmask);
+      __syncthreads();
+    }
     if (threadIdx.x < 32) {
       int* s_ccount = reinterpret_cast<int*>(fsm + ((Lt.total + 15) & ~15LL));
       FrontHooks hooks{&f, W, f.cp.partial_chunks, C, E, epoch, hist, s_dst, s_ccoff, s_ccount,
-                       f.cp.ctl_per_chunk, 0};
-      ctl::control_warp_run(f.cp, dims, fsm, s_dst, s_ccoff, s_egmask, 0, n_desc, true, hooks, s_vmc);
+                       f.cp.ctl_per_chunk, 0, NT > 0 ? NT : 1};
+      if (packed && !s_dup)
+        ctl::control_warp_run_packed(f.cp, dims, fsm, s_dst, s_ccoff, s_egmask, pv, 0, n_desc, hooks);
+      else
+        ctl::control_warp_run(f.cp, dims, fsm, s_dst, s_ccoff, s_egmask, 0, n_desc, true, hooks, s_vmc);
       __syncwarp();
       for (int e = threadIdx.x; e < E; e += 32) f.dp.sent_base[e] = hist[e];
     }
@@ -381,7 +414,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   if (f.rp.chunk_bias)
     for (int i = threadIdx.x; i < C * E; i += blockDim.x) s_cbias[i] = f.rp.chunk_bias[i];
   // this lane's weight slice, held in registers across chunks (rows of 8 x 32 vectors)
-  constexpr int kWP = NT > 0 ? EP : 1;
+  constexpr int kWP = NT > 0 ? EP : 1;  // (== EP wherever router_group is called)
   uint4 wpre[kWP];
   const int nvec_row = f.rp.hidden * (int)sizeof(T) / 16;
   const bool use_wpre = NT > 0 && nvec_row == 8 * 32;
@@ -391,37 +424,78 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       wpre[e] = e < E ? __ldg((const uint4*)(wts + (long long)e * f.rp.hidden) + warp * 32 + lane) : make_uint4(0, 0, 0, 0);
   }
   // inputs resident at launch (not streamed in by the copy engine during this call)
-  const bool resident = f.tok_ready == nullptr || ld_acquire_gpu_u64(f.tok_ready_all) >= epoch;
-  // pull this worker's token rows into L2 a little ahead of routing them:
-  // chunks 0 and 1 now, chunk c + 2 when chunk c starts (pulling every chunk
-  // at once would queue chunk 0's rows behind the whole batch)
+  const unsigned long long ready_all = f.tok_ready == nullptr ? ~0ULL : ld_acquire_gpu_u64(f.tok_ready_all);
+  const bool resident = ready_all >= epoch;
+  if (f.cta_clock != nullptr && threadIdx.x == 0) {  // diagnostics: what this CTA saw at its start
+    unsigned int smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    unsigned long long* row = f.cta_clock + (long long)blockIdx.x * 64;
+    row[18] = smid;
+    row[19] = ready_all;
+    row[20] = epoch;
+  }
   const int row_bytes = f.rp.hidden * (int)sizeof(T);
-  auto prefetch_chunk = [&](int c) {
-    if constexpr (NT > 0) {
-      if (!resident || c >= C) return;
-      int cum = 0;  // token groups of the chunks before c (the assignment below)
-      for (int cc = 0; cc < c; ++cc) cum += (s_coff[cc + 1] - s_coff[cc] + NT - 1) / NT;
-      const int t0 = s_coff[c], t1 = s_coff[c + 1];
-      const int ngroups = (t1 - t0 + NT - 1) / NT;
-      for (int g = first_share(w, cum, W); g < ngroups; g += W) {
-        const int tf = t0 + g * NT, nt = min(NT, t1 - tf);
-        const char* base = (const char*)f.rp.tokens + (long long)tf * row_bytes;
-        for (int off = threadIdx.x * 128; off < nt * row_bytes; off += blockDim.x * 128)
-          asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
-      }
+  // bulk-copy ring (resident batch, group router): this worker's token groups
+  // stream into shared memory ring_slots groups ahead of the routing
+  constexpr int kRingMax = 8;
+  __shared__ __align__(8) uint64_t s_rbar[kRingMax];
+  const bool ring = NT > 0 && resident && f.ring_slots >= 2 && f.ring_slots <= kRingMax;
+  const int R = ring ? f.ring_slots : 1;
+  const long long unit_bytes = (long long)(NT > 0 ? NT : 1) * row_bytes;
+  uint8_t* ring_base = fsm + f.ring_off;
+  int pc = 0, pg = 0, pcum = 0;          // producer (thread 0): next group to copy, chunk / group / units before
+  long long issued = 0, consumed = 0;    // groups copied / routed
+  auto unit_norm = [&]() {
+    #pragma unroll 1
+    while (pc < C) {
+      const int ng = (s_coff[pc + 1] - s_coff[pc] + (NT > 0 ? NT : 1) - 1) / (NT > 0 ? NT : 1);
+      if (pg < ng) return;
+      pcum += ng;
+      if (++pc < C) pg = first_share(w, pcum, W);
     }
   };
-  prefetch_chunk(0);
-  prefetch_chunk(1);
+  auto issue_next = [&]() {  // thread 0: copy the next group into its slot
+    if (pc >= C) return;
+    const int slot = (int)(issued % R);
+    const int tf = s_coff[pc] + pg * NT, nt = min(NT, s_coff[pc + 1] - tf);
+    const uint32_t bytes = (uint32_t)((long long)nt * row_bytes);
+    mbar_arrive_expect_tx(&s_rbar[slot], bytes);
+    bulk_load_g2s(ring_base + slot * unit_bytes, (const char*)f.rp.tokens + (long long)tf * row_bytes, bytes,
+                  &s_rbar[slot]);
+    ++issued;
+    pg += W;
+    unit_norm();
+  };
+  if (ring && threadIdx.x == 0) {
+    for (int i = 0; i < R; ++i) mbar_init(&s_rbar[i], 1);
+    fence_mbarrier_init();
+    fence_proxy_async_smem();
+    pg = first_share(w, 0, W);
+    unit_norm();
+    for (int i = 0; i < R; ++i) issue_next();
+  }
   cta_stamp(f, 0);
   __syncthreads();
   cta_stamp(f, 1);
   int next = 0;
   int cum_units = 0;  // routing units (token groups, or tokens) of the chunks before c
   for (int c = 0; c < C; ++c) {
+    // this worker's routing units in chunk c (token groups, or tokens over its warps)
+    int my_units = 0;
+    if constexpr (NT > 0) {
+      my_units = share_count(first_share(w, cum_units, W), chunk_units(s_coff, c, NT), W);
+    } else {
+      const int slots = W * nwarps;
+      for (int k = 0; k < nwarps; ++k)
+        my_units += share_count(first_share(w * nwarps + k, cum_units, slots), chunk_units(s_coff, c, 1), slots);
+    }
+    if (resident && my_units == 0) {  // nothing to route or to report for this chunk
+      if (c < 8) { cta_stamp(f, 2 + 2 * c); cta_stamp(f, 52 + c); cta_stamp(f, 3 + 2 * c); }
+      cum_units += chunk_units(s_coff, c, NT > 0 ? NT : 1);
+      continue;
+    }
     TraceSlot* rslot = f.phase_trace ? &f.phase_trace[c] : nullptr;
     if (threadIdx.x == 0) trace_begin(rslot);
-    prefetch_chunk(c + 2);
     if (c < 8) cta_stamp(f, 2 + 2 * c);
     // early arm: this chunk's poll of the next release is a relaxed load issued
     // before the routing work and read after it (a fence makes it an acquire
@@ -474,8 +548,20 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       const int ngroups = (t1 - t0 + NT - 1) / NT;
       for (int g = first_share(w, cum_units, W); g < ngroups; g += W) {
         const int tf = t0 + g * NT;
+        const T* srows = nullptr;
+        if (ring) {
+          const int slot = (int)(consumed % R);
+          // a wait that runs out records the status (the call fails) and routes what is there
+          mbar_wait_bounded(&s_rbar[slot], (uint32_t)((consumed / R) & 1), f.dp.status, kFrontKernelId + 2,
+                            f.timeout_ns);
+          srows = reinterpret_cast<const T*>(ring_base + slot * unit_bytes);
+        }
         router_group<T, NT, EP>(f.rp, s_rbias, cbias, f.rp.block_mask ? s_rmask : nullptr, tf, min(NT, t1 - tf),
-                                red, run, use_wpre ? wpre : nullptr, digest ? &dsink : nullptr);
+                                red, run, wpre, use_wpre, digest ? &dsink : nullptr, srows);
+        if (ring) {  // router_group ended on a CTA barrier: the slot is free again
+          if (threadIdx.x == 0) issue_next();
+          ++consumed;
+        }
       }
       cum_units += ngroups;
     } else {
@@ -504,8 +590,10 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       if (run[e]) atomicAdd(&f.chunk_counts[(long long)c * E + e], run[e]);
     __syncthreads();
     if (threadIdx.x == 0) {
-      __threadfence();
-      atomicAdd(&f.chunk_done[c], 1);
+      if (my_units > 0) {
+        __threadfence();
+        atomicAdd(&f.chunk_done[c], my_units);
+      }
       trace_end(rslot);
     }
     if (c < 8) cta_stamp(f, 3 + 2 * c);
@@ -528,6 +616,14 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       }
     }
   }
+  if (ring && threadIdx.x == 0) {
+    // every copy issued was routed; after a failed wait, let any copy still in
+    // flight land before the CTA moves on (bounded)
+    #pragma unroll 1
+    for (; consumed < issued; ++consumed)
+      mbar_wait_bounded(&s_rbar[(int)(consumed % R)], (uint32_t)((consumed / R) & 1), f.dp.status,
+                        kFrontKernelId + 2, f.timeout_ns);
+  }
   if (!dispatcher) return;  // routing done: this SM is free for the expert side
   if (f.delayed && wait_released(f, n_desc - 1, epoch, &s_flag, true) != 1) return;
   while (next < n_desc) {
@@ -536,7 +632,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     // the control warp works, so the release is followed by the copy alone
     const int rel = wait_released(f, next, epoch, &s_flag, false);
     bool indexed = false;
-    if (rel == 0 && chunks_complete(f, next, W, &s_flag)) {
+    if (rel == 0 && chunks_complete(f, next, s_coff, NT > 0 ? NT : 1, &s_flag)) {
       worker_index(f, next, w, Wd, hist, run, item_pos, s_coff);
       indexed = true;
     }
@@ -582,10 +678,27 @@ bool launch_frontend(const FrontendParams& f, bool bf16, int sms, cudaStream_t s
   // read through the read-only path
   // CTA 0: control blob + per-(chunk, expert) router counts; workers: per-chunk bias rows
   const size_t cwords = (size_t)f.dp.dims.chunks * f.dp.dims.experts * sizeof(int);
-  const size_t smem = std::max(((control_smem_bytes(f.cp) + 15) & ~(size_t)15) + cwords, cwords);
-#define RAICCL_FRONT(T, NT, EP, EM) return launch_one_frontend<T, NT, EP, EM>(f, sms, smem, s)
   const int E = f.rp.experts;
-  if (router_group_ok(E, f.rp.hidden, bf16 ? 2 : 4)) {
+  const bool group = router_group_ok(E, f.rp.hidden, bf16 ? 2 : 4);
+  // workers: per-chunk bias rows, then the ring of token groups (group router,
+  // two to eight groups within kRingBudget bytes)
+  FrontendParams g = f;
+  const size_t ring_off = (cwords + 127) & ~(size_t)127;
+  const int nt = !group ? 0 : E <= 4 ? 8 : E <= 8 ? 4 : E <= 16 ? 2 : 1;
+  const size_t unit = (size_t)nt * f.rp.hidden * (bf16 ? 2 : 4);
+  constexpr size_t kRingBudget = 160 * 1024;
+  g.ring_slots = (f.ring_slots && unit) ? (int)std::min<size_t>(8, kRingBudget / unit) : 0;
+  if (g.ring_slots < 2) g.ring_slots = 0;
+  g.ring_off = (int)ring_off;
+  // control CTA: blob, per-(chunk, expert) router counts, then the packed
+  // control path's tables and per-ordinal words when the plan fits it
+  const size_t ctl_base = ((control_smem_bytes(f.cp) + 15) & ~(size_t)15) + ((cwords + 15) & ~(size_t)15);
+  const ControlDims cd = control_dims(f.cp);
+  g.ctl_packed_off = ctl::packed_path_ok(cd) ? (int)ctl_base : 0;
+  const size_t ctl_bytes = ctl_base + (g.ctl_packed_off ? (size_t)ctl::packed_smem_bytes(cd) : 0);
+  const size_t smem = std::max(ctl_bytes, g.ring_slots ? ring_off + g.ring_slots * unit : cwords);
+#define RAICCL_FRONT(T, NT, EP, EM) return launch_one_frontend<T, NT, EP, EM>(g, sms, smem, s)
+  if (group) {
     if (E <= 4) {
       if (bf16) RAICCL_FRONT(__nv_bfloat16, 8, 4, 4); else RAICCL_FRONT(float, 8, 4, 4);
     } else if (E <= 8) {

@@ -122,6 +122,7 @@ class MoELayerRunner {
                        tensors.contains("tile_list") && tensors.contains("tile_word") &&
                        tensors.contains("ticket_counter") && tensors.contains("pair_tickets");
     dispatch_ctas_ = ints.contains("dispatch_ctas") ? geti(ints, "dispatch_ctas") : 0;
+    router_ring_ = !ints.contains("router_ring") || geti(ints, "router_ring") != 0;
     max_cands_ = geti(ints, "max_cands");
     log_stride_ = geti(ints, "log_stride");
     max_ctl_tokens_ = geti(ints, "max_ctl_tokens");
@@ -378,6 +379,7 @@ class MoELayerRunner {
       fp.tok_ready_all = tok_ready_all_;
       fp.early_dependents = progressive ? 1 : 0;
       fp.dispatch_ctas = progressive ? dispatch_ctas_ : 0;
+      fp.ring_slots = router_ring_ ? 1 : 0;  // a request: launch_frontend sizes the ring
       const size_t mark = trace_labels_.size();
       fp.trace = trace_slot("frontend", -1);
       raiccl::TraceSlot* first = nullptr;
@@ -733,6 +735,7 @@ class MoELayerRunner {
   int swap1_ = 0, swap2_ = 0;            // GEMM 1 / 2 swapped-tail row limit (0: off)
   bool progressive_req_ = false;         // progressive GEMM-1 requested and possible with the pair kernel
   int dispatch_ctas_ = 0;                // front-end workers that dispatch in progressive mode (0: all)
+  bool router_ring_ = true;              // resident batches: token groups stream into shared memory by bulk copies
   bool pdl_ = true;  // plan, GEMMs and combine as programmatic dependents of their predecessors
   int max_cands_ = 0, log_stride_ = 0, max_ctl_tokens_ = 0, grid_sms_ = 148;
   bool control_serial_ = false;  // run the CTA control kernel even where the single-warp one fits

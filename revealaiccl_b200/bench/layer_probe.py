@@ -225,10 +225,13 @@ def _cta_clocks(layer) -> dict:
     wk = (clk[1:] - t0) / 1e3
     wk[clk[1:] == 0] = np.nan
     r = lambda x: round(float(x), 2)
-    out = {"chunks": [], "descriptors": [], "triggers": []}
+    out = {"chunks": [], "descriptors": [], "triggers": [],
+           "worker_start": {"med": r(np.nanmedian(wk[:, 0])), "max": r(np.nanmax(wk[:, 0]))}}
     for c in range(min(8, layer.cfg.chunks)):
-        b, e = wk[:, 2 + 2 * c], wk[:, 3 + 2 * c]
+        b, e, routed = wk[:, 2 + 2 * c], wk[:, 3 + 2 * c], wk[:, 52 + c]
         out["chunks"].append({"chunk": c, "begin_med": r(np.nanmedian(b)), "dur_med": r(np.nanmedian(e - b)),
+                              "route_med": r(np.nanmedian(routed - b)), "publish_med": r(np.nanmedian(e - routed)),
+                              "end_p50": r(np.nanmedian(e)), "end_p90": r(np.nanpercentile(e, 90)),
                               "end_max": r(np.nanmax(e))})
     for q in range(min(8, layer.cfg.n_desc)):
         b, mid, e = wk[:, 24 + 2 * q], wk[:, 44 + q], wk[:, 25 + 2 * q]

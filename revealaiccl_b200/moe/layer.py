@@ -58,7 +58,7 @@ class ProgressiveMoELayer:
                  timeout_s: float = 10.0, seed: int = 0, control_topology=None,
                  control_path: str = "auto", trace: bool = False, frontend: str = "persistent",
                  gemm_pair: bool = True, pdl: bool = True, gemm_swap_max: int = 128,
-                 progressive: bool = False, dispatch_ctas: int = 0) -> None:
+                 progressive: bool = False, dispatch_ctas: int = 0, router_ring: bool = True) -> None:
         self.cfg = cfg
         if world is None:
             world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -151,6 +151,9 @@ class ProgressiveMoELayer:
             # leave after routing (dispatch_ctas workers stay to dispatch)
             "progressive": int(bool(progressive)),
             "dispatch_ctas": int(dispatch_ctas),
+            # resident batches: each front-end worker streams its token groups
+            # into a shared-memory ring with bulk copies ahead of routing them
+            "router_ring": int(bool(router_ring)),
         }
         self.layout = self._k.sym_layout(ints)
         self.channel = PeerChannel(self.layout["total"], dev, group=group)

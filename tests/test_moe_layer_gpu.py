@@ -175,16 +175,19 @@ def test_warp_control_plane_matches_cta_kernel(case):
     assert torch.equal(res["auto"][3], res["serial"][3])
 
 
-@pytest.mark.parametrize("name", ["r4_reference", "full_tf32"])
+@pytest.mark.parametrize("name", ["r4_reference", "full_tf32", "r4:skewed", "r4:empty_shard",
+                                  "r4:multiple_progressive_shards"])
 def test_persistent_frontend_matches_step_pipeline(name):
-    """The persistent cooperative front end and the one-launch-per-step pipeline
-    produce identical outputs, control state and log rows, in both arms."""
-    from revealaiccl_b200.moe.config import preset
+    """The persistent cooperative front end (packed control path) and the
+    one-launch-per-step pipeline (byte-per-entry control path) produce identical
+    outputs, control state and log rows, in both arms."""
+    from revealaiccl_b200.moe.config import preset, r4_case
     from revealaiccl_b200.moe.layer import LOG_HEADER, ProgressiveMoELayer
 
+    cfg = r4_case(name[3:]) if name.startswith("r4:") else preset(name)
     res = {}
     for fe in ("persistent", "steps"):
-        layer = ProgressiveMoELayer(preset(name), timeout_s=5.0, frontend=fe)
+        layer = ProgressiveMoELayer(cfg, timeout_s=5.0, frontend=fe)
         try:
             outs = []
             for arm in ("early", "delayed"):
@@ -193,6 +196,9 @@ def test_persistent_frontend_matches_step_pipeline(name):
                 assert rep["pass"], (fe, arm, rep["violations"])
                 outs.append(layer.out.clone())
             assert layer.runner.persistent_frontend() == (fe == "persistent")
+            if fe == "persistent":
+                log15 = layer.tensors["ctl_log"].cpu().view(layer.cfg.n_desc, layer.log_stride)[:, 15]
+                assert bool((log15 == 2).all())  # every trigger ran on the packed path
             lay = layer.control_layout
             blob = layer.tensors["ctl_blob"].cpu()
             log = layer.tensors["ctl_log"].cpu().view(layer.cfg.n_desc, layer.log_stride)
@@ -484,3 +490,29 @@ def test_progressive_gemm1_matches_and_starts_early(name, over):
             layer.close()
     for key in ("early", "delayed", "graph"):
         assert torch.equal(outs[(False, key)], outs[(True, key)]), key
+
+
+@pytest.mark.parametrize("name", ["r4_reference", "full_tf32", "skewed_bf16"])
+def test_router_ring_matches_global_loads(name):
+    """Routing token groups out of the shared-memory ring (bulk copies issued
+    ahead) gives the same expert ids, gates and layer output as reading them
+    from global memory."""
+    from revealaiccl_b200.moe.config import preset
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    cfg = preset(name)
+    if cfg.tokens_per_rank > 4096:
+        n = cfg.chunks
+        cfg = cfg.with_overrides(tokens_per_rank=4096, chunk_sizes=(4096 // n,) * n)
+    res = {}
+    for ring in (True, False):
+        layer = ProgressiveMoELayer(cfg, timeout_s=5.0, router_ring=ring)
+        try:
+            for arm in ("early", "early"):
+                layer.forward(arm)
+                assert layer.verify()["pass"], ring
+            res[ring] = (layer.expert_ids.clone(), layer.gates.clone(), layer.out.clone())
+        finally:
+            layer.close()
+    for a, b in zip(res[True], res[False]):
+        assert torch.equal(a, b)
