@@ -146,9 +146,14 @@ __device__ __forceinline__ void router_finish(const RouterParams& p, const float
       logit[e] = ninf;
     }
   }
-  // the choice loop stays rolled: unrolled over k x EMAX it makes compile time explode
+  // The choice loop stays rolled (unrolled over k x EMAX it makes compile time
+  // explode); the k <= 8 choices land in register slots through unrolled
+  // compare-and-select, never at a run-time index (that would put them in local
+  // memory, which misses L1 when the kernel holds most of shared memory).
   float sel_logit[8];
   int sel[8];
+#pragma unroll
+  for (int s = 0; s < 8; ++s) { sel[s] = -1; sel_logit[s] = ninf; }
 #pragma unroll 1
   for (int j = 0; j < p.top_k; ++j) {
     int best = -1;
@@ -159,27 +164,37 @@ __device__ __forceinline__ void router_finish(const RouterParams& p, const float
 #pragma unroll
     for (int e = 0; e < EMAX; ++e)
       if (e == best) taken[e] = true;
-    sel[j] = best;
-    sel_logit[j] = bv;
+#pragma unroll
+    for (int s = 0; s < 8; ++s)
+      if (s == j) { sel[s] = best; sel_logit[s] = bv; }
   }
+  const int k = p.top_k;
   float g[8];
   if (p.gate_mode == 1) {
     float sum = 0.f;
-    for (int j = 0; j < p.top_k; ++j) { g[j] = __expf(sel_logit[j] - sel_logit[0]); sum += g[j]; }
-    for (int j = 0; j < p.top_k; ++j) g[j] /= sum;
+#pragma unroll
+    for (int s = 0; s < 8; ++s)
+      if (s < k) { g[s] = __expf(sel_logit[s] - sel_logit[0]); sum += g[s]; }
+#pragma unroll
+    for (int s = 0; s < 8; ++s) g[s] = s < k ? g[s] / sum : 0.f;
   } else if (p.gate_mode == 2) {
     float mx = sel_logit[0], sum = 0.f;
 #pragma unroll
     for (int e = 0; e < EMAX; ++e)
       if (e < E && logit[e] != ninf) sum += __expf(logit[e] - mx);
-    for (int j = 0; j < p.top_k; ++j) g[j] = __expf(sel_logit[j] - mx) / sum;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) g[s] = s < k ? __expf(sel_logit[s] - mx) / sum : 0.f;
   } else {
-    for (int j = 0; j < p.top_k; ++j) g[j] = 1.f;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) g[s] = 1.f;
   }
-  for (int j = 0; j < p.top_k; ++j) {
-    p.expert_ids[(long long)t * p.top_k + j] = sel[j];
-    p.gates[(long long)t * p.top_k + j] = g[j];
-    if (sel_out) sel_out[j] = sel[j];
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    if (s < k) {
+      p.expert_ids[(long long)t * k + s] = sel[s];
+      p.gates[(long long)t * k + s] = g[s];
+      if (sel_out) sel_out[s] = sel[s];
+    }
   }
 }
 
@@ -363,7 +378,9 @@ __device__ __forceinline__ void router_group(const RouterParams& p, const float*
       int sel[8];
       router_finish<EP>(p, bias, chunk_bias, block_mask, t_first + lane, acc, sel);
       if (sel_counts)
-        for (int j = 0; j < p.top_k; ++j) atomicAdd(&sel_counts[sel[j]], 1);
+#pragma unroll
+        for (int s = 0; s < 8; ++s)
+          if (s < p.top_k) atomicAdd(&sel_counts[sel[s]], 1);
     }
   }
   __syncthreads();

@@ -194,6 +194,10 @@ struct FrontendParams {
   // per-ordinal words in dynamic shared memory (set by launch_frontend when
   // the plan fits that path; 0: the byte-per-entry path).
   int ctl_packed_off;
+  // 1: each descriptor is dispatched by its own group of workers (when there
+  // are at least as many dispatching workers as descriptors); 0: every
+  // worker takes a share of every descriptor.
+  int dispatch_groups;
 };
 
 // Returns false (nothing launched) when the device cannot co-schedule the grid.

@@ -477,7 +477,27 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   cta_stamp(f, 0);
   __syncthreads();
   cta_stamp(f, 1);
-  int next = 0;
+  // Descriptors this worker dispatches.  With at least as many dispatching
+  // workers as descriptors, each descriptor has its own group of workers (in
+  // proportion to its tokens), so released descriptors are dispatched side by
+  // side; otherwise every worker takes a share of every descriptor.
+  int my_q0 = 0, my_q1 = n_desc, wi = w, wn = Wd;
+  if (f.dispatch_groups && n_desc <= Wd && dispatcher) {
+    const int P = f.cp.partial_chunks;
+    const long long total = s_coff[C] - s_coff[0];
+    long long cum = 0;
+    int lo = 0;
+    for (int q = 0; q < n_desc; ++q) {
+      cum += s_coff[trigger_last_chunk(q, P, C) + 1] - s_coff[trigger_first_chunk(q, P)];
+      int hi = total > 0 ? (int)((long long)Wd * cum / total) : lo + 1;
+      hi = max(hi, lo + 1);
+      hi = min(hi, Wd - (n_desc - 1 - q));
+      if (q == n_desc - 1) hi = Wd;
+      if (w >= lo && w < hi) { my_q0 = q; my_q1 = q + 1; wi = w - lo; wn = hi - lo; }
+      lo = hi;
+    }
+  }
+  int next = my_q0;
   int cum_units = 0;  // routing units (token groups, or tokens) of the chunks before c
   for (int c = 0; c < C; ++c) {
     // this worker's routing units in chunk c (token groups, or tokens over its warps)
@@ -501,7 +521,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     // before the routing work and read after it (a fence makes it an acquire
     // when it saw the release)
     unsigned long long early_v = 0;
-    if (threadIdx.x == 0 && !f.delayed && next < n_desc) early_v = ld_relaxed_gpu_u64(&f.desc_ready[next]);
+    if (threadIdx.x == 0 && !f.delayed && next < my_q1) early_v = ld_relaxed_gpu_u64(&f.desc_ready[next]);
     for (int e = threadIdx.x; e < E; e += blockDim.x) run[e] = 0;  // per-chunk expert counts
     if (!resident) {
       // streamed: wait for this chunk's rows; early arm: dispatch every
@@ -514,7 +534,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
             if (ld_acquire_sys_u64(reinterpret_cast<const uint64_t*>(&f.tok_ready[c])) >= epoch ||
                 ld_acquire_sys_u64(reinterpret_cast<const uint64_t*>(f.tok_ready_all)) >= epoch) {
               st = 1;
-            } else if (dispatcher && !f.delayed && next < n_desc &&
+            } else if (dispatcher && !f.delayed && next < my_q1 &&
                        ld_relaxed_gpu_u64(&f.desc_ready[next]) == epoch) {
               __threadfence();  // acquire the release seen by the relaxed poll
               st = 2;
@@ -531,10 +551,10 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
         const int st = s_flag;
         __syncthreads();
         if (st == 1) break;
-        worker_dispatch<T>(f, next, w, Wd, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, true);
+        worker_dispatch<T>(f, next, wi, wn, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, true);
         ++next;
       }
-      if (threadIdx.x == 0 && !f.delayed && next < n_desc) early_v = ld_relaxed_gpu_u64(&f.desc_ready[next]);
+      if (threadIdx.x == 0 && !f.delayed && next < my_q1) early_v = ld_relaxed_gpu_u64(&f.desc_ready[next]);
       for (int e = threadIdx.x; e < E; e += blockDim.x) run[e] = 0;  // worker_dispatch used it
     }
     __syncthreads();
@@ -555,9 +575,11 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
           mbar_wait_bounded(&s_rbar[slot], (uint32_t)((consumed / R) & 1), f.dp.status, kFrontKernelId + 2,
                             f.timeout_ns);
           srows = reinterpret_cast<const T*>(ring_base + slot * unit_bytes);
+          if (consumed == 0) cta_stamp(f, 21);  // first group in shared memory
         }
         router_group<T, NT, EP>(f.rp, s_rbias, cbias, f.rp.block_mask ? s_rmask : nullptr, tf, min(NT, t1 - tf),
                                 red, run, wpre, use_wpre, digest ? &dsink : nullptr, srows);
+        if (ring && consumed == 0) cta_stamp(f, 22);  // first group routed
         if (ring) {  // router_group ended on a CTA barrier: the slot is free again
           if (threadIdx.x == 0) issue_next();
           ++consumed;
@@ -571,7 +593,9 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
         int sel[8];
         router_token<T, EMAX, false>(f.rp, cbias, t, wts, sel);
         if (lane == 0)
-          for (int j = 0; j < f.rp.top_k; ++j) atomicAdd(&run[sel[j]], 1);
+#pragma unroll
+          for (int s = 0; s < 8; ++s)
+            if (s < f.rp.top_k) atomicAdd(&run[sel[s]], 1);
         if (digest) {
           const long long dg = warp_row_digest((const uint4*)((const T*)f.rp.tokens + (long long)t * f.rp.hidden),
                                                nvec_tok);
@@ -609,10 +633,10 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       __syncthreads();
       bool ready = s_flag == 1;
       __syncthreads();
-      while (next < n_desc && ready) {
-        worker_dispatch<T>(f, next, w, Wd, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident);
+      while (next < my_q1 && ready) {
+        worker_dispatch<T>(f, next, wi, wn, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident);
         ++next;
-        ready = next < n_desc && wait_released(f, next, epoch, &s_flag, false) == 1;
+        ready = next < my_q1 && wait_released(f, next, epoch, &s_flag, false) == 1;
       }
     }
   }
@@ -626,18 +650,18 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   }
   if (!dispatcher) return;  // routing done: this SM is free for the expert side
   if (f.delayed && wait_released(f, n_desc - 1, epoch, &s_flag, true) != 1) return;
-  while (next < n_desc) {
+  while (next < my_q1) {
     // a descriptor not yet released whose chunks are routed: compute its
     // index part (prefix counts and ranks, from the expert ids only) while
     // the control warp works, so the release is followed by the copy alone
     const int rel = wait_released(f, next, epoch, &s_flag, false);
     bool indexed = false;
     if (rel == 0 && chunks_complete(f, next, s_coff, NT > 0 ? NT : 1, &s_flag)) {
-      worker_index(f, next, w, Wd, hist, run, item_pos, s_coff);
+      worker_index(f, next, wi, wn, hist, run, item_pos, s_coff);
       indexed = true;
     }
     if (rel != 1 && wait_released(f, next, epoch, &s_flag, true) != 1) return;
-    worker_dispatch<T>(f, next, w, Wd, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident, indexed);
+    worker_dispatch<T>(f, next, wi, wn, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident, indexed);
     ++next;
   }
 }

@@ -123,6 +123,7 @@ class MoELayerRunner {
                        tensors.contains("ticket_counter") && tensors.contains("pair_tickets");
     dispatch_ctas_ = ints.contains("dispatch_ctas") ? geti(ints, "dispatch_ctas") : 0;
     router_ring_ = !ints.contains("router_ring") || geti(ints, "router_ring") != 0;
+    dispatch_groups_ = !ints.contains("dispatch_groups") || geti(ints, "dispatch_groups") != 0;
     max_cands_ = geti(ints, "max_cands");
     log_stride_ = geti(ints, "log_stride");
     max_ctl_tokens_ = geti(ints, "max_ctl_tokens");
@@ -380,6 +381,7 @@ class MoELayerRunner {
       fp.early_dependents = progressive ? 1 : 0;
       fp.dispatch_ctas = progressive ? dispatch_ctas_ : 0;
       fp.ring_slots = router_ring_ ? 1 : 0;  // a request: launch_frontend sizes the ring
+      fp.dispatch_groups = dispatch_groups_ ? 1 : 0;
       const size_t mark = trace_labels_.size();
       fp.trace = trace_slot("frontend", -1);
       raiccl::TraceSlot* first = nullptr;
@@ -736,6 +738,7 @@ class MoELayerRunner {
   bool progressive_req_ = false;         // progressive GEMM-1 requested and possible with the pair kernel
   int dispatch_ctas_ = 0;                // front-end workers that dispatch in progressive mode (0: all)
   bool router_ring_ = true;              // resident batches: token groups stream into shared memory by bulk copies
+  bool dispatch_groups_ = true;          // one worker group per descriptor (dispatched side by side)
   bool pdl_ = true;  // plan, GEMMs and combine as programmatic dependents of their predecessors
   int max_cands_ = 0, log_stride_ = 0, max_ctl_tokens_ = 0, grid_sms_ = 148;
   bool control_serial_ = false;  // run the CTA control kernel even where the single-warp one fits

@@ -225,8 +225,13 @@ def _cta_clocks(layer) -> dict:
     wk = (clk[1:] - t0) / 1e3
     wk[clk[1:] == 0] = np.nan
     r = lambda x: round(float(x), 2)
+    first = ~np.isnan(wk[:, 21]) & ~np.isnan(wk[:, 22]) & (wk[:, 21] >= wk[:, 0])
     out = {"chunks": [], "descriptors": [], "triggers": [],
-           "worker_start": {"med": r(np.nanmedian(wk[:, 0])), "max": r(np.nanmax(wk[:, 0]))}}
+           "worker_start": {"med": r(np.nanmedian(wk[:, 0])), "max": r(np.nanmax(wk[:, 0]))},
+           # resident batches: first token group in shared memory / routed (workers with a group)
+           "first_group": ({"landed_med": r(np.median(wk[first, 21])), "landed_max": r(np.max(wk[first, 21])),
+                            "routed_med": r(np.median(wk[first, 22])), "routed_max": r(np.max(wk[first, 22]))}
+                           if first.any() else None)}
     for c in range(min(8, layer.cfg.chunks)):
         b, e, routed = wk[:, 2 + 2 * c], wk[:, 3 + 2 * c], wk[:, 52 + c]
         out["chunks"].append({"chunk": c, "begin_med": r(np.nanmedian(b)), "dur_med": r(np.nanmedian(e - b)),

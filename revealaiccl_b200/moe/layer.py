@@ -58,7 +58,8 @@ class ProgressiveMoELayer:
                  timeout_s: float = 10.0, seed: int = 0, control_topology=None,
                  control_path: str = "auto", trace: bool = False, frontend: str = "persistent",
                  gemm_pair: bool = True, pdl: bool = True, gemm_swap_max: int = 128,
-                 progressive: bool = False, dispatch_ctas: int = 0, router_ring: bool = True) -> None:
+                 progressive: bool = False, dispatch_ctas: int = 0, router_ring: bool = True,
+                 dispatch_groups: bool = True) -> None:
         self.cfg = cfg
         if world is None:
             world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -154,6 +155,10 @@ class ProgressiveMoELayer:
             # resident batches: each front-end worker streams its token groups
             # into a shared-memory ring with bulk copies ahead of routing them
             "router_ring": int(bool(router_ring)),
+            # one group of front-end workers per descriptor, so released
+            # descriptors are dispatched side by side (0: every worker takes a
+            # share of every descriptor, one descriptor after the other)
+            "dispatch_groups": int(bool(dispatch_groups)),
         }
         self.layout = self._k.sym_layout(ints)
         self.channel = PeerChannel(self.layout["total"], dev, group=group)

@@ -516,3 +516,27 @@ def test_router_ring_matches_global_loads(name):
             layer.close()
     for a, b in zip(res[True], res[False]):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("name", ["r4_reference", "full_tf32"])
+def test_dispatch_groups_match_shared_dispatch(name):
+    """Descriptors dispatched by their own worker groups, side by side, leave the
+    same rows, counts and layer output as every worker sharing every
+    descriptor, in both arms."""
+    from revealaiccl_b200.moe.config import preset
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    res = {}
+    for groups in (True, False):
+        layer = ProgressiveMoELayer(preset(name), timeout_s=5.0, dispatch_groups=groups)
+        try:
+            outs = []
+            for arm in ("early", "delayed"):
+                layer.forward(arm)
+                assert layer.verify()["pass"], (groups, arm)
+                outs.append(layer.out.clone())
+            res[groups] = outs
+        finally:
+            layer.close()
+    for a, b in zip(res[True], res[False]):
+        assert torch.equal(a, b)
