@@ -68,8 +68,11 @@ __device__ __forceinline__ unsigned lanemask_lt() {
 
 // kFetchesTokens: before(desc) has already placed the control-token
 // destinations of every chunk the trigger needs in s_dst[c * cpc + j].
+// kPublishesPermit: after(desc, permitted) writes the descriptor's permit
+// word itself (the control warp then leaves it alone).
 struct NoHooks {
   static constexpr bool kFetchesTokens = false;
+  static constexpr bool kPublishesPermit = false;
   __device__ __forceinline__ bool before(int) { return true; }
   __device__ __forceinline__ void after(int, bool) {}
 };
@@ -516,7 +519,7 @@ __device__ void control_warp_run(const ControlParams& p, const ControlDims& dims
     #pragma unroll 1
     for (int c = c_lo; c <= c_hi; ++c) dispatched |= 1LL << c;
   if (lane == 0) {
-    p.permit[desc] = (accepted && gate_ok) ? epoch_v : 0ULL;
+    if (!Hooks::kPublishesPermit) p.permit[desc] = (accepted && gate_ok) ? epoch_v : 0ULL;
     if (!(accepted && gate_ok)) cold_status(p.status, kTimeoutPermit, 62, desc, code);
   }
   __syncwarp();

@@ -436,7 +436,7 @@ __device__ void control_warp_run_packed(const ControlParams& p, const ControlDim
       #pragma unroll 1
       for (int c = c_lo; c <= c_hi; ++c) dispatched |= 1LL << c;
     if (lane == 0) {
-      p.permit[desc] = (accepted && gate_ok) ? epoch_v : 0ULL;
+      if (!Hooks::kPublishesPermit) p.permit[desc] = (accepted && gate_ok) ? epoch_v : 0ULL;
       if (!(accepted && gate_ok)) cold_status(p.status, kTimeoutPermit, 62, desc, code);
     }
     __syncwarp();

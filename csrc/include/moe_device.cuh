@@ -127,87 +127,64 @@ constexpr int kDispatchMaxChunks = 128;  // chunk-offset table staged in shared 
 // -> gates; writes expert_ids / gates of row t (one thread per token).
 // bias / chunk_bias / block_mask may point at global memory or at shared
 // copies; the values, and so the routing, are the same.
-template <int EMAX>
-__device__ __forceinline__ void router_finish(const RouterParams& p, const float* bias, const float* chunk_bias,
-                                              const uint8_t* block_mask, int t, const float (&acc)[EMAX],
-                                              int* sel_out) {
-  const int E = p.experts;
-  float logit[EMAX];
-  bool taken[EMAX];
+// Finish token t from its E raw dot products, held in shared memory lg[0, E):
+// logits (bias, chunk bias, masked experts -inf), stable descending top-k (the
+// smaller expert id wins ties), gates per gate_mode; writes expert_ids / gates
+// of row t and counts every choice in sel_counts (shared, or nullptr).  One
+// thread; sel is 8 ints of this thread's shared scratch.  The loops stay
+// rolled: the code runs once per token, largely from a cold instruction
+// cache, so its size matters more than its loop overhead.
+__device__ inline void router_finish(const RouterParams& p, const float* bias, const float* chunk_bias,
+                                     const uint8_t* block_mask, int t, float* lg, int* sel, int* sel_counts) {
+  const int E = p.experts, k = p.top_k;
   const float ninf = -__int_as_float(0x7f800000);
-#pragma unroll
-  for (int e = 0; e < EMAX; ++e) {
-    taken[e] = false;
-    if (e < E) {
-      float l = acc[e] + bias[e] + (chunk_bias ? chunk_bias[e] : 0.f);
-      const bool masked = (p.mask_mode == 1 && e == (t % E)) || (block_mask && block_mask[e]);
-      logit[e] = masked ? ninf : l;
-    } else {
-      logit[e] = ninf;
-    }
-  }
-  // The choice loop stays rolled (unrolled over k x EMAX it makes compile time
-  // explode); the k <= 8 choices land in register slots through unrolled
-  // compare-and-select, never at a run-time index (that would put them in local
-  // memory, which misses L1 when the kernel holds most of shared memory).
-  float sel_logit[8];
-  int sel[8];
-#pragma unroll
-  for (int s = 0; s < 8; ++s) { sel[s] = -1; sel_logit[s] = ninf; }
 #pragma unroll 1
-  for (int j = 0; j < p.top_k; ++j) {
+  for (int e = 0; e < E; ++e) {
+    const float l = lg[e] + bias[e] + (chunk_bias ? chunk_bias[e] : 0.f);
+    const bool masked = (p.mask_mode == 1 && e == (t % E)) || (block_mask && block_mask[e]);
+    lg[e] = masked ? ninf : l;
+  }
+  unsigned long long taken = 0;  // E <= 64
+#pragma unroll 1
+  for (int j = 0; j < k; ++j) {
     int best = -1;
     float bv = ninf;
-#pragma unroll
-    for (int e = 0; e < EMAX; ++e)
-      if (e < E && !taken[e] && (best < 0 || logit[e] > bv)) { best = e; bv = logit[e]; }
-#pragma unroll
-    for (int e = 0; e < EMAX; ++e)
-      if (e == best) taken[e] = true;
-#pragma unroll
-    for (int s = 0; s < 8; ++s)
-      if (s == j) { sel[s] = best; sel_logit[s] = bv; }
+#pragma unroll 1
+    for (int e = 0; e < E; ++e)
+      if (!((taken >> e) & 1ull) && (best < 0 || lg[e] > bv)) { best = e; bv = lg[e]; }
+    taken |= 1ull << best;
+    sel[j] = best;
+    p.expert_ids[(long long)t * k + j] = best;
+    if (sel_counts) atomicAdd(&sel_counts[best], 1);
   }
-  const int k = p.top_k;
-  float g[8];
+  const float l0 = lg[sel[0]];
+  float sum = 1.f;
   if (p.gate_mode == 1) {
-    float sum = 0.f;
-#pragma unroll
-    for (int s = 0; s < 8; ++s)
-      if (s < k) { g[s] = __expf(sel_logit[s] - sel_logit[0]); sum += g[s]; }
-#pragma unroll
-    for (int s = 0; s < 8; ++s) g[s] = s < k ? g[s] / sum : 0.f;
+    sum = 0.f;
+#pragma unroll 1
+    for (int j = 0; j < k; ++j) sum += __expf(lg[sel[j]] - l0);
   } else if (p.gate_mode == 2) {
-    float mx = sel_logit[0], sum = 0.f;
-#pragma unroll
-    for (int e = 0; e < EMAX; ++e)
-      if (e < E && logit[e] != ninf) sum += __expf(logit[e] - mx);
-#pragma unroll
-    for (int s = 0; s < 8; ++s) g[s] = s < k ? __expf(sel_logit[s] - mx) / sum : 0.f;
-  } else {
-#pragma unroll
-    for (int s = 0; s < 8; ++s) g[s] = 1.f;
+    sum = 0.f;
+#pragma unroll 1
+    for (int e = 0; e < E; ++e)
+      if (lg[e] != ninf) sum += __expf(lg[e] - l0);
   }
-#pragma unroll
-  for (int s = 0; s < 8; ++s) {
-    if (s < k) {
-      p.expert_ids[(long long)t * k + s] = sel[s];
-      p.gates[(long long)t * k + s] = g[s];
-      if (sel_out) sel_out[s] = sel[s];
-    }
-  }
+#pragma unroll 1
+  for (int j = 0; j < k; ++j)
+    p.gates[(long long)t * k + j] = p.gate_mode == 0 ? 1.f : __expf(lg[sel[j]] - l0) / sum;
 }
 
 // ---------------------------------------------------------------------------
 // Router of one token (warp collective): logits = x_t . W_e + b_e (+ chunk
 // bias), masked experts -inf, stable descending top-k (the smaller expert id
-// wins ties), gates per gate_mode; writes expert_ids / gates of row t.
-// Lane 0 returns the selected experts in sel_out[0..k).
-// SMEM_W: w points at a shared-memory copy of the weights.
+// wins ties), gates per gate_mode; writes expert_ids / gates of row t and
+// counts the choices in sel_counts (shared, or nullptr).  s_lg: EMAX + 8 words
+// of this warp's shared scratch.  SMEM_W: w points at a shared-memory copy of
+// the weights.
 // ---------------------------------------------------------------------------
 template <typename T, int EMAX, bool SMEM_W>
 __device__ __forceinline__ void router_token(const RouterParams& p, const float* chunk_bias, int t,
-                                             const T* __restrict__ w, int* sel_out) {
+                                             const T* __restrict__ w, float* s_lg, int* sel_counts) {
   const T* __restrict__ tokens = (const T*)p.tokens;
   const int D = p.hidden, E = p.experts;
   const int lane = threadIdx.x & 31;
@@ -253,7 +230,10 @@ __device__ __forceinline__ void router_token(const RouterParams& p, const float*
     }
   }
   if (lane != 0) return;
-  router_finish<EMAX>(p, p.bias, chunk_bias, p.block_mask, t, acc, sel_out);
+#pragma unroll
+  for (int e = 0; e < EMAX; ++e)
+    if (e < E) s_lg[e] = acc[e];
+  router_finish(p, p.bias, chunk_bias, p.block_mask, t, s_lg, reinterpret_cast<int*>(s_lg + EMAX), sel_counts);
 }
 
 // Recursive-halving transpose reduction: each lane enters with 32 partial
@@ -300,7 +280,8 @@ template <typename T, int NT, int EP>
 __device__ __forceinline__ void router_group(const RouterParams& p, const float* bias, const float* chunk_bias,
                                              const uint8_t* block_mask, int t_first, int nt, float* red,
                                              int* sel_counts, const uint4 (&wpre)[EP], bool use_wpre,
-                                             const DigestSink* dsink = nullptr, const T* srows = nullptr) {
+                                             const DigestSink* dsink = nullptr, const T* srows = nullptr,
+                                             unsigned long long* dbg = nullptr) {
   static_assert(NT * EP == 32, "one (token, expert) sum per lane");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int D = p.hidden, E = p.experts;
@@ -342,7 +323,11 @@ __device__ __forceinline__ void router_group(const RouterParams& p, const float*
       }
     }
   }
+  // dbg (diagnostics, thread 0): %globaltimer after the products, the warp
+  // reduction, the first barrier and the top-k
+  if (dbg != nullptr && threadIdx.x == 0) dbg[0] = globaltimer_ns();
   warp_transpose_reduce32(v);
+  if (dbg != nullptr && threadIdx.x == 0) dbg[1] = globaltimer_ns();
   red[warp * 32 + lane] = v[0];
   if (dsink != nullptr) {
 #pragma unroll
@@ -354,6 +339,7 @@ __device__ __forceinline__ void router_group(const RouterParams& p, const float*
     }
   }
   __syncthreads();
+  if (dbg != nullptr && threadIdx.x == 0) dbg[2] = globaltimer_ns();
   if (dsink != nullptr && warp == 1 && lane < nt) {  // warp 0 runs the top-k below
     uint64_t a = 0;
 #pragma unroll
@@ -371,17 +357,12 @@ __device__ __forceinline__ void router_group(const RouterParams& p, const float*
     __syncwarp();
     red[lane] = tot;
     __syncwarp();
-    if (lane < nt) {
-      float acc[EP];
-#pragma unroll
-      for (int e = 0; e < EP; ++e) acc[e] = red[lane * EP + e];
-      int sel[8];
-      router_finish<EP>(p, bias, chunk_bias, block_mask, t_first + lane, acc, sel);
-      if (sel_counts)
-#pragma unroll
-        for (int s = 0; s < 8; ++s)
-          if (s < p.top_k) atomicAdd(&sel_counts[sel[s]], 1);
-    }
+    // token `lane` finishes in place from red[lane EP, lane EP + E), with 8
+    // words of scratch behind the sums (the warps' partials are all read)
+    if (lane < nt)
+      router_finish(p, bias, chunk_bias, block_mask, t_first + lane, red + lane * EP,
+                    reinterpret_cast<int*>(red + 32 + lane * 8), sel_counts);
+    if (dbg != nullptr && lane == 0) dbg[3] = globaltimer_ns();
   }
   __syncthreads();
 }
@@ -457,9 +438,11 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
   const int k = d.top_k;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   if (!indexed) dispatch_index(p, t0, a, b, hist, run, item_pos);
-  // copy features + identity rows, one warp per item
   const long long nitems = (long long)(b - a) * k;
-  const int vec_per_row = d.hidden * d.feat_bytes / 16;
+  const long long row_bytes = (long long)d.hidden * d.feat_bytes;
+  const int vec_per_row = (int)(row_bytes / 16);
+  // identity rows, one warp per item (small stores; an item whose row falls
+  // outside the receive region records the status here and is skipped below)
   for (long long li = warp; li < nitems; li += nwarps) {
     const long long i = (long long)a * k + li;
     const int t = (int)(i / k), j = (int)(i % k);
@@ -467,38 +450,16 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
     const int e = (int)((unsigned)packed >> 24);
     const int r = expert_owner(d, e), le = expert_slot(d, e);
     const long long row = (long long)base_e[e] + hist[e] + (packed & 0xFFFFFF);
-    // the identity fields' global loads go out before the row copy
-    long long pre = 0;
-    float gate = 1.f;
-    if (lane == 0) pre = p.token_ids[t];
-    else if (lane == 7) pre = p.feat_digest[t];
-    else if (lane == 8) pre = p.checksum_base[t];
-    else if (lane == 17 && d.gate_mode) gate = p.gates[i];
     if (row >= d.cap || r >= d.world || le >= d.expert_slots) {
       if (lane == 0) record_status(p.status, kBoundsViolation, 21, row, d.cap);
       continue;
     }
     const long long grow = ((long long)le * d.world + d.rank) * d.cap + row;
     uint8_t* base = (uint8_t*)p.peers.base[r];
-    uint4* dst = (uint4*)(base + p.layout.recv_feat + grow * d.hidden * d.feat_bytes);
-    const uint4* src = (const uint4*)((const uint8_t*)p.tokens + (long long)t * d.hidden * d.feat_bytes);
-    constexpr int U = 8;  // 16-byte loads in flight per lane before the stores
-    for (int v0 = 0; v0 < vec_per_row; v0 += 32 * U) {
-      uint4 rr[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int v = v0 + u * 32 + lane;
-        // rows streamed in during the launch are read through L2 only; resident
-        // rows through the read-only path (the second choice of a token hits L1)
-        if (v < vec_per_row) rr[u] = streamed ? __ldcg(src + v) : __ldg(src + v);
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int v = v0 + u * 32 + lane;
-        if (v < vec_per_row) dst[v] = rr[u];
-      }
-    }
     if (lane < kFwdMetaFields) {
+      long long pre = 0;
+      if (lane == 0 || lane == 8) pre = lane == 0 ? p.token_ids[t] : p.checksum_base[t];
+      else if (lane == 7) pre = p.feat_digest[t];
       int c = 0;
       while (c + 1 < nc && s_coff[c + 1] <= t) ++c;
       while (c + 1 < d.chunks && p.chunk_offsets[c + 1] <= t) ++c;  // beyond the staged table
@@ -523,8 +484,46 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
     } else if (lane == 16) {
       ((int*)(base + p.layout.recv_retrow))[grow] = t * k + j;
     } else if (lane == 17) {
-      ((float*)(base + p.layout.recv_gate))[grow] = gate;
+      ((float*)(base + p.layout.recv_gate))[grow] = d.gate_mode ? p.gates[i] : 1.f;
     }
+  }
+  // feature rows: the share's items as one run of 16-byte vectors copied by the
+  // whole CTA, U loads in flight per thread before their stores, so the copy
+  // keeps as many bytes in flight as the registers allow across item ends
+  // (32-bit index arithmetic: a share holds at most kDispatchMaxItems items;
+  // a row of a power-of-two number of vectors is split with shifts)
+  constexpr int U = 12;
+  const int nvec = (int)nitems * vec_per_row;
+  const bool pow2 = (vec_per_row & (vec_per_row - 1)) == 0;
+  const int vshift = __ffs(vec_per_row) - 1;
+  for (int g0 = threadIdx.x; g0 < nvec; g0 += U * (int)blockDim.x) {
+    uint4 rr[U];
+    uint4* dsts[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int g = g0 + u * (int)blockDim.x;
+      dsts[u] = nullptr;
+      if (g < nvec) {
+        const int li = pow2 ? g >> vshift : g / vec_per_row;
+        const int v = g - li * vec_per_row;
+        const int t = a + li / k;
+        const int packed = item_pos[li];
+        const int e = (int)((unsigned)packed >> 24);
+        const int r = expert_owner(d, e), le = expert_slot(d, e);
+        const long long row = (long long)base_e[e] + hist[e] + (packed & 0xFFFFFF);
+        if (row < d.cap && r < d.world && le < d.expert_slots) {
+          const long long grow = ((long long)le * d.world + d.rank) * d.cap + row;
+          dsts[u] = (uint4*)((uint8_t*)p.peers.base[r] + p.layout.recv_feat + grow * row_bytes) + v;
+          const uint4* src = (const uint4*)((const uint8_t*)p.tokens + (long long)t * row_bytes) + v;
+          // rows streamed in during the launch are read through L2 only; resident
+          // rows through the read-only path (the second choice of a token hits L1)
+          rr[u] = streamed ? __ldcg(src) : __ldg(src);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (dsts[u] != nullptr) *dsts[u] = rr[u];
   }
 }
 

@@ -168,7 +168,7 @@ struct FrontendParams {
   unsigned long long timeout_ns;
   TraceSlot* phase_trace;   // [C + 2 n_desc]: router c, control q, dispatch q; or nullptr
   TraceSlot* trace;         // the launch
-  unsigned long long* cta_clock;  // [grid, 64] per-CTA %globaltimer stamps, or nullptr
+  unsigned long long* cta_clock;  // [grid, 128] per-CTA %globaltimer stamps (diagnostics), or nullptr
   // Per-token feature digests and checksum bases written by the workers while
   // they route (null: precomputed by the digest / checksum-base kernels).
   long long* digest_out;    // [T]

@@ -8,12 +8,14 @@
 // from global memory at every trigger.  Here the grid (one CTA per SM) stays
 // resident for the whole front end:
 //
-//   CTA 0, warp 0 — the control plane (control_warp.cuh) for triggers 0..n_desc-1.
-//       Plan and scheduler state stay in shared memory across triggers.  Before
-//       trigger q it waits (bounded) until every worker CTA has finished the
-//       router chunks q depends on.  After it, the warp turns the chunks' per-expert
-//       router counts into the descriptor's receive bases and counts and
-//       releases desc_ready[q] = epoch.
+//   CTA 0, warp 0 — the control plane (control_warp_packed.cuh, or
+//       control_warp.cuh when the plan does not fit the packed path) for
+//       triggers 0..n_desc-1.  Plan and scheduler state stay in shared memory
+//       across triggers.  Before trigger q it waits (bounded) until the router
+//       chunks q depends on are routed.  After it, it hands the decision to
+//       warp 1, which turns the chunks' per-expert router counts into the
+//       descriptor's receive bases and counts, writes the permit and releases
+//       desc_ready[q] = epoch while warp 0 goes on with the next trigger.
 //   CTAs 1..W — workers.  For each router chunk: route a share of its tokens
 //       (groups of tokens per CTA, or one warp per token for more than 32
 //       experts), add the per-expert counts, and add the routed units to
@@ -85,8 +87,9 @@ __device__ __forceinline__ void trace_end(TraceSlot* s) {
 }
 
 // Per-CTA timeline (diagnostics): stamp k of this CTA, thread 0 only.
+constexpr int kCtaClockSlots = 128;  // stamps per CTA in FrontendParams::cta_clock
 __device__ __forceinline__ void cta_stamp(const FrontendParams& f, int k) {
-  if (f.cta_clock != nullptr && threadIdx.x == 0) f.cta_clock[(long long)blockIdx.x * 64 + k] = globaltimer_ns();
+  if (f.cta_clock != nullptr && threadIdx.x == 0) f.cta_clock[(long long)blockIdx.x * kCtaClockSlots + k] = globaltimer_ns();
 }
 
 // Routing work is dealt out over the workers as one sequence across chunks:
@@ -115,13 +118,28 @@ __device__ __forceinline__ int chunk_units(const int* s_coff, int c, int unit) {
 __device__ __forceinline__ int trigger_first_chunk(int q, int P) { return q < P ? q : P; }
 __device__ __forceinline__ int trigger_last_chunk(int q, int P, int C) { return q < P ? q : C - 1; }
 
+__device__ __forceinline__ void st_release_cta_shared_s32(int* p, int v) {
+  asm volatile("st.release.cta.shared.s32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_cta_shared_s32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.cta.shared.s32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+
+// Hand-off words from the control warp to the publisher warp, one per descriptor.
+constexpr int kPubNone = 0, kPubPermitted = 1, kPubDenied = 2, kPubStop = 3;
+
 // Control-warp hooks.  before(q): wait (bounded) for the router chunks trigger q
 // needs, then, in one round trip, fetch the control-token destinations and the
 // per-expert router counts of EVERY chunk complete by now into shared memory,
-// so later triggers usually read no global memory.  after(q): turn the chunks'
-// counts into the descriptor's receive bases and counts, then release it.
+// so later triggers usually read no global memory.  after(q): hand the
+// decision to the publisher warp (publish_descriptors), which writes the
+// permit, the descriptor's receive bases and counts and releases it, so the
+// release's memory fence is not on the control warp's chain of triggers.
 struct FrontHooks {
   static constexpr bool kFetchesTokens = true;
+  static constexpr bool kPublishesPermit = true;
   const FrontendParams* f;
   int workers, P, C, E;
   unsigned long long epoch;
@@ -132,6 +150,7 @@ struct FrontHooks {
   int cpc;
   int chunks_ready;    // chunks [0, chunks_ready) complete and fetched
   int unit;            // tokens per routing unit
+  int* s_pub;          // [n_desc] hand-off words to the publisher warp (shared)
 
   __device__ bool before(int q) {
     const int lane = threadIdx.x & 31;
@@ -197,6 +216,43 @@ struct FrontHooks {
 
   __device__ void after(int q, bool permitted) {
     const int lane = threadIdx.x & 31;
+    if (q < 16) cta_stamp(*f, 3 + 2 * q);
+    if (lane == 0) {
+      if (f->phase_trace) trace_end(&f->phase_trace[C + q]);
+      // the warp barrier before after() ordered every lane's shared-memory
+      // writes (router counts fetched by before()); the release makes them
+      // visible to the publisher warp with the decision
+      st_release_cta_shared_s32(&s_pub[q], permitted ? kPubPermitted : kPubDenied);
+    }
+    __syncwarp();
+  }
+};
+
+// Publisher warp of the control CTA: for each descriptor in order, wait
+// (bounded) for the control warp's decision, then write the permit word, the
+// descriptor's receive bases and per-expert counts, and release desc_ready[q].
+// s_sent (rows already assigned per expert) is this warp's alone.
+__device__ void publish_descriptors(const FrontendParams& f, int P, int C, int E, int n_desc, unsigned long long epoch,
+                                    const int* s_pub, int* s_sent, const int* s_ccount) {
+  const int lane = threadIdx.x & 31;
+  #pragma unroll 1
+  for (int q = 0; q < n_desc; ++q) {
+    int st = kPubNone;
+    if (lane == 0) {
+      const uint64_t deadline = globaltimer_ns() + f.timeout_ns;
+      #pragma unroll 1
+      while ((st = ld_acquire_cta_shared_s32(&s_pub[q])) == kPubNone) {
+        if (globaltimer_ns() > deadline) {
+          record_status(f.dp.status, kTimeoutPermit, kFrontKernelId + 3, q, 0);
+          st = kPubStop;
+          break;
+        }
+      }
+    }
+    st = __shfl_sync(0xffffffffu, st, 0);
+    __syncwarp();  // lane 0's acquire orders the other lanes' reads below
+    if (st == kPubStop) return;
+    const bool permitted = st == kPubPermitted;
     const int c_lo = trigger_first_chunk(q, P), c_hi = trigger_last_chunk(q, P, C);
     #pragma unroll 1
     for (int e = lane; e < E; e += 32) {
@@ -204,21 +260,18 @@ struct FrontHooks {
       #pragma unroll 1
       for (int c = c_lo; c <= c_hi; ++c) cnt += s_ccount[c * E + e];
       const int base = s_sent[e];
-      f->disp_base[(long long)q * E + e] = base;
-      f->dp.desc_counts[(long long)q * E + e] = permitted ? cnt : 0;
+      f.disp_base[(long long)q * E + e] = base;
+      f.dp.desc_counts[(long long)q * E + e] = permitted ? cnt : 0;
       if (permitted) s_sent[e] = base + cnt;
     }
+    if (lane == 0) f.cp.permit[q] = permitted ? epoch : 0ULL;
     __syncwarp();
-    if (q < 16) cta_stamp(*f, 3 + 2 * q);
-    if (lane == 0) {
-      if (f->phase_trace) trace_end(&f->phase_trace[C + q]);
-      // the warp barrier above orders every lane's stores (bases, counts,
-      // permit, log) before this release, which publishes them at gpu scope
-      st_release_gpu_u64(&f->desc_ready[q], epoch);
-    }
+    // the warp barrier orders every lane's stores (permit, bases, counts)
+    // before this release, which publishes them at gpu scope
+    if (lane == 0) st_release_gpu_u64(&f.desc_ready[q], epoch);
     __syncwarp();
   }
-};
+}
 
 // One worker's share of descriptor q (collective over the CTA).
 template <typename T>
@@ -379,18 +432,27 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
                                       dims.E, s_egmask);
       __syncthreads();
     }
+    __shared__ int s_pub[ctl::kCtlMaxChunks];
+    for (int q = threadIdx.x; q < ctl::kCtlMaxChunks; q += blockDim.x) s_pub[q] = kPubNone;
+    __syncthreads();
+    int* s_ccount = reinterpret_cast<int*>(fsm + ((Lt.total + 15) & ~15LL));
     if (threadIdx.x < 32) {
-      int* s_ccount = reinterpret_cast<int*>(fsm + ((Lt.total + 15) & ~15LL));
       FrontHooks hooks{&f, W, f.cp.partial_chunks, C, E, epoch, hist, s_dst, s_ccoff, s_ccount,
-                       f.cp.ctl_per_chunk, 0, NT > 0 ? NT : 1};
+                       f.cp.ctl_per_chunk, 0, NT > 0 ? NT : 1, s_pub};
       if (packed && !s_dup)
         ctl::control_warp_run_packed(f.cp, dims, fsm, s_dst, s_ccoff, s_egmask, pv, 0, n_desc, hooks);
       else
         ctl::control_warp_run(f.cp, dims, fsm, s_dst, s_ccoff, s_egmask, 0, n_desc, true, hooks, s_vmc);
       __syncwarp();
-      for (int e = threadIdx.x; e < E; e += 32) f.dp.sent_base[e] = hist[e];
+      // descriptors the control warp did not reach (a wait ran out) release nothing
+      if (threadIdx.x == 0)
+        for (int q = 0; q < n_desc; ++q)
+          if (ld_acquire_cta_shared_s32(&s_pub[q]) == kPubNone) st_release_cta_shared_s32(&s_pub[q], kPubStop);
+    } else if (threadIdx.x < 64) {
+      publish_descriptors(f, f.cp.partial_chunks, C, E, n_desc, epoch, s_pub, hist, s_ccount);
     }
     __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) f.dp.sent_base[e] = hist[e];
     ctl::copy16(reinterpret_cast<uint4*>(f.cp.blob + Lt.state_begin),
                 reinterpret_cast<const uint4*>(fsm + Lt.state_begin), (Lt.state_end - Lt.state_begin) / 16);
     return;
@@ -429,7 +491,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   if (f.cta_clock != nullptr && threadIdx.x == 0) {  // diagnostics: what this CTA saw at its start
     unsigned int smid;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-    unsigned long long* row = f.cta_clock + (long long)blockIdx.x * 64;
+    unsigned long long* row = f.cta_clock + (long long)blockIdx.x * kCtaClockSlots;
     row[18] = smid;
     row[19] = ready_all;
     row[20] = epoch;
@@ -577,8 +639,13 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
           srows = reinterpret_cast<const T*>(ring_base + slot * unit_bytes);
           if (consumed == 0) cta_stamp(f, 21);  // first group in shared memory
         }
+        // diagnostics: the first and second groups' phases in stamps 40..43 and 64..67
+        unsigned long long* dbg =
+            (f.cta_clock == nullptr || !ring || consumed > 1)
+                ? nullptr
+                : f.cta_clock + (long long)blockIdx.x * kCtaClockSlots + (consumed == 0 ? 40 : 64);
         router_group<T, NT, EP>(f.rp, s_rbias, cbias, f.rp.block_mask ? s_rmask : nullptr, tf, min(NT, t1 - tf),
-                                red, run, wpre, use_wpre, digest ? &dsink : nullptr, srows);
+                                red, run, wpre, use_wpre, digest ? &dsink : nullptr, srows, dbg);
         if (ring && consumed == 0) cta_stamp(f, 22);  // first group routed
         if (ring) {  // router_group ended on a CTA barrier: the slot is free again
           if (threadIdx.x == 0) issue_next();
@@ -587,15 +654,11 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       }
       cum_units += ngroups;
     } else {
+      __shared__ float s_lg[8][EMAX + 8];  // per-warp logit scratch of router_token
       const int nvec_tok = f.rp.hidden * (int)sizeof(T) / 16;
       const int slots = W * nwarps;
       for (int t = t0 + first_share(w * nwarps + warp, cum_units, slots); t < t1; t += slots) {
-        int sel[8];
-        router_token<T, EMAX, false>(f.rp, cbias, t, wts, sel);
-        if (lane == 0)
-#pragma unroll
-          for (int s = 0; s < 8; ++s)
-            if (s < f.rp.top_k) atomicAdd(&run[sel[s]], 1);
+        router_token<T, EMAX, false>(f.rp, cbias, t, wts, s_lg[warp], run);
         if (digest) {
           const long long dg = warp_row_digest((const uint4*)((const T*)f.rp.tokens + (long long)t * f.rp.hidden),
                                                nvec_tok);
@@ -650,6 +713,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   }
   if (!dispatcher) return;  // routing done: this SM is free for the expert side
   if (f.delayed && wait_released(f, n_desc - 1, epoch, &s_flag, true) != 1) return;
+  int n_indexed = 0;  // descriptors whose index part ran before their release (diagnostics)
   while (next < my_q1) {
     // a descriptor not yet released whose chunks are routed: compute its
     // index part (prefix counts and ranks, from the expert ids only) while
@@ -659,11 +723,13 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     if (rel == 0 && chunks_complete(f, next, s_coff, NT > 0 ? NT : 1, &s_flag)) {
       worker_index(f, next, wi, wn, hist, run, item_pos, s_coff);
       indexed = true;
+      ++n_indexed;
     }
     if (rel != 1 && wait_released(f, next, epoch, &s_flag, true) != 1) return;
     worker_dispatch<T>(f, next, wi, wn, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident, indexed);
     ++next;
   }
+  if (f.cta_clock != nullptr && threadIdx.x == 0) f.cta_clock[(long long)blockIdx.x * kCtaClockSlots + 23] = 1 + n_indexed;
 }
 
 template <typename T, int NT, int EP, int EMAX>

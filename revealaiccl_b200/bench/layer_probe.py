@@ -77,7 +77,7 @@ def main() -> None:
     try:
         if args.cta_clocks:
             sms = torch.cuda.get_device_properties(layer.device).multi_processor_count
-            layer.tensors["fe_clock"] = torch.zeros(sms * 64, dtype=torch.int64, device=layer.device)
+            layer.tensors["fe_clock"] = torch.zeros(sms * FE_CLOCK_SLOTS, dtype=torch.int64, device=layer.device)
         layer.forward(args.arm)
         if args.graph:
             layer.capture(args.arm)
@@ -181,12 +181,18 @@ def _roofline(layer, evs, before, after) -> dict:
     delta = [{k: after[p][k] - before[p][k] for k in after[p]} for p in range(W)]
     out_bytes = sum(delta[p]["bytes_transferred"] for p in range(W) if p != r)
     ret_bytes = sum(delta[p]["return_bytes"] for p in range(W) if p != r)
-    # per kind: the sum of its launches' (or phases') spans; descriptors are
-    # dispatched one after another, so for the dispatch this is its busy time,
-    # not the time it waits for the scheduler between descriptors
+    # per kind: the sum of its launches' (or phases') spans, and the wall
+    # time from the first start to the last end; descriptors are dispatched
+    # side by side, so the dispatch is measured over its wall time
     us: dict[str, float] = {}
+    first: dict[str, int] = {}
+    last: dict[str, int] = {}
     for e in evs:
-        us[e["kind"]] = us.get(e["kind"], 0.0) + (e["end_ns"] - e["start_ns"]) / 1e3
+        k = e["kind"]
+        us[k] = us.get(k, 0.0) + (e["end_ns"] - e["start_ns"]) / 1e3
+        first[k] = min(first.get(k, e["start_ns"]), e["start_ns"])
+        last[k] = max(last.get(k, e["end_ns"]), e["end_ns"])
+    wall = {k: (last[k] - first[k]) / 1e3 for k in us}
     rows = int(layer.rows_out.sum().item())
     f1 = 2.0 * rows * cfg.hidden * cfg.gemm1_n
     f2 = 2.0 * rows * cfg.ffn_hidden * cfg.out_dim
@@ -197,9 +203,10 @@ def _roofline(layer, evs, before, after) -> dict:
     res = {"rank": r, "peaks": pk, "rows": rows}
     if "dispatch" in us:
         tgt = out_bytes / (pk["nvlink_gbs"] * 1e3)
-        res["dispatch"] = {"nvlink_bytes": out_bytes, "span_us": round(us["dispatch"], 2),
-                           "achieved_gbs": round(out_bytes / (us["dispatch"] * 1e3), 1) if us["dispatch"] else None,
-                           "roofline_us": round(tgt, 2), "fraction": frac(tgt, us["dispatch"])}
+        span = wall["dispatch"]
+        res["dispatch"] = {"nvlink_bytes": out_bytes, "span_us": round(span, 2), "busy_us": round(us["dispatch"], 2),
+                           "achieved_gbs": round(out_bytes / (span * 1e3), 1) if span else None,
+                           "roofline_us": round(tgt, 2), "fraction": frac(tgt, span)}
     if "gemm1" in us:
         tgt = f1 / (tensor_tflops * 1e6)
         res["gemm1"] = {"gflop": round(f1 / 1e9, 2), "span_us": round(us["gemm1"], 2),
@@ -213,6 +220,9 @@ def _roofline(layer, evs, before, after) -> dict:
     return res
 
 
+FE_CLOCK_SLOTS = 128  # per-CTA stamps of the front end (kCtaClockSlots in csrc/kernels/moe_frontend.cu)
+
+
 def _cta_clocks(layer) -> dict:
     """Summarise the front end's per-CTA %globaltimer stamps (us from the first
     worker's start): row 0 is the control CTA (trigger q begin / end at slots
@@ -220,7 +230,7 @@ def _cta_clocks(layer) -> dict:
     3 + 2c, descriptor q begin / rows done / end at 24 + 2q / 44 + q / 25 + 2q)."""
     import numpy as np
 
-    clk = layer.tensors["fe_clock"].cpu().numpy().reshape(-1, 64).astype(np.float64)
+    clk = layer.tensors["fe_clock"].cpu().numpy().reshape(-1, FE_CLOCK_SLOTS).astype(np.float64)
     t0 = clk[1:, 0][clk[1:, 0] > 0].min()
     wk = (clk[1:] - t0) / 1e3
     wk[clk[1:] == 0] = np.nan
@@ -232,6 +242,15 @@ def _cta_clocks(layer) -> dict:
            "first_group": ({"landed_med": r(np.median(wk[first, 21])), "landed_max": r(np.max(wk[first, 21])),
                             "routed_med": r(np.median(wk[first, 22])), "routed_max": r(np.max(wk[first, 22]))}
                            if first.any() else None)}
+    if first.any():  # the first group's router phases (stamps 40..43), us after it landed
+        ph = [r(np.median(wk[first, 40 + i] - wk[first, 21])) for i in range(4)] + \
+             [r(np.median(wk[first, 22] - wk[first, 21]))]
+        out["first_group"]["phases_after_landing"] = dict(zip(
+            ("products", "warp_reduce", "barrier1", "topk", "done"), ph))
+        second = first & ~np.isnan(wk[:, 64]) & ~np.isnan(wk[:, 67]) & (wk[:, 64] > wk[:, 22])
+        if second.any():  # the second group's phases (stamps 64..67), us after the first was routed
+            out["second_group"] = dict(zip(("products", "warp_reduce", "barrier1", "topk"),
+                                           [r(np.median(wk[second, 64 + i] - wk[second, 22])) for i in range(4)]))
     for c in range(min(8, layer.cfg.chunks)):
         b, e, routed = wk[:, 2 + 2 * c], wk[:, 3 + 2 * c], wk[:, 52 + c]
         out["chunks"].append({"chunk": c, "begin_med": r(np.nanmedian(b)), "dur_med": r(np.nanmedian(e - b)),

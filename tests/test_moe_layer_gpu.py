@@ -540,3 +540,33 @@ def test_dispatch_groups_match_shared_dispatch(name):
             layer.close()
     for a, b in zip(res[True], res[False]):
         assert torch.equal(a, b)
+
+
+def test_prereleased_index_and_plain_dispatch_paths_both_run():
+    """A worker whose descriptor is still held computes the descriptor's index
+    part (prefix counts and ranks) before the release and then only copies;
+    a worker whose descriptor is already released does both after it.  The
+    early arm takes the first path for every descriptor still held when its
+    workers reach it, the delayed arm always the second, and both arms leave
+    the same verified output."""
+    from revealaiccl_b200.bench.layer_probe import FE_CLOCK_SLOTS
+    from revealaiccl_b200.moe.config import preset
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    layer = ProgressiveMoELayer(preset("full_tf32"), timeout_s=5.0)
+    try:
+        sms = torch.cuda.get_device_properties(layer.device).multi_processor_count
+        outs, indexed = {}, {}
+        for arm in ("early", "delayed"):
+            layer.tensors["fe_clock"] = torch.zeros(sms * FE_CLOCK_SLOTS, dtype=torch.int64, device=layer.device)
+            layer.forward(arm)
+            assert layer.verify()["pass"], arm
+            stamps = layer.tensors["fe_clock"].cpu().view(sms, FE_CLOCK_SLOTS)[1:, 23]
+            ran = stamps[stamps > 0] - 1  # descriptors indexed before release, per dispatching worker
+            indexed[arm] = (int(ran.sum()), int((ran == 0).sum()), int(ran.numel()))
+            outs[arm] = layer.out.clone()
+        assert indexed["early"][0] > 0, indexed
+        assert indexed["delayed"][0] == 0 and indexed["delayed"][2] > 0, indexed
+        assert torch.equal(outs["early"], outs["delayed"])
+    finally:
+        layer.close()
