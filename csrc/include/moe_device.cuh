@@ -108,16 +108,6 @@ __device__ __forceinline__ long long token_checksum_base(long long token_id, int
   return (long long)acc;
 }
 
-// Where a router pass writes the per-token digests and checksum bases of the
-// rows it reads (tokens of router chunk `chunk`, which starts at chunk_first).
-struct DigestSink {
-  long long* digest;
-  long long* csbase;
-  const long long* token_ids;
-  int rank, chunk, chunk_first;
-  unsigned long long* red;  // shared scratch: 8 warps x NT partial sums
-};
-
 constexpr int kRouterUnroll = 8;
 constexpr int kDispatchMaxItems = 4096;
 constexpr int kMaxExperts = 256;
@@ -178,28 +168,32 @@ __device__ inline void router_finish(const RouterParams& p, const float* bias, c
 // Router of one token (warp collective): logits = x_t . W_e + b_e (+ chunk
 // bias), masked experts -inf, stable descending top-k (the smaller expert id
 // wins ties), gates per gate_mode; writes expert_ids / gates of row t and
-// counts the choices in sel_counts (shared, or nullptr).  s_lg: EMAX + 8 words
-// of this warp's shared scratch.  SMEM_W: w points at a shared-memory copy of
-// the weights.
+// counts the choices in sel_counts (shared, or nullptr).  x: the token's row,
+// in shared memory (x_shared) or in global memory.  s_lg: EMAX + 8 words of
+// this warp's shared scratch.  SMEM_W: w points at a shared-memory copy of the
+// weights.  Every lane sums its vectors in row order, then a butterfly adds
+// the lanes: the same order wherever the row comes from.
 // ---------------------------------------------------------------------------
 template <typename T, int EMAX, bool SMEM_W>
-__device__ __forceinline__ void router_token(const RouterParams& p, const float* chunk_bias, int t,
-                                             const T* __restrict__ w, float* s_lg, int* sel_counts) {
-  const T* __restrict__ tokens = (const T*)p.tokens;
+__device__ __forceinline__ void router_token(const RouterParams& p, const float* chunk_bias, int t, const T* x,
+                                             bool x_shared, const T* __restrict__ w, float* s_lg, int* sel_counts) {
   const int D = p.hidden, E = p.experts;
   const int lane = threadIdx.x & 31;
   constexpr int VEC = 16 / sizeof(T);
   float acc[EMAX];
 #pragma unroll
   for (int e = 0; e < EMAX; ++e) acc[e] = 0.f;
-  const T* x = tokens + (long long)t * D;
   constexpr int STEP = 32 * VEC * kRouterUnroll;
   for (int base0 = 0; base0 < D; base0 += STEP) {
     uint4 xr[kRouterUnroll];
 #pragma unroll
     for (int u = 0; u < kRouterUnroll; ++u) {
       const int base = base0 + (u * 32 + lane) * VEC;
-      xr[u] = base < D ? __ldcg((const uint4*)(x + base)) : make_uint4(0, 0, 0, 0);
+      // a row in shared memory, or in global memory read through L2 only
+      // (streamed rows land while the launch runs)
+      xr[u] = base >= D  ? make_uint4(0, 0, 0, 0)
+              : x_shared ? *(const uint4*)(x + base)
+                         : __ldcg((const uint4*)(x + base));
     }
 #pragma unroll
     for (int u = 0; u < kRouterUnroll; ++u) {
@@ -234,137 +228,6 @@ __device__ __forceinline__ void router_token(const RouterParams& p, const float*
   for (int e = 0; e < EMAX; ++e)
     if (e < E) s_lg[e] = acc[e];
   router_finish(p, p.bias, chunk_bias, p.block_mask, t, s_lg, reinterpret_cast<int*>(s_lg + EMAX), sel_counts);
-}
-
-// Recursive-halving transpose reduction: each lane enters with 32 partial
-// sums v[0..31]; lane L leaves with the warp total of index L in v[0]
-// (5 exchange steps, 31 shuffles in all).
-__device__ __forceinline__ void warp_transpose_reduce32(float (&v)[32]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int s = 16; s >= 1; s >>= 1) {
-    const bool upper = (lane & s) != 0;
-#pragma unroll
-    for (int i = 0; i < s; ++i) {
-      const float send = upper ? v[i] : v[i + s];
-      const float recv = __shfl_xor_sync(0xffffffffu, send, s);
-      v[i] = (upper ? v[i + s] : v[i]) + recv;
-    }
-  }
-}
-
-// Whether router_group handles this shape: E <= 32 experts and a row of
-// 16-byte vectors that splits evenly over a CTA's 8 warps.
-__host__ __device__ __forceinline__ bool router_group_ok(int experts, int hidden, int elem_bytes) {
-  const int nv = hidden * elem_bytes / 16;
-  return experts <= 32 && (hidden * elem_bytes) % 16 == 0 && nv % 8 == 0 && nv > 0;
-}
-
-// Router of NT consecutive tokens [t_first, t_first + nt) by one CTA of 8 warps
-// (NT * EP = 32, EP >= experts): the hidden dimension is split over the warps;
-// every lane accumulates NT x EP partial dot products from 16-byte vectors, so
-// each weight vector is loaded once for all NT tokens; a transpose reduction
-// leaves one (token, expert) sum per lane; the 8 warp partials are added in
-// warp order; lane j of warp 0 finishes token j.  sel_counts (shared, per
-// expert, or nullptr) counts the selected experts.  Collective over the CTA;
-// red is 256 floats of shared scratch.
-//
-// wpre (optional): this lane's weight vectors wpre[e] = W_e[warp * 32 + lane]
-// when a row has exactly 8 x 32 vectors, held in registers across calls;
-// bias / block_mask: global or shared copies of the router tables.
-// srows (optional): the group's nt token rows already in shared memory
-// (landed there by a bulk copy), read instead of global memory.
-// Inlined into its callers so that wpre stays in registers (an array whose
-// address reaches a call lives in local memory).
-template <typename T, int NT, int EP>
-__device__ __forceinline__ void router_group(const RouterParams& p, const float* bias, const float* chunk_bias,
-                                             const uint8_t* block_mask, int t_first, int nt, float* red,
-                                             int* sel_counts, const uint4 (&wpre)[EP], bool use_wpre,
-                                             const DigestSink* dsink = nullptr, const T* srows = nullptr,
-                                             unsigned long long* dbg = nullptr) {
-  static_assert(NT * EP == 32, "one (token, expert) sum per lane");
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int D = p.hidden, E = p.experts;
-  constexpr int VEC = 16 / sizeof(T);
-  const int vpw = D / VEC / 8;
-  const T* __restrict__ tok = (const T*)p.tokens;
-  const T* __restrict__ w = (const T*)p.weight;
-  float v[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = 0.f;
-  uint64_t dg[NT];  // digest partial sums of the group's rows (with a sink only)
-#pragma unroll
-  for (int j = 0; j < NT; ++j) dg[j] = 0;
-  for (int vi = warp * vpw + lane; vi < (warp + 1) * vpw; vi += 32) {
-    uint4 x[NT];
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-      x[j] = j >= nt  ? make_uint4(0, 0, 0, 0)
-             : srows ? reinterpret_cast<const uint4*>(srows + (long long)j * D)[vi]
-                     : __ldcg((const uint4*)(tok + (long long)(t_first + j) * D) + vi);
-    if (dsink != nullptr) {
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-        if (j < nt) dg[j] += digest_vec(x[j], vi);
-    }
-#pragma unroll
-    for (int e = 0; e < EP; ++e) {
-      if (e < E) {
-        const uint4 wr = use_wpre ? wpre[e] : __ldg((const uint4*)(w + (long long)e * D) + vi);
-        const T* wv = (const T*)&wr;
-#pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          const T* xv = (const T*)&x[j];
-          float s = 0.f;
-#pragma unroll
-          for (int q = 0; q < VEC; ++q) s = fmaf(to_f(xv[q]), to_f(wv[q]), s);
-          v[j * EP + e] += s;
-        }
-      }
-    }
-  }
-  // dbg (diagnostics, thread 0): %globaltimer after the products, the warp
-  // reduction, the first barrier and the top-k
-  if (dbg != nullptr && threadIdx.x == 0) dbg[0] = globaltimer_ns();
-  warp_transpose_reduce32(v);
-  if (dbg != nullptr && threadIdx.x == 0) dbg[1] = globaltimer_ns();
-  red[warp * 32 + lane] = v[0];
-  if (dsink != nullptr) {
-#pragma unroll
-    for (int j = 0; j < NT; ++j) {
-      uint64_t a = dg[j];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-      if (lane == 0) dsink->red[warp * NT + j] = a;
-    }
-  }
-  __syncthreads();
-  if (dbg != nullptr && threadIdx.x == 0) dbg[2] = globaltimer_ns();
-  if (dsink != nullptr && warp == 1 && lane < nt) {  // warp 0 runs the top-k below
-    uint64_t a = 0;
-#pragma unroll
-    for (int w8 = 0; w8 < 8; ++w8) a += dsink->red[w8 * NT + lane];
-    const long long dgt = (long long)(a & ((1ULL << 62) - 1));
-    const int t = t_first + lane;
-    dsink->digest[t] = dgt;
-    dsink->csbase[t] = token_checksum_base(dsink->token_ids[t], dsink->rank, dsink->chunk, t - dsink->chunk_first,
-                                           t, dgt);
-  }
-  if (warp == 0) {
-    float tot = 0.f;
-#pragma unroll
-    for (int w8 = 0; w8 < 8; ++w8) tot += red[w8 * 32 + lane];
-    __syncwarp();
-    red[lane] = tot;
-    __syncwarp();
-    // token `lane` finishes in place from red[lane EP, lane EP + E), with 8
-    // words of scratch behind the sums (the warps' partials are all read)
-    if (lane < nt)
-      router_finish(p, bias, chunk_bias, block_mask, t_first + lane, red + lane * EP,
-                    reinterpret_cast<int*>(red + 32 + lane * 8), sel_counts);
-    if (dbg != nullptr && lane == 0) dbg[3] = globaltimer_ns();
-  }
-  __syncthreads();
 }
 
 // ---------------------------------------------------------------------------
@@ -430,10 +293,23 @@ __device__ inline void dispatch_index(const DispatchParams& p, int t0, int a, in
   __syncthreads();
 }
 
+// Staging area for dispatch_rows: the share's token rows come into shared
+// memory by bulk copies (two halves, double-buffered), so all of a half's
+// bytes are in flight at once, and go out with plain 16-byte stores.
+struct DispatchStage {
+  uint8_t* buf;      // shared memory, 16-byte aligned
+  int bytes;         // size of buf (two halves)
+  uint64_t* bar;     // [2] mbarriers, initialised with count 1
+  uint32_t* uses;    // [2] completed phases of each barrier (shared)
+  unsigned long long timeout_ns;  // bound of each wait for a half
+};
+
 // indexed: hist / run / item_pos already hold dispatch_index's result.
+// stage (optional): stage rows through shared memory (see DispatchStage).
 template <typename T>
 __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, const int* base_e, int* hist, int* run,
-                              int* item_pos, const int* s_coff, int nc, bool streamed = false, bool indexed = false) {
+                              int* item_pos, const int* s_coff, int nc, bool streamed = false, bool indexed = false,
+                              const DispatchStage* stage = nullptr) {
   const MoEDims& d = p.dims;
   const int k = d.top_k;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
@@ -441,6 +317,22 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
   const long long nitems = (long long)(b - a) * k;
   const long long row_bytes = (long long)d.hidden * d.feat_bytes;
   const int vec_per_row = (int)(row_bytes / 16);
+  // staged rows: tokens per half, and the first half's copy issued before the
+  // identity rows so that it is in flight while they are written
+  const int half_rows = stage ? (int)((stage->bytes / 2) / row_bytes) : 0;
+  const bool staged = half_rows > 0 && b > a;
+  auto issue_half = [&](int h, int tb) {  // thread 0: tokens [tb, tb + rows) into half h
+    const int rows = min(half_rows, b - tb);
+    const uint32_t bytes = (uint32_t)(rows * row_bytes);
+    fence_proxy_async_global();  // rows written by generic stores or the copy engine, read by the bulk copy
+    mbar_arrive_expect_tx(&stage->bar[h], bytes);
+    bulk_load_g2s(stage->buf + (long long)h * half_rows * row_bytes,
+                  (const uint8_t*)p.tokens + (long long)tb * row_bytes, bytes, &stage->bar[h]);
+  };
+  if (staged && threadIdx.x == 0) {
+    issue_half(0, a);
+    if (a + half_rows < b) issue_half(1, a + half_rows);
+  }
   // identity rows, one warp per item (small stores; an item whose row falls
   // outside the receive region records the status here and is skipped below)
   for (long long li = warp; li < nitems; li += nwarps) {
@@ -487,43 +379,78 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
       ((float*)(base + p.layout.recv_gate))[grow] = d.gate_mode ? p.gates[i] : 1.f;
     }
   }
-  // feature rows: the share's items as one run of 16-byte vectors copied by the
-  // whole CTA, U loads in flight per thread before their stores, so the copy
-  // keeps as many bytes in flight as the registers allow across item ends
-  // (32-bit index arithmetic: a share holds at most kDispatchMaxItems items;
-  // a row of a power-of-two number of vectors is split with shifts)
-  constexpr int U = 12;
-  const int nvec = (int)nitems * vec_per_row;
-  const bool pow2 = (vec_per_row & (vec_per_row - 1)) == 0;
-  const int vshift = __ffs(vec_per_row) - 1;
-  for (int g0 = threadIdx.x; g0 < nvec; g0 += U * (int)blockDim.x) {
-    uint4 rr[U];
-    uint4* dsts[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int g = g0 + u * (int)blockDim.x;
-      dsts[u] = nullptr;
-      if (g < nvec) {
-        const int li = pow2 ? g >> vshift : g / vec_per_row;
-        const int v = g - li * vec_per_row;
-        const int t = a + li / k;
+  if (staged) {
+    // feature rows from shared memory: batch n holds tokens [a + n half_rows, ...)
+    // in half n % 2; a warp stores one item (token, choice) at a time
+    int n = 0;
+    for (int tb = a; tb < b; tb += half_rows, ++n) {
+      const int h = n & 1;
+      const int rows = min(half_rows, b - tb);
+      mbar_wait_bounded(&stage->bar[h], stage->uses[h] & 1u, p.status, 23, stage->timeout_ns);
+      const uint4* sbase = (const uint4*)(stage->buf + (long long)h * half_rows * row_bytes);
+      for (int li_b = warp; li_b < rows * k; li_b += nwarps) {
+        const long long li = (long long)(tb - a) * k + li_b;
         const int packed = item_pos[li];
         const int e = (int)((unsigned)packed >> 24);
         const int r = expert_owner(d, e), le = expert_slot(d, e);
         const long long row = (long long)base_e[e] + hist[e] + (packed & 0xFFFFFF);
-        if (row < d.cap && r < d.world && le < d.expert_slots) {
-          const long long grow = ((long long)le * d.world + d.rank) * d.cap + row;
-          dsts[u] = (uint4*)((uint8_t*)p.peers.base[r] + p.layout.recv_feat + grow * row_bytes) + v;
-          const uint4* src = (const uint4*)((const uint8_t*)p.tokens + (long long)t * row_bytes) + v;
-          // rows streamed in during the launch are read through L2 only; resident
-          // rows through the read-only path (the second choice of a token hits L1)
-          rr[u] = streamed ? __ldcg(src) : __ldg(src);
-        }
+        if (row >= d.cap || r >= d.world || le >= d.expert_slots) continue;  // recorded above
+        const long long grow = ((long long)le * d.world + d.rank) * d.cap + row;
+        uint4* dst = (uint4*)((uint8_t*)p.peers.base[r] + p.layout.recv_feat + grow * row_bytes);
+        const uint4* src = sbase + (long long)(li_b / k) * vec_per_row;
+        for (int v = lane; v < vec_per_row; v += 32) dst[v] = src[v];
+      }
+      __syncthreads();  // every warp is done with this half
+      if (threadIdx.x == 0) {
+        stage->uses[h] += 1;
+        if (tb + 2 * half_rows < b) issue_half(h, tb + 2 * half_rows);
+      }
+      __syncthreads();
+    }
+    return;
+  }
+  // feature rows: each warp copies two items at a time, eight 16-byte loads
+  // per lane and item in flight before their stores (the item's source and
+  // destination rows are worked out once per item, not per vector)
+  constexpr int U = 8;
+  auto row_ptrs = [&](long long li, const uint4*& src, uint4*& dst) -> bool {
+    const long long i = (long long)a * k + li;
+    const int t = (int)(i / k);
+    const int packed = item_pos[li];
+    const int e = (int)((unsigned)packed >> 24);
+    const int r = expert_owner(d, e), le = expert_slot(d, e);
+    const long long row = (long long)base_e[e] + hist[e] + (packed & 0xFFFFFF);
+    if (row >= d.cap || r >= d.world || le >= d.expert_slots) return false;
+    const long long grow = ((long long)le * d.world + d.rank) * d.cap + row;
+    dst = (uint4*)((uint8_t*)p.peers.base[r] + p.layout.recv_feat + grow * row_bytes);
+    src = (const uint4*)((const uint8_t*)p.tokens + (long long)t * row_bytes);
+    return true;
+  };
+  for (long long la = warp; la < nitems; la += 2LL * nwarps) {
+    const long long lb = la + nwarps;
+    const uint4* sa = nullptr;
+    const uint4* sb = nullptr;
+    uint4* da = nullptr;
+    uint4* db = nullptr;
+    const bool oka = row_ptrs(la, sa, da);
+    const bool okb = lb < nitems && row_ptrs(lb, sb, db);
+    for (int v0 = 0; v0 < vec_per_row; v0 += 32 * U) {
+      uint4 ra[U], rb[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int v = v0 + u * 32 + lane;
+        // rows streamed in during the launch are read through L2 only; resident
+        // rows through the read-only path (the second choice of a token hits L1)
+        if (oka && v < vec_per_row) ra[u] = streamed ? __ldcg(sa + v) : __ldg(sa + v);
+        if (okb && v < vec_per_row) rb[u] = streamed ? __ldcg(sb + v) : __ldg(sb + v);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int v = v0 + u * 32 + lane;
+        if (oka && v < vec_per_row) da[v] = ra[u];
+        if (okb && v < vec_per_row) db[v] = rb[u];
       }
     }
-#pragma unroll
-    for (int u = 0; u < U; ++u)
-      if (dsts[u] != nullptr) *dsts[u] = rr[u];
   }
 }
 

@@ -400,6 +400,12 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* p) {
 // Device-scope acquire-release fetch-add: orders this thread's prior writes
 // (and, through bar.sync, its CTA's) before the increment, and makes every
 // write released by earlier incrementers visible after it.
+// Release reduction: the caller's earlier writes (and those ordered before it
+// by a CTA barrier) become visible to a thread that acquires the counter.
+__device__ __forceinline__ void red_add_release_gpu(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
   int old;
   asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");

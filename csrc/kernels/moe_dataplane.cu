@@ -17,6 +17,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <stdexcept>
 
 #include "launchers.h"
 #include "moe_kernels.h"
@@ -79,21 +80,8 @@ __global__ void __launch_bounds__(256) moe_router_kernel(RouterParams p) {
   const int warps = blockDim.x >> 5;
   const int t = p.row0 + blockIdx.x * warps + (threadIdx.x >> 5);
   if (t >= p.row1) return;
-  router_token<T, EMAX, SMEM_W>(p, p.chunk_bias, t, w, s_lg[threadIdx.x >> 5], nullptr);
-}
-
-// One router chunk with NT tokens per CTA (router_group).  Shapes router_group
-// handles use this kernel in the step pipeline and the same device function in
-// the persistent front end, so both paths compute bit-identical logits.
-template <typename T, int NT, int EP>
-__global__ void __launch_bounds__(256) moe_router_group_kernel(RouterParams p) {
-  TraceScope trace_scope(p.trace);
-  __shared__ float red[256];
-  const int t_first = p.row0 + blockIdx.x * NT;
-  const int nt = min(NT, p.row1 - t_first);
-  if (nt <= 0) return;
-  const uint4 no_wpre[EP] = {};
-  router_group<T, NT, EP>(p, p.bias, p.chunk_bias, p.block_mask, t_first, nt, red, nullptr, no_wpre, false);
+  router_token<T, EMAX, SMEM_W>(p, p.chunk_bias, t, (const T*)p.tokens + (long long)t * p.hidden, false, w,
+                                s_lg[threadIdx.x >> 5], nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -665,20 +653,7 @@ void launch_checksum_base(const long long* token_ids, const long long* digest, c
 void launch_router(const RouterParams& p, bool bf16, cudaStream_t s) {
   const int rows = p.row1 - p.row0;
   if (rows <= 0) return;
-  if (router_group_ok(p.experts, p.hidden, bf16 ? 2 : 4)) {
-#define RAICCL_ROUTER_GROUP(NT, EP)                                                  \
-  do {                                                                               \
-    const dim3 g((rows + NT - 1) / NT);                                              \
-    if (bf16) moe_router_group_kernel<__nv_bfloat16, NT, EP><<<g, 256, 0, s>>>(p);   \
-    else moe_router_group_kernel<float, NT, EP><<<g, 256, 0, s>>>(p);                \
-  } while (0)
-    if (p.experts <= 4) RAICCL_ROUTER_GROUP(8, 4);
-    else if (p.experts <= 8) RAICCL_ROUTER_GROUP(4, 8);
-    else if (p.experts <= 16) RAICCL_ROUTER_GROUP(2, 16);
-    else RAICCL_ROUTER_GROUP(1, 32);
-#undef RAICCL_ROUTER_GROUP
-    return;
-  }
+  if (p.experts > 64) throw std::invalid_argument("the router handles at most 64 experts");
   const int warps = 8;
   const dim3 grid((rows + warps - 1) / warps);
   const long long wbytes = (long long)p.experts * p.hidden * (bf16 ? 2 : 4);

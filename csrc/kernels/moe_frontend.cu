@@ -277,7 +277,8 @@ __device__ void publish_descriptors(const FrontendParams& f, int P, int C, int E
 template <typename T>
 __device__ void worker_dispatch(const FrontendParams& f, int q, int w, int W, unsigned long long epoch,
                                 int* hist, int* run, int* item_pos, int* s_base, const int* s_coff, int nc,
-                                int* s_flag, bool streamed, bool indexed = false) {
+                                int* s_flag, bool streamed, bool indexed = false,
+                                const DispatchStage* stage = nullptr) {
   const MoEDims& d = f.dp.dims;
   const int P = f.cp.partial_chunks, C = d.chunks, E = d.experts, k = d.top_k;
   const int t0 = s_coff[trigger_first_chunk(q, P)];
@@ -303,7 +304,7 @@ __device__ void worker_dispatch(const FrontendParams& f, int q, int w, int W, un
   if (permitted && (long long)(b - a) * k > kDispatchMaxItems) {
     if (threadIdx.x == 0) record_status(f.dp.status, kBadConfig, 22, (long long)(b - a) * k, kDispatchMaxItems);
   } else if (permitted && a < b) {
-    dispatch_rows<T>(f.dp, t0, a, b, s_base, hist, run, item_pos, s_coff, nc, streamed, indexed);
+    dispatch_rows<T>(f.dp, t0, a, b, s_base, hist, run, item_pos, s_coff, nc, streamed, indexed, stage);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -381,11 +382,15 @@ __device__ int wait_released(const FrontendParams& f, int q, unsigned long long 
   return v;
 }
 
-// NT > 0: CTA-group router (router_group: NT tokens x EP experts per CTA step);
-// NT == 0: one warp per token (router_token, up to EMAX experts).  The step
-// pipeline makes the same choice (launch_router), so both route identically.
-template <typename T, int NT, int EP, int EMAX>
+// Routing: a worker routes units of kUnitTokens consecutive tokens, one token
+// per warp (router_token, up to EMAX experts), from the shared-memory ring
+// (resident batch) or from global memory; the step pipeline's router kernel
+// runs the same per-token code, so both route identically.
+constexpr int kUnitTokens = 8;
+
+template <typename T, int EMAX>
 __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __grid_constant__ FrontendParams f) {
+  constexpr int NT = kUnitTokens;
   extern __shared__ __align__(16) uint8_t fsm[];
   __shared__ int hist[kMaxExperts];
   __shared__ int run[kMaxExperts];
@@ -393,8 +398,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   __shared__ int item_pos[kDispatchMaxItems];
   __shared__ int s_coff[kDispatchMaxChunks + 1];
   __shared__ int s_flag;
-  __shared__ float red[256];
-  __shared__ unsigned long long s_dred[8 * 8];  // digest partial sums: 8 warps x up to 8 tokens
+  __shared__ float s_lg[8][EMAX + 8];  // per-warp logit scratch of router_token
   TraceScope trace_scope(f.trace);
   const MoEDims& d = f.dp.dims;
   const int C = d.chunks, E = d.experts, n_desc = d.n_desc;
@@ -438,7 +442,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     int* s_ccount = reinterpret_cast<int*>(fsm + ((Lt.total + 15) & ~15LL));
     if (threadIdx.x < 32) {
       FrontHooks hooks{&f, W, f.cp.partial_chunks, C, E, epoch, hist, s_dst, s_ccoff, s_ccount,
-                       f.cp.ctl_per_chunk, 0, NT > 0 ? NT : 1, s_pub};
+                       f.cp.ctl_per_chunk, 0, NT, s_pub};
       if (packed && !s_dup)
         ctl::control_warp_run_packed(f.cp, dims, fsm, s_dst, s_ccoff, s_egmask, pv, 0, n_desc, hooks);
       else
@@ -464,27 +468,10 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   const int Wd = f.dispatch_ctas > 0 ? min(W, f.dispatch_ctas) : W;
   const bool dispatcher = w < Wd;
   const T* wts = (const T*)f.rp.weight;
-  // router tables in shared memory for the whole launch: bias, block mask and
-  // (behind the blob area) the per-chunk bias rows
-  __shared__ float s_rbias[kMaxExperts];
-  __shared__ uint8_t s_rmask[kMaxExperts];
+  // the per-chunk router bias rows in shared memory (behind the blob area)
   float* s_cbias = reinterpret_cast<float*>(fsm);
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    s_rbias[e] = f.rp.bias[e];
-    s_rmask[e] = f.rp.block_mask ? f.rp.block_mask[e] : 0;
-  }
   if (f.rp.chunk_bias)
     for (int i = threadIdx.x; i < C * E; i += blockDim.x) s_cbias[i] = f.rp.chunk_bias[i];
-  // this lane's weight slice, held in registers across chunks (rows of 8 x 32 vectors)
-  constexpr int kWP = NT > 0 ? EP : 1;  // (== EP wherever router_group is called)
-  uint4 wpre[kWP];
-  const int nvec_row = f.rp.hidden * (int)sizeof(T) / 16;
-  const bool use_wpre = NT > 0 && nvec_row == 8 * 32;
-  if (use_wpre) {
-#pragma unroll
-    for (int e = 0; e < kWP; ++e)
-      wpre[e] = e < E ? __ldg((const uint4*)(wts + (long long)e * f.rp.hidden) + warp * 32 + lane) : make_uint4(0, 0, 0, 0);
-  }
   // inputs resident at launch (not streamed in by the copy engine during this call)
   const unsigned long long ready_all = f.tok_ready == nullptr ? ~0ULL : ld_acquire_gpu_u64(f.tok_ready_all);
   const bool resident = ready_all >= epoch;
@@ -497,20 +484,20 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     row[20] = epoch;
   }
   const int row_bytes = f.rp.hidden * (int)sizeof(T);
-  // bulk-copy ring (resident batch, group router): this worker's token groups
-  // stream into shared memory ring_slots groups ahead of the routing
+  // bulk-copy ring (resident batch): this worker's routing units stream into
+  // shared memory ring_slots units ahead of the routing
   constexpr int kRingMax = 8;
   __shared__ __align__(8) uint64_t s_rbar[kRingMax];
-  const bool ring = NT > 0 && resident && f.ring_slots >= 2 && f.ring_slots <= kRingMax;
+  const bool ring = resident && f.ring_slots >= 2 && f.ring_slots <= kRingMax;
   const int R = ring ? f.ring_slots : 1;
-  const long long unit_bytes = (long long)(NT > 0 ? NT : 1) * row_bytes;
+  const long long unit_bytes = (long long)NT * row_bytes;
   uint8_t* ring_base = fsm + f.ring_off;
   int pc = 0, pg = 0, pcum = 0;          // producer (thread 0): next group to copy, chunk / group / units before
   long long issued = 0, consumed = 0;    // groups copied / routed
   auto unit_norm = [&]() {
     #pragma unroll 1
     while (pc < C) {
-      const int ng = (s_coff[pc + 1] - s_coff[pc] + (NT > 0 ? NT : 1) - 1) / (NT > 0 ? NT : 1);
+      const int ng = chunk_units(s_coff, pc, NT);
       if (pg < ng) return;
       pcum += ng;
       if (++pc < C) pg = first_share(w, pcum, W);
@@ -528,6 +515,19 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     pg += W;
     unit_norm();
   };
+  // dispatch staging: the ring's memory, free once routing is done (or never
+  // used by a streamed batch), holds the rows of a dispatch share
+  __shared__ __align__(8) uint64_t s_dbar[2];
+  __shared__ uint32_t s_duses[2];
+  const DispatchStage dstage{ring_base, f.ring_slots * (int)unit_bytes, s_dbar, s_duses, f.timeout_ns};
+  const DispatchStage* stage = f.ring_slots >= 2 ? &dstage : nullptr;
+  if (threadIdx.x == 0) {
+    mbar_init(&s_dbar[0], 1);
+    mbar_init(&s_dbar[1], 1);
+    s_duses[0] = s_duses[1] = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();  // the chunk offsets in shared memory are complete before thread 0 walks them
   if (ring && threadIdx.x == 0) {
     for (int i = 0; i < R; ++i) mbar_init(&s_rbar[i], 1);
     fence_mbarrier_init();
@@ -539,41 +539,43 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   cta_stamp(f, 0);
   __syncthreads();
   cta_stamp(f, 1);
-  // Descriptors this worker dispatches.  With at least as many dispatching
-  // workers as descriptors, each descriptor has its own group of workers (in
-  // proportion to its tokens), so released descriptors are dispatched side by
-  // side; otherwise every worker takes a share of every descriptor.
-  int my_q0 = 0, my_q1 = n_desc, wi = w, wn = Wd;
-  if (f.dispatch_groups && n_desc <= Wd && dispatcher) {
+  // Descriptors this worker dispatches.  When every partial descriptor can
+  // have workers of its own, the partial descriptors get disjoint worker
+  // groups (in proportion to their tokens), so released descriptors are
+  // dispatched side by side, and every worker then also takes a share of the
+  // final descriptor, the one the layer waits for after the last trigger.
+  // Otherwise every worker takes a share of every descriptor in turn.
+  const bool grouped = f.dispatch_groups && n_desc >= 2 && n_desc - 1 <= Wd && dispatcher;
+  int qa = 0, wia = w, wna = Wd;  // grouped: this worker's partial descriptor, its index and group size
+  if (grouped) {
     const int P = f.cp.partial_chunks;
-    const long long total = s_coff[C] - s_coff[0];
+    const int np = n_desc - 1;
+    const long long total = s_coff[trigger_first_chunk(np, P)] - s_coff[0];
     long long cum = 0;
     int lo = 0;
-    for (int q = 0; q < n_desc; ++q) {
+    for (int q = 0; q < np; ++q) {
       cum += s_coff[trigger_last_chunk(q, P, C) + 1] - s_coff[trigger_first_chunk(q, P)];
       int hi = total > 0 ? (int)((long long)Wd * cum / total) : lo + 1;
       hi = max(hi, lo + 1);
-      hi = min(hi, Wd - (n_desc - 1 - q));
-      if (q == n_desc - 1) hi = Wd;
-      if (w >= lo && w < hi) { my_q0 = q; my_q1 = q + 1; wi = w - lo; wn = hi - lo; }
+      hi = min(hi, Wd - (np - 1 - q));
+      if (q == np - 1) hi = Wd;
+      if (w >= lo && w < hi) { qa = q; wia = w - lo; wna = hi - lo; }
       lo = hi;
     }
   }
-  int next = my_q0;
+  // cursor over this worker's descriptors: the descriptor, the worker's share
+  // index in it and the number of workers sharing it (n_desc: no more)
+  int k_cur = 0;
+  auto cq = [&]() { return grouped ? (k_cur == 0 ? qa : k_cur == 1 ? n_desc - 1 : n_desc) : k_cur; };
+  auto cwi = [&]() { return grouped && k_cur == 0 ? wia : w; };
+  auto cwn = [&]() { return grouped && k_cur == 0 ? wna : Wd; };
   int cum_units = 0;  // routing units (token groups, or tokens) of the chunks before c
   for (int c = 0; c < C; ++c) {
     // this worker's routing units in chunk c (token groups, or tokens over its warps)
-    int my_units = 0;
-    if constexpr (NT > 0) {
-      my_units = share_count(first_share(w, cum_units, W), chunk_units(s_coff, c, NT), W);
-    } else {
-      const int slots = W * nwarps;
-      for (int k = 0; k < nwarps; ++k)
-        my_units += share_count(first_share(w * nwarps + k, cum_units, slots), chunk_units(s_coff, c, 1), slots);
-    }
+    const int my_units = share_count(first_share(w, cum_units, W), chunk_units(s_coff, c, NT), W);
     if (resident && my_units == 0) {  // nothing to route or to report for this chunk
       if (c < 8) { cta_stamp(f, 2 + 2 * c); cta_stamp(f, 52 + c); cta_stamp(f, 3 + 2 * c); }
-      cum_units += chunk_units(s_coff, c, NT > 0 ? NT : 1);
+      cum_units += chunk_units(s_coff, c, NT);
       continue;
     }
     TraceSlot* rslot = f.phase_trace ? &f.phase_trace[c] : nullptr;
@@ -583,7 +585,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     // before the routing work and read after it (a fence makes it an acquire
     // when it saw the release)
     unsigned long long early_v = 0;
-    if (threadIdx.x == 0 && !f.delayed && next < my_q1) early_v = ld_relaxed_gpu_u64(&f.desc_ready[next]);
+    if (threadIdx.x == 0 && !f.delayed && cq() < n_desc) early_v = ld_relaxed_gpu_u64(&f.desc_ready[cq()]);
     for (int e = threadIdx.x; e < E; e += blockDim.x) run[e] = 0;  // per-chunk expert counts
     if (!resident) {
       // streamed: wait for this chunk's rows; early arm: dispatch every
@@ -596,8 +598,8 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
             if (ld_acquire_sys_u64(reinterpret_cast<const uint64_t*>(&f.tok_ready[c])) >= epoch ||
                 ld_acquire_sys_u64(reinterpret_cast<const uint64_t*>(f.tok_ready_all)) >= epoch) {
               st = 1;
-            } else if (dispatcher && !f.delayed && next < my_q1 &&
-                       ld_relaxed_gpu_u64(&f.desc_ready[next]) == epoch) {
+            } else if (dispatcher && !f.delayed && cq() < n_desc &&
+                       ld_relaxed_gpu_u64(&f.desc_ready[cq()]) == epoch) {
               __threadfence();  // acquire the release seen by the relaxed poll
               st = 2;
             } else if (globaltimer_ns() > deadline) {
@@ -613,10 +615,11 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
         const int st = s_flag;
         __syncthreads();
         if (st == 1) break;
-        worker_dispatch<T>(f, next, wi, wn, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, true);
-        ++next;
+        worker_dispatch<T>(f, cq(), cwi(), cwn(), epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, true, false,
+                           stage);
+        ++k_cur;
       }
-      if (threadIdx.x == 0 && !f.delayed && next < my_q1) early_v = ld_relaxed_gpu_u64(&f.desc_ready[next]);
+      if (threadIdx.x == 0 && !f.delayed && cq() < n_desc) early_v = ld_relaxed_gpu_u64(&f.desc_ready[cq()]);
       for (int e = threadIdx.x; e < E; e += blockDim.x) run[e] = 0;  // worker_dispatch used it
     }
     __syncthreads();
@@ -625,51 +628,38 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     // streamed batches: the workers digest the rows they route (feature digest
     // + checksum base); a resident batch had them computed when it was loaded
     const bool digest = !resident && f.digest_out != nullptr;
-    DigestSink dsink{f.digest_out, f.csbase_out, f.dp.token_ids, f.dp.dims.rank, c, t0, s_dred};
-    if constexpr (NT > 0) {
-      const int ngroups = (t1 - t0 + NT - 1) / NT;
-      for (int g = first_share(w, cum_units, W); g < ngroups; g += W) {
-        const int tf = t0 + g * NT;
-        const T* srows = nullptr;
-        if (ring) {
-          const int slot = (int)(consumed % R);
-          // a wait that runs out records the status (the call fails) and routes what is there
-          mbar_wait_bounded(&s_rbar[slot], (uint32_t)((consumed / R) & 1), f.dp.status, kFrontKernelId + 2,
-                            f.timeout_ns);
-          srows = reinterpret_cast<const T*>(ring_base + slot * unit_bytes);
-          if (consumed == 0) cta_stamp(f, 21);  // first group in shared memory
-        }
-        // diagnostics: the first and second groups' phases in stamps 40..43 and 64..67
-        unsigned long long* dbg =
-            (f.cta_clock == nullptr || !ring || consumed > 1)
-                ? nullptr
-                : f.cta_clock + (long long)blockIdx.x * kCtaClockSlots + (consumed == 0 ? 40 : 64);
-        router_group<T, NT, EP>(f.rp, s_rbias, cbias, f.rp.block_mask ? s_rmask : nullptr, tf, min(NT, t1 - tf),
-                                red, run, wpre, use_wpre, digest ? &dsink : nullptr, srows, dbg);
-        if (ring && consumed == 0) cta_stamp(f, 22);  // first group routed
-        if (ring) {  // router_group ended on a CTA barrier: the slot is free again
-          if (threadIdx.x == 0) issue_next();
-          ++consumed;
-        }
+    const int ngroups = chunk_units(s_coff, c, NT);
+    for (int g = first_share(w, cum_units, W); g < ngroups; g += W) {
+      const int tf = t0 + g * NT, nt = min(NT, t1 - tf);
+      const T* srows = nullptr;
+      if (ring) {
+        const int slot = (int)(consumed % R);
+        // a wait that runs out records the status (the call fails) and routes what is there
+        mbar_wait_bounded(&s_rbar[slot], (uint32_t)((consumed / R) & 1), f.dp.status, kFrontKernelId + 2,
+                          f.timeout_ns);
+        srows = reinterpret_cast<const T*>(ring_base + slot * unit_bytes);
+        if (consumed == 0) cta_stamp(f, 21);  // first unit in shared memory
       }
-      cum_units += ngroups;
-    } else {
-      __shared__ float s_lg[8][EMAX + 8];  // per-warp logit scratch of router_token
-      const int nvec_tok = f.rp.hidden * (int)sizeof(T) / 16;
-      const int slots = W * nwarps;
-      for (int t = t0 + first_share(w * nwarps + warp, cum_units, slots); t < t1; t += slots) {
-        router_token<T, EMAX, false>(f.rp, cbias, t, wts, s_lg[warp], run);
+      if (warp < nt) {  // token tf + warp, one warp each
+        const int t = tf + warp;
+        const T* x = srows ? srows + (long long)warp * f.rp.hidden : (const T*)f.rp.tokens + (long long)t * f.rp.hidden;
+        router_token<T, EMAX, false>(f.rp, cbias, t, x, srows != nullptr, wts, s_lg[warp], run);
         if (digest) {
-          const long long dg = warp_row_digest((const uint4*)((const T*)f.rp.tokens + (long long)t * f.rp.hidden),
-                                               nvec_tok);
+          const long long dg = warp_row_digest((const uint4*)x, row_bytes / 16);
           if (lane == 0) {
             f.digest_out[t] = dg;
             f.csbase_out[t] = token_checksum_base(f.dp.token_ids[t], f.dp.dims.rank, c, t - t0, t, dg);
           }
         }
       }
-      cum_units += t1 - t0;
+      __syncthreads();  // every warp is done with the unit's rows
+      if (ring) {
+        if (consumed == 0) cta_stamp(f, 22);  // first unit routed
+        if (threadIdx.x == 0) issue_next();
+        ++consumed;
+      }
     }
+    cum_units += ngroups;
     if (c < 8) cta_stamp(f, 52 + c);
     __syncthreads();
     if (c < 4) cta_stamp(f, 60 + c);
@@ -677,10 +667,9 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       if (run[e]) atomicAdd(&f.chunk_counts[(long long)c * E + e], run[e]);
     __syncthreads();
     if (threadIdx.x == 0) {
-      if (my_units > 0) {
-        __threadfence();
-        atomicAdd(&f.chunk_done[c], my_units);
-      }
+      // the CTA barrier above ordered every thread's expert ids, gates and
+      // counts before this release
+      if (my_units > 0) red_add_release_gpu(&f.chunk_done[c], my_units);
       trace_end(rslot);
     }
     if (c < 8) cta_stamp(f, 3 + 2 * c);
@@ -696,10 +685,11 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       __syncthreads();
       bool ready = s_flag == 1;
       __syncthreads();
-      while (next < my_q1 && ready) {
-        worker_dispatch<T>(f, next, wi, wn, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident);
-        ++next;
-        ready = next < my_q1 && wait_released(f, next, epoch, &s_flag, false) == 1;
+      while (cq() < n_desc && ready) {
+        worker_dispatch<T>(f, cq(), cwi(), cwn(), epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident,
+                           false, stage);
+        ++k_cur;
+        ready = cq() < n_desc && wait_released(f, cq(), epoch, &s_flag, false) == 1;
       }
     }
   }
@@ -714,27 +704,29 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   if (!dispatcher) return;  // routing done: this SM is free for the expert side
   if (f.delayed && wait_released(f, n_desc - 1, epoch, &s_flag, true) != 1) return;
   int n_indexed = 0;  // descriptors whose index part ran before their release (diagnostics)
-  while (next < my_q1) {
+  while (cq() < n_desc) {
+    const int next = cq();
     // a descriptor not yet released whose chunks are routed: compute its
     // index part (prefix counts and ranks, from the expert ids only) while
     // the control warp works, so the release is followed by the copy alone
     const int rel = wait_released(f, next, epoch, &s_flag, false);
     bool indexed = false;
-    if (rel == 0 && chunks_complete(f, next, s_coff, NT > 0 ? NT : 1, &s_flag)) {
-      worker_index(f, next, wi, wn, hist, run, item_pos, s_coff);
+    if (rel == 0 && chunks_complete(f, next, s_coff, NT, &s_flag)) {
+      worker_index(f, next, cwi(), cwn(), hist, run, item_pos, s_coff);
       indexed = true;
       ++n_indexed;
     }
     if (rel != 1 && wait_released(f, next, epoch, &s_flag, true) != 1) return;
-    worker_dispatch<T>(f, next, wi, wn, epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident, indexed);
-    ++next;
+    worker_dispatch<T>(f, next, cwi(), cwn(), epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident,
+                       indexed, stage);
+    ++k_cur;
   }
   if (f.cta_clock != nullptr && threadIdx.x == 0) f.cta_clock[(long long)blockIdx.x * kCtaClockSlots + 23] = 1 + n_indexed;
 }
 
-template <typename T, int NT, int EP, int EMAX>
+template <typename T, int EMAX>
 bool launch_one_frontend(const FrontendParams& f, int sms, size_t smem, cudaStream_t s) {
-  auto kern = moe_frontend_kernel<T, NT, EP, EMAX>;
+  auto kern = moe_frontend_kernel<T, EMAX>;
   static size_t configured = 0;
   if (smem > configured) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
@@ -761,23 +753,19 @@ bool launch_one_frontend(const FrontendParams& f, int sms, size_t smem, cudaStre
 }  // namespace
 
 bool launch_frontend(const FrontendParams& f, bool bf16, int sms, cudaStream_t s) {
-  if (sms < 2 || !control_warp_path_ok(f.cp) || f.dp.dims.experts > kMaxExperts || f.rp.top_k > 8 ||
-      f.dp.dims.chunks > kDispatchMaxChunks)
-    return false;
-  // dynamic shared memory holds the control blob (CTA 0); router weights are
-  // read through the read-only path
-  // CTA 0: control blob + per-(chunk, expert) router counts; workers: per-chunk bias rows
-  const size_t cwords = (size_t)f.dp.dims.chunks * f.dp.dims.experts * sizeof(int);
   const int E = f.rp.experts;
-  const bool group = router_group_ok(E, f.rp.hidden, bf16 ? 2 : 4);
-  // workers: per-chunk bias rows, then the ring of token groups (group router,
-  // two to eight groups within kRingBudget bytes)
+  if (sms < 2 || !control_warp_path_ok(f.cp) || E > 64 || f.rp.top_k > 8 || f.dp.dims.chunks > kDispatchMaxChunks ||
+      (f.rp.hidden * (bf16 ? 2 : 4)) % 16 != 0)
+    return false;
+  // dynamic shared memory: the control blob (CTA 0); the workers' per-chunk
+  // bias rows and then the ring of routing units (two to eight units of
+  // kUnitTokens rows within kRingBudget bytes)
+  const size_t cwords = (size_t)f.dp.dims.chunks * f.dp.dims.experts * sizeof(int);
   FrontendParams g = f;
   const size_t ring_off = (cwords + 127) & ~(size_t)127;
-  const int nt = !group ? 0 : E <= 4 ? 8 : E <= 8 ? 4 : E <= 16 ? 2 : 1;
-  const size_t unit = (size_t)nt * f.rp.hidden * (bf16 ? 2 : 4);
+  const size_t unit = (size_t)kUnitTokens * f.rp.hidden * (bf16 ? 2 : 4);
   constexpr size_t kRingBudget = 160 * 1024;
-  g.ring_slots = (f.ring_slots && unit) ? (int)std::min<size_t>(8, kRingBudget / unit) : 0;
+  g.ring_slots = f.ring_slots ? (int)std::min<size_t>(8, kRingBudget / unit) : 0;
   if (g.ring_slots < 2) g.ring_slots = 0;
   g.ring_off = (int)ring_off;
   // control CTA: blob, per-(chunk, expert) router counts, then the packed
@@ -787,26 +775,11 @@ bool launch_frontend(const FrontendParams& f, bool bf16, int sms, cudaStream_t s
   g.ctl_packed_off = ctl::packed_path_ok(cd) ? (int)ctl_base : 0;
   const size_t ctl_bytes = ctl_base + (g.ctl_packed_off ? (size_t)ctl::packed_smem_bytes(cd) : 0);
   const size_t smem = std::max(ctl_bytes, g.ring_slots ? ring_off + g.ring_slots * unit : cwords);
-#define RAICCL_FRONT(T, NT, EP, EM) return launch_one_frontend<T, NT, EP, EM>(g, sms, smem, s)
-  if (group) {
-    if (E <= 4) {
-      if (bf16) RAICCL_FRONT(__nv_bfloat16, 8, 4, 4); else RAICCL_FRONT(float, 8, 4, 4);
-    } else if (E <= 8) {
-      if (bf16) RAICCL_FRONT(__nv_bfloat16, 4, 8, 8); else RAICCL_FRONT(float, 4, 8, 8);
-    } else if (E <= 16) {
-      if (bf16) RAICCL_FRONT(__nv_bfloat16, 2, 16, 16); else RAICCL_FRONT(float, 2, 16, 16);
-    } else {
-      if (bf16) RAICCL_FRONT(__nv_bfloat16, 1, 32, 32); else RAICCL_FRONT(float, 1, 32, 32);
-    }
-  } else if (E <= 8) {
-    if (bf16) RAICCL_FRONT(__nv_bfloat16, 0, 0, 8); else RAICCL_FRONT(float, 0, 0, 8);
-  } else if (E <= 16) {
-    if (bf16) RAICCL_FRONT(__nv_bfloat16, 0, 0, 16); else RAICCL_FRONT(float, 0, 0, 16);
-  } else if (E <= 64) {
-    if (bf16) RAICCL_FRONT(__nv_bfloat16, 0, 0, 64); else RAICCL_FRONT(float, 0, 0, 64);
-  }
-#undef RAICCL_FRONT
-  return false;
+  if (E <= 8) return bf16 ? launch_one_frontend<__nv_bfloat16, 8>(g, sms, smem, s)
+                          : launch_one_frontend<float, 8>(g, sms, smem, s);
+  if (E <= 16) return bf16 ? launch_one_frontend<__nv_bfloat16, 16>(g, sms, smem, s)
+                           : launch_one_frontend<float, 16>(g, sms, smem, s);
+  return bf16 ? launch_one_frontend<__nv_bfloat16, 64>(g, sms, smem, s) : launch_one_frontend<float, 64>(g, sms, smem, s);
 }
 
 }  // namespace raiccl

@@ -53,6 +53,10 @@ def main() -> None:
     ap.add_argument("--progressive", type=int, default=0, choices=(0, 1),
                     help="GEMM-1 takes tiles as descriptors arrive (1) or after the whole batch (0)")
     ap.add_argument("--dispatch-ctas", type=int, default=0, help="front-end workers that dispatch (0: all)")
+    ap.add_argument("--router-ring", type=int, default=1, choices=(0, 1),
+                    help="resident batches reach shared memory by bulk copies (routing and dispatch staging)")
+    ap.add_argument("--dispatch-groups", type=int, default=1, choices=(0, 1),
+                    help="one worker group per partial descriptor, dispatched side by side")
     args = ap.parse_args()
     import os
 
@@ -73,7 +77,8 @@ def main() -> None:
         cfg = cfg.with_overrides(tokens_per_rank=args.tokens, chunk_sizes=(args.tokens // n,) * n)
     layer = ProgressiveMoELayer(cfg, device=dev, timeout_s=10.0, trace=bool(args.trace or args.roofline),
                                 frontend=args.frontend, gemm_swap_max=args.gemm_swap_max,
-                                progressive=bool(args.progressive), dispatch_ctas=args.dispatch_ctas)
+                                progressive=bool(args.progressive), dispatch_ctas=args.dispatch_ctas,
+                                router_ring=bool(args.router_ring), dispatch_groups=bool(args.dispatch_groups))
     try:
         if args.cta_clocks:
             sms = torch.cuda.get_device_properties(layer.device).multi_processor_count

@@ -494,9 +494,9 @@ def test_progressive_gemm1_matches_and_starts_early(name, over):
 
 @pytest.mark.parametrize("name", ["r4_reference", "full_tf32", "skewed_bf16"])
 def test_router_ring_matches_global_loads(name):
-    """Routing token groups out of the shared-memory ring (bulk copies issued
-    ahead) gives the same expert ids, gates and layer output as reading them
-    from global memory."""
+    """Routing token units out of the shared-memory ring (bulk copies issued
+    ahead), and dispatching rows staged through that memory, give the same
+    expert ids, gates and layer output as reading both from global memory."""
     from revealaiccl_b200.moe.config import preset
     from revealaiccl_b200.moe.layer import ProgressiveMoELayer
 
