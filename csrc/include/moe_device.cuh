@@ -309,29 +309,56 @@ struct DispatchStage {
 template <typename T>
 __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, const int* base_e, int* hist, int* run,
                               int* item_pos, const int* s_coff, int nc, bool streamed = false, bool indexed = false,
-                              const DispatchStage* stage = nullptr) {
+                              const DispatchStage* stage = nullptr, unsigned long long* dbg = nullptr) {
+  // dbg (diagnostics, thread 0): %globaltimer after the index part, the
+  // identity rows and the staged feature rows
+  auto stamp = [&](int i) {
+    if (dbg != nullptr && threadIdx.x == 0) dbg[i] = globaltimer_ns();
+  };
   const MoEDims& d = p.dims;
   const int k = d.top_k;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   if (!indexed) dispatch_index(p, t0, a, b, hist, run, item_pos);
+  stamp(0);
   const long long nitems = (long long)(b - a) * k;
   const long long row_bytes = (long long)d.hidden * d.feat_bytes;
   const int vec_per_row = (int)(row_bytes / 16);
-  // staged rows: tokens per half, and the first half's copy issued before the
-  // identity rows so that it is in flight while they are written
-  const int half_rows = stage ? (int)((stage->bytes / 2) / row_bytes) : 0;
+  // staging layout: the share's identity inputs (token id, digest and
+  // checksum base per token, the gate per item) when they fit a quarter of
+  // the buffer, then two halves of token rows; the first half's copy is
+  // issued before the identity rows so that it is in flight while they are
+  // written
+  const long long ntok = b > a ? b - a : 0;
+  const long long id_bytes = (ntok * 24 + nitems * 4 + 15) & ~15LL;
+  const bool stage_ids = stage != nullptr && ntok > 0 && id_bytes <= stage->bytes / 4;
+  long long* s_tid = stage_ids ? reinterpret_cast<long long*>(stage->buf) : nullptr;
+  long long* s_dig = s_tid + ntok;
+  long long* s_csb = s_dig + ntok;
+  float* s_gate = reinterpret_cast<float*>(s_csb + ntok);
+  uint8_t* rows_buf = stage ? stage->buf + (stage_ids ? id_bytes : 0) : nullptr;
+  const int half_rows = stage ? (int)(((stage->bytes - (stage_ids ? id_bytes : 0)) / 2) / row_bytes) : 0;
   const bool staged = half_rows > 0 && b > a;
   auto issue_half = [&](int h, int tb) {  // thread 0: tokens [tb, tb + rows) into half h
     const int rows = min(half_rows, b - tb);
     const uint32_t bytes = (uint32_t)(rows * row_bytes);
     fence_proxy_async_global();  // rows written by generic stores or the copy engine, read by the bulk copy
     mbar_arrive_expect_tx(&stage->bar[h], bytes);
-    bulk_load_g2s(stage->buf + (long long)h * half_rows * row_bytes,
+    bulk_load_g2s(rows_buf + (long long)h * half_rows * row_bytes,
                   (const uint8_t*)p.tokens + (long long)tb * row_bytes, bytes, &stage->bar[h]);
   };
   if (staged && threadIdx.x == 0) {
     issue_half(0, a);
     if (a + half_rows < b) issue_half(1, a + half_rows);
+  }
+  if (stage_ids) {  // one round trip for every item's identity inputs
+    for (long long i = threadIdx.x; i < ntok; i += blockDim.x) {
+      s_tid[i] = p.token_ids[a + i];
+      s_dig[i] = p.feat_digest[a + i];
+      s_csb[i] = p.checksum_base[a + i];
+    }
+    if (d.gate_mode)
+      for (long long i = threadIdx.x; i < nitems; i += blockDim.x) s_gate[i] = p.gates[(long long)a * k + i];
+    __syncthreads();
   }
   // identity rows, one warp per item (small stores; an item whose row falls
   // outside the receive region records the status here and is skipped below)
@@ -350,8 +377,15 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
     uint8_t* base = (uint8_t*)p.peers.base[r];
     if (lane < kFwdMetaFields) {
       long long pre = 0;
-      if (lane == 0 || lane == 8) pre = lane == 0 ? p.token_ids[t] : p.checksum_base[t];
-      else if (lane == 7) pre = p.feat_digest[t];
+      if (stage_ids) {
+        if (lane == 0) pre = s_tid[t - a];
+        else if (lane == 8) pre = s_csb[t - a];
+        else if (lane == 7) pre = s_dig[t - a];
+      } else if (lane == 0 || lane == 8) {
+        pre = lane == 0 ? p.token_ids[t] : p.checksum_base[t];
+      } else if (lane == 7) {
+        pre = p.feat_digest[t];
+      }
       int c = 0;
       while (c + 1 < nc && s_coff[c + 1] <= t) ++c;
       while (c + 1 < d.chunks && p.chunk_offsets[c + 1] <= t) ++c;  // beyond the staged table
@@ -376,9 +410,10 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
     } else if (lane == 16) {
       ((int*)(base + p.layout.recv_retrow))[grow] = t * k + j;
     } else if (lane == 17) {
-      ((float*)(base + p.layout.recv_gate))[grow] = d.gate_mode ? p.gates[i] : 1.f;
+      ((float*)(base + p.layout.recv_gate))[grow] = !d.gate_mode ? 1.f : stage_ids ? s_gate[li] : p.gates[i];
     }
   }
+  stamp(1);
   if (staged) {
     // feature rows from shared memory: batch n holds tokens [a + n half_rows, ...)
     // in half n % 2; a warp stores one item (token, choice) at a time
@@ -387,7 +422,7 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
       const int h = n & 1;
       const int rows = min(half_rows, b - tb);
       mbar_wait_bounded(&stage->bar[h], stage->uses[h] & 1u, p.status, 23, stage->timeout_ns);
-      const uint4* sbase = (const uint4*)(stage->buf + (long long)h * half_rows * row_bytes);
+      const uint4* sbase = (const uint4*)(rows_buf + (long long)h * half_rows * row_bytes);
       for (int li_b = warp; li_b < rows * k; li_b += nwarps) {
         const long long li = (long long)(tb - a) * k + li_b;
         const int packed = item_pos[li];
@@ -407,6 +442,7 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
       }
       __syncthreads();
     }
+    stamp(2);
     return;
   }
   // feature rows: each warp copies two items at a time, eight 16-byte loads

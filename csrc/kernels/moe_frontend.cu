@@ -304,7 +304,10 @@ __device__ void worker_dispatch(const FrontendParams& f, int q, int w, int W, un
   if (permitted && (long long)(b - a) * k > kDispatchMaxItems) {
     if (threadIdx.x == 0) record_status(f.dp.status, kBadConfig, 22, (long long)(b - a) * k, kDispatchMaxItems);
   } else if (permitted && a < b) {
-    dispatch_rows<T>(f.dp, t0, a, b, s_base, hist, run, item_pos, s_coff, nc, streamed, indexed, stage);
+    // diagnostics: descriptor q's phases in stamps 68 + 4 q .. (q < 8)
+    unsigned long long* dbg =
+        (f.cta_clock != nullptr && q < 8) ? f.cta_clock + (long long)blockIdx.x * kCtaClockSlots + 68 + 4 * q : nullptr;
+    dispatch_rows<T>(f.dp, t0, a, b, s_base, hist, run, item_pos, s_coff, nc, streamed, indexed, stage, dbg);
   }
   __syncthreads();
   if (threadIdx.x == 0) {

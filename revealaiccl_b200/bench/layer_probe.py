@@ -264,9 +264,13 @@ def _cta_clocks(layer) -> dict:
                               "end_max": r(np.nanmax(e))})
     for q in range(min(8, layer.cfg.n_desc)):
         b, mid, e = wk[:, 24 + 2 * q], wk[:, 44 + q], wk[:, 25 + 2 * q]
+        ix, idn, rw = wk[:, 68 + 4 * q], wk[:, 69 + 4 * q], wk[:, 70 + 4 * q]
+        ok = (ix >= b) & (rw <= mid)  # this call's stamps (staged rows only)
+        phase = ({"index_med": r(np.median(ix[ok] - b[ok])), "identity_med": r(np.median(idn[ok] - ix[ok])),
+                  "rows_med": r(np.median(rw[ok] - idn[ok]))} if ok.any() else None)
         out["descriptors"].append({"desc": q, "begin_min": r(np.nanmin(b)), "begin_med": r(np.nanmedian(b)),
                                    "rows_med": r(np.nanmedian(mid - b)), "publish_max": r(np.nanmax(e - mid)),
-                                   "end_max": r(np.nanmax(e))})
+                                   "end_max": r(np.nanmax(e)), "phases": phase})
     c0 = (clk[0] - t0) / 1e3
     for q in range(min(7, layer.cfg.n_desc)):
         out["triggers"].append({"trigger": q, "begin": r(c0[2 + 2 * q]), "end": r(c0[3 + 2 * q])})
