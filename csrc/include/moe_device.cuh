@@ -176,7 +176,8 @@ __device__ inline void router_finish(const RouterParams& p, const float* bias, c
 // ---------------------------------------------------------------------------
 template <typename T, int EMAX, bool SMEM_W>
 __device__ __forceinline__ void router_token(const RouterParams& p, const float* chunk_bias, int t, const T* x,
-                                             bool x_shared, const T* __restrict__ w, float* s_lg, int* sel_counts) {
+                                             bool x_shared, const T* __restrict__ w, float* s_lg, int* sel_counts,
+                                             unsigned long long* dbg = nullptr) {
   const int D = p.hidden, E = p.experts;
   const int lane = threadIdx.x & 31;
   constexpr int VEC = 16 / sizeof(T);
@@ -215,6 +216,8 @@ __device__ __forceinline__ void router_token(const RouterParams& p, const float*
       }
     }
   }
+  // dbg (diagnostics, lane 0): %globaltimer after the products and after the finish
+  if (dbg != nullptr && lane == 0) dbg[0] = globaltimer_ns();
 #pragma unroll
   for (int e = 0; e < EMAX; ++e) {
     if (e < E) {
@@ -228,6 +231,7 @@ __device__ __forceinline__ void router_token(const RouterParams& p, const float*
   for (int e = 0; e < EMAX; ++e)
     if (e < E) s_lg[e] = acc[e];
   router_finish(p, p.bias, chunk_bias, p.block_mask, t, s_lg, reinterpret_cast<int*>(s_lg + EMAX), sel_counts);
+  if (dbg != nullptr) dbg[1] = globaltimer_ns();
 }
 
 // ---------------------------------------------------------------------------
@@ -360,11 +364,12 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
       for (long long i = threadIdx.x; i < nitems; i += blockDim.x) s_gate[i] = p.gates[(long long)a * k + i];
     __syncthreads();
   }
+  stamp(3);
   // identity rows, one warp per item (small stores; an item whose row falls
   // outside the receive region records the status here and is skipped below)
-  for (long long li = warp; li < nitems; li += nwarps) {
+  for (int li = warp; li < (int)nitems; li += nwarps) {  // nitems <= kDispatchMaxItems
     const long long i = (long long)a * k + li;
-    const int t = (int)(i / k), j = (int)(i % k);
+    const int t = a + li / k, j = li % k;
     const int packed = item_pos[li];
     const int e = (int)((unsigned)packed >> 24);
     const int r = expert_owner(d, e), le = expert_slot(d, e);
@@ -386,9 +391,16 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
       } else if (lane == 7) {
         pre = p.feat_digest[t];
       }
+      // chunk of token t: the last c with offset[c] <= t, by bisection of the
+      // staged offsets [0, nc]; global offsets only past the staged table
       int c = 0;
-      while (c + 1 < nc && s_coff[c + 1] <= t) ++c;
-      while (c + 1 < d.chunks && p.chunk_offsets[c + 1] <= t) ++c;  // beyond the staged table
+      for (int hi = nc; c < hi;) {
+        const int mid = (c + hi + 1) >> 1;
+        if (s_coff[mid] <= t) c = mid;
+        else hi = mid - 1;
+      }
+      if (c == nc)
+        while (c + 1 < d.chunks && p.chunk_offsets[c + 1] <= t) ++c;
       long long val;
       switch (lane) {
         case 0: val = pre; break;

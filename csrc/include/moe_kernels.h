@@ -198,6 +198,11 @@ struct FrontendParams {
   // are at least as many dispatching workers as descriptors); 0: every
   // worker takes a share of every descriptor.
   int dispatch_groups;
+  // Router weights [E, D] copied into each worker's dynamic shared memory at
+  // byte w_off by one bulk copy at the start (the caller passes 1 to ask for
+  // the copy, 0 to read the weights from global memory; launch_frontend
+  // places them when they fit and sets 0 otherwise).
+  int w_off;
 };
 
 // Returns false (nothing launched) when the device cannot co-schedule the grid.

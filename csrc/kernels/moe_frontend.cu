@@ -466,11 +466,14 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   }
 
   // ---------------- worker CTAs
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // workers [0, Wd) dispatch; the others only route and then leave
   const int Wd = f.dispatch_ctas > 0 ? min(W, f.dispatch_ctas) : W;
   const bool dispatcher = w < Wd;
-  const T* wts = (const T*)f.rp.weight;
+  // router weights: a shared-memory copy when the launch made room for one
+  const bool w_smem = f.w_off > 0;
+  const T* wts = w_smem ? reinterpret_cast<const T*>(fsm + f.w_off) : (const T*)f.rp.weight;
+  __shared__ __align__(8) uint64_t s_wbar;
   // the per-chunk router bias rows in shared memory (behind the blob area)
   float* s_cbias = reinterpret_cast<float*>(fsm);
   if (f.rp.chunk_bias)
@@ -531,6 +534,14 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     fence_mbarrier_init();
   }
   __syncthreads();  // the chunk offsets in shared memory are complete before thread 0 walks them
+  if (w_smem && threadIdx.x == 0) {  // weights first: every routing unit needs them
+    mbar_init(&s_wbar, 1);
+    fence_mbarrier_init();
+    fence_proxy_async_smem();
+    const uint32_t wb = (uint32_t)((long long)E * row_bytes);
+    mbar_arrive_expect_tx(&s_wbar, wb);
+    bulk_load_g2s(fsm + f.w_off, f.rp.weight, wb, &s_wbar);
+  }
   if (ring && threadIdx.x == 0) {
     for (int i = 0; i < R; ++i) mbar_init(&s_rbar[i], 1);
     fence_mbarrier_init();
@@ -573,6 +584,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   auto cwi = [&]() { return grouped && k_cur == 0 ? wia : w; };
   auto cwn = [&]() { return grouped && k_cur == 0 ? wna : Wd; };
   int cum_units = 0;  // routing units (token groups, or tokens) of the chunks before c
+  bool w_wait = w_smem;  // the weights' copy has not been waited for yet
   for (int c = 0; c < C; ++c) {
     // this worker's routing units in chunk c (token groups, or tokens over its warps)
     const int my_units = share_count(first_share(w, cum_units, W), chunk_units(s_coff, c, NT), W);
@@ -643,10 +655,22 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
         srows = reinterpret_cast<const T*>(ring_base + slot * unit_bytes);
         if (consumed == 0) cta_stamp(f, 21);  // first unit in shared memory
       }
+      // diagnostics: the first two units' phases (landed, warp 0's products,
+      // its finish, the CTA barrier) in stamps 40.. and 64..
+      unsigned long long* udbg = (f.cta_clock != nullptr && consumed < 2)
+                                     ? f.cta_clock + (long long)blockIdx.x * kCtaClockSlots + (consumed == 0 ? 40 : 64)
+                                     : nullptr;
+      if (udbg != nullptr && threadIdx.x == 0) udbg[0] = globaltimer_ns();
+      if (w_wait) {  // the weights' copy, once (a wait that runs out fails the call)
+        mbar_wait_bounded(&s_wbar, 0, f.dp.status, kFrontKernelId + 4, f.timeout_ns);
+        w_wait = false;
+      }
       if (warp < nt) {  // token tf + warp, one warp each
         const int t = tf + warp;
         const T* x = srows ? srows + (long long)warp * f.rp.hidden : (const T*)f.rp.tokens + (long long)t * f.rp.hidden;
-        router_token<T, EMAX, false>(f.rp, cbias, t, x, srows != nullptr, wts, s_lg[warp], run);
+        unsigned long long* tdbg = (udbg != nullptr && warp == 0) ? udbg + 1 : nullptr;
+        if (w_smem) router_token<T, EMAX, true>(f.rp, cbias, t, x, srows != nullptr, wts, s_lg[warp], run, tdbg);
+        else router_token<T, EMAX, false>(f.rp, cbias, t, x, srows != nullptr, wts, s_lg[warp], run, tdbg);
         if (digest) {
           const long long dg = warp_row_digest((const uint4*)x, row_bytes / 16);
           if (lane == 0) {
@@ -656,6 +680,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
         }
       }
       __syncthreads();  // every warp is done with the unit's rows
+      if (udbg != nullptr && threadIdx.x == 0) udbg[3] = globaltimer_ns();
       if (ring) {
         if (consumed == 0) cta_stamp(f, 22);  // first unit routed
         if (threadIdx.x == 0) issue_next();
@@ -704,6 +729,9 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       mbar_wait_bounded(&s_rbar[(int)(consumed % R)], (uint32_t)((consumed / R) & 1), f.dp.status,
                         kFrontKernelId + 2, f.timeout_ns);
   }
+  // a worker that routed nothing still lets the weights' copy land before
+  // its shared memory is reused or released
+  if (w_wait) mbar_wait_bounded(&s_wbar, 0, f.dp.status, kFrontKernelId + 4, f.timeout_ns);
   if (!dispatcher) return;  // routing done: this SM is free for the expert side
   if (f.delayed && wait_released(f, n_desc - 1, epoch, &s_flag, true) != 1) return;
   int n_indexed = 0;  // descriptors whose index part ran before their release (diagnostics)
@@ -765,12 +793,25 @@ bool launch_frontend(const FrontendParams& f, bool bf16, int sms, cudaStream_t s
   // kUnitTokens rows within kRingBudget bytes)
   const size_t cwords = (size_t)f.dp.dims.chunks * f.dp.dims.experts * sizeof(int);
   FrontendParams g = f;
-  const size_t ring_off = (cwords + 127) & ~(size_t)127;
+  // Workers: [bias rows][router weights, when they fit][ring].  The weights
+  // (at most kWeightBudget bytes) come out of the ring's share of
+  // kSmemBudget, as long as the ring keeps two slots; kSmemBudget leaves room
+  // for the kernel's static shared memory (about 31 KB) under the 227 KB limit.
+  const size_t w_bytes = (size_t)E * f.rp.hidden * (bf16 ? 2 : 4);
+  constexpr size_t kSmemBudget = 196 * 1024, kWeightBudget = 64 * 1024, kRingMaxBudget = 160 * 1024;
+  const size_t w_off = (cwords + 127) & ~(size_t)127;
   const size_t unit = (size_t)kUnitTokens * f.rp.hidden * (bf16 ? 2 : 4);
-  constexpr size_t kRingBudget = 160 * 1024;
-  g.ring_slots = f.ring_slots ? (int)std::min<size_t>(8, kRingBudget / unit) : 0;
-  if (g.ring_slots < 2) g.ring_slots = 0;
+  auto ring_slots_from = [&](size_t off) {
+    const size_t budget = off < kSmemBudget ? std::min(kRingMaxBudget, kSmemBudget - off) : 0;
+    const int n = (int)std::min<size_t>(8, budget / unit);
+    return n >= 2 ? n : 0;
+  };
+  const size_t w_end = (w_off + w_bytes + 127) & ~(size_t)127;
+  const bool w_smem = f.ring_slots != 0 && f.w_off != 0 && w_bytes <= kWeightBudget && ring_slots_from(w_end) > 0;
+  const size_t ring_off = w_smem ? w_end : w_off;
+  g.ring_slots = f.ring_slots ? ring_slots_from(ring_off) : 0;
   g.ring_off = (int)ring_off;
+  g.w_off = w_smem ? (int)w_off : 0;
   // control CTA: blob, per-(chunk, expert) router counts, then the packed
   // control path's tables and per-ordinal words when the plan fits it
   const size_t ctl_base = ((control_smem_bytes(f.cp) + 15) & ~(size_t)15) + ((cwords + 15) & ~(size_t)15);

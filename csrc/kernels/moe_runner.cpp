@@ -124,6 +124,7 @@ class MoELayerRunner {
     dispatch_ctas_ = ints.contains("dispatch_ctas") ? geti(ints, "dispatch_ctas") : 0;
     router_ring_ = !ints.contains("router_ring") || geti(ints, "router_ring") != 0;
     dispatch_groups_ = !ints.contains("dispatch_groups") || geti(ints, "dispatch_groups") != 0;
+    router_wsmem_ = !ints.contains("router_wsmem") || geti(ints, "router_wsmem") != 0;
     max_cands_ = geti(ints, "max_cands");
     log_stride_ = geti(ints, "log_stride");
     max_ctl_tokens_ = geti(ints, "max_ctl_tokens");
@@ -382,6 +383,7 @@ class MoELayerRunner {
       fp.dispatch_ctas = progressive ? dispatch_ctas_ : 0;
       fp.ring_slots = router_ring_ ? 1 : 0;  // a request: launch_frontend sizes the ring
       fp.dispatch_groups = dispatch_groups_ ? 1 : 0;
+      fp.w_off = router_wsmem_ ? 1 : 0;  // a request: launch_frontend places the weights
       const size_t mark = trace_labels_.size();
       fp.trace = trace_slot("frontend", -1);
       raiccl::TraceSlot* first = nullptr;
@@ -739,6 +741,7 @@ class MoELayerRunner {
   int dispatch_ctas_ = 0;                // front-end workers that dispatch in progressive mode (0: all)
   bool router_ring_ = true;              // resident batches: token groups stream into shared memory by bulk copies
   bool dispatch_groups_ = true;          // one worker group per descriptor (dispatched side by side)
+  bool router_wsmem_ = true;             // router weights copied into each worker's shared memory
   bool pdl_ = true;  // plan, GEMMs and combine as programmatic dependents of their predecessors
   int max_cands_ = 0, log_stride_ = 0, max_ctl_tokens_ = 0, grid_sms_ = 148;
   bool control_serial_ = false;  // run the CTA control kernel even where the single-warp one fits

@@ -57,6 +57,8 @@ def main() -> None:
                     help="resident batches reach shared memory by bulk copies (routing and dispatch staging)")
     ap.add_argument("--dispatch-groups", type=int, default=1, choices=(0, 1),
                     help="one worker group per partial descriptor, dispatched side by side")
+    ap.add_argument("--router-wsmem", type=int, default=1, choices=(0, 1),
+                    help="router weights copied into each front-end worker's shared memory")
     args = ap.parse_args()
     import os
 
@@ -78,7 +80,8 @@ def main() -> None:
     layer = ProgressiveMoELayer(cfg, device=dev, timeout_s=10.0, trace=bool(args.trace or args.roofline),
                                 frontend=args.frontend, gemm_swap_max=args.gemm_swap_max,
                                 progressive=bool(args.progressive), dispatch_ctas=args.dispatch_ctas,
-                                router_ring=bool(args.router_ring), dispatch_groups=bool(args.dispatch_groups))
+                                router_ring=bool(args.router_ring), dispatch_groups=bool(args.dispatch_groups),
+                                router_wsmem=bool(args.router_wsmem))
     try:
         if args.cta_clocks:
             sms = torch.cuda.get_device_properties(layer.device).multi_processor_count
@@ -247,15 +250,14 @@ def _cta_clocks(layer) -> dict:
            "first_group": ({"landed_med": r(np.median(wk[first, 21])), "landed_max": r(np.max(wk[first, 21])),
                             "routed_med": r(np.median(wk[first, 22])), "routed_max": r(np.max(wk[first, 22]))}
                            if first.any() else None)}
-    if first.any():  # the first group's router phases (stamps 40..43), us after it landed
-        ph = [r(np.median(wk[first, 40 + i] - wk[first, 21])) for i in range(4)] + \
-             [r(np.median(wk[first, 22] - wk[first, 21]))]
-        out["first_group"]["phases_after_landing"] = dict(zip(
-            ("products", "warp_reduce", "barrier1", "topk", "done"), ph))
-        second = first & ~np.isnan(wk[:, 64]) & ~np.isnan(wk[:, 67]) & (wk[:, 64] > wk[:, 22])
-        if second.any():  # the second group's phases (stamps 64..67), us after the first was routed
-            out["second_group"] = dict(zip(("products", "warp_reduce", "barrier1", "topk"),
-                                           [r(np.median(wk[second, 64 + i] - wk[second, 22])) for i in range(4)]))
+    # the first two units' phases (stamps 40.. and 64..: landed, warp 0's
+    # products, its top-k finish, the CTA barrier), medians in us
+    for name, b in (("unit0", 40), ("unit1", 64)):
+        ok = ~np.isnan(wk[:, b]) & ~np.isnan(wk[:, b + 3]) & (wk[:, b] >= wk[:, 0])
+        if ok.any():
+            d = lambda i, j: r(np.median(wk[ok, b + j] - wk[ok, b + i]))
+            out[name] = {"landed_med": r(np.median(wk[ok, b])), "products": d(0, 1), "finish": d(1, 2),
+                         "barrier": d(2, 3), "workers": int(ok.sum())}
     for c in range(min(8, layer.cfg.chunks)):
         b, e, routed = wk[:, 2 + 2 * c], wk[:, 3 + 2 * c], wk[:, 52 + c]
         out["chunks"].append({"chunk": c, "begin_med": r(np.nanmedian(b)), "dur_med": r(np.nanmedian(e - b)),
@@ -264,9 +266,10 @@ def _cta_clocks(layer) -> dict:
                               "end_max": r(np.nanmax(e))})
     for q in range(min(8, layer.cfg.n_desc)):
         b, mid, e = wk[:, 24 + 2 * q], wk[:, 44 + q], wk[:, 25 + 2 * q]
-        ix, idn, rw = wk[:, 68 + 4 * q], wk[:, 69 + 4 * q], wk[:, 70 + 4 * q]
-        ok = (ix >= b) & (rw <= mid)  # this call's stamps (staged rows only)
-        phase = ({"index_med": r(np.median(ix[ok] - b[ok])), "identity_med": r(np.median(idn[ok] - ix[ok])),
+        ix, idn, rw, ids = wk[:, 68 + 4 * q], wk[:, 69 + 4 * q], wk[:, 70 + 4 * q], wk[:, 71 + 4 * q]
+        ok = (ix >= b) & (rw <= mid) & (ids >= ix)  # this call's stamps (staged rows only)
+        phase = ({"index_med": r(np.median(ix[ok] - b[ok])), "id_inputs_med": r(np.median(ids[ok] - ix[ok])),
+                  "identity_med": r(np.median(idn[ok] - ids[ok])),
                   "rows_med": r(np.median(rw[ok] - idn[ok]))} if ok.any() else None)
         out["descriptors"].append({"desc": q, "begin_min": r(np.nanmin(b)), "begin_med": r(np.nanmedian(b)),
                                    "rows_med": r(np.nanmedian(mid - b)), "publish_max": r(np.nanmax(e - mid)),
