@@ -2,7 +2,8 @@
 // one-launch-per-step kernels (csrc/kernels/moe_dataplane.cu) and the
 // persistent front-end kernel (csrc/kernels/moe_frontend.cu):
 //   * identity-checksum arithmetic mod 2^63 - 25;
-//   * router_token  — one warp routes one token (logits, mask, stable top-k, gates);
+//   * router_token  — one warp routes one token (logits, mask, stable top-k, gates,
+//                     the finish lane-parallel over experts);
 //   * dispatch_rows — one CTA packs and stores its share of a revealed
 //                     descriptor's rows into the owners' receive regions;
 //   * dispatch_publish — the last CTA of a descriptor publishes its per-expert
@@ -113,55 +114,93 @@ constexpr int kDispatchMaxItems = 4096;
 constexpr int kMaxExperts = 256;
 constexpr int kDispatchMaxChunks = 128;  // chunk-offset table staged in shared memory
 
-// Logits -> mask -> stable descending top-k (the smaller expert id wins ties)
-// -> gates; writes expert_ids / gates of row t (one thread per token).
-// bias / chunk_bias / block_mask may point at global memory or at shared
-// copies; the values, and so the routing, are the same.
-// Finish token t from its E raw dot products, held in shared memory lg[0, E):
-// logits (bias, chunk bias, masked experts -inf), stable descending top-k (the
-// smaller expert id wins ties), gates per gate_mode; writes expert_ids / gates
-// of row t and counts every choice in sel_counts (shared, or nullptr).  One
-// thread; sel is 8 ints of this thread's shared scratch.  The loops stay
-// rolled: the code runs once per token, largely from a cold instruction
-// cache, so its size matters more than its loop overhead.
-__device__ inline void router_finish(const RouterParams& p, const float* bias, const float* chunk_bias,
-                                     const uint8_t* block_mask, int t, float* lg, int* sel, int* sel_counts) {
-  const int E = p.experts, k = p.top_k;
+// Order of the router's top-k candidates: rank 2 (a number) above rank 1
+// (NaN) above rank 0 (no candidate: an id >= E, or already chosen); numbers
+// by value; equal values, and equal ranks below 2, by the smaller expert id.
+__device__ __forceinline__ bool router_better(int ra, float va, int ea, int rb, float vb, int eb) {
+  if (ra != rb) return ra > rb;
+  if (ra == 2 && va != vb) return va > vb;
+  return ea < eb;
+}
+
+// Warp-parallel finish of token t; every lane holds every expert's raw dot
+// product in acc.  Lane e takes expert e (and e + 32 when EMAX is 64): logit =
+// raw + bias + chunk bias, -inf when masked.  Top-k is k rounds of a warp
+// arg-max in router_better's order (a strict total order, so every lane of
+// the butterfly agrees); lane j keeps choice j and writes its expert id, its
+// count in sel_counts (shared, or nullptr) and its gate per gate_mode.
+template <int EMAX>
+__device__ __forceinline__ void router_finish_warp(const RouterParams& p, const float* chunk_bias, int t,
+                                                   const float (&acc)[EMAX], int* sel_counts) {
+  constexpr int PER = EMAX > 32 ? 2 : 1;
+  const int E = p.experts, k = p.top_k, lane = threadIdx.x & 31;
   const float ninf = -__int_as_float(0x7f800000);
-#pragma unroll 1
-  for (int e = 0; e < E; ++e) {
-    const float l = lg[e] + bias[e] + (chunk_bias ? chunk_bias[e] : 0.f);
-    const bool masked = (p.mask_mode == 1 && e == (t % E)) || (block_mask && block_mask[e]);
-    lg[e] = masked ? ninf : l;
+  float v[PER];
+  int rank[PER];
+#pragma unroll
+  for (int h = 0; h < PER; ++h) {
+    const int e = lane + 32 * h;
+    float raw = 0.f;
+#pragma unroll
+    for (int i = 32 * h; i < EMAX && i < 32 * h + 32; ++i)
+      if (i == e) raw = acc[i];
+    if (e < E) {
+      const float l = raw + __ldg(p.bias + e) + (chunk_bias ? chunk_bias[e] : 0.f);
+      const bool masked = (p.mask_mode == 1 && e == (t % E)) || (p.block_mask && __ldg(p.block_mask + e));
+      v[h] = masked ? ninf : l;
+      rank[h] = v[h] == v[h] ? 2 : 1;
+    } else {
+      v[h] = ninf;
+      rank[h] = 0;
+    }
   }
-  unsigned long long taken = 0;  // E <= 64
+  float l0 = 0.f, my_l = ninf;
+  int my_e = -1;
 #pragma unroll 1
   for (int j = 0; j < k; ++j) {
-    int best = -1;
-    float bv = ninf;
-#pragma unroll 1
-    for (int e = 0; e < E; ++e)
-      if (!((taken >> e) & 1ull) && (best < 0 || lg[e] > bv)) { best = e; bv = lg[e]; }
-    taken |= 1ull << best;
-    sel[j] = best;
-    p.expert_ids[(long long)t * k + j] = best;
-    if (sel_counts) atomicAdd(&sel_counts[best], 1);
+    float bv = v[0];
+    int br = rank[0], be = lane;
+    if (PER == 2 && router_better(rank[PER - 1], v[PER - 1], lane + 32, br, bv, be)) {
+      bv = v[PER - 1];
+      br = rank[PER - 1];
+      be = lane + 32;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int orank = __shfl_xor_sync(0xffffffffu, br, o), oe = __shfl_xor_sync(0xffffffffu, be, o);
+      if (router_better(orank, ov, oe, br, bv, be)) {
+        bv = ov;
+        br = orank;
+        be = oe;
+      }
+    }
+    if ((be & 31) == lane) rank[be >> 5] = 0;  // chosen: out of the later rounds
+    if (lane == j) {
+      my_e = be;
+      my_l = bv;
+    }
+    if (j == 0) l0 = bv;
   }
-  const float l0 = lg[sel[0]];
   float sum = 1.f;
-  if (p.gate_mode == 1) {
-    sum = 0.f;
-#pragma unroll 1
-    for (int j = 0; j < k; ++j) sum += __expf(lg[sel[j]] - l0);
-  } else if (p.gate_mode == 2) {
-    sum = 0.f;
-#pragma unroll 1
-    for (int e = 0; e < E; ++e)
-      if (lg[e] != ninf) sum += __expf(lg[e] - l0);
+  if (p.gate_mode != 0) {
+    float part = 0.f;
+    if (p.gate_mode == 1) {
+      if (lane < k) part = __expf(my_l - l0);
+    } else {
+#pragma unroll
+      for (int h = 0; h < PER; ++h)
+        if (lane + 32 * h < E && v[h] != ninf) part += __expf(v[h] - l0);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    sum = part;
   }
-#pragma unroll 1
-  for (int j = 0; j < k; ++j)
-    p.gates[(long long)t * k + j] = p.gate_mode == 0 ? 1.f : __expf(lg[sel[j]] - l0) / sum;
+  if (lane < k) {
+    p.expert_ids[(long long)t * k + lane] = my_e;
+    if (sel_counts) atomicAdd(&sel_counts[my_e], 1);
+    p.gates[(long long)t * k + lane] = p.gate_mode == 0 ? 1.f : __expf(my_l - l0) / sum;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -169,14 +208,14 @@ __device__ inline void router_finish(const RouterParams& p, const float* bias, c
 // bias), masked experts -inf, stable descending top-k (the smaller expert id
 // wins ties), gates per gate_mode; writes expert_ids / gates of row t and
 // counts the choices in sel_counts (shared, or nullptr).  x: the token's row,
-// in shared memory (x_shared) or in global memory.  s_lg: EMAX + 8 words of
-// this warp's shared scratch.  SMEM_W: w points at a shared-memory copy of the
-// weights.  Every lane sums its vectors in row order, then a butterfly adds
-// the lanes: the same order wherever the row comes from.
+// in shared memory (x_shared) or in global memory.  SMEM_W: w points at a
+// shared-memory copy of the weights.  Every lane sums its vectors in row
+// order, then a butterfly adds the lanes (every lane ends with the same sums):
+// the same order wherever the row comes from.
 // ---------------------------------------------------------------------------
 template <typename T, int EMAX, bool SMEM_W>
 __device__ __forceinline__ void router_token(const RouterParams& p, const float* chunk_bias, int t, const T* x,
-                                             bool x_shared, const T* __restrict__ w, float* s_lg, int* sel_counts,
+                                             bool x_shared, const T* __restrict__ w, int* sel_counts,
                                              unsigned long long* dbg = nullptr) {
   const int D = p.hidden, E = p.experts;
   const int lane = threadIdx.x & 31;
@@ -226,12 +265,8 @@ __device__ __forceinline__ void router_token(const RouterParams& p, const float*
       acc[e] = v;
     }
   }
-  if (lane != 0) return;
-#pragma unroll
-  for (int e = 0; e < EMAX; ++e)
-    if (e < E) s_lg[e] = acc[e];
-  router_finish(p, p.bias, chunk_bias, p.block_mask, t, s_lg, reinterpret_cast<int*>(s_lg + EMAX), sel_counts);
-  if (dbg != nullptr) dbg[1] = globaltimer_ns();
+  router_finish_warp<EMAX>(p, chunk_bias, t, acc, sel_counts);
+  if (dbg != nullptr && lane == 0) dbg[1] = globaltimer_ns();
 }
 
 // ---------------------------------------------------------------------------

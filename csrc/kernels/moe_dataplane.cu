@@ -76,12 +76,11 @@ __global__ void __launch_bounds__(256) moe_router_kernel(RouterParams p) {
     __syncthreads();
     w = (const T*)router_smem;
   }
-  __shared__ float s_lg[8][EMAX + 8];  // per-warp logit scratch of router_token
   const int warps = blockDim.x >> 5;
   const int t = p.row0 + blockIdx.x * warps + (threadIdx.x >> 5);
   if (t >= p.row1) return;
   router_token<T, EMAX, SMEM_W>(p, p.chunk_bias, t, (const T*)p.tokens + (long long)t * p.hidden, false, w,
-                                s_lg[threadIdx.x >> 5], nullptr);
+                                nullptr);
 }
 
 // ---------------------------------------------------------------------------

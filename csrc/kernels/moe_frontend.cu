@@ -401,7 +401,6 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   __shared__ int item_pos[kDispatchMaxItems];
   __shared__ int s_coff[kDispatchMaxChunks + 1];
   __shared__ int s_flag;
-  __shared__ float s_lg[8][EMAX + 8];  // per-warp logit scratch of router_token
   TraceScope trace_scope(f.trace);
   const MoEDims& d = f.dp.dims;
   const int C = d.chunks, E = d.experts, n_desc = d.n_desc;
@@ -669,8 +668,8 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
         const int t = tf + warp;
         const T* x = srows ? srows + (long long)warp * f.rp.hidden : (const T*)f.rp.tokens + (long long)t * f.rp.hidden;
         unsigned long long* tdbg = (udbg != nullptr && warp == 0) ? udbg + 1 : nullptr;
-        if (w_smem) router_token<T, EMAX, true>(f.rp, cbias, t, x, srows != nullptr, wts, s_lg[warp], run, tdbg);
-        else router_token<T, EMAX, false>(f.rp, cbias, t, x, srows != nullptr, wts, s_lg[warp], run, tdbg);
+        if (w_smem) router_token<T, EMAX, true>(f.rp, cbias, t, x, srows != nullptr, wts, run, tdbg);
+        else router_token<T, EMAX, false>(f.rp, cbias, t, x, srows != nullptr, wts, run, tdbg);
         if (digest) {
           const long long dg = warp_row_digest((const uint4*)x, row_bytes / 16);
           if (lane == 0) {
