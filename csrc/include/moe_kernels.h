@@ -2,6 +2,7 @@
 // (plain data shared by the host bindings and the .cu launch units).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -203,10 +204,26 @@ struct FrontendParams {
   // the copy, 0 to read the weights from global memory; launch_frontend
   // places them when they fit and sets 0 otherwise).
   int w_off;
+  // Tensor-core router (bf16 batches, E <= 64, D a multiple of 64): workers
+  // route units of 128 tokens as one tcgen05 MMA tile (M = 128 tokens, N =
+  // tc_npad = E rounded up to 16) from tc_stages TMA stages carved from the
+  // ring memory (set by launch_frontend; the caller passes tc_router = 1 to
+  // ask for it).  tmap_x / tmap_w: the token matrix [T, D] and the router
+  // weights [E, D] as 2-D tensor maps with 64 x 128 and 64 x tc_npad boxes,
+  // 128-byte swizzle (built once by the caller).
+  int tc_router;
+  int tc_stages;
+  int tc_npad;
+  // Bytes of the ring memory (routing ring or tensor-core stages) that the
+  // dispatch stages rows through once routing is done (0: no staging).
+  int ring_bytes;
+  CUtensorMap tmap_x;
+  CUtensorMap tmap_w;
 };
 
 // Returns false (nothing launched) when the device cannot co-schedule the grid.
-bool launch_frontend(const FrontendParams& f, bool bf16, int sms, cudaStream_t s);
+// tc_used (optional): 1 when the launch routes on the tensor cores.
+bool launch_frontend(const FrontendParams& f, bool bf16, int sms, cudaStream_t s, int* tc_used = nullptr);
 size_t control_smem_bytes(const ControlParams& p);
 ControlDims control_dims(const ControlParams& p);
 bool control_warp_path_ok(const ControlParams& p);

@@ -40,11 +40,13 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <type_traits>
 
 #include "control_warp.cuh"
 #include "control_warp_packed.cuh"
 #include "launchers.h"
 #include "moe_device.cuh"
+#include "router_tc.cuh"
 #include "moe_kernels.h"
 #include "sm100_ptx.cuh"
 
@@ -388,12 +390,16 @@ __device__ int wait_released(const FrontendParams& f, int q, unsigned long long 
 // Routing: a worker routes units of kUnitTokens consecutive tokens, one token
 // per warp (router_token, up to EMAX experts), from the shared-memory ring
 // (resident batch) or from global memory; the step pipeline's router kernel
-// runs the same per-token code, so both route identically.
+// runs the same per-token code, so both route identically.  With the
+// tensor-core router (bf16, f.tc_router) a unit is kTcRows tokens, one MMA
+// tile (router_tc.cuh).
 constexpr int kUnitTokens = 8;
 
 template <typename T, int EMAX>
 __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __grid_constant__ FrontendParams f) {
-  constexpr int NT = kUnitTokens;
+  // tokens per routing unit (the control CTA counts chunk completion in the same units)
+  const bool tc = std::is_same<T, __nv_bfloat16>::value && f.tc_router != 0;
+  const int NT = tc ? kTcRows : kUnitTokens;
   extern __shared__ __align__(16) uint8_t fsm[];
   __shared__ int hist[kMaxExperts];
   __shared__ int run[kMaxExperts];
@@ -410,8 +416,9 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   const int nc = min(C, kDispatchMaxChunks);
   for (int c = threadIdx.x; c <= nc; c += blockDim.x) s_coff[c] = f.dp.chunk_offsets[c];
   // the progressive expert planner (next launch) may start now: it waits on
-  // the ready words itself
-  if (f.early_dependents) griddep_launch_dependents();
+  // the ready words itself (workers signal it once their TMEM columns, if
+  // any, are allocated, so a dependent CTA never holds TMEM before them)
+  if (f.early_dependents && blockIdx.x == 0) griddep_launch_dependents();
 
   if (blockIdx.x == 0) {
     // ---------------- control CTA
@@ -524,8 +531,40 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   // used by a streamed batch), holds the rows of a dispatch share
   __shared__ __align__(8) uint64_t s_dbar[2];
   __shared__ uint32_t s_duses[2];
-  const DispatchStage dstage{ring_base, f.ring_slots * (int)unit_bytes, s_dbar, s_duses, f.timeout_ns};
-  const DispatchStage* stage = f.ring_slots >= 2 ? &dstage : nullptr;
+  // tensor-core router: stages at the first 1024-byte boundary of the ring memory
+  uint8_t* tc_base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ring_base) + 1023) & ~(uintptr_t)1023);
+  const DispatchStage dstage{tc ? tc_base : ring_base, f.ring_bytes, s_dbar, s_duses, f.timeout_ns};
+  const DispatchStage* stage = f.ring_bytes > 0 ? &dstage : nullptr;
+  __shared__ __align__(8) uint64_t s_tcbar[2 * kTcMaxStages + 1];
+  __shared__ uint32_t s_tmem;
+  TcRouter tcr{};
+  if (tc) {
+    tcr.stages = tc_base;
+    tcr.npad = f.tc_npad;
+    tcr.n_stages = f.tc_stages;
+    tcr.kblocks = f.rp.hidden / kTcBK;
+    tcr.lg = reinterpret_cast<float*>(tc_base + (long long)f.tc_stages * tcr.stage_bytes());
+    tcr.sel = tcr.lg + f.tc_npad * kTcRows;
+    tcr.full = s_tcbar;
+    tcr.empty = s_tcbar + kTcMaxStages;
+    tcr.done = s_tcbar + 2 * kTcMaxStages;
+    if (threadIdx.x == 0) {
+      for (int i = 0; i < f.tc_stages; ++i) {
+        mbar_init(&tcr.full[i], 1);
+        mbar_init(&tcr.empty[i], 1);
+      }
+      mbar_init(tcr.done, 1);
+      fence_mbarrier_init();
+      tma_prefetch_desc(&f.tmap_x);
+      tma_prefetch_desc(&f.tmap_w);
+    }
+    // the accumulator's TMEM columns (a power of two >= 32), held while routing
+    if (warp == 4) {
+      tmem_alloc(&s_tmem, f.tc_npad <= 32 ? 32u : 64u);
+      tmem_relinquish();
+    }
+    tc_fence_before_sync();
+  }
   if (threadIdx.x == 0) {
     mbar_init(&s_dbar[0], 1);
     mbar_init(&s_dbar[1], 1);
@@ -551,6 +590,11 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   }
   cta_stamp(f, 0);
   __syncthreads();
+  if (tc) {
+    tc_fence_after_sync();
+    tcr.tmem = s_tmem;
+  }
+  if (f.early_dependents) griddep_launch_dependents();
   cta_stamp(f, 1);
   // Descriptors this worker dispatches.  When every partial descriptor can
   // have workers of its own, the partial descriptors get disjoint worker
@@ -645,6 +689,41 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     const int ngroups = chunk_units(s_coff, c, NT);
     for (int g = first_share(w, cum_units, W); g < ngroups; g += W) {
       const int tf = t0 + g * NT, nt = min(NT, t1 - tf);
+      if (tc) {
+        // tensor-core unit: thread 128 (warp 4) issues the loads and MMAs,
+        // warps 0-3 finish one token each; diagnostics of the first two units
+        // in stamps 40.. and 64.. (issue, MMAs done, finish, barrier)
+        unsigned long long* tdbg = (f.cta_clock != nullptr && tcr.n_units < 2)
+                                       ? f.cta_clock + (long long)blockIdx.x * kCtaClockSlots +
+                                             (tcr.n_units == 0 ? 40 : 64)
+                                       : nullptr;
+        if (tdbg != nullptr && threadIdx.x == 0) tdbg[0] = globaltimer_ns();
+        if (threadIdx.x == 128)
+          tc_router_issue(tcr, &f.tmap_x, &f.tmap_w, tf, f.dp.status, kFrontKernelId + 5, f.timeout_ns);
+        if (threadIdx.x < 128) {
+          tc_router_finish<EMAX>(f.rp, cbias, tcr, tf, nt, run, f.dp.status, kFrontKernelId + 5, f.timeout_ns,
+                                 tdbg != nullptr ? tdbg + 1 : nullptr);
+          if (tdbg != nullptr && threadIdx.x == 0) tdbg[2] = globaltimer_ns();
+        }
+        tc_fence_before_sync();
+        __syncthreads();
+        tc_fence_after_sync();
+        ++tcr.n_units;
+        if (digest) {  // streamed rows: feature digest and checksum base, one warp per token
+          for (int i = warp; i < nt; i += kFrontThreads / 32) {
+            const int t = tf + i;
+            const long long dg =
+                warp_row_digest((const uint4*)((const T*)f.rp.tokens + (long long)t * f.rp.hidden), row_bytes / 16);
+            if (lane == 0) {
+              f.digest_out[t] = dg;
+              f.csbase_out[t] = token_checksum_base(f.dp.token_ids[t], f.dp.dims.rank, c, t - t0, t, dg);
+            }
+          }
+          __syncthreads();
+        }
+        if (tdbg != nullptr && threadIdx.x == 0) tdbg[3] = globaltimer_ns();
+        continue;
+      }
       const T* srows = nullptr;
       if (ring) {
         const int slot = (int)(consumed % R);
@@ -731,6 +810,12 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   // a worker that routed nothing still lets the weights' copy land before
   // its shared memory is reused or released
   if (w_wait) mbar_wait_bounded(&s_wbar, 0, f.dp.status, kFrontKernelId + 4, f.timeout_ns);
+  if (tc) {  // every unit's MMAs completed and were read: give the TMEM columns back
+    tc_fence_before_sync();
+    __syncthreads();
+    tc_fence_after_sync();
+    if (warp == 4) tmem_dealloc(tcr.tmem, f.tc_npad <= 32 ? 32u : 64u);
+  }
   if (!dispatcher) return;  // routing done: this SM is free for the expert side
   if (f.delayed && wait_released(f, n_desc - 1, epoch, &s_flag, true) != 1) return;
   int n_indexed = 0;  // descriptors whose index part ran before their release (diagnostics)
@@ -782,7 +867,7 @@ bool launch_one_frontend(const FrontendParams& f, int sms, size_t smem, cudaStre
 
 }  // namespace
 
-bool launch_frontend(const FrontendParams& f, bool bf16, int sms, cudaStream_t s) {
+bool launch_frontend(const FrontendParams& f, bool bf16, int sms, cudaStream_t s, int* tc_used) {
   const int E = f.rp.experts;
   if (sms < 2 || !control_warp_path_ok(f.cp) || E > 64 || f.rp.top_k > 8 || f.dp.dims.chunks > kDispatchMaxChunks ||
       (f.rp.hidden * (bf16 ? 2 : 4)) % 16 != 0)
@@ -811,13 +896,36 @@ bool launch_frontend(const FrontendParams& f, bool bf16, int sms, cudaStream_t s
   g.ring_slots = f.ring_slots ? ring_slots_from(ring_off) : 0;
   g.ring_off = (int)ring_off;
   g.w_off = w_smem ? (int)w_off : 0;
+  g.ring_bytes = g.ring_slots * (int)unit;
+  size_t worker_bytes = g.ring_slots ? ring_off + g.ring_slots * unit : cwords;
+  // Tensor-core router (bf16): TMA stages in place of the ring and the weight
+  // copy, at a 1024-byte boundary, then the finish's logit scratch.
+  g.tc_router = 0;
+  if (bf16 && f.tc_router && f.rp.hidden % kTcBK == 0 && f.rp.top_k <= kTcSelStride) {
+    const int npad = std::max(16, (E + 15) / 16 * 16);
+    const size_t stage = (size_t)kTcRows * 128 + (size_t)npad * 128;
+    const size_t sel = (size_t)tc_router_scratch_bytes(npad);
+    const size_t avail = kSmemBudget > w_off + 1024 + sel ? kSmemBudget - w_off - 1024 - sel : 0;
+    const int stages = (int)std::min<size_t>(kTcMaxStages, avail / stage);
+    if (stages >= 2) {
+      g.tc_router = 1;
+      g.tc_stages = stages;
+      g.tc_npad = npad;
+      g.ring_slots = 0;
+      g.w_off = 0;
+      g.ring_off = (int)w_off;
+      g.ring_bytes = (int)(stages * stage);
+      worker_bytes = w_off + 1024 + stages * stage + sel;
+    }
+  }
   // control CTA: blob, per-(chunk, expert) router counts, then the packed
   // control path's tables and per-ordinal words when the plan fits it
   const size_t ctl_base = ((control_smem_bytes(f.cp) + 15) & ~(size_t)15) + ((cwords + 15) & ~(size_t)15);
   const ControlDims cd = control_dims(f.cp);
   g.ctl_packed_off = ctl::packed_path_ok(cd) ? (int)ctl_base : 0;
   const size_t ctl_bytes = ctl_base + (g.ctl_packed_off ? (size_t)ctl::packed_smem_bytes(cd) : 0);
-  const size_t smem = std::max(ctl_bytes, g.ring_slots ? ring_off + g.ring_slots * unit : cwords);
+  const size_t smem = std::max(ctl_bytes, worker_bytes);
+  if (tc_used != nullptr) *tc_used = g.tc_router;
   if (E <= 8) return bf16 ? launch_one_frontend<__nv_bfloat16, 8>(g, sms, smem, s)
                           : launch_one_frontend<float, 8>(g, sms, smem, s);
   if (E <= 16) return bf16 ? launch_one_frontend<__nv_bfloat16, 16>(g, sms, smem, s)

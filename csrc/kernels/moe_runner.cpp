@@ -125,6 +125,7 @@ class MoELayerRunner {
     router_ring_ = !ints.contains("router_ring") || geti(ints, "router_ring") != 0;
     dispatch_groups_ = !ints.contains("dispatch_groups") || geti(ints, "dispatch_groups") != 0;
     router_wsmem_ = !ints.contains("router_wsmem") || geti(ints, "router_wsmem") != 0;
+    router_tc_ = !ints.contains("router_tc") || geti(ints, "router_tc") != 0;
     max_cands_ = geti(ints, "max_cands");
     log_stride_ = geti(ints, "log_stride");
     max_ctl_tokens_ = geti(ints, "max_ctl_tokens");
@@ -150,6 +151,16 @@ class MoELayerRunner {
     ta1n_ = raiccl::make_tmap_2d_sw128(recv_feat, dt, eb, rows, d.hidden, d.hidden, 8, bk);
     ta2n_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "h"), dt, eb, rows, ffn_, ffn_, 8, bk);
     tb2_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "w2"), dt, eb, (uint64_t)d.expert_slots * d.out_dim, ffn_, ffn_, pair2_ ? bn2_ / 2 : bn2_, bk);
+    // tensor-core router (bf16): the token matrix in 128-token boxes and the
+    // router weights in one box of E rounded up to 16 rows (rows past E read as zero)
+    if (feat_bf16_ && router_tc_ && d.hidden % 64 == 0 && d.experts <= 64 && d.top_k <= 8) {
+      const uint32_t npad = (uint32_t)std::max(16, (d.experts + 15) / 16 * 16);
+      tx_router_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "tokens"), dt, eb, (uint64_t)d.tokens, d.hidden,
+                                              d.hidden, 128, bk);
+      tw_router_ = raiccl::make_tmap_2d_sw128(ptr<void>(tensors, "router_w"), dt, eb, (uint64_t)d.experts, d.hidden,
+                                              d.hidden, npad, bk);
+      have_tc_router_ = true;
+    }
 
     {
       int coop = 0;
@@ -384,6 +395,11 @@ class MoELayerRunner {
       fp.ring_slots = router_ring_ ? 1 : 0;  // a request: launch_frontend sizes the ring
       fp.dispatch_groups = dispatch_groups_ ? 1 : 0;
       fp.w_off = router_wsmem_ ? 1 : 0;  // a request: launch_frontend places the weights
+      if (have_tc_router_) {  // a request: launch_frontend sizes the stages
+        fp.tc_router = 1;
+        fp.tmap_x = tx_router_;
+        fp.tmap_w = tw_router_;
+      }
       const size_t mark = trace_labels_.size();
       fp.trace = trace_slot("frontend", -1);
       raiccl::TraceSlot* first = nullptr;
@@ -395,7 +411,10 @@ class MoELayerRunner {
       for (int q = 0; q < d.n_desc; ++q) trace_slot("dispatch", q);
       fp.phase_trace = (first != nullptr && trace_labels_.size() == mark + 1 + d.chunks + 2 * d.n_desc) ? first
                                                                                                        : nullptr;
-      if (raiccl::launch_frontend(fp, feat_bf16_, grid_sms_, comm_)) {
+      int tcu = 0;
+      const bool launched = raiccl::launch_frontend(fp, feat_bf16_, grid_sms_, comm_, &tcu);
+      tc_used_ = launched ? tcu : 0;
+      if (launched) {
         ++launches;
       } else {
         trace_labels_.resize(mark);
@@ -698,6 +717,8 @@ class MoELayerRunner {
   // Takes effect at the next forward() / capture().
   void inject_skip_signal(int desc) { fault_skip_signal_desc_ = desc; }
   bool persistent_frontend() const { return use_frontend_; }
+  // the last front-end launch routed on the tensor cores
+  bool router_tc_used() const { return use_frontend_ && tc_used_ != 0; }
   bool progressive() const { return progressive_req_ && use_frontend_; }
 
   py::list trace_labels() const {
@@ -742,6 +763,10 @@ class MoELayerRunner {
   bool router_ring_ = true;              // resident batches: token groups stream into shared memory by bulk copies
   bool dispatch_groups_ = true;          // one worker group per descriptor (dispatched side by side)
   bool router_wsmem_ = true;             // router weights copied into each worker's shared memory
+  bool router_tc_ = true;                // bf16 batches: tensor-core router units of 128 tokens
+  bool have_tc_router_ = false;          // router tensor maps built (bf16, D % 64 == 0, E <= 64)
+  int tc_used_ = 0;                      // the last front-end launch routed on the tensor cores
+  CUtensorMap tx_router_{}, tw_router_{};
   bool pdl_ = true;  // plan, GEMMs and combine as programmatic dependents of their predecessors
   int max_cands_ = 0, log_stride_ = 0, max_ctl_tokens_ = 0, grid_sms_ = 148;
   bool control_serial_ = false;  // run the CTA control kernel even where the single-warp one fits
@@ -920,6 +945,7 @@ void register_moe(py::module_& m) {
       .def("trace_labels", &MoELayerRunner::trace_labels)
       .def("inject_skip_signal", &MoELayerRunner::inject_skip_signal, py::arg("desc"))
       .def("persistent_frontend", &MoELayerRunner::persistent_frontend)
+      .def("router_tc_used", &MoELayerRunner::router_tc_used)
       .def("progressive", &MoELayerRunner::progressive)
       .def("layout", &MoELayerRunner::layout);
   m.def("router_topk", &router_topk, py::arg("tokens"), py::arg("weight"), py::arg("bias"),

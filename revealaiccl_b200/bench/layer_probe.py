@@ -59,6 +59,8 @@ def main() -> None:
                     help="one worker group per partial descriptor, dispatched side by side")
     ap.add_argument("--router-wsmem", type=int, default=1, choices=(0, 1),
                     help="router weights copied into each front-end worker's shared memory")
+    ap.add_argument("--router-tc", type=int, default=1, choices=(0, 1),
+                    help="bf16 batches: 128-token router units on the tensor cores")
     args = ap.parse_args()
     import os
 
@@ -81,7 +83,7 @@ def main() -> None:
                                 frontend=args.frontend, gemm_swap_max=args.gemm_swap_max,
                                 progressive=bool(args.progressive), dispatch_ctas=args.dispatch_ctas,
                                 router_ring=bool(args.router_ring), dispatch_groups=bool(args.dispatch_groups),
-                                router_wsmem=bool(args.router_wsmem))
+                                router_wsmem=bool(args.router_wsmem), router_tc=bool(args.router_tc))
     try:
         if args.cta_clocks:
             sms = torch.cuda.get_device_properties(layer.device).multi_processor_count

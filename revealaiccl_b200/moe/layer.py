@@ -59,7 +59,7 @@ class ProgressiveMoELayer:
                  control_path: str = "auto", trace: bool = False, frontend: str = "persistent",
                  gemm_pair: bool = True, pdl: bool = True, gemm_swap_max: int = 128,
                  progressive: bool = False, dispatch_ctas: int = 0, router_ring: bool = True,
-                 dispatch_groups: bool = True, router_wsmem: bool = True) -> None:
+                 dispatch_groups: bool = True, router_wsmem: bool = True, router_tc: bool = True) -> None:
         self.cfg = cfg
         if world is None:
             world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -162,6 +162,9 @@ class ProgressiveMoELayer:
             # the router weights reach each worker's shared memory by one bulk
             # copy at the start of the front end (when they fit, 64 KiB)
             "router_wsmem": int(bool(router_wsmem)),
+            # bf16 batches: front-end workers route 128-token units on the
+            # tensor cores (tcgen05 MMA, TMA-staged tokens and weights)
+            "router_tc": int(bool(router_tc)),
         }
         self.layout = self._k.sym_layout(ints)
         self.channel = PeerChannel(self.layout["total"], dev, group=group)

@@ -570,3 +570,50 @@ def test_prereleased_index_and_plain_dispatch_paths_both_run():
         assert torch.equal(outs["early"], outs["delayed"])
     finally:
         layer.close()
+
+
+TC_SHAPES = {
+    "skewed_bf16": dict(tokens_per_rank=2048, chunk_sizes=(128,) * 16),
+    "deepseek_v2_lite": dict(tokens_per_rank=2048, chunk_sizes=(128,) * 16),
+    "mixtral_8x7b": dict(tokens_per_rank=1024, chunk_sizes=(96,) * 8 + (128, 96, 32) + (0,) * 21),
+}
+
+
+@pytest.mark.parametrize("name", sorted(TC_SHAPES))
+def test_tensor_core_router_matches_warp_router(name):
+    """bf16 batches route 128-token units on the tensor cores (tcgen05 MMA fed
+    by TMA, accumulator in TMEM).  Against the warp router (CUDA-core dot
+    products) the choices agree wherever the top-k is not a near tie, the gates
+    agree to fp32 rounding, both pass the fail-closed checker against the fp32
+    oracle, and a streamed end-to-end call routes exactly like a resident one
+    (ragged and empty chunks included)."""
+    from revealaiccl_b200.moe.config import preset
+    from revealaiccl_b200.moe.layer import ProgressiveMoELayer
+
+    cfg = preset(name, **TC_SHAPES[name])
+    res = {}
+    for tc in (True, False):
+        layer = ProgressiveMoELayer(cfg, timeout_s=5.0, router_tc=tc)
+        try:
+            layer.forward("early")
+            assert layer.verify()["pass"], tc
+            assert layer.runner.router_tc_used() == tc
+            ids, gates, out = layer.expert_ids.clone(), layer.gates.clone(), layer.out.clone()
+            layer.forward("delayed")
+            assert layer.verify()["pass"] and torch.equal(out, layer.out)
+            if tc:  # streamed end to end: the same routing as the resident call
+                host_in = torch.empty(layer.inputs.tokens.shape, dtype=layer.inputs.tokens.dtype, pin_memory=True)
+                host_in.copy_(layer.inputs.tokens.cpu())
+                host_out = torch.empty(layer.out.shape, dtype=layer.out.dtype, pin_memory=True)
+                layer(host_in, host_out, arm="early")
+                torch.cuda.synchronize()
+                assert layer.runner.router_tc_used()
+                assert torch.equal(layer.expert_ids, ids) and torch.equal(layer.gates, gates)
+                assert torch.equal(host_out, out.cpu())
+            res[tc] = (ids, gates)
+        finally:
+            layer.close()
+    (ia, ga), (ib, gb) = res[True], res[False]
+    same = (ia == ib).all(dim=1)
+    assert same.float().mean() > 0.99
+    torch.testing.assert_close(ga[same], gb[same], atol=1e-5, rtol=1e-4)
