@@ -400,65 +400,53 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
     __syncthreads();
   }
   stamp(3);
-  // identity rows, one warp per item (small stores; an item whose row falls
-  // outside the receive region records the status here and is skipped below)
-  for (int li = warp; li < (int)nitems; li += nwarps) {  // nitems <= kDispatchMaxItems
-    const long long i = (long long)a * k + li;
+  // identity rows, one thread per item: its nine metadata words, its
+  // return-row index and its gate (an item whose row falls outside the
+  // receive region records the status here and is skipped below).  A thread
+  // works out the item's destination and chunk once, so the items of a share
+  // are written side by side instead of one item per warp in turn.
+  for (int li = threadIdx.x; li < (int)nitems; li += blockDim.x) {  // nitems <= kDispatchMaxItems
     const int t = a + li / k, j = li % k;
     const int packed = item_pos[li];
     const int e = (int)((unsigned)packed >> 24);
     const int r = expert_owner(d, e), le = expert_slot(d, e);
     const long long row = (long long)base_e[e] + hist[e] + (packed & 0xFFFFFF);
     if (row >= d.cap || r >= d.world || le >= d.expert_slots) {
-      if (lane == 0) record_status(p.status, kBoundsViolation, 21, row, d.cap);
+      record_status(p.status, kBoundsViolation, 21, row, d.cap);
       continue;
     }
     const long long grow = ((long long)le * d.world + d.rank) * d.cap + row;
     uint8_t* base = (uint8_t*)p.peers.base[r];
-    if (lane < kFwdMetaFields) {
-      long long pre = 0;
-      if (stage_ids) {
-        if (lane == 0) pre = s_tid[t - a];
-        else if (lane == 8) pre = s_csb[t - a];
-        else if (lane == 7) pre = s_dig[t - a];
-      } else if (lane == 0 || lane == 8) {
-        pre = lane == 0 ? p.token_ids[t] : p.checksum_base[t];
-      } else if (lane == 7) {
-        pre = p.feat_digest[t];
-      }
-      // chunk of token t: the last c with offset[c] <= t, by bisection of the
-      // staged offsets [0, nc]; global offsets only past the staged table
-      int c = 0;
-      for (int hi = nc; c < hi;) {
-        const int mid = (c + hi + 1) >> 1;
-        if (s_coff[mid] <= t) c = mid;
-        else hi = mid - 1;
-      }
-      if (c == nc)
-        while (c + 1 < d.chunks && p.chunk_offsets[c + 1] <= t) ++c;
-      long long val;
-      switch (lane) {
-        case 0: val = pre; break;
-        case 1: val = d.rank; break;
-        case 2: val = r; break;
-        case 3: val = e; break;
-        case 4: val = c; break;
-        case 5: val = t - (c <= nc ? s_coff[c] : p.chunk_offsets[c]); break;
-        case 6: val = t; break;
-        case 7: val = pre; break;
-        default: {
-          uint64_t cs = (uint64_t)pre;
-          cs = addmod(cs, mulmod_coeff((uint64_t)r, c_checksum_coeff[2]));
-          cs = addmod(cs, mulmod_coeff((uint64_t)e, c_checksum_coeff[3]));
-          val = (long long)cs;
-        }
-      }
-      ((long long*)(base + p.layout.recv_meta))[grow * kFwdMetaFields + lane] = val;
-    } else if (lane == 16) {
-      ((int*)(base + p.layout.recv_retrow))[grow] = t * k + j;
-    } else if (lane == 17) {
-      ((float*)(base + p.layout.recv_gate))[grow] = !d.gate_mode ? 1.f : stage_ids ? s_gate[li] : p.gates[i];
+    const long long tid = stage_ids ? s_tid[t - a] : p.token_ids[t];
+    const long long dig = stage_ids ? s_dig[t - a] : p.feat_digest[t];
+    const long long csb = stage_ids ? s_csb[t - a] : p.checksum_base[t];
+    const float gate = !d.gate_mode ? 1.f : stage_ids ? s_gate[li] : p.gates[(long long)a * k + li];
+    // chunk of token t: the last c with offset[c] <= t, by bisection of the
+    // staged offsets [0, nc]; global offsets only past the staged table
+    int c = 0;
+    for (int hi = nc; c < hi;) {
+      const int mid = (c + hi + 1) >> 1;
+      if (s_coff[mid] <= t) c = mid;
+      else hi = mid - 1;
     }
+    if (c == nc)
+      while (c + 1 < d.chunks && p.chunk_offsets[c + 1] <= t) ++c;
+    const int c_off = c <= nc ? s_coff[c] : p.chunk_offsets[c];
+    uint64_t cs = (uint64_t)csb;
+    cs = addmod(cs, mulmod_coeff((uint64_t)r, c_checksum_coeff[2]));
+    cs = addmod(cs, mulmod_coeff((uint64_t)e, c_checksum_coeff[3]));
+    long long* m = (long long*)(base + p.layout.recv_meta) + grow * kFwdMetaFields;
+    m[0] = tid;
+    m[1] = d.rank;
+    m[2] = r;
+    m[3] = e;
+    m[4] = c;
+    m[5] = t - c_off;
+    m[6] = t;
+    m[7] = dig;
+    m[8] = (long long)cs;
+    ((int*)(base + p.layout.recv_retrow))[grow] = t * k + j;
+    ((float*)(base + p.layout.recv_gate))[grow] = gate;
   }
   stamp(1);
   if (staged) {
