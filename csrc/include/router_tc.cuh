@@ -36,7 +36,7 @@ constexpr int kTcSelStride = 8;    // selected logits kept per token (top_k <= 8
 struct TcRouter {
   uint8_t* stages;     // 1024-aligned shared memory: n_stages x [tokens 128 x 128 B | weights npad x 128 B]
   float* lg;           // [npad, kTcRows] shared: the unit's logits, expert-major
-  float* sel;          // [kTcSelStride, kTcRows] shared: each token's chosen logits
+  float* sel;          // shared: half 1's candidate list and softmax part (tc_router_scratch_bytes)
   uint64_t* full;      // [n_stages] TMA bytes landed
   uint64_t* empty;     // [n_stages] the stage's MMAs completed
   uint64_t* done;      // the unit's MMAs completed
@@ -46,11 +46,6 @@ struct TcRouter {
 
   __device__ int stage_bytes() const { return kTcRows * 128 + npad * 128; }
 };
-
-// Shared scratch of tc_router_finish: logits [npad, kTcRows] and choices [kTcSelStride, kTcRows].
-__host__ __device__ constexpr int tc_router_scratch_bytes(int npad) {
-  return (npad + kTcSelStride) * kTcRows * 4;
-}
 
 // One thread: the TMA loads and MMAs of the unit whose first token row is
 // row0; arrives on `done` once every MMA completed.  A stage is refilled one
@@ -94,35 +89,52 @@ __device__ inline void tc_router_issue(TcRouter& s, const CUtensorMap* tx, const
   umma_commit(s.done);
 }
 
-// Threads 0..127 (warps 0-3, one TMEM lane quarter each): wait for the unit's
-// MMAs, read token row threadIdx.x's logits into shared memory (expert-major,
-// so the lanes of a warp touch consecutive words) and finish the token (rows
-// < nt only; the tile's other rows belong to later tokens and are dropped).
-// Same order as router_finish_warp: the larger logit, then the smaller expert
-// id; NaN below every number.  The loops stay rolled (small code, few live
-// registers in a kernel that is at its register limit).
+// Sort key of a router candidate, larger = preferred: rank 2 (a number) above
+// rank 1 (NaN) above 0 (no candidate); numbers by value (an order-preserving
+// map of the float bits, -0 taken as +0); then the smaller expert id.  The
+// same order as router_better, in one 64-bit compare.
+__device__ __forceinline__ unsigned long long tc_router_key(float v, int e) {
+  if (v != v) return (1ull << 40) | (unsigned long long)(255 - e);
+  const uint32_t b = __float_as_uint(v == 0.f ? 0.f : v);
+  const uint32_t u = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (2ull << 40) | ((unsigned long long)u << 8) | (unsigned long long)(255 - e);
+}
+
+// Finish of the unit's tokens, every thread of the CTA: token r = threadIdx.x
+// % 128 (warps w and w + 4 share TMEM lane quarter w % 4), half h =
+// threadIdx.x / 128.  (1) Half h reads the 16-column groups c with c % 2 == h
+// of its tokens' accumulator rows and stores logit = raw + bias + chunk bias
+// (-inf when masked) expert-major in shared memory.  (2) Half h keeps the
+// best k of the experts [h Eh, (h + 1) Eh), Eh = ceil(E / 2), in a sorted
+// register list of tc_router_key values, and its sum of exp(logit - its best)
+// for softmax-over-all gates.  (3) Half 0 merges the two lists, writes the
+// choices, their counts in sel_counts and the gates.  Rows >= nt belong to
+// later tokens (or lie past the matrix) and are dropped.
 template <int EMAX>
-__device__ inline void tc_router_finish(const RouterParams& p, const float* chunk_bias, TcRouter& s, int tf, int nt,
+__device__ __noinline__ void tc_router_finish(const RouterParams& p, const float* chunk_bias, TcRouter& s, int tf, int nt,
                                         int* sel_counts, DeviceStatus* st, int kid, unsigned long long lim,
                                         unsigned long long* dbg = nullptr) {
-  constexpr int EP = EMAX < 16 ? 16 : EMAX;  // TMEM columns read (multiple of 16)
-  const int r = threadIdx.x, t = tf + r, E = p.experts, k = p.top_k;
+  constexpr int EP = EMAX < 16 ? 16 : EMAX;  // TMEM columns at most (multiple of 16)
+  const int r = threadIdx.x & (kTcRows - 1), h = threadIdx.x >> 7;
+  const int t = tf + r, E = p.experts, k = p.top_k;
+  const bool valid = r < nt;
   const float ninf = -__int_as_float(0x7f800000);
   mbar_wait_bounded(s.done, s.n_units & 1u, st, kid, lim);
+  __syncwarp();
   tc_fence_after_sync();
-  if (dbg != nullptr && r == 0) *dbg = globaltimer_ns();  // diagnostics: the unit's MMAs completed
-  float* lg = s.lg + r;  // lg[e * kTcRows]: expert e's logit of this token
-  const uint32_t taddr = s.tmem + ((uint32_t)((r >> 5) * 32) << 16);
+  if (dbg != nullptr && threadIdx.x == 0) *dbg = globaltimer_ns();  // diagnostics: the unit's MMAs completed
+  float* lg = s.lg + r;  // lg[e * kTcRows]: expert e's logit of token r
+  const uint32_t taddr = s.tmem + ((uint32_t)(((threadIdx.x >> 5) & 3) * 32) << 16);
 #pragma unroll
   for (int c = 0; c < EP / 16; ++c) {
-    if (c * 16 < s.npad) {
+    if (c * 16 < s.npad && (c & 1) == h) {
       uint32_t raw[16];
       tmem_ld16(taddr + c * 16, raw);
       tmem_ld_wait();
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int e = c * 16 + i;
-        if (e < E && r < nt) {
+        if (e < E && valid) {
           const float l = __uint_as_float(raw[i]) + __ldg(p.bias + e) + (chunk_bias ? chunk_bias[e] : 0.f);
           const bool masked = (p.mask_mode == 1 && e == (t % E)) || (p.block_mask && __ldg(p.block_mask + e));
           lg[e * kTcRows] = masked ? ninf : l;
@@ -130,45 +142,81 @@ __device__ inline void tc_router_finish(const RouterParams& p, const float* chun
       }
     }
   }
-  if (r >= nt) return;
-  float* sel = s.sel + r;  // sel[j * kTcRows]: choice j's logit
-  unsigned long long taken = 0;
-  float l0 = 0.f;
-#pragma unroll 1
-  for (int j = 0; j < k; ++j) {
-    int best = -1, br = 0;
-    float bv = ninf;
-#pragma unroll 1
-    for (int e = 0; e < E; ++e) {
-      if ((taken >> e) & 1ull) continue;
-      const float v = lg[e * kTcRows];
-      const int re = v == v ? 2 : 1;
-      if (best < 0 || router_better(re, v, e, br, bv, best)) {
-        best = e;
-        bv = v;
-        br = re;
+  tc_fence_before_sync();
+  __syncthreads();  // every logit of the unit is in shared memory
+  const int eh = (E + 1) >> 1, e0 = h * eh, e1 = min(E, e0 + eh);
+  unsigned long long key[kTcSelStride];
+#pragma unroll
+  for (int q = 0; q < kTcSelStride; ++q) key[q] = 0ull;
+  float part = 0.f;
+  if (valid) {
+#pragma unroll 4
+    for (int e = e0; e < e1; ++e) {
+      const unsigned long long x = tc_router_key(lg[e * kTcRows], e);
+      // insert x into the sorted list of the best k (slots >= k stay empty)
+#pragma unroll
+      for (int q = kTcSelStride - 1; q >= 0; --q) {
+        if (q < k && x > key[q]) {
+          if (q > 0) key[q] = x > key[q - 1] ? key[q - 1] : x;
+          else key[q] = x;
+        }
       }
     }
-    taken |= 1ull << best;
-    sel[j * kTcRows] = bv;
-    if (j == 0) l0 = bv;
-    p.expert_ids[(long long)t * k + j] = best;
-    if (sel_counts) atomicAdd(&sel_counts[best], 1);
+    if (p.gate_mode == 2 && key[0] != 0ull) {  // this half's softmax terms, relative to its best
+      const float m = lg[(255 - (int)(key[0] & 0xFF)) * kTcRows];
+#pragma unroll 4
+      for (int e = e0; e < e1; ++e)
+        if (lg[e * kTcRows] != ninf) part += __expf(lg[e * kTcRows] - m);
+    }
   }
-  float sum = 1.f;
-  if (p.gate_mode == 1) {
-    sum = 0.f;
-#pragma unroll 1
-    for (int j = 0; j < k; ++j) sum += __expf(sel[j * kTcRows] - l0);
-  } else if (p.gate_mode == 2) {
-    sum = 0.f;
-#pragma unroll 1
-    for (int e = 0; e < E; ++e)
-      if (lg[e * kTcRows] != ninf) sum += __expf(lg[e * kTcRows] - l0);
+  // half 1 hands its list (and its softmax part) to half 0 through shared memory
+  unsigned long long* lst = reinterpret_cast<unsigned long long*>(s.sel) + r;  // [kTcSelStride][kTcRows]
+  float* prt = reinterpret_cast<float*>(reinterpret_cast<unsigned long long*>(s.sel) + kTcSelStride * kTcRows) + r;
+  if (h == 1 && valid) {
+#pragma unroll
+    for (int q = 0; q < kTcSelStride; ++q) lst[q * kTcRows] = key[q];
+    prt[0] = part;
+  }
+  __syncthreads();
+  if (h != 0 || !valid) return;
+  int ib = 0, iq = 0;  // next entry of half 1's list / of this thread's list
+  float l0 = 0.f, gsum = 0.f;
+#pragma unroll
+  for (int j = 0; j < kTcSelStride; ++j) {
+    if (j < k) {
+      unsigned long long a = 0ull;
+#pragma unroll
+      for (int q = 0; q < kTcSelStride; ++q)
+        if (q == iq) a = key[q];
+      const unsigned long long b = ib < k ? lst[ib * kTcRows] : 0ull;
+      const unsigned long long x = a > b ? a : b;
+      if (a > b) ++iq;
+      else ++ib;
+      const int e = 255 - (int)(x & 0xFF);
+      const float v = lg[e * kTcRows];
+      if (j == 0) l0 = v;
+      p.expert_ids[(long long)t * k + j] = e;
+      if (sel_counts) atomicAdd(&sel_counts[e], 1);
+      if (p.gate_mode == 1) gsum += __expf(v - l0);
+    }
+  }
+  if (p.gate_mode == 2) {  // both halves' parts, each rescaled from its own best to l0
+    const float m0 = key[0] != 0ull ? lg[(255 - (int)(key[0] & 0xFF)) * kTcRows] : ninf;
+    const unsigned long long k1 = lst[0];
+    const float m1 = k1 != 0ull ? lg[(255 - (int)(k1 & 0xFF)) * kTcRows] : ninf;
+    gsum = (m0 != ninf ? part * __expf(m0 - l0) : 0.f) + (m1 != ninf ? prt[0] * __expf(m1 - l0) : 0.f);
   }
 #pragma unroll 1
-  for (int j = 0; j < k; ++j)
-    p.gates[(long long)t * k + j] = p.gate_mode == 0 ? 1.f : __expf(sel[j * kTcRows] - l0) / sum;
+  for (int j = 0; j < k; ++j) {
+    const int e = p.expert_ids[(long long)t * k + j];
+    p.gates[(long long)t * k + j] = p.gate_mode == 0 ? 1.f : __expf(lg[e * kTcRows] - l0) / gsum;
+  }
+}
+
+// Shared scratch of tc_router_finish: logits [npad, kTcRows], half 1's list
+// [kTcSelStride, kTcRows] (64-bit keys) and its softmax part [kTcRows].
+__host__ __device__ constexpr int tc_router_scratch_bytes(int npad) {
+  return npad * kTcRows * 4 + kTcSelStride * kTcRows * 8 + kTcRows * 4;
 }
 
 }  // namespace raiccl

@@ -544,7 +544,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     tcr.n_stages = f.tc_stages;
     tcr.kblocks = f.rp.hidden / kTcBK;
     tcr.lg = reinterpret_cast<float*>(tc_base + (long long)f.tc_stages * tcr.stage_bytes());
-    tcr.sel = tcr.lg + f.tc_npad * kTcRows;
+    tcr.sel = tcr.lg + f.tc_npad * kTcRows;  // 8-byte aligned: npad * kTcRows words is even
     tcr.full = s_tcbar;
     tcr.empty = s_tcbar + kTcMaxStages;
     tcr.done = s_tcbar + 2 * kTcMaxStages;
@@ -691,7 +691,7 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       const int tf = t0 + g * NT, nt = min(NT, t1 - tf);
       if (tc) {
         // tensor-core unit: thread 128 (warp 4) issues the loads and MMAs,
-        // warps 0-3 finish one token each; diagnostics of the first two units
+        // then two threads finish each token; diagnostics of the first two units
         // in stamps 40.. and 64.. (issue, MMAs done, finish, barrier)
         unsigned long long* tdbg = (f.cta_clock != nullptr && tcr.n_units < 2)
                                        ? f.cta_clock + (long long)blockIdx.x * kCtaClockSlots +
@@ -700,11 +700,9 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
         if (tdbg != nullptr && threadIdx.x == 0) tdbg[0] = globaltimer_ns();
         if (threadIdx.x == 128)
           tc_router_issue(tcr, &f.tmap_x, &f.tmap_w, tf, f.dp.status, kFrontKernelId + 5, f.timeout_ns);
-        if (threadIdx.x < 128) {
-          tc_router_finish<EMAX>(f.rp, cbias, tcr, tf, nt, run, f.dp.status, kFrontKernelId + 5, f.timeout_ns,
-                                 tdbg != nullptr ? tdbg + 1 : nullptr);
-          if (tdbg != nullptr && threadIdx.x == 0) tdbg[2] = globaltimer_ns();
-        }
+        tc_router_finish<EMAX>(f.rp, cbias, tcr, tf, nt, run, f.dp.status, kFrontKernelId + 5, f.timeout_ns,
+                               tdbg != nullptr ? tdbg + 1 : nullptr);
+        if (tdbg != nullptr && threadIdx.x == 0) tdbg[2] = globaltimer_ns();
         tc_fence_before_sync();
         __syncthreads();
         tc_fence_after_sync();
