@@ -28,7 +28,8 @@ namespace raiccl {
 constexpr int kTcRows = 128;       // tokens per unit (the MMA's M)
 constexpr int kTcBK = 64;          // bf16 elements per K step: one 128-byte swizzle row
 constexpr int kTcMaxStages = 8;
-constexpr int kTcSelStride = 8;    // selected logits kept per token (top_k <= 8)
+constexpr int kTcSelStride = 8;    // candidates kept per token and half (top_k <= 8)
+constexpr int kTcMaxE = 64;        // experts at most
 
 // Per-CTA state.  n_load / n_mma count K steps over every unit this CTA
 // routed (the issuing thread's copy is the one that matters); n_units counts
@@ -36,7 +37,7 @@ constexpr int kTcSelStride = 8;    // selected logits kept per token (top_k <= 8
 struct TcRouter {
   uint8_t* stages;     // 1024-aligned shared memory: n_stages x [tokens 128 x 128 B | weights npad x 128 B]
   float* lg;           // [npad, kTcRows] shared: the unit's logits, expert-major
-  float* sel;          // shared: half 1's candidate list and softmax part (tc_router_scratch_bytes)
+  float* sel;          // shared: the finish's bias row, candidate lists and choices (tc_router_scratch_bytes)
   uint64_t* full;      // [n_stages] TMA bytes landed
   uint64_t* empty;     // [n_stages] the stage's MMAs completed
   uint64_t* done;      // the unit's MMAs completed
@@ -102,44 +103,51 @@ __device__ __forceinline__ unsigned long long tc_router_key(float v, int e) {
 
 // Finish of the unit's tokens, every thread of the CTA: token r = threadIdx.x
 // % 128 (warps w and w + 4 share TMEM lane quarter w % 4), half h =
-// threadIdx.x / 128.  (1) Half h reads the 16-column groups c with c % 2 == h
-// of its tokens' accumulator rows and stores logit = raw + bias + chunk bias
-// (-inf when masked) expert-major in shared memory.  (2) Half h keeps the
-// best k of the experts [h Eh, (h + 1) Eh), Eh = ceil(E / 2), in a sorted
-// register list of tc_router_key values, and its sum of exp(logit - its best)
-// for softmax-over-all gates.  (3) Half 0 merges the two lists, writes the
+// threadIdx.x / 128.  (1) The unit's bias row (bias + chunk bias, and the
+// block mask) goes to shared memory; half h reads the 16-column groups c with
+// c % 2 == h of its tokens' accumulator rows and stores the logits
+// expert-major in shared memory (-inf when masked).  (2) Half h keeps the
+// best k of the experts [h Eh, (h + 1) Eh), Eh = ceil(E / 2), as a sorted
+// list of tc_router_key values, and its sum of exp(logit - its best) for
+// softmax-over-all gates.  (3) Half 0 merges the two lists and writes the
 // choices, their counts in sel_counts and the gates.  Rows >= nt belong to
-// later tokens (or lie past the matrix) and are dropped.
+// later tokens (or lie past the matrix) and are dropped.  This code runs a
+// few times per launch, mostly from a cold instruction cache, so its loops
+// stay rolled wherever the body is not a fixed-size register array.
 template <int EMAX>
-__device__ __noinline__ void tc_router_finish(const RouterParams& p, const float* chunk_bias, TcRouter& s, int tf, int nt,
-                                        int* sel_counts, DeviceStatus* st, int kid, unsigned long long lim,
-                                        unsigned long long* dbg = nullptr) {
-  constexpr int EP = EMAX < 16 ? 16 : EMAX;  // TMEM columns at most (multiple of 16)
+__device__ __noinline__ void tc_router_finish(const RouterParams& p, const float* chunk_bias, TcRouter& s, int tf,
+                                              int nt, int* sel_counts, DeviceStatus* st, int kid,
+                                              unsigned long long lim, unsigned long long* dbg = nullptr) {
   const int r = threadIdx.x & (kTcRows - 1), h = threadIdx.x >> 7;
   const int t = tf + r, E = p.experts, k = p.top_k;
   const bool valid = r < nt;
   const float ninf = -__int_as_float(0x7f800000);
+  float* sb = s.sel;                                       // [E] bias + chunk bias
+  int* sbm = reinterpret_cast<int*>(s.sel + kTcMaxE);      // [E] 1: masked for every token
+  unsigned long long* lst = reinterpret_cast<unsigned long long*>(s.sel + 2 * kTcMaxE);  // [2][k][kTcRows]
+  int* chosen = reinterpret_cast<int*>(lst + 2 * kTcSelStride * kTcRows);                 // [k][kTcRows]
+  float* prt = reinterpret_cast<float*>(chosen + kTcSelStride * kTcRows);                 // [kTcRows]
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    sb[e] = p.bias[e] + (chunk_bias ? chunk_bias[e] : 0.f);
+    sbm[e] = p.block_mask ? (int)p.block_mask[e] : 0;
+  }
   mbar_wait_bounded(s.done, s.n_units & 1u, st, kid, lim);
   __syncwarp();
   tc_fence_after_sync();
   if (dbg != nullptr && threadIdx.x == 0) *dbg = globaltimer_ns();  // diagnostics: the unit's MMAs completed
+  __syncthreads();  // the bias row is in shared memory
   float* lg = s.lg + r;  // lg[e * kTcRows]: expert e's logit of token r
   const uint32_t taddr = s.tmem + ((uint32_t)(((threadIdx.x >> 5) & 3) * 32) << 16);
+  const int tm = p.mask_mode == 1 ? t % E : -1;
+#pragma unroll 1
+  for (int c = h; c * 16 < s.npad; c += 2) {
+    uint32_t raw[16];
+    tmem_ld16(taddr + c * 16, raw);
+    tmem_ld_wait();
 #pragma unroll
-  for (int c = 0; c < EP / 16; ++c) {
-    if (c * 16 < s.npad && (c & 1) == h) {
-      uint32_t raw[16];
-      tmem_ld16(taddr + c * 16, raw);
-      tmem_ld_wait();
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int e = c * 16 + i;
-        if (e < E && valid) {
-          const float l = __uint_as_float(raw[i]) + __ldg(p.bias + e) + (chunk_bias ? chunk_bias[e] : 0.f);
-          const bool masked = (p.mask_mode == 1 && e == (t % E)) || (p.block_mask && __ldg(p.block_mask + e));
-          lg[e * kTcRows] = masked ? ninf : l;
-        }
-      }
+    for (int i = 0; i < 16; ++i) {
+      const int e = c * 16 + i;
+      if (e < E && valid) lg[e * kTcRows] = (e == tm || sbm[e]) ? ninf : __uint_as_float(raw[i]) + sb[e];
     }
   }
   tc_fence_before_sync();
@@ -150,7 +158,7 @@ __device__ __noinline__ void tc_router_finish(const RouterParams& p, const float
   for (int q = 0; q < kTcSelStride; ++q) key[q] = 0ull;
   float part = 0.f;
   if (valid) {
-#pragma unroll 4
+#pragma unroll 1
     for (int e = e0; e < e1; ++e) {
       const unsigned long long x = tc_router_key(lg[e * kTcRows], e);
       // insert x into the sorted list of the best k (slots >= k stay empty)
@@ -164,59 +172,57 @@ __device__ __noinline__ void tc_router_finish(const RouterParams& p, const float
     }
     if (p.gate_mode == 2 && key[0] != 0ull) {  // this half's softmax terms, relative to its best
       const float m = lg[(255 - (int)(key[0] & 0xFF)) * kTcRows];
-#pragma unroll 4
+#pragma unroll 1
       for (int e = e0; e < e1; ++e)
         if (lg[e * kTcRows] != ninf) part += __expf(lg[e * kTcRows] - m);
     }
-  }
-  // half 1 hands its list (and its softmax part) to half 0 through shared memory
-  unsigned long long* lst = reinterpret_cast<unsigned long long*>(s.sel) + r;  // [kTcSelStride][kTcRows]
-  float* prt = reinterpret_cast<float*>(reinterpret_cast<unsigned long long*>(s.sel) + kTcSelStride * kTcRows) + r;
-  if (h == 1 && valid) {
+    unsigned long long* mine = lst + h * kTcSelStride * kTcRows + r;
 #pragma unroll
-    for (int q = 0; q < kTcSelStride; ++q) lst[q * kTcRows] = key[q];
-    prt[0] = part;
+    for (int q = 0; q < kTcSelStride; ++q)
+      if (q < k) mine[q * kTcRows] = key[q];
+    if (h == 1) prt[r] = part;
   }
   __syncthreads();
   if (h != 0 || !valid) return;
-  int ib = 0, iq = 0;  // next entry of half 1's list / of this thread's list
+  const unsigned long long* la = lst + r;
+  const unsigned long long* lb = lst + kTcSelStride * kTcRows + r;
+  const int nb = min(k, E - eh);  // entries of half 1's list
+  int ia = 0, ib = 0;
   float l0 = 0.f, gsum = 0.f;
-#pragma unroll
-  for (int j = 0; j < kTcSelStride; ++j) {
-    if (j < k) {
-      unsigned long long a = 0ull;
-#pragma unroll
-      for (int q = 0; q < kTcSelStride; ++q)
-        if (q == iq) a = key[q];
-      const unsigned long long b = ib < k ? lst[ib * kTcRows] : 0ull;
-      const unsigned long long x = a > b ? a : b;
-      if (a > b) ++iq;
-      else ++ib;
-      const int e = 255 - (int)(x & 0xFF);
-      const float v = lg[e * kTcRows];
-      if (j == 0) l0 = v;
-      p.expert_ids[(long long)t * k + j] = e;
-      if (sel_counts) atomicAdd(&sel_counts[e], 1);
-      if (p.gate_mode == 1) gsum += __expf(v - l0);
-    }
-  }
-  if (p.gate_mode == 2) {  // both halves' parts, each rescaled from its own best to l0
-    const float m0 = key[0] != 0ull ? lg[(255 - (int)(key[0] & 0xFF)) * kTcRows] : ninf;
-    const unsigned long long k1 = lst[0];
-    const float m1 = k1 != 0ull ? lg[(255 - (int)(k1 & 0xFF)) * kTcRows] : ninf;
-    gsum = (m0 != ninf ? part * __expf(m0 - l0) : 0.f) + (m1 != ninf ? prt[0] * __expf(m1 - l0) : 0.f);
-  }
 #pragma unroll 1
   for (int j = 0; j < k; ++j) {
-    const int e = p.expert_ids[(long long)t * k + j];
-    p.gates[(long long)t * k + j] = p.gate_mode == 0 ? 1.f : __expf(lg[e * kTcRows] - l0) / gsum;
+    const unsigned long long a = ia < k ? la[ia * kTcRows] : 0ull;
+    const unsigned long long b = ib < nb ? lb[ib * kTcRows] : 0ull;
+    const unsigned long long x = a > b ? a : b;
+    if (a > b) ++ia;
+    else ++ib;
+    const int e = 255 - (int)(x & 0xFF);
+    const float v = lg[e * kTcRows];
+    if (j == 0) l0 = v;
+    chosen[j * kTcRows + r] = e;
+    p.expert_ids[(long long)t * k + j] = e;
+    if (sel_counts) atomicAdd(&sel_counts[e], 1);
+    if (p.gate_mode == 1) gsum += __expf(v - l0);
   }
+  if (p.gate_mode == 2) {  // both halves' parts, each rescaled from its own best to l0
+    const unsigned long long k1 = nb > 0 ? lb[0] : 0ull;
+    const float m0 = key[0] != 0ull ? lg[(255 - (int)(key[0] & 0xFF)) * kTcRows] : ninf;
+    const float m1 = k1 != 0ull ? lg[(255 - (int)(k1 & 0xFF)) * kTcRows] : ninf;
+    gsum = (m0 != ninf ? part * __expf(m0 - l0) : 0.f) + (m1 != ninf ? prt[r] * __expf(m1 - l0) : 0.f);
+  }
+#pragma unroll 1
+  for (int j = 0; j < k; ++j)
+    p.gates[(long long)t * k + j] =
+        p.gate_mode == 0 ? 1.f : __expf(lg[chosen[j * kTcRows + r] * kTcRows] - l0) / gsum;
 }
 
-// Shared scratch of tc_router_finish: logits [npad, kTcRows], half 1's list
-// [kTcSelStride, kTcRows] (64-bit keys) and its softmax part [kTcRows].
+// Shared scratch of tc_router_finish: logits [npad, kTcRows], then the bias
+// row and mask [kTcMaxE] each, both halves' lists [2, kTcSelStride, kTcRows]
+// (64-bit keys), the choices [kTcSelStride, kTcRows] and half 1's softmax
+// parts [kTcRows].
 __host__ __device__ constexpr int tc_router_scratch_bytes(int npad) {
-  return npad * kTcRows * 4 + kTcSelStride * kTcRows * 8 + kTcRows * 4;
+  return npad * kTcRows * 4 + 2 * kTcMaxE * 4 + 2 * kTcSelStride * kTcRows * 8 + kTcSelStride * kTcRows * 4 +
+         kTcRows * 4;
 }
 
 }  // namespace raiccl
