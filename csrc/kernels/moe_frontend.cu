@@ -599,11 +599,14 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   // Descriptors this worker dispatches.  When every partial descriptor can
   // have workers of its own, the partial descriptors get disjoint worker
   // groups (in proportion to their tokens), so released descriptors are
-  // dispatched side by side, and every worker then also takes a share of the
-  // final descriptor, the one the layer waits for after the last trigger.
+  // dispatched side by side, and the workers of every group but the last then
+  // also take a share of the final descriptor, the one the layer waits for
+  // after the last trigger (the last partial descriptor is released just
+  // before it, so its group is still busy when the final one is released).
   // Otherwise every worker takes a share of every descriptor in turn.
   const bool grouped = f.dispatch_groups && n_desc >= 2 && n_desc - 1 <= Wd && dispatcher;
   int qa = 0, wia = w, wna = Wd;  // grouped: this worker's partial descriptor, its index and group size
+  int fin_n = Wd;                 // grouped: workers [0, fin_n) share the final descriptor
   if (grouped) {
     const int P = f.cp.partial_chunks;
     const int np = n_desc - 1;
@@ -615,7 +618,10 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       int hi = total > 0 ? (int)((long long)Wd * cum / total) : lo + 1;
       hi = max(hi, lo + 1);
       hi = min(hi, Wd - (np - 1 - q));
-      if (q == np - 1) hi = Wd;
+      if (q == np - 1) {
+        hi = Wd;
+        if (np >= 2 && lo >= 1) fin_n = lo;
+      }
       if (w >= lo && w < hi) { qa = q; wia = w - lo; wna = hi - lo; }
       lo = hi;
     }
@@ -623,9 +629,11 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
   // cursor over this worker's descriptors: the descriptor, the worker's share
   // index in it and the number of workers sharing it (n_desc: no more)
   int k_cur = 0;
-  auto cq = [&]() { return grouped ? (k_cur == 0 ? qa : k_cur == 1 ? n_desc - 1 : n_desc) : k_cur; };
+  auto cq = [&]() {
+    return grouped ? (k_cur == 0 ? qa : k_cur == 1 && w < fin_n ? n_desc - 1 : n_desc) : k_cur;
+  };
   auto cwi = [&]() { return grouped && k_cur == 0 ? wia : w; };
-  auto cwn = [&]() { return grouped && k_cur == 0 ? wna : Wd; };
+  auto cwn = [&]() { return grouped ? (k_cur == 0 ? wna : fin_n) : Wd; };
   int cum_units = 0;  // routing units (token groups, or tokens) of the chunks before c
   bool w_wait = w_smem;  // the weights' copy has not been waited for yet
   for (int c = 0; c < C; ++c) {
