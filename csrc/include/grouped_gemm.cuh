@@ -75,6 +75,26 @@ __device__ __forceinline__ int find_segment(const int* prefix, int nseg, int til
 // bias and store latency.
 constexpr int kEpiWarps = 8;
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+constexpr int kSplitMinKBlocks = 4;  // K blocks per split at least (split-K)
+
+// bar.sync on a named barrier among `threads` threads (the epilogue warps).
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// The same barrier, returning whether `pred` holds in every participating thread.
+__device__ __forceinline__ bool named_barrier_and(int id, int threads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %3, 0;\n\t"
+      "bar.red.and.pred q, %1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"(threads), "r"((uint32_t)pred)
+      : "memory");
+  return r != 0;
+}
 
 __device__ __forceinline__ void store16(float* dst, const float (&v)[16]) {
 #pragma unroll
@@ -166,6 +186,61 @@ __device__ __forceinline__ void gemm_epilogue_row(const GroupedGemmParams& p, co
         }
       }
     }
+  }
+}
+
+// Split-K epilogue, partial part: the row's accumulator columns [c0, c1) as
+// fp32 into its split's partial tile (rows of 128, BN columns).
+template <int BN>
+__device__ __forceinline__ void gemm_partial_row(float* part_row, uint32_t t_row, int c0, int c1) {
+#pragma unroll 1
+  for (int c = c0; c < c1; c += 16) {
+    uint32_t r[16];
+    tmem_ld16(t_row + c, r);
+    tmem_ld_wait();
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+    store16(part_row + c, v);
+  }
+}
+
+// Split-K epilogue, final part (the tile's last split): the row's columns
+// [c0, c1) summed over the S partial tiles in split order (read through L2:
+// other SMs wrote them), then bias, activation, row scale and the output
+// store as in gemm_epilogue_row.  part0: the row in split 0's partial tile;
+// stride: floats from one split's partial tile to the next.
+template <int BN, Act ACT, typename OutT>
+__device__ __forceinline__ void gemm_sum_row(const GroupedGemmParams& p, const GemmSegment& seg, int nb, int r_local,
+                                             const float* part0, long long stride, int S, int c0, int c1) {
+  if (r_local >= seg.rows) return;
+  const int arow = seg.a_row0 + r_local;
+  const long long orow = p.row_map ? (long long)__ldg(p.row_map + arow) : (long long)(seg.out_row0 + r_local);
+  const float scale = p.row_scale ? __ldg(p.row_scale + arow) : 1.f;
+  OutT* out = (OutT*)p.out_ptrs[seg.out_slot];
+  const float* bias = p.bias ? p.bias + (long long)seg.expert * p.N + nb * BN : nullptr;
+#pragma unroll 1
+  for (int c = c0; c < c1; c += 16) {
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+#pragma unroll 1
+    for (int s = 0; s < S; ++s) {
+      const float4* src = (const float4*)(part0 + s * stride + c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 q = __ldcg(src + j);
+        acc[4 * j] += q.x;
+        acc[4 * j + 1] += q.y;
+        acc[4 * j + 2] += q.z;
+        acc[4 * j + 3] += q.w;
+      }
+    }
+    float b[16], v[16];
+    load_bias16(bias ? bias + c : nullptr, b);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = apply_act(acc[j] + b[j], ACT) * scale;
+    store16(out + orow * p.ldo + nb * BN + c, v);
   }
 }
 
@@ -297,20 +372,35 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
   const int nblocks = p.N / BN;
   const int kblocks = (p.K + C::BK - 1) / C::BK;
   const uint64_t lim = p.timeout_ns;
+  // split K: every CTA derives the same split count from the tile count;
+  // work item t is tile t % total_tiles, split t / total_tiles, K blocks
+  // [split * kbs, min(kblocks, (split + 1) * kbs)) (no split is empty)
+  int S = 1;
+  if (ACT != Act::kSwiGLU && p.ksplit_partial != nullptr && p.ksplit_ticket != nullptr && total_tiles > 0) {
+    S = min(p.ksplit_max, (int)gridDim.x / total_tiles);
+    S = min(S, kblocks / kSplitMinKBlocks);
+    S = min(S, p.ksplit_entries / total_tiles);
+    if (S < 1) S = 1;
+  }
+  const int kbs = (kblocks + S - 1) / S;
+  if (S > 1) S = (kblocks + kbs - 1) / kbs;
+  const int work = total_tiles * S;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
       int stage = 0; uint32_t phase = 0;
-      for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-        const int s = find_segment(p.tile_prefix, p.num_segs, t);
+      for (int t = blockIdx.x; t < work; t += gridDim.x) {
+        const int tile = t % total_tiles, split = t / total_tiles;
+        const int s = find_segment(p.tile_prefix, p.num_segs, tile);
         const GemmSegment seg = p.segs[s];
-        const int local = t - p.tile_prefix[s];
+        const int local = tile - p.tile_prefix[s];
         const int mb = local / nblocks, nb = local % nblocks;
         const int arow = seg.a_row0 + mb * C::BM;
         const int brow = seg.expert * p.N + nb * BN;
+        const int kb0 = split * kbs, kb1 = min(kblocks, kb0 + kbs);
         bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, p.status, kKernelId, lim)) { ok = false; break; }
           uint8_t* sa = stage_base + stage * C::STAGE_BYTES;
           mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
@@ -325,14 +415,15 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     // ------------------------------------------------------------ MMA issuer
     if (elect_one_sync()) {
       int stage = 0; uint32_t phase = 0; int iter = 0;
-      for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++iter) {
+      for (int t = blockIdx.x; t < work; t += gridDim.x, ++iter) {
         const int acc = iter & 1;
         const uint32_t acc_phase = (iter >> 1) & 1;
         if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1u, p.status, kKernelId, lim)) break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * BN;
+        const int kb0 = (t / total_tiles) * kbs, kb1 = min(kblocks, kb0 + kbs);
         bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&full_bar[stage], phase, p.status, kKernelId, lim)) { ok = false; break; }
           tc_fence_after_sync();
           const uint32_t a_addr = smem_u32(stage_base + stage * C::STAGE_BYTES);
@@ -341,7 +432,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
           for (int k = 0; k < C::BK / C::UK; ++k) {
             const uint64_t ad = umma_desc_k_sw128(a_addr + k * 32);
             const uint64_t bd = umma_desc_k_sw128(b_addr + k * 32);
-            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            const uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
             if (TF32) umma_tf32(d_tmem, ad, bd, C::IDESC, accum);
             else umma_f16(d_tmem, ad, bd, C::IDESC, accum);
           }
@@ -362,21 +453,46 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     int c0, c1;
     epi_columns(warp - 2, ACT == Act::kSwiGLU ? BN / 2 : BN, c0, c1);
     int iter = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++iter) {
+    __shared__ int s_last;  // split K: this CTA holds the tile's last split
+    for (int t = blockIdx.x; t < work; t += gridDim.x, ++iter) {
       const int acc = iter & 1;
       const uint32_t acc_phase = (iter >> 1) & 1;
-      const int s = find_segment(p.tile_prefix, p.num_segs, t);
+      const int tile = t % total_tiles, split = t / total_tiles;
+      const int s = find_segment(p.tile_prefix, p.num_segs, tile);
       const GemmSegment seg = p.segs[s];
-      const int local = t - p.tile_prefix[s];
+      const int local = tile - p.tile_prefix[s];
       const int mb = local / nblocks, nb = local % nblocks;
-      if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.status, kKernelId, lim)) break;
+      bool ok = mbar_wait_bounded(&tfull_bar[acc], acc_phase, p.status, kKernelId, lim);
+      // split K: the epilogue warps meet at named barriers, so they stop together
+      if (S > 1) ok = named_barrier_and(2, kEpiWarps * 32, ok);
+      if (!ok) break;
       tc_fence_after_sync();
       const int r_local = mb * C::BM + row_in_tile;
-      gemm_epilogue_row<BN, ACT, OutT>(p, seg, nb, r_local, tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
-                                       c0, c1);
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      if (S == 1) {
+        gemm_epilogue_row<BN, ACT, OutT>(p, seg, nb, r_local, t_row, c0, c1);
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+        continue;
+      }
+      // split K: this split's partial tile, then one ticket per tile; the
+      // last split adds every partial in split order and runs the epilogue
+      const long long stride = (long long)total_tiles * C::BM * BN;
+      float* part_row = p.ksplit_partial + ((long long)tile * C::BM + row_in_tile) * BN;
+      gemm_partial_row<BN>(part_row + split * stride, t_row, c0, c1);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      __threadfence();  // this thread's partial stores before the tile's ticket
+      named_barrier_sync(1, kEpiWarps * 32);
+      if (warp == 2 && lane == 0) s_last = atomicAdd(&p.ksplit_ticket[tile], 1) == S - 1 ? 1 : 0;
+      named_barrier_sync(1, kEpiWarps * 32);
+      if (s_last) {
+        __threadfence();  // every split's partial stores (ordered by their tickets) before the reads
+        gemm_sum_row<BN, ACT, OutT>(p, seg, nb, r_local, part_row, stride, S, c0, c1);
+      }
+      named_barrier_sync(1, kEpiWarps * 32);  // s_last is read before the next tile's ticket
     }
   }
 

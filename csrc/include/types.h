@@ -87,6 +87,18 @@ struct GroupedGemmParams {
   unsigned int* ticket_counter;
   unsigned long long* pair_tickets;     // [pairs][kPairTicketRing][2]: tag | ticket, packed tile
   const unsigned long long* epoch;      // this call's sequence number
+  // Split K (one-CTA kernel, activations other than SwiGLU): when the tiles
+  // are few and K is long, each tile's K range is split over up to ksplit_max
+  // CTAs (chosen on the device from the tile count: one (tile, split) per CTA,
+  // at least kSplitMinKBlocks K blocks per split, at most ksplit_entries
+  // partial tiles).  Each split stores its fp32 partial tile in
+  // ksplit_partial [entries, 128, BN]; the tile's last split (ksplit_ticket
+  // [tiles], zeroed per call) adds the partials in split order and runs the
+  // epilogue, so results do not depend on arrival order.  nullptr: no split.
+  float* ksplit_partial;
+  int* ksplit_ticket;
+  int ksplit_entries;
+  int ksplit_max;
 };
 
 constexpr int kPairTicketRing = 32;

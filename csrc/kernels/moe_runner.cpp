@@ -126,6 +126,7 @@ class MoELayerRunner {
     dispatch_groups_ = !ints.contains("dispatch_groups") || geti(ints, "dispatch_groups") != 0;
     router_wsmem_ = !ints.contains("router_wsmem") || geti(ints, "router_wsmem") != 0;
     router_tc_ = !ints.contains("router_tc") || geti(ints, "router_tc") != 0;
+    gemm_ksplit_ = !ints.contains("gemm_ksplit") || geti(ints, "gemm_ksplit") != 0;
     max_cands_ = geti(ints, "max_cands");
     log_stride_ = geti(ints, "log_stride");
     max_ctl_tokens_ = geti(ints, "max_ctl_tokens");
@@ -170,7 +171,16 @@ class MoELayerRunner {
                       tensors.contains("desc_ready");
       if (tensors.contains("chunk_words")) {
         chunk_words_ = ptr<int>(tensors, "chunk_words");
-        n_chunk_words_ = d.chunks * (1 + d.experts);
+        // [C] chunk_done, [C, E] chunk_counts, then GEMM-1's split-K tile
+        // tickets (whatever the tensor holds beyond), all zeroed per call
+        n_chunk_words_ = (int)tensors["chunk_words"].cast<torch::Tensor>().numel();
+        const int base = d.chunks * (1 + d.experts);
+        if (n_chunk_words_ > base && tensors.contains("ksplit_partial") && !tensors["ksplit_partial"].is_none()) {
+          ksplit_partial_ = ptr<float>(tensors, "ksplit_partial");
+          ksplit_ticket_ = chunk_words_ + base;
+          const long long rows = tensors["ksplit_partial"].cast<torch::Tensor>().numel() / (128LL * bn1_);
+          ksplit_entries_ = (int)std::min<long long>(n_chunk_words_ - base, rows);
+        }
       }
     }
     ck(cudaEventCreateWithFlags(&ev_start_, cudaEventDisableTiming), "cudaEventCreate");
@@ -530,6 +540,12 @@ class MoELayerRunner {
     g1.pair = pair1_ ? 1 : 0;
     g1.pdl = pdl_ ? 1 : 0;
     g1.trace = trace_slot("gemm1", -1);
+    if (!pair1_ && gemm_ksplit_ && ksplit_partial_ != nullptr) {  // few tiles, long K: split K over idle SMs
+      g1.ksplit_partial = ksplit_partial_;
+      g1.ksplit_ticket = ksplit_ticket_;
+      g1.ksplit_entries = ksplit_entries_;
+      g1.ksplit_max = 8;
+    }
     if (progressive) {
       g1.progressive = 1;
       g1.pdl = 1;
@@ -764,6 +780,7 @@ class MoELayerRunner {
   bool dispatch_groups_ = true;          // one worker group per descriptor (dispatched side by side)
   bool router_wsmem_ = true;             // router weights copied into each worker's shared memory
   bool router_tc_ = true;                // bf16 batches: tensor-core router units of 128 tokens
+  bool gemm_ksplit_ = true;              // one-CTA GEMM-1: split K when the tiles are few
   bool have_tc_router_ = false;          // router tensor maps built (bf16, D % 64 == 0, E <= 64)
   int tc_used_ = 0;                      // the last front-end launch routed on the tensor cores
   CUtensorMap tx_router_{}, tw_router_{};
@@ -779,6 +796,9 @@ class MoELayerRunner {
   int fault_skip_signal_desc_ = -1;
   bool use_frontend_ = false;      // persistent cooperative front end (else one launch per step)
   int* chunk_words_ = nullptr;     // [C] chunk_done + [C * E] chunk_counts, zeroed per call
+  float* ksplit_partial_ = nullptr;  // GEMM-1 split-K partial tiles [entries, 128, bn1], or nullptr
+  int* ksplit_ticket_ = nullptr;     // GEMM-1 split-K tile tickets (inside chunk_words)
+  int ksplit_entries_ = 0;
   int n_chunk_words_ = 0;  // host-side fault injection: descriptor whose ready flags are withheld
   // device trace ring (optional tensor "trace"): one slot per launch of a call
   raiccl::TraceSlot* trace_ = nullptr;

@@ -44,6 +44,7 @@ LOG_HEADER = 16  # 8-word decision record + 8 phase-clock words
 TRACE_SLOTS = 256
 GUARD_CANARY = 0x5CA1AB1E0DDC0FFE  # fills the guard band after every array of the symmetric region
 PAIR_TICKET_RING = 32  # ticket slots (two words each) per GEMM CTA pair (kPairTicketRing in csrc/include/types.h)
+KSPLIT_ENTRIES = 296  # GEMM-1 split-K partial tiles (two per SM); tickets as many
 
 
 @dataclass
@@ -59,7 +60,8 @@ class ProgressiveMoELayer:
                  control_path: str = "auto", trace: bool = False, frontend: str = "persistent",
                  gemm_pair: bool = True, pdl: bool = True, gemm_swap_max: int = 128,
                  progressive: bool = False, dispatch_ctas: int = 0, router_ring: bool = True,
-                 dispatch_groups: bool = True, router_wsmem: bool = True, router_tc: bool = True) -> None:
+                 dispatch_groups: bool = True, router_wsmem: bool = True, router_tc: bool = True,
+                 gemm_ksplit: bool = True) -> None:
         self.cfg = cfg
         if world is None:
             world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -165,6 +167,8 @@ class ProgressiveMoELayer:
             # bf16 batches: front-end workers route 128-token units on the
             # tensor cores (tcgen05 MMA, TMA-staged tokens and weights)
             "router_tc": int(bool(router_tc)),
+            # one-CTA GEMM-1 with few tiles and a long K: K split over idle SMs
+            "gemm_ksplit": int(bool(gemm_ksplit)),
         }
         self.layout = self._k.sym_layout(ints)
         self.channel = PeerChannel(self.layout["total"], dev, group=group)
@@ -203,7 +207,11 @@ class ProgressiveMoELayer:
             "done_counter": torch.zeros(cfg.n_desc, dtype=torch.int32, device=dev),
             "permit": torch.zeros(cfg.n_desc, dtype=torch.int64, device=dev),
             # persistent front end: chunk_done [C] + chunk_counts [C, E]; receive bases; release words
-            "chunk_words": torch.zeros(cfg.chunks * (1 + E), dtype=torch.int32, device=dev),
+            # (+ GEMM-1 split-K tile tickets, zeroed with them every call)
+            "chunk_words": torch.zeros(cfg.chunks * (1 + E) + KSPLIT_ENTRIES, dtype=torch.int32, device=dev),
+            # GEMM-1 split-K partial tiles (one-CTA GEMM only: tile width < 64, no SwiGLU)
+            "ksplit_partial": (torch.empty(KSPLIT_ENTRIES * 128 * self.bn1, dtype=torch.float32, device=dev)
+                               if self.bn1 < 64 and cfg.activation != "swiglu" else None),
             "disp_base": torch.zeros(cfg.n_desc * E, dtype=torch.int32, device=dev),
             "desc_ready": torch.zeros(cfg.n_desc, dtype=torch.int64, device=dev),
             "epoch": self.epoch, "status": self.status,
