@@ -623,25 +623,31 @@ def test_gemm1_split_k_matches_unsplit():
     """R4's GEMM-1 (2048 -> 32, 32 row tiles) splits K over otherwise idle SMs:
     each split stores a partial tile, the tile's last split adds them in split
     order.  The split ran (each tile's ticket counted its splits), the layer
-    passes the checker, the outputs agree with the unsplit GEMM to fp32
-    rounding and repeat bit for bit across calls and arms."""
+    passes the checker, GEMM-1's activations agree with the unsplit GEMM's to
+    fp32 rounding (only the order of the fp32 additions differs), the layer
+    outputs agree within the tf32 tolerance (GEMM-2 rounds its inputs to tf32,
+    so a last-bit change of an activation can move an output by ~1e-3), and
+    results repeat bit for bit across calls and arms."""
     from revealaiccl_b200.moe.config import preset
     from revealaiccl_b200.moe.layer import ProgressiveMoELayer
 
     cfg = preset("r4_reference")
-    outs, tickets = {}, {}
+    outs, tickets, hidden = {}, {}, {}
     for ks in (True, False):
         layer = ProgressiveMoELayer(cfg, timeout_s=5.0, gemm_ksplit=ks)
         try:
+            layer.tensors["h"].zero_()  # rows GEMM-1 does not write stay equal in both layers
             layer.forward("early")
             assert layer.verify()["pass"], ks
             first = layer.out.clone()
             base = cfg.chunks * (1 + cfg.experts)
             tickets[ks] = layer.tensors["chunk_words"][base:].cpu()
+            hidden[ks] = layer.tensors["h"].clone()
             layer.forward("delayed")
             assert layer.verify()["pass"] and torch.equal(first, layer.out)
             outs[ks] = first
         finally:
             layer.close()
     assert int(tickets[True].max()) > 1 and int(tickets[False].abs().sum()) == 0
-    torch.testing.assert_close(outs[True], outs[False], atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(hidden[True], hidden[False], atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(outs[True], outs[False], atol=5e-3, rtol=5e-3)
