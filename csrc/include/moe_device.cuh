@@ -343,12 +343,39 @@ struct DispatchStage {
   unsigned long long timeout_ns;  // bound of each wait for a half
 };
 
+// Identity inputs of share [a, b) (token id, digest and checksum base per
+// token, the gate per item) into the head of the staging buffer, when they
+// fit a quarter of it; returns whether they were staged.  Reads only what the
+// router wrote, so it may run before the descriptor is released once its
+// chunks are complete.  Collective over the CTA (ends with a barrier).
+__device__ inline bool dispatch_stage_ids(const DispatchParams& p, int a, int b, const DispatchStage* stage) {
+  const int k = p.dims.top_k;
+  const long long ntok = b > a ? b - a : 0, nitems = ntok * k;
+  const long long id_bytes = (ntok * 24 + nitems * 4 + 15) & ~15LL;
+  if (stage == nullptr || ntok == 0 || id_bytes > stage->bytes / 4) return false;
+  long long* s_tid = reinterpret_cast<long long*>(stage->buf);
+  long long* s_dig = s_tid + ntok;
+  long long* s_csb = s_dig + ntok;
+  float* s_gate = reinterpret_cast<float*>(s_csb + ntok);
+  for (long long i = threadIdx.x; i < ntok; i += blockDim.x) {
+    s_tid[i] = p.token_ids[a + i];
+    s_dig[i] = p.feat_digest[a + i];
+    s_csb[i] = p.checksum_base[a + i];
+  }
+  if (p.dims.gate_mode)
+    for (long long i = threadIdx.x; i < nitems; i += blockDim.x) s_gate[i] = p.gates[(long long)a * k + i];
+  __syncthreads();
+  return true;
+}
+
 // indexed: hist / run / item_pos already hold dispatch_index's result.
 // stage (optional): stage rows through shared memory (see DispatchStage).
+// ids_ready: dispatch_stage_ids already staged the identity inputs.
 template <typename T>
 __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, const int* base_e, int* hist, int* run,
                               int* item_pos, const int* s_coff, int nc, bool streamed = false, bool indexed = false,
-                              const DispatchStage* stage = nullptr, unsigned long long* dbg = nullptr) {
+                              const DispatchStage* stage = nullptr, unsigned long long* dbg = nullptr,
+                              bool ids_ready = false) {
   // dbg (diagnostics, thread 0): %globaltimer after the index part, the
   // identity rows and the staged feature rows
   auto stamp = [&](int i) {
@@ -389,16 +416,7 @@ __device__ void dispatch_rows(const DispatchParams& p, int t0, int a, int b, con
     issue_half(0, a);
     if (a + half_rows < b) issue_half(1, a + half_rows);
   }
-  if (stage_ids) {  // one round trip for every item's identity inputs
-    for (long long i = threadIdx.x; i < ntok; i += blockDim.x) {
-      s_tid[i] = p.token_ids[a + i];
-      s_dig[i] = p.feat_digest[a + i];
-      s_csb[i] = p.checksum_base[a + i];
-    }
-    if (d.gate_mode)
-      for (long long i = threadIdx.x; i < nitems; i += blockDim.x) s_gate[i] = p.gates[(long long)a * k + i];
-    __syncthreads();
-  }
+  if (stage_ids && !ids_ready) dispatch_stage_ids(p, a, b, stage);  // one round trip for every item's inputs
   stamp(3);
   // identity rows, one thread per item: its nine metadata words, its
   // return-row index and its gate (an item whose row falls outside the

@@ -280,7 +280,7 @@ template <typename T>
 __device__ void worker_dispatch(const FrontendParams& f, int q, int w, int W, unsigned long long epoch,
                                 int* hist, int* run, int* item_pos, int* s_base, const int* s_coff, int nc,
                                 int* s_flag, bool streamed, bool indexed = false,
-                                const DispatchStage* stage = nullptr) {
+                                const DispatchStage* stage = nullptr, bool ids_ready = false) {
   const MoEDims& d = f.dp.dims;
   const int P = f.cp.partial_chunks, C = d.chunks, E = d.experts, k = d.top_k;
   const int t0 = s_coff[trigger_first_chunk(q, P)];
@@ -309,7 +309,8 @@ __device__ void worker_dispatch(const FrontendParams& f, int q, int w, int W, un
     // diagnostics: descriptor q's phases in stamps 68 + 4 q .. (q < 8)
     unsigned long long* dbg =
         (f.cta_clock != nullptr && q < 8) ? f.cta_clock + (long long)blockIdx.x * kCtaClockSlots + 68 + 4 * q : nullptr;
-    dispatch_rows<T>(f.dp, t0, a, b, s_base, hist, run, item_pos, s_coff, nc, streamed, indexed, stage, dbg);
+    dispatch_rows<T>(f.dp, t0, a, b, s_base, hist, run, item_pos, s_coff, nc, streamed, indexed, stage, dbg,
+                     ids_ready);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -327,8 +328,8 @@ __device__ void worker_dispatch(const FrontendParams& f, int q, int w, int W, un
 // This worker's index part of descriptor q (dispatch_index), computed while
 // the release is still pending; worker_dispatch(..., indexed = true) then
 // only loads the bases and copies.  Collective over the CTA.
-__device__ void worker_index(const FrontendParams& f, int q, int w, int W, int* hist, int* run, int* item_pos,
-                             const int* s_coff) {
+__device__ bool worker_index(const FrontendParams& f, int q, int w, int W, int* hist, int* run, int* item_pos,
+                             const int* s_coff, const DispatchStage* stage) {
   const MoEDims& d = f.dp.dims;
   const int P = f.cp.partial_chunks, C = d.chunks, E = d.experts;
   const int t0 = s_coff[trigger_first_chunk(q, P)];
@@ -344,6 +345,8 @@ __device__ void worker_index(const FrontendParams& f, int q, int w, int W, int* 
   __syncthreads();
   if (a < b && (long long)(b - a) * d.top_k <= kDispatchMaxItems) dispatch_index(f.dp, t0, a, b, hist, run, item_pos);
   __syncthreads();
+  // the share's identity inputs too (staging memory is free once routing is done)
+  return a < b && (long long)(b - a) * d.top_k <= kDispatchMaxItems && dispatch_stage_ids(f.dp, a, b, stage);
 }
 
 // Whether every router chunk of descriptor q is complete (all its routing
@@ -831,15 +834,15 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
     // index part (prefix counts and ranks, from the expert ids only) while
     // the control warp works, so the release is followed by the copy alone
     const int rel = wait_released(f, next, epoch, &s_flag, false);
-    bool indexed = false;
+    bool indexed = false, ids_ready = false;
     if (rel == 0 && chunks_complete(f, next, s_coff, NT, &s_flag)) {
-      worker_index(f, next, cwi(), cwn(), hist, run, item_pos, s_coff);
+      ids_ready = worker_index(f, next, cwi(), cwn(), hist, run, item_pos, s_coff, stage);
       indexed = true;
       ++n_indexed;
     }
     if (rel != 1 && wait_released(f, next, epoch, &s_flag, true) != 1) return;
     worker_dispatch<T>(f, next, cwi(), cwn(), epoch, hist, run, item_pos, s_base, s_coff, nc, &s_flag, !resident,
-                       indexed, stage);
+                       indexed, stage, ids_ready);
     ++k_cur;
   }
   if (f.cta_clock != nullptr && threadIdx.x == 0) f.cta_clock[(long long)blockIdx.x * kCtaClockSlots + 23] = 1 + n_indexed;
