@@ -131,7 +131,7 @@ __device__ __forceinline__ bool router_better(int ra, float va, int ea, int rb, 
 // count in sel_counts (shared, or nullptr) and its gate per gate_mode.
 template <int EMAX>
 __device__ __forceinline__ void router_finish_warp(const RouterParams& p, const float* chunk_bias, int t,
-                                                   const float (&acc)[EMAX], int* sel_counts, bool dry = false) {
+                                                   const float (&acc)[EMAX], int* sel_counts) {
   constexpr int PER = EMAX > 32 ? 2 : 1;
   const int E = p.experts, k = p.top_k, lane = threadIdx.x & 31;
   const float ninf = -__int_as_float(0x7f800000);
@@ -196,7 +196,7 @@ __device__ __forceinline__ void router_finish_warp(const RouterParams& p, const 
     for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
     sum = part;
   }
-  if (lane < k && !dry) {  // dry: a pass that only warms the instruction cache writes nothing
+  if (lane < k) {
     p.expert_ids[(long long)t * k + lane] = my_e;
     if (sel_counts) atomicAdd(&sel_counts[my_e], 1);
     p.gates[(long long)t * k + lane] = p.gate_mode == 0 ? 1.f : __expf(my_l - l0) / sum;
@@ -216,7 +216,7 @@ __device__ __forceinline__ void router_finish_warp(const RouterParams& p, const 
 template <typename T, int EMAX, bool SMEM_W>
 __device__ __forceinline__ void router_token(const RouterParams& p, const float* chunk_bias, int t, const T* x,
                                              bool x_shared, const T* __restrict__ w, int* sel_counts,
-                                             unsigned long long* dbg = nullptr, bool dry = false) {
+                                             unsigned long long* dbg = nullptr) {
   const int D = p.hidden, E = p.experts;
   const int lane = threadIdx.x & 31;
   constexpr int VEC = 16 / sizeof(T);
@@ -265,7 +265,7 @@ __device__ __forceinline__ void router_token(const RouterParams& p, const float*
       acc[e] = v;
     }
   }
-  router_finish_warp<EMAX>(p, chunk_bias, t, acc, sel_counts, dry);
+  router_finish_warp<EMAX>(p, chunk_bias, t, acc, sel_counts);
   if (dbg != nullptr && lane == 0) dbg[1] = globaltimer_ns();
 }
 

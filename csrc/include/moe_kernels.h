@@ -217,10 +217,6 @@ struct FrontendParams {
   // Bytes of the ring memory (routing ring or tensor-core stages) that the
   // dispatch stages rows through once routing is done (0: no staging).
   int ring_bytes;
-  // 1: a resident batch's first routing unit runs a dry pass first (rows from
-  // global memory, nothing written) while its copy lands, so the real pass
-  // runs from a warm instruction cache.
-  int warm_first;
   CUtensorMap tmap_x;
   CUtensorMap tmap_w;
 };

@@ -733,20 +733,8 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
         if (tdbg != nullptr && threadIdx.x == 0) tdbg[3] = globaltimer_ns();
         continue;
       }
-      unsigned long long* udbg = nullptr;
-      // The first unit of a resident batch runs twice: a dry pass over its
-      // rows in global memory while their bulk copy lands (it only brings the
-      // routing code into the instruction cache, and writes nothing), then
-      // the real pass from shared memory.  Both passes run this one body.
-#pragma unroll 1
-      for (int pass = (ring && consumed == 0 && f.warm_first) ? 0 : 1; pass < 2; ++pass) {
-      const bool dry = pass == 0;
-      if (w_wait) {  // the weights' copy, once (a wait that runs out fails the call)
-        mbar_wait_bounded(&s_wbar, 0, f.dp.status, kFrontKernelId + 4, f.timeout_ns);
-        w_wait = false;
-      }
       const T* srows = nullptr;
-      if (ring && !dry) {
+      if (ring) {
         const int slot = (int)(consumed % R);
         // a wait that runs out records the status (the call fails) and routes what is there
         mbar_wait_bounded(&s_rbar[slot], (uint32_t)((consumed / R) & 1), f.dp.status, kFrontKernelId + 2,
@@ -756,24 +744,27 @@ __global__ void __launch_bounds__(kFrontThreads, 1) moe_frontend_kernel(const __
       }
       // diagnostics: the first two units' phases (landed, warp 0's products,
       // its finish, the CTA barrier) in stamps 40.. and 64..
-      udbg = (f.cta_clock != nullptr && consumed < 2 && !dry)
-                 ? f.cta_clock + (long long)blockIdx.x * kCtaClockSlots + (consumed == 0 ? 40 : 64)
-                 : nullptr;
+      unsigned long long* udbg = (f.cta_clock != nullptr && consumed < 2)
+                                     ? f.cta_clock + (long long)blockIdx.x * kCtaClockSlots + (consumed == 0 ? 40 : 64)
+                                     : nullptr;
       if (udbg != nullptr && threadIdx.x == 0) udbg[0] = globaltimer_ns();
+      if (w_wait) {  // the weights' copy, once (a wait that runs out fails the call)
+        mbar_wait_bounded(&s_wbar, 0, f.dp.status, kFrontKernelId + 4, f.timeout_ns);
+        w_wait = false;
+      }
       if (warp < nt) {  // token tf + warp, one warp each
         const int t = tf + warp;
         const T* x = srows ? srows + (long long)warp * f.rp.hidden : (const T*)f.rp.tokens + (long long)t * f.rp.hidden;
         unsigned long long* tdbg = (udbg != nullptr && warp == 0) ? udbg + 1 : nullptr;
-        if (w_smem) router_token<T, EMAX, true>(f.rp, cbias, t, x, srows != nullptr, wts, run, tdbg, dry);
-        else router_token<T, EMAX, false>(f.rp, cbias, t, x, srows != nullptr, wts, run, tdbg, dry);
-        if (digest && !dry) {
+        if (w_smem) router_token<T, EMAX, true>(f.rp, cbias, t, x, srows != nullptr, wts, run, tdbg);
+        else router_token<T, EMAX, false>(f.rp, cbias, t, x, srows != nullptr, wts, run, tdbg);
+        if (digest) {
           const long long dg = warp_row_digest((const uint4*)x, row_bytes / 16);
           if (lane == 0) {
             f.digest_out[t] = dg;
             f.csbase_out[t] = token_checksum_base(f.dp.token_ids[t], f.dp.dims.rank, c, t - t0, t, dg);
           }
         }
-      }
       }
       __syncthreads();  // every warp is done with the unit's rows
       if (udbg != nullptr && threadIdx.x == 0) udbg[3] = globaltimer_ns();

@@ -127,7 +127,6 @@ class MoELayerRunner {
     router_wsmem_ = !ints.contains("router_wsmem") || geti(ints, "router_wsmem") != 0;
     router_tc_ = !ints.contains("router_tc") || geti(ints, "router_tc") != 0;
     gemm_ksplit_ = !ints.contains("gemm_ksplit") || geti(ints, "gemm_ksplit") != 0;
-    router_warm_ = !ints.contains("router_warm") || geti(ints, "router_warm") != 0;
     max_cands_ = geti(ints, "max_cands");
     log_stride_ = geti(ints, "log_stride");
     max_ctl_tokens_ = geti(ints, "max_ctl_tokens");
@@ -406,7 +405,6 @@ class MoELayerRunner {
       fp.ring_slots = router_ring_ ? 1 : 0;  // a request: launch_frontend sizes the ring
       fp.dispatch_groups = dispatch_groups_ ? 1 : 0;
       fp.w_off = router_wsmem_ ? 1 : 0;  // a request: launch_frontend places the weights
-      fp.warm_first = router_warm_ ? 1 : 0;
       if (have_tc_router_) {  // a request: launch_frontend sizes the stages
         fp.tc_router = 1;
         fp.tmap_x = tx_router_;
@@ -783,7 +781,6 @@ class MoELayerRunner {
   bool router_wsmem_ = true;             // router weights copied into each worker's shared memory
   bool router_tc_ = true;                // bf16 batches: tensor-core router units of 128 tokens
   bool gemm_ksplit_ = true;              // one-CTA GEMM-1: split K when the tiles are few
-  bool router_warm_ = true;              // dry first routing pass (warm instruction cache)
   bool have_tc_router_ = false;          // router tensor maps built (bf16, D % 64 == 0, E <= 64)
   int tc_used_ = 0;                      // the last front-end launch routed on the tensor cores
   CUtensorMap tx_router_{}, tw_router_{};

@@ -61,7 +61,7 @@ class ProgressiveMoELayer:
                  gemm_pair: bool = True, pdl: bool = True, gemm_swap_max: int = 128,
                  progressive: bool = False, dispatch_ctas: int = 0, router_ring: bool = True,
                  dispatch_groups: bool = True, router_wsmem: bool = True, router_tc: bool = True,
-                 gemm_ksplit: bool = True, router_warm: bool = True) -> None:
+                 gemm_ksplit: bool = True) -> None:
         self.cfg = cfg
         if world is None:
             world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -169,9 +169,6 @@ class ProgressiveMoELayer:
             "router_tc": int(bool(router_tc)),
             # one-CTA GEMM-1 with few tiles and a long K: K split over idle SMs
             "gemm_ksplit": int(bool(gemm_ksplit)),
-            # a resident batch's first routing unit runs a dry pass first, so
-            # the routing code is in the instruction cache when its rows land
-            "router_warm": int(bool(router_warm)),
         }
         self.layout = self._k.sym_layout(ints)
         self.channel = PeerChannel(self.layout["total"], dev, group=group)
